@@ -1,0 +1,193 @@
+"""Headline benchmark: output tok/s, TPOT and TTFT of the Qwen3.5-27B-shaped hybrid model
+with INT2 KV + MTP (3 drafts) at 32 concurrent 16K-token requests.
+
+    python bench.py --gpus N --steps K --warmup W          (N > 1: under torchrun, one rank per GPU)
+    python bench.py --impl reference ...                   (the reference arm)
+
+Synthetic data: uniform-random prompt tokens (seeded), random-init weights of the
+model's shape, a seeded draft-acceptance pattern with mean 2 of 3 drafts accepted.
+Timed region: exactly K engine steps (each a verify step of every request plus its
+MTP drafting) bracketed by a barrier and a device synchronisation on both sides.
+``value`` uses the device-busy time of the model's GPU work (CUDA events around every
+GPU segment, max over ranks); ``e2e`` is the wall clock of the same K calls of the
+public ``LLMEngine.step`` API, which includes building the step's metadata on the
+host, its host-to-device copies from pinned memory and the device-to-host read of
+the sampled tokens.  Every step streams all weights (27 GB at TP1), far more than
+the 126 MB L2, so no L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+METRIC = "output tok/s @32 conc, TPOT, TTFT: Qwen3.5-27B-shape TP4 INT2-KV+MTP"
+# Closest published reference figure: OSCAR generation throughput after the 8.5x
+# step fix, Qwen3.5-27B W8A8 + MTP, TP4 on 4x Ascend 910B4
+# (plan/audits/PERFORMANCE-20260908.md:76).
+BASELINE_TOK_S = 11.3
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", choices=["oscar", "reference"], default="oscar")
+    ap.add_argument("--model", default="qwen35-27b")
+    ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid for the headline)")
+    ap.add_argument("--requests", type=int, default=32)
+    ap.add_argument("--prompt-len", type=int, default=16384)
+    ap.add_argument("--output-len", type=int, default=1024)
+    ap.add_argument("--num-spec", type=int, default=3)
+    ap.add_argument("--accept-mean", type=float, default=2.0)
+    ap.add_argument("--kv", choices=["int2", "bf16"], default="int2")
+    ap.add_argument("--prefill-policy", choices=["fcfs", "wide"], default="wide")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+def reference_arm(args):
+    msg = ("reference is a vLLM-Ascend plugin (oscar-ascend 0.2.0) that hard-requires torch_npu and "
+           "vllm_ascend on Ascend NPUs; it has no CUDA serving path to run on B200")
+    print(json.dumps({"impl": "reference", "unavailable": msg, "metric": METRIC, "n_gpus": args.gpus}))
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from oscar_b200.config import OscarConfig
+    from oscar_b200.engine.engine import LLMEngine, SeededAcceptance
+    from oscar_b200.models.config import CONFIGS
+    from oscar_b200.models.qwen35 import HybridModel
+    from oscar_b200.parallel.groups import init_distributed, make_groups
+    from oscar_b200.utils import launches
+    from oscar_b200.utils.clocks import ClockSampler
+
+    rank, world, local = init_distributed(timeout_s=600)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    tp = make_groups(tp=world, dp=1)
+    overrides = {} if args.layers is None else {"num_layers": args.layers}
+    cfg = CONFIGS[args.model](**overrides)
+    oscar = OscarConfig.from_env(head_dim=cfg.head_dim)
+    t0 = time.perf_counter()
+    model = HybridModel(cfg, tp, device=dev, seed=args.seed, oscar=oscar, kv_mode=args.kv, rotation="random")
+    torch.cuda.synchronize()
+    t_init = time.perf_counter() - t0
+    R = args.requests
+    per_req = args.prompt_len + args.output_len + 16 * (args.num_spec + 2)
+    num_blocks = R * ((per_req + 127) // 128) + 64
+    acc = SeededAcceptance(args.num_spec, args.accept_mean, seed=args.seed + 1)
+    eng = LLMEngine(model, num_blocks=num_blocks, max_slots=R, num_spec=args.num_spec, acceptance=acc,
+                    prefill_policy=args.prefill_policy)
+    rng = np.random.default_rng(args.seed)
+    prompts = rng.integers(0, cfg.vocab_size, size=(R, args.prompt_len)).tolist()
+    ids = [eng.add_request(p, args.output_len) for p in prompts]
+
+    def barrier_sync():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---------------- prefill (TTFT), untimed for the throughput metric
+    barrier_sync()
+    tp0 = time.perf_counter()
+    for r in eng.requests.values():
+        r.arrival = tp0
+    while any(not eng.requests[i].output for i in ids):
+        eng.step()
+    barrier_sync()
+    t_prefill = time.perf_counter() - tp0
+    ttft = [eng.requests[i].first_token_time - eng.requests[i].arrival for i in ids]
+
+    # ---------------- warm-up decode steps
+    for _ in range(args.warmup):
+        eng.step()
+    barrier_sync()
+
+    # ---------------- timed region: exactly K steps
+    out0 = eng.stats["tokens_out"]
+    eng.record_device_time = True
+    eng.device_ms()
+    launches.reset()
+    gpu_ids = None
+    try:
+        gpu_ids = [str(torch.cuda.get_device_properties(local).uuid)]
+        gpu_ids = ["GPU-" + g if not g.startswith("GPU-") else g for g in gpu_ids]
+    except Exception:
+        gpu_ids = None
+    sampler = ClockSampler(gpu_ids if local == 0 else None)
+    with (sampler if local == 0 else _Null()):
+        barrier_sync()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        start.record()
+        for _ in range(args.steps):
+            eng.step()
+        end.record()
+        barrier_sync()
+        wall = time.perf_counter() - w0
+    span_ms = start.elapsed_time(end)
+    busy_ms = eng.device_ms()
+    n_launch = launches.count()
+    tokens = eng.stats["tokens_out"] - out0
+    # max over ranks of the timed quantities
+    t = torch.tensor([busy_ms, span_ms, wall], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    busy_ms, span_ms, wall = t.tolist()
+    value = tokens / (busy_ms / 1e3)
+    e2e = tokens / wall
+    steps_tok = tokens / args.steps / R  # output tokens per request per step
+    tpot = (busy_ms / args.steps) / steps_tok
+    mem = torch.cuda.max_memory_allocated(dev) / 2**30
+    if rank == 0:
+        clocks = sampler.summary() if local == 0 else {}
+        h2d = eng.stats.get("h2d_bytes", 0)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(busy_ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": round(value / BASELINE_TOK_S, 2), "dtype": "bf16",
+            "data": "synthetic (uniform-random prompt tokens, random-init weights, seeded acceptance pattern)",
+            "config": {"model": cfg.name, "layers": cfg.num_layers, "global_batch": R, "seq_len": args.prompt_len,
+                       "output_len": args.output_len, "parallelism": f"tp{world}", "kv": args.kv,
+                       "quantization": "W8A8 int8 linear layers, INT2 KV (FULL layers), BF16 MTP shadow KV",
+                       "mtp_drafts": args.num_spec, "accept_mean": args.accept_mean,
+                       "l2": "inputs larger than L2 (all weights streamed every step)",
+                       "baseline_value_tok_s": BASELINE_TOK_S,
+                       "baseline_source": "plan/audits/PERFORMANCE-20260908.md:76 (910B4 x4)"},
+            "tpot_ms": round(tpot, 3), "ttft_ms_mean": round(1e3 * float(np.mean(ttft)), 1),
+            "ttft_ms_max": round(1e3 * float(np.max(ttft)), 1), "prefill_s": round(t_prefill, 2),
+            "span_ms_per_step": round(span_ms / args.steps, 3), "tokens_timed": tokens,
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": eng.stats.get("h2d_bytes_step", 0),
+                    "d2h_bytes_per_step": eng.stats.get("d2h_bytes_step", 0)},
+            "gpu_launches": n_launch, "clocks": clocks, "peak_hbm_gib": round(mem, 2),
+            "init_s": round(t_init, 1),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+if __name__ == "__main__":
+    sys.exit(main())

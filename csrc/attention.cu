@@ -1,0 +1,489 @@
+// Paged multi-query GQA attention over INT2 (or BF16) KV pages, plus the
+// split-KV merge that also rotates the output back (o_rot @ R_v^T), applies the
+// sigmoid output gate and quantises the result per token for the o_proj GEMM.
+//
+// Work decomposition: one CTA per (work item, KV head).  A work item is
+// (request, 64-row block, KV token range); the 64 rows of a block are
+// (query token, head-in-group) pairs row = t * g + h, so all g query heads that
+// share a KV head read each KV tile once.  Each KV tile of 64 tokens is built in
+// shared memory as fp16 by the whole CTA from its source:
+//   * position >= prefix                  -> unquantised k/v of the current chunk
+//   * staged (owner tag == physical block) -> fp32 sink/recent staging
+//   * otherwise                            -> INT2 codes * scale + zero  (or BF16 page)
+// which reproduces the reference read semantics (paged_attention.py:136-260).
+// Scores and P.V run on the tensor cores (m16n8k16, fp32 accumulate) with an
+// online softmax; each CTA writes a normalised partial output and its LSE.
+#include "common.cuh"
+#include "params.h"
+
+namespace oscar {
+
+
+
+namespace {
+
+constexpr int kRows = 64;
+constexpr int kTile = 64;
+constexpr int kD = 256;
+constexpr int kRowBytes = kD * 2;  // fp16 row of a tile
+constexpr int kThreads = 128;
+constexpr int kPage = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+
+OSCAR_DEVICE uint32_t swz(int row, int chunk) {  // byte offset of a 16 B chunk in a 512 B row
+  return row * kRowBytes + ((chunk ^ (row & 7)) << 4);
+}
+
+OSCAR_DEVICE void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+OSCAR_DEVICE void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+OSCAR_DEVICE void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                           uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+OSCAR_DEVICE uint32_t h2_u32(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Dequantise 16 INT2 codes (one 32-bit word, code k at bits 2k) into 16 fp16.
+OSCAR_DEVICE void dequant16(uint32_t w, float s, float z, uint4& lo, uint4& hi) {
+  float v[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = fmaf((float)((w >> (2 * k)) & 3u), s, z);
+  lo.x = h2_u32(v[0], v[1]);
+  lo.y = h2_u32(v[2], v[3]);
+  lo.z = h2_u32(v[4], v[5]);
+  lo.w = h2_u32(v[6], v[7]);
+  hi.x = h2_u32(v[8], v[9]);
+  hi.y = h2_u32(v[10], v[11]);
+  hi.z = h2_u32(v[12], v[13]);
+  hi.w = h2_u32(v[14], v[15]);
+}
+
+struct TileCtx {
+  int req, hk, prefix, q0, kv_end;
+  const int* bt;
+};
+
+// Raw INT2 data of one (token, half) owned by a thread: 32 code bytes of K and of V.
+struct RawInt2 {
+  uint4 k0, k1, v0, v1;
+  float ks, kz, vs, vz;
+  int kind;  // 0 invalid, 1 int2, 2 fresh, 3 staged, 4 bf16
+  int blk, off, srow;
+};
+
+OSCAR_DEVICE void load_raw(const AttnParams& p, const TileCtx& c, int pos, int half, RawInt2& r) {
+  r.kind = 0;
+  if (pos >= c.kv_end) return;
+  if (pos >= c.prefix) {
+    r.kind = 2;
+    return;
+  }
+  const int page = pos / kPage, off = pos % kPage;
+  const int blk = c.bt[page];
+  r.blk = blk;
+  r.off = off;
+  if (p.stage_rows > 0) {
+    const int row = blk % p.stage_rows;
+    if (p.owner[row * kPage + off] == blk) {
+      r.kind = 3;
+      r.srow = row;
+      return;
+    }
+  }
+  if (p.kv_mode == 1) {
+    r.kind = 4;
+    return;
+  }
+  r.kind = 1;
+  const uint8_t* pg = p.pool + ((long long)blk * p.Hk + c.hk) * p.page_bytes;
+  const int cb = p.D / 4;  // 64
+  const uint4* kp = reinterpret_cast<const uint4*>(pg + off * cb + half * (cb / 2));
+  const uint4* vp = reinterpret_cast<const uint4*>(pg + kPage * cb + off * cb + half * (cb / 2));
+  r.k0 = __ldg(kp);
+  r.k1 = __ldg(kp + 1);
+  r.v0 = __ldg(vp);
+  r.v1 = __ldg(vp + 1);
+  const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * cb);
+  r.ks = __half2float(meta[off]);
+  r.kz = __half2float(meta[kPage + off]);
+  r.vs = __half2float(meta[2 * kPage + off]);
+  r.vz = __half2float(meta[3 * kPage + off]);
+}
+
+// Write one thread's (token, half) = 128 dims of K and V into the fp16 tiles.
+OSCAR_DEVICE void store_tile(const AttnParams& p, const TileCtx& c, int tok, int pos, int half,
+                             const RawInt2& r, uint8_t* ks, uint8_t* vs) {
+  const int d0 = half * 128;
+  const int chunk0 = d0 / 8;
+  if (r.kind == 1) {
+    const uint32_t kw[8] = {r.k0.x, r.k0.y, r.k0.z, r.k0.w, r.k1.x, r.k1.y, r.k1.z, r.k1.w};
+    const uint32_t vw[8] = {r.v0.x, r.v0.y, r.v0.z, r.v0.w, r.v1.x, r.v1.y, r.v1.z, r.v1.w};
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      uint4 lo, hi;
+      dequant16(kw[w], r.ks, r.kz, lo, hi);
+      *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + 2 * w)) = lo;
+      *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + 2 * w + 1)) = hi;
+      dequant16(vw[w], r.vs, r.vz, lo, hi);
+      *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + 2 * w)) = lo;
+      *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + 2 * w + 1)) = hi;
+    }
+    return;
+  }
+  if (r.kind == 0) {
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + j)) = zero;
+      *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + j)) = zero;
+    }
+    return;
+  }
+  if (r.kind == 2) {
+    const long long t = c.q0 + (pos - c.prefix);
+    const uint4* kf = reinterpret_cast<const uint4*>(p.k_fresh + (t * p.Hk + c.hk) * p.D + d0);
+    const uint4* vf = reinterpret_cast<const uint4*>(p.v_fresh + (t * p.Hk + c.hk) * p.D + d0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + j)) = __ldg(kf + j);
+      *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + j)) = __ldg(vf + j);
+    }
+    return;
+  }
+  if (r.kind == 3) {
+    const long long base = ((long long)(r.srow * kPage + r.off) * p.Hk + c.hk) * p.D + d0;
+    const float4* kf = reinterpret_cast<const float4*>(p.stage_k + base);
+    const float4* vf = reinterpret_cast<const float4*>(p.stage_v + base);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float4 a = __ldg(kf + 2 * j), b = __ldg(kf + 2 * j + 1);
+      *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + j)) =
+          make_uint4(h2_u32(a.x, a.y), h2_u32(a.z, a.w), h2_u32(b.x, b.y), h2_u32(b.z, b.w));
+      const float4 e = __ldg(vf + 2 * j), f = __ldg(vf + 2 * j + 1);
+      *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + j)) =
+          make_uint4(h2_u32(e.x, e.y), h2_u32(e.z, e.w), h2_u32(f.x, f.y), h2_u32(f.z, f.w));
+    }
+    return;
+  }
+  // kind 4: BF16 page
+  const long long base = ((long long)(r.blk * kPage + r.off) * p.Hk + c.hk) * p.D + d0;
+  const uint4* kb = reinterpret_cast<const uint4*>(p.kc + base);
+  const uint4* vb = reinterpret_cast<const uint4*>(p.vc + base);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    uint4 a = __ldg(kb + j), b = __ldg(vb + j);
+    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+    uint4 ka, va;
+    uint32_t* pka = reinterpret_cast<uint32_t*>(&ka);
+    uint32_t* pva = reinterpret_cast<uint32_t*>(&va);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 fa = __bfloat1622float2(pa[e]);
+      const float2 fb = __bfloat1622float2(pb[e]);
+      pka[e] = h2_u32(fa.x, fa.y);
+      pva[e] = h2_u32(fb.x, fb.y);
+    }
+    *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + j)) = ka;
+    *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + j)) = va;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 2) paged_attention_kernel(AttnParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* qs = smem;                       // [64][256] fp16
+  uint8_t* ks = smem + kRows * kRowBytes;   // [64][256]
+  uint8_t* vs = ks + kTile * kRowBytes;     // [64][256]
+  const int item = blockIdx.x, hk = blockIdx.y;
+  const int4 w = p.work[item];
+  const int req = w.x, row0 = w.y, kv_begin = w.z, kv_end_item = w.w;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = p.Hq / p.Hk;
+  const int q0 = p.q_start[req];
+  const int qlen = p.q_start[req + 1] - q0;
+  const int seq = p.seq_lens[req];
+  TileCtx c;
+  c.req = req;
+  c.hk = hk;
+  c.prefix = seq - qlen;
+  c.q0 = q0;
+  c.kv_end = kv_end_item;
+  c.bt = p.block_tables + (long long)req * p.bt_stride;
+
+  // ---- Q tile -----------------------------------------------------------------------
+  for (int idx = tid; idx < kRows * 32; idx += kThreads) {
+    const int r = idx >> 5, ch = idx & 31;
+    const int gr = row0 + r;
+    const int t = gr / g, h = gr % g;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < qlen) v = __ldg(reinterpret_cast<const uint4*>(p.q + ((long long)(q0 + t) * p.Hq + hk * g + h) * kD) + ch);
+    *reinterpret_cast<uint4*>(qs + swz(r, ch)) = v;
+  }
+
+  // Per-thread row bookkeeping: rows ra = warp*16 + lane/4 and rb = ra + 8.
+  const int ra = warp * 16 + (lane >> 2), rb = ra + 8;
+  const int ta = (row0 + ra) / g, tb = (row0 + rb) / g;
+  const int lim_a = ta < qlen ? c.prefix + ta : -1;  // last visible key position
+  const int lim_b = tb < qlen ? c.prefix + tb : -1;
+  const float sl2 = p.scale * kLog2e;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  float o[32][4];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+
+  const uint32_t qs_a = smem_u32(qs), ks_a = smem_u32(ks), vs_a = smem_u32(vs);
+
+  // Highest key position any row of this block may see.
+  int row_last = min(row0 + kRows, qlen * g) - 1;
+  const int kv_stop = min(kv_end_item, row_last >= 0 ? c.prefix + row_last / g + 1 : 0);
+  c.kv_end = kv_stop;
+  const int ntiles = kv_stop > kv_begin ? (kv_stop - kv_begin + kTile - 1) / kTile : 0;
+
+  const int my_tok = tid >> 1, my_half = tid & 1;
+  RawInt2 raw;
+  if (ntiles > 0) load_raw(p, c, kv_begin + my_tok, my_half, raw);
+
+  for (int it = 0; it < ntiles; ++it) {
+    const int tile0 = kv_begin + it * kTile;
+    __syncthreads();  // previous tile fully consumed
+    store_tile(p, c, my_tok, tile0 + my_tok, my_half, raw, ks, vs);
+    __syncthreads();
+    if (it + 1 < ntiles) load_raw(p, c, tile0 + kTile + my_tok, my_half, raw);
+
+    // ---- S = Q K^T for this warp's 16 rows x 64 tokens ----
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      {
+        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int ch = 2 * kk + (lane >> 4);
+        ldsm_x4(qs_a + swz(r, ch), a0, a1, a2, a3);
+      }
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int tr = np * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int ch = 2 * kk + ((lane >> 3) & 1);
+        ldsm_x4(ks_a + swz(tr, ch), b0, b1, b2, b3);
+        mma16816(s[2 * np], a0, a1, a2, a3, b0, b1);
+        mma16816(s[2 * np + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // ---- online softmax ----
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int pos = tile0 + j * 8 + 2 * (lane & 3);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int pp = pos + e;
+        const bool va = pp <= lim_a && pp < kv_stop;
+        const bool vb = pp <= lim_b && pp < kv_stop;
+        s[j][e] = va ? s[j][e] * sl2 : -INFINITY;
+        s[j][2 + e] = vb ? s[j][2 + e] * sl2 : -INFINITY;
+        mx_a = fmaxf(mx_a, s[j][e]);
+        mx_b = fmaxf(mx_b, s[j][2 + e]);
+      }
+    }
+#pragma unroll
+    for (int o2 = 1; o2 <= 2; o2 <<= 1) {
+      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o2));
+      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o2));
+    }
+    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+    const float base_a = mn_a == -INFINITY ? 0.f : mn_a;
+    const float base_b = mn_b == -INFINITY ? 0.f : mn_b;
+    const float ca = exp2f(m_a - base_a), cb = exp2f(m_b - base_b);
+    float sum_a = 0.f, sum_b = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      s[j][0] = exp2f(s[j][0] - base_a);
+      s[j][1] = exp2f(s[j][1] - base_a);
+      s[j][2] = exp2f(s[j][2] - base_b);
+      s[j][3] = exp2f(s[j][3] - base_b);
+      sum_a += s[j][0] + s[j][1];
+      sum_b += s[j][2] + s[j][3];
+    }
+    l_a = l_a * ca + sum_a;
+    l_b = l_b * cb + sum_b;
+    m_a = mn_a;
+    m_b = mn_b;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      o[j][0] *= ca;
+      o[j][1] *= ca;
+      o[j][2] *= cb;
+      o[j][3] *= cb;
+    }
+    // ---- O += P V ----
+#pragma unroll
+    for (int sg = 0; sg < 4; ++sg) {
+      const uint32_t a0 = h2_u32(s[2 * sg][0], s[2 * sg][1]);
+      const uint32_t a1 = h2_u32(s[2 * sg][2], s[2 * sg][3]);
+      const uint32_t a2 = h2_u32(s[2 * sg + 1][0], s[2 * sg + 1][1]);
+      const uint32_t a3 = h2_u32(s[2 * sg + 1][2], s[2 * sg + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < 16; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        const int tr = sg * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int ch = 2 * dp + (lane >> 4);
+        ldsm_x4_t(vs_a + swz(tr, ch), b0, b1, b2, b3);
+        mma16816(o[2 * dp], a0, a1, a2, a3, b0, b1);
+        mma16816(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+  }
+
+  // ---- finalise: row sums across the 4 lanes of a row, normalise, write partials ----
+#pragma unroll
+  for (int o2 = 1; o2 <= 2; o2 <<= 1) {
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, o2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, o2);
+  }
+  const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f;
+  const float inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
+  float* po = p.part_o + ((long long)item * p.Hk + hk) * kRows * kD;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int d = j * 8 + 2 * (lane & 3);
+    *reinterpret_cast<float2*>(po + ra * kD + d) = make_float2(o[j][0] * inv_a, o[j][1] * inv_a);
+    *reinterpret_cast<float2*>(po + rb * kD + d) = make_float2(o[j][2] * inv_b, o[j][3] * inv_b);
+  }
+  if ((lane & 3) == 0) {
+    float* pl = p.part_lse + ((long long)item * p.Hk + hk) * kRows;
+    pl[ra] = l_a > 0.f ? (m_a + log2f(l_a)) / kLog2e : -INFINITY;
+    pl[rb] = l_b > 0.f ? (m_b + log2f(l_b)) / kLog2e : -INFINITY;
+  }
+}
+
+// ------------------------------------------------------------------ merge
+// One CTA (256 threads, thread = output dim) per query token.
+__global__ void __launch_bounds__(256) attn_merge_kernel(MergeParams p) {
+  extern __shared__ float msm[];
+  float* orot = msm;  // [Hq][D]
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int D = p.D, Hq = p.Hq, g = p.Hq / p.Hk;
+  const int req = p.tok_req[t];
+  const int tt = t - p.q_start[req];
+  // combine the split partials of every head
+  for (int h = 0; h < Hq; ++h) {
+    const int hk = h / g, hg = h % g;
+    const int row = tt * g + hg;
+    const int rb = row / kRows, r = row % kRows;
+    const int first = p.item_first[req * p.max_rb + rb];
+    const int cnt = p.item_count[req * p.max_rb + rb];
+    float mx = -INFINITY;
+    for (int s = 0; s < cnt; ++s) mx = fmaxf(mx, p.part_lse[((long long)(first + s) * p.Hk + hk) * kRows + r]);
+    float acc = 0.f, wsum = 0.f;
+    if (mx > -INFINITY) {
+      for (int s = 0; s < cnt; ++s) {
+        const long long base = ((long long)(first + s) * p.Hk + hk) * kRows + r;
+        const float wgt = __expf(p.part_lse[base] - mx);
+        wsum += wgt;
+        if (tid < D) acc = fmaf(wgt, p.part_o[base * kD + tid], acc);
+      }
+    }
+    if (tid < D) orot[h * D + tid] = wsum > 0.f ? acc / wsum : 0.f;
+  }
+  __syncthreads();
+  // rotate back (o = o_rot @ R_v^T), gate, and collect the token's absmax
+  float amax = 0.f;
+  constexpr int kHB = 8;
+  for (int h0 = 0; h0 < Hq; h0 += kHB) {
+    float acc[kHB];
+#pragma unroll
+    for (int j = 0; j < kHB; ++j) acc[j] = 0.f;
+    const int nh = min(kHB, Hq - h0);
+    if (tid < D) {
+      if (p.RvT) {
+        for (int i = 0; i < D; ++i) {
+          const float rv = __ldg(p.RvT + (long long)i * D + tid);
+#pragma unroll
+          for (int j = 0; j < kHB; ++j)
+            if (j < nh) acc[j] = fmaf(orot[(h0 + j) * D + i], rv, acc[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kHB; ++j)
+          if (j < nh) acc[j] = orot[(h0 + j) * D + tid];
+      }
+#pragma unroll
+      for (int j = 0; j < kHB; ++j) {
+        if (j >= nh) break;
+        float v = acc[j];
+        if (p.gate) v *= sigmoidf_(__bfloat162float(p.gate[(long long)t * p.gate_ld + (h0 + j) * p.gate_hstride + tid]));
+        // round like a bf16 activation before quantisation
+        v = __bfloat162float(__float2bfloat16(v));
+        acc[j] = v;
+        amax = fmaxf(amax, fabsf(v));
+        if (p.out_bf16) p.out_bf16[(long long)t * Hq * D + (h0 + j) * D + tid] = __float2bfloat16(v);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kHB; ++j)
+      if (j < nh && tid < D) orot[(h0 + j) * D + tid] = acc[j];
+    __syncthreads();
+  }
+  if (p.out_i8) {
+    amax = block_max<8>(amax, red);
+    const float sc = amax > 0.f ? amax / 127.f : 1.f;
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+    if (tid < D)
+      for (int h = 0; h < Hq; ++h) p.out_i8[(long long)t * Hq * D + h * D + tid] = quant_i8(orot[h * D + tid], inv);
+    if (tid == 0) p.out_scale[t] = sc;
+  }
+}
+
+}  // namespace
+}  // namespace oscar
+
+extern "C" int oscar_paged_attention(const oscar::AttnParams* params, cudaStream_t stream) {
+  using namespace oscar;
+  const AttnParams& p = *params;
+  if (p.n_work <= 0) return 0;
+  if (p.D != kD) return -300;
+  const size_t smem = (kRows + 2 * kTile) * kRowBytes;
+  static bool attr = false;
+  if (!attr) {
+    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = true;
+  }
+  dim3 grid(p.n_work, p.Hk);
+  paged_attention_kernel<<<grid, kThreads, smem, stream>>>(p);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int oscar_attn_merge(const oscar::MergeParams* params, cudaStream_t stream) {
+  using namespace oscar;
+  const MergeParams& p = *params;
+  if (p.T <= 0) return 0;
+  if (p.D != kD) return -301;
+  const size_t smem = (size_t)p.Hq * p.D * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(attn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr = true;
+  }
+  attn_merge_kernel<<<p.T, 256, smem, stream>>>(p);
+  return (int)cudaGetLastError();
+}

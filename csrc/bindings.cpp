@@ -1,0 +1,343 @@
+// torch bindings of the sm_100a kernels.  Every entry point checks devices,
+// dtypes and contiguity, launches on the current CUDA stream and raises on a
+// launch error.  There is no CPU fallback here: the Python layer uses the
+// pure-torch oracle only for CPU tensors.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "params.h"
+
+extern "C" {
+int oscar_gemm_i8(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                  const float* scale_a, const float* scale_b, void* out, long long ldo, int mode, int trans, int bn,
+                  int splits, int* status, cudaStream_t stream);
+int oscar_num_sms();
+int oscar_kv_store(const oscar::StoreParams* p, cudaStream_t stream);
+int oscar_paged_attention(const oscar::AttnParams* p, cudaStream_t stream);
+int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
+int oscar_gdn_step(const oscar::GdnParams* p, int smem_state, cudaStream_t stream);
+int oscar_rmsnorm_quant(float* x, long long ldx, const float* delta, long long ldd, const float* w, float off,
+                        float eps, int T, int H, int8_t* out, float* scale, __nv_bfloat16* out_bf16, cudaStream_t s);
+int oscar_swiglu_quant(const __nv_bfloat16* gu, long long ld, int T, int I, int8_t* out, float* scale,
+                       cudaStream_t s);
+int oscar_act_quant(const __nv_bfloat16* x, long long ld, int T, int K, int8_t* out, float* scale, cudaStream_t s);
+int oscar_embed(const int* tok, const __nv_bfloat16* table, int T, int H, int vocab_begin, int vocab_end, float* out,
+                cudaStream_t s);
+int oscar_argmax(const __nv_bfloat16* logits, long long ld, int T, int V, int index_offset, float* best_val,
+                 int* best_idx, cudaStream_t s);
+int oscar_f32_to_bf16(const float* x, long long n, __nv_bfloat16* y, cudaStream_t s);
+}
+
+namespace {
+
+using at::Tensor;
+using c10::optional;
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define CHECK_DTYPE(x, dt) TORCH_CHECK((x).scalar_type() == (dt), #x " has dtype ", (x).scalar_type(), ", expected ", (dt))
+
+template <typename T>
+T* ptr(const Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+template <typename T>
+T* optr(const optional<Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+void check_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, what, " failed with code ", rc,
+              rc > 0 ? std::string(" (") + cudaGetErrorString((cudaError_t)rc) + ")" : std::string());
+}
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void gemm_i8(const Tensor& A, const Tensor& B, const Tensor& scale_a, const Tensor& scale_b, Tensor& out, int64_t mode,
+             int64_t trans, int64_t bn, int64_t splits, const optional<Tensor>& status) {
+  CHECK_CUDA(A);
+  CHECK_CUDA(B);
+  CHECK_DTYPE(A, at::kChar);
+  CHECK_DTYPE(B, at::kChar);
+  CHECK_DTYPE(scale_a, at::kFloat);
+  CHECK_DTYPE(scale_b, at::kFloat);
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_i8: A [M,K], B [N,K]");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_i8: K must be contiguous");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  TORCH_CHECK(scale_a.numel() >= M && scale_b.numel() >= N, "gemm_i8: scale sizes");
+  if (mode == 0) {
+    CHECK_DTYPE(out, at::kBFloat16);
+  } else {
+    CHECK_DTYPE(out, at::kFloat);
+  }
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "gemm_i8: out must be row-major 2-D");
+  if (trans) {
+    TORCH_CHECK(out.size(0) >= N && out.size(1) >= M, "gemm_i8: out shape (transposed)");
+  } else {
+    TORCH_CHECK(out.size(0) >= M && out.size(1) >= N, "gemm_i8: out shape");
+  }
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_rc(oscar_gemm_i8(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), M, N, K, ptr<float>(scale_a),
+                         ptr<float>(scale_b), out.data_ptr(), out.stride(0), (int)mode, (int)trans, (int)bn,
+                         (int)splits, optr<int>(status), stream()),
+           "gemm_i8");
+}
+
+int64_t num_sms() { return oscar_num_sms(); }
+
+void kv_store(const Tensor& qkv, int64_t q_off, int64_t q_head_stride, int64_t k_off, int64_t v_off, int64_t Hq,
+              int64_t Hk, int64_t D, const optional<Tensor>& q_norm_w, const optional<Tensor>& k_norm_w, double eps,
+              double norm_offset, const Tensor& positions, const optional<Tensor>& rope_cos,
+              const optional<Tensor>& rope_sin, int64_t rot_dim, const optional<Tensor>& Rk,
+              const optional<Tensor>& Rv, int64_t k_clip_idx, int64_t v_clip_idx, Tensor& q_out, Tensor& k_fresh,
+              Tensor& v_fresh, int64_t kv_mode, const optional<Tensor>& pool, const optional<Tensor>& kc,
+              const optional<Tensor>& vc, const Tensor& slots, const optional<Tensor>& stage_k,
+              const optional<Tensor>& stage_v, const optional<Tensor>& stage_seat, const optional<Tensor>& owner,
+              const optional<Tensor>& owner_seat, const optional<Tensor>& owner_val, const optional<Tensor>& status) {
+  CHECK_CUDA(qkv);
+  CHECK_DTYPE(qkv, at::kBFloat16);
+  TORCH_CHECK(qkv.stride(1) == 1, "qkv rows must be contiguous");
+  CHECK_DTYPE(q_out, at::kHalf);
+  CHECK_DTYPE(k_fresh, at::kHalf);
+  CHECK_DTYPE(slots, at::kInt);
+  CHECK_DTYPE(positions, at::kInt);
+  if (kv_mode == 0) {
+    TORCH_CHECK(pool.has_value() && pool->scalar_type() == at::kByte && pool->is_contiguous(), "INT2 pool");
+  } else {
+    TORCH_CHECK(kc.has_value() && kc->scalar_type() == at::kBFloat16 && kc->is_contiguous(), "BF16 pool");
+  }
+  oscar::StoreParams p{};
+  p.qkv = ptr<__nv_bfloat16>(qkv);
+  p.ld_qkv = qkv.stride(0);
+  p.q_off = q_off;
+  p.q_head_stride = q_head_stride;
+  p.k_off = k_off;
+  p.v_off = v_off;
+  p.Hq = Hq;
+  p.Hk = Hk;
+  p.D = D;
+  p.q_norm_w = optr<float>(q_norm_w);
+  p.k_norm_w = optr<float>(k_norm_w);
+  p.eps = eps;
+  p.norm_offset = norm_offset;
+  p.positions = ptr<int>(positions);
+  p.rope_cos = optr<float>(rope_cos);
+  p.rope_sin = optr<float>(rope_sin);
+  p.rot_dim = rot_dim;
+  p.Rk = optr<float>(Rk);
+  p.Rv = optr<float>(Rv);
+  p.k_clip_idx = k_clip_idx;
+  p.v_clip_idx = v_clip_idx;
+  p.q_out = ptr<__half>(q_out);
+  p.k_fresh = ptr<__half>(k_fresh);
+  p.v_fresh = ptr<__half>(v_fresh);
+  p.kv_mode = kv_mode;
+  p.pool = optr<uint8_t>(pool);
+  p.page_bytes = kv_mode == 0 ? pool->size(2) : 0;
+  p.kc = optr<__nv_bfloat16>(kc);
+  p.vc = optr<__nv_bfloat16>(vc);
+  p.slots = ptr<int>(slots);
+  p.stage_k = optr<float>(stage_k);
+  p.stage_v = optr<float>(stage_v);
+  p.stage_seat = optr<int>(stage_seat);
+  p.owner = optr<int>(owner);
+  p.owner_seat = optr<int>(owner_seat);
+  p.owner_val = optr<int>(owner_val);
+  p.n_owner = owner_seat.has_value() && owner_seat->defined() ? owner_seat->numel() : 0;
+  p.T = qkv.size(0);
+  p.status = optr<int>(status);
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  check_rc(oscar_kv_store(&p, stream()), "kv_store");
+}
+
+void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fresh, int64_t Hq, int64_t Hk, int64_t D,
+                     double scale, int64_t kv_mode, const optional<Tensor>& pool, const optional<Tensor>& kc,
+                     const optional<Tensor>& vc, const optional<Tensor>& stage_k, const optional<Tensor>& stage_v,
+                     const optional<Tensor>& owner, int64_t stage_rows, const Tensor& block_tables,
+                     const Tensor& q_start, const Tensor& seq_lens, const Tensor& work, Tensor& part_o,
+                     Tensor& part_lse, const optional<Tensor>& status) {
+  CHECK_CUDA(q);
+  CHECK_DTYPE(q, at::kHalf);
+  CHECK_DTYPE(k_fresh, at::kHalf);
+  CHECK_DTYPE(block_tables, at::kInt);
+  CHECK_DTYPE(work, at::kInt);
+  CHECK_CONTIG(q);
+  CHECK_CONTIG(k_fresh);
+  CHECK_CONTIG(v_fresh);
+  CHECK_CONTIG(block_tables);
+  oscar::AttnParams p{};
+  p.q = ptr<__half>(q);
+  p.k_fresh = ptr<__half>(k_fresh);
+  p.v_fresh = ptr<__half>(v_fresh);
+  p.Hq = Hq;
+  p.Hk = Hk;
+  p.D = D;
+  p.scale = scale;
+  p.kv_mode = kv_mode;
+  p.pool = optr<uint8_t>(pool);
+  p.page_bytes = pool.has_value() && pool->defined() ? pool->size(2) : 0;
+  p.kc = optr<__nv_bfloat16>(kc);
+  p.vc = optr<__nv_bfloat16>(vc);
+  p.stage_k = optr<float>(stage_k);
+  p.stage_v = optr<float>(stage_v);
+  p.owner = optr<int>(owner);
+  p.stage_rows = stage_rows;
+  p.block_tables = ptr<int>(block_tables);
+  p.bt_stride = block_tables.stride(0);
+  p.q_start = ptr<int>(q_start);
+  p.seq_lens = ptr<int>(seq_lens);
+  p.work = reinterpret_cast<const int4*>(work.data_ptr());
+  p.n_work = work.size(0);
+  p.part_o = ptr<float>(part_o);
+  p.part_lse = ptr<float>(part_lse);
+  p.status = optr<int>(status);
+  TORCH_CHECK(part_o.numel() >= (int64_t)p.n_work * Hk * 64 * D, "part_o too small");
+  const c10::cuda::CUDAGuard guard(q.device());
+  check_rc(oscar_paged_attention(&p, stream()), "paged_attention");
+}
+
+void attn_merge(const Tensor& part_o, const Tensor& part_lse, const Tensor& item_first, const Tensor& item_count,
+                int64_t max_rb, const Tensor& tok_req, const Tensor& q_start, int64_t Hq, int64_t Hk, int64_t D,
+                const optional<Tensor>& RvT, const optional<Tensor>& gate, int64_t gate_ld, int64_t gate_hstride,
+                const optional<Tensor>& out_bf16, const optional<Tensor>& out_i8, const optional<Tensor>& out_scale,
+                int64_t T) {
+  oscar::MergeParams p{};
+  p.part_o = ptr<float>(part_o);
+  p.part_lse = ptr<float>(part_lse);
+  p.item_first = ptr<int>(item_first);
+  p.item_count = ptr<int>(item_count);
+  p.max_rb = max_rb;
+  p.tok_req = ptr<int>(tok_req);
+  p.q_start = ptr<int>(q_start);
+  p.Hq = Hq;
+  p.Hk = Hk;
+  p.D = D;
+  p.RvT = optr<float>(RvT);
+  p.gate = optr<__nv_bfloat16>(gate);
+  p.gate_ld = gate_ld;
+  p.gate_hstride = gate_hstride;
+  p.out_bf16 = optr<__nv_bfloat16>(out_bf16);
+  p.out_i8 = optr<int8_t>(out_i8);
+  p.out_scale = optr<float>(out_scale);
+  p.T = T;
+  const c10::cuda::CUDAGuard guard(part_o.device());
+  check_rc(oscar_attn_merge(&p, stream()), "attn_merge");
+}
+
+void gdn_step(const Tensor& qkvz, const Tensor& ba, int64_t Hk, int64_t Hv, int64_t dk, int64_t dv,
+              const Tensor& conv_w, const Tensor& A_log, const Tensor& dt_bias, const Tensor& norm_w, double eps,
+              Tensor& state, Tensor& conv_state, Tensor& pend_x, Tensor& pend_ba, const Tensor& parity,
+              const Tensor& req_slot, const Tensor& q_start, const Tensor& n_commit, const Tensor& keep_pending,
+              Tensor& out, int64_t smem_state, const optional<Tensor>& status) {
+  CHECK_DTYPE(qkvz, at::kBFloat16);
+  CHECK_DTYPE(state, at::kBFloat16);
+  CHECK_DTYPE(conv_state, at::kBFloat16);
+  TORCH_CHECK(qkvz.stride(1) == 1 && ba.stride(1) == 1, "gdn_step: rows must be contiguous");
+  oscar::GdnParams p{};
+  p.qkvz = ptr<__nv_bfloat16>(qkvz);
+  p.ld_qkvz = qkvz.stride(0);
+  p.ba = ptr<__nv_bfloat16>(ba);
+  p.ld_ba = ba.stride(0);
+  p.Hk = Hk;
+  p.Hv = Hv;
+  p.dk = dk;
+  p.dv = dv;
+  p.conv_w = ptr<float>(conv_w);
+  p.A_log = ptr<float>(A_log);
+  p.dt_bias = ptr<float>(dt_bias);
+  p.norm_w = ptr<float>(norm_w);
+  p.eps = eps;
+  p.state = ptr<__nv_bfloat16>(state);
+  p.conv_state = ptr<__nv_bfloat16>(conv_state);
+  p.pend_x = ptr<__nv_bfloat16>(pend_x);
+  p.pend_ba = ptr<__nv_bfloat16>(pend_ba);
+  p.parity = ptr<int>(parity);
+  p.slots = state.size(0);
+  p.P = pend_ba.size(1);
+  p.req_slot = ptr<int>(req_slot);
+  p.q_start = ptr<int>(q_start);
+  p.n_commit = ptr<int>(n_commit);
+  p.keep_pending = ptr<int>(keep_pending);
+  p.out = ptr<__nv_bfloat16>(out);
+  p.R = req_slot.numel();
+  p.status = optr<int>(status);
+  const c10::cuda::CUDAGuard guard(qkvz.device());
+  check_rc(oscar_gdn_step(&p, (int)smem_state, stream()), "gdn_step");
+}
+
+void rmsnorm_quant(Tensor& x, const optional<Tensor>& delta, const Tensor& w, double off, double eps,
+                   const optional<Tensor>& out, const optional<Tensor>& scale, const optional<Tensor>& out_bf16) {
+  CHECK_DTYPE(x, at::kFloat);
+  CHECK_DTYPE(w, at::kFloat);
+  TORCH_CHECK(x.stride(1) == 1, "rmsnorm_quant: rows must be contiguous");
+  const bool has_d = delta.has_value() && delta->defined();
+  if (has_d) TORCH_CHECK(delta->scalar_type() == at::kFloat && delta->stride(1) == 1, "delta must be fp32 rows");
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(oscar_rmsnorm_quant(ptr<float>(x), x.stride(0), optr<float>(delta), has_d ? delta->stride(0) : 0,
+                               ptr<float>(w), off, eps, x.size(0), x.size(1), optr<int8_t>(out), optr<float>(scale),
+                               optr<__nv_bfloat16>(out_bf16), stream()),
+           "rmsnorm_quant");
+}
+
+void swiglu_quant(const Tensor& gu, int64_t I, Tensor& out, Tensor& scale) {
+  CHECK_DTYPE(gu, at::kBFloat16);
+  TORCH_CHECK(gu.stride(1) == 1, "swiglu_quant: rows must be contiguous");
+  const c10::cuda::CUDAGuard guard(gu.device());
+  check_rc(oscar_swiglu_quant(ptr<__nv_bfloat16>(gu), gu.stride(0), gu.size(0), I, ptr<int8_t>(out),
+                              ptr<float>(scale), stream()),
+           "swiglu_quant");
+}
+
+void act_quant(const Tensor& x, Tensor& out, Tensor& scale) {
+  CHECK_DTYPE(x, at::kBFloat16);
+  TORCH_CHECK(x.stride(1) == 1, "act_quant: rows must be contiguous");
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(oscar_act_quant(ptr<__nv_bfloat16>(x), x.stride(0), x.size(0), x.size(1), ptr<int8_t>(out),
+                           ptr<float>(scale), stream()),
+           "act_quant");
+}
+
+void embed(const Tensor& tok, const Tensor& table, int64_t vocab_begin, int64_t vocab_end, Tensor& out) {
+  CHECK_DTYPE(tok, at::kInt);
+  CHECK_DTYPE(table, at::kBFloat16);
+  CHECK_DTYPE(out, at::kFloat);
+  const c10::cuda::CUDAGuard guard(tok.device());
+  check_rc(oscar_embed(ptr<int>(tok), ptr<__nv_bfloat16>(table), tok.numel(), table.size(1), vocab_begin, vocab_end,
+                       ptr<float>(out), stream()),
+           "embed");
+}
+
+void argmax(const Tensor& logits, int64_t index_offset, Tensor& best_val, Tensor& best_idx) {
+  CHECK_DTYPE(logits, at::kBFloat16);
+  TORCH_CHECK(logits.stride(1) == 1, "argmax: rows must be contiguous");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  check_rc(oscar_argmax(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), logits.size(1), index_offset,
+                        ptr<float>(best_val), ptr<int>(best_idx), stream()),
+           "argmax");
+}
+
+void f32_to_bf16(const Tensor& x, Tensor& y) {
+  CHECK_CONTIG(x);
+  CHECK_CONTIG(y);
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(oscar_f32_to_bf16(ptr<float>(x), x.numel(), ptr<__nv_bfloat16>(y), stream()), "f32_to_bf16");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "oscar_b200 sm_100a kernels";
+  m.def("gemm_i8", &gemm_i8);
+  m.def("num_sms", &num_sms);
+  m.def("kv_store", &kv_store);
+  m.def("paged_attention", &paged_attention);
+  m.def("attn_merge", &attn_merge);
+  m.def("gdn_step", &gdn_step);
+  m.def("rmsnorm_quant", &rmsnorm_quant);
+  m.def("swiglu_quant", &swiglu_quant);
+  m.def("act_quant", &act_quant);
+  m.def("embed", &embed);
+  m.def("argmax", &argmax);
+  m.def("f32_to_bf16", &f32_to_bf16);
+}

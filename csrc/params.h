@@ -1,0 +1,129 @@
+// Launch-parameter structs shared by the CUDA kernels and the torch bindings.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace oscar {
+struct GemmEpi {
+  const float* scale_a;  // [M]
+  const float* scale_b;  // [N]
+  void* out;
+  long long ldo;         // elements between consecutive output rows
+  int mode;              // 0: bf16 store, 1: fp32 atomic add, 2: fp32 store
+  int trans;             // 0: out[m * ldo + n], 1: out[n * ldo + m]
+};
+
+struct StoreParams {
+  const __nv_bfloat16* qkv;
+  long long ld_qkv;
+  int q_off, q_head_stride, k_off, v_off;
+  int Hq, Hk, D;
+  const float* q_norm_w;  // [D] or nullptr (no norm)
+  const float* k_norm_w;
+  float eps;
+  float norm_offset;  // 1.0 for x * (1 + w)
+  const int* positions;  // [T]
+  const float* rope_cos;  // [max_pos, rot_dim/2]
+  const float* rope_sin;
+  int rot_dim;
+  const float* Rk;  // [D, D] or nullptr (identity)
+  const float* Rv;
+  int k_clip_idx, v_clip_idx;  // ascending-sort index of the clip threshold, -1 = no clip
+  __half* q_out;    // [T, Hq, D]
+  __half* k_fresh;  // [T, Hk, D]
+  __half* v_fresh;
+  int kv_mode;      // 0: INT2 pool, 1: BF16 pool (kc / vc, no quantisation)
+  uint8_t* pool;    // [blocks, Hk, page_bytes]
+  int page_bytes;
+  __nv_bfloat16* kc;  // [blocks, 128, Hk, D]
+  __nv_bfloat16* vc;
+  const int* slots;  // [T]
+  float* stage_k;    // [rows * 128, Hk, D]
+  float* stage_v;
+  const int* stage_seat;  // [T]: seat if this token is kept and wins its seat, else -1
+  int* owner;             // [rows * 128]
+  const int* owner_seat;  // [n_owner]
+  const int* owner_val;
+  int n_owner;
+  int T;
+  int* status;
+};
+
+struct AttnParams {
+  const __half* q;  // [T, Hq, D]
+  const __half* k_fresh;
+  const __half* v_fresh;  // [T, Hk, D]
+  int Hq, Hk, D;
+  float scale;
+  int kv_mode;  // 0: INT2 pool, 1: BF16 pool
+  const uint8_t* pool;
+  int page_bytes;
+  const __nv_bfloat16* kc;  // [blocks, 128, Hk, D]
+  const __nv_bfloat16* vc;
+  const float* stage_k;  // [rows * 128, Hk, D]
+  const float* stage_v;
+  const int* owner;  // [rows * 128]
+  int stage_rows;    // 0: staging disabled
+  const int* block_tables;
+  int bt_stride;
+  const int* q_start;   // [R + 1]
+  const int* seq_lens;  // [R]
+  const int4* work;     // {req, row0, kv_begin, kv_end}
+  int n_work;
+  float* part_o;    // [n_work, Hk, 64, D]
+  float* part_lse;  // [n_work, Hk, 64]
+  int* status;
+};
+
+struct MergeParams {
+  const float* part_o;
+  const float* part_lse;
+  const int* item_first;  // [R * max_rb]
+  const int* item_count;
+  int max_rb;
+  const int* tok_req;  // [T] request of each query token
+  const int* q_start;  // [R + 1]
+  int Hq, Hk, D;
+  const float* RvT;  // [D, D] (o = o_rot @ R_v^T) or nullptr
+  const __nv_bfloat16* gate;  // gate[t * gate_ld + h * gate_hstride + d] or nullptr
+  long long gate_ld;
+  int gate_hstride;
+  __nv_bfloat16* out_bf16;  // [T, Hq * D] or nullptr
+  int8_t* out_i8;           // [T, Hq * D] or nullptr
+  float* out_scale;         // [T]
+  int T;
+};
+
+struct GdnParams {
+  const __nv_bfloat16* qkvz;  // [T, ld_qkvz]; per k-head group: q(dk) k(dk) v(r*dv) z(r*dv)
+  long long ld_qkvz;
+  const __nv_bfloat16* ba;  // [T, ld_ba]; per k-head group: b(r) a(r)
+  long long ld_ba;
+  int Hk, Hv, dk, dv;
+  const float* conv_w;   // [conv_dim, 4]; channels [q heads | k heads | v heads]
+  const float* A_log;    // [Hv]
+  const float* dt_bias;  // [Hv]
+  const float* norm_w;   // [dv]
+  float eps;
+  __nv_bfloat16* state;  // [slots, Hv, dk, dv]
+  // The conv window and the pending raw inputs are ping-ponged per slot (buffer
+  // `parity` is read, 1 - parity written): the q/k channels of a key head are
+  // shared by the r value-head CTAs of that group.
+  __nv_bfloat16* conv_state;  // [2, slots, conv_dim, 3] raw inputs, oldest first
+  __nv_bfloat16* pend_x;      // [2, slots, P, conv_dim]
+  __nv_bfloat16* pend_ba;     // [slots, P, 2 * Hv]  (b then a, per v head; owned per head)
+  const int* parity;          // [R]
+  int slots;
+  int P;
+  const int* req_slot;      // [R]
+  const int* q_start;       // [R + 1]
+  const int* n_commit;      // [R]
+  const int* keep_pending;  // [R]
+  __nv_bfloat16* out;       // [T, Hv * dv]
+  int R;
+  int* status;
+};
+
+}  // namespace oscar

@@ -1,0 +1,410 @@
+"""Serving engine: continuous batching, chunked prefill, MTP speculative decoding.
+
+One ``LLMEngine`` drives one tensor-parallel model replica (every rank of the TP
+group runs the same engine loop on identical host state; only rank 0 reports).
+A step:
+
+1. schedules verify groups (``1 + num_spec`` tokens) for decoding requests and
+   prefill chunks (FCFS) within ``max_batched_tokens`` (15,360 by default, the
+   reference's packed serve setting ``delivery/serve_oscar.sh:64-74``);
+2. builds all step metadata on the host (block tables, slots, staging seat plan,
+   attention work list, GDN commit counts) and uploads it once;
+3. runs the main model, verifies drafts (greedy or a seeded acceptance pattern),
+   then runs the MTP head over the step's rows and chains ``num_spec - 1`` more
+   single-token draft passes.
+
+The GDN layers use deferred commit (see :mod:`oscar_b200.ops.gdn`), so a rejected
+draft costs no state rollback; FULL-layer KV of rejected positions is simply
+overwritten by the next step.
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ..models.qwen35 import HybridModel, StepBatch
+from ..ops import attention as A
+from ..ops.functional import num_sms
+from .block_manager import BlockManager, SlotManager
+from .staging import seat_plan
+
+
+@dataclass
+class Request:
+    rid: int
+    prompt: list
+    max_new_tokens: int
+    output: list = field(default_factory=list)
+    num_computed: int = 0          # positions whose KV / state are final
+    last_token: int | None = None  # token at position num_computed (next to feed)
+    drafts: list = field(default_factory=list)
+    pending_commit: int = 0
+    slot: int = -1
+    arrival: float = 0.0
+    first_token_time: float | None = None
+    finish_time: float | None = None
+    accepted: list = field(default_factory=list)
+
+    @property
+    def prefill_done(self) -> bool:
+        return self.num_computed >= len(self.prompt)
+
+    @property
+    def finished(self) -> bool:
+        return len(self.output) >= self.max_new_tokens
+
+
+class SeededAcceptance:
+    """Deterministic acceptance pattern: accepted drafts per (request, step) ~ target mean."""
+
+    def __init__(self, num_spec: int, mean_accepted: float, seed: int = 0):
+        self.k = num_spec
+        p = min(max(mean_accepted / num_spec, 0.0), 1.0)
+        self.rng = np.random.default_rng(seed)
+        self.p = p
+
+    def __call__(self, rid: int) -> int:
+        return int(self.rng.binomial(self.k, self.p))
+
+
+class LLMEngine:
+    def __init__(self, model: HybridModel, num_blocks: int, max_slots: int, max_batched_tokens: int = 15360,
+                 num_spec: int = 3, acceptance: SeededAcceptance | None = None, prefill_policy: str = "fcfs",
+                 timer=time.perf_counter):
+        self.model = model
+        self.dev = model.device
+        self.num_spec = num_spec if model.mtp is not None else 0
+        self.bm = BlockManager(num_blocks)
+        self.slots = SlotManager(max_slots)
+        self.max_batched_tokens = max_batched_tokens
+        self.acceptance = acceptance
+        self.prefill_policy = prefill_policy
+        self.requests: dict[int, Request] = {}
+        self.waiting: list[int] = []
+        self.running: list[int] = []
+        self.finished: list[int] = []
+        self._ids = itertools.count()
+        self.timer = timer
+        self.stats = {"steps": 0, "tokens_out": 0, "drafts_proposed": 0, "drafts_accepted": 0}
+        # device-busy time of the model work (CUDA events around every GPU segment)
+        self.record_device_time = False
+        self._events: list = []
+        model.allocate_cache(num_blocks, max_slots)
+        cfg = model.oscar
+        self.stage_rows = model.stage_rows
+        self.sink, self.recent = cfg.sink_tokens, cfg.recent_tokens
+        self.g = model.full_layers[0].Hq // model.full_layers[0].Hk if model.full_layers else 1
+        self.Hk = model.full_layers[0].Hk if model.full_layers else 1
+        self.sms = num_sms(self.dev) if self.dev.type == "cuda" else 148
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, prompt, max_new_tokens: int) -> int:
+        rid = next(self._ids)
+        self.requests[rid] = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer())
+        self.waiting.append(rid)
+        return rid
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def generate(self, prompts, max_new_tokens: int) -> list[list[int]]:
+        ids = [self.add_request(p, max_new_tokens) for p in prompts]
+        while self.has_work():
+            self.step()
+        return [self.requests[i].output[:max_new_tokens] for i in ids]
+
+    # ------------------------------------------------------------------ scheduling
+    def _schedule(self):
+        """Returns a list of (rid, kind, n_tokens) with kind in {"verify", "prefill"}."""
+        sched = []
+        budget = self.max_batched_tokens
+        for rid in self.running:
+            r = self.requests[rid]
+            if not r.prefill_done:
+                continue
+            n = 1 + len(r.drafts)
+            extra = 2 * self.num_spec + 2
+            if not self.bm.can_allocate(rid, r.num_computed + n + extra):
+                continue  # no space this step (preemption is not needed for fixed-size batches)
+            self.bm.ensure(rid, r.num_computed + n + extra)
+            sched.append((rid, "verify", n))
+            budget -= n
+        candidates = [rid for rid in self.running if not self.requests[rid].prefill_done] + list(self.waiting)
+        if self.prefill_policy == "wide" and candidates:
+            share = max(1, budget // len(candidates))
+        for rid in candidates:
+            if budget <= 0:
+                break
+            r = self.requests[rid]
+            remaining = len(r.prompt) - r.num_computed
+            n = min(remaining, budget if self.prefill_policy == "fcfs" else min(share, budget))
+            if n <= 0:
+                continue
+            extra = 2 * self.num_spec + 2 if n == remaining else 0
+            if not self.bm.can_allocate(rid, r.num_computed + n + extra) or (r.slot < 0 and not self.slots.free_slots):
+                break
+            self.bm.ensure(rid, r.num_computed + n + extra)
+            if r.slot < 0:
+                r.slot = self.slots.acquire(rid)
+            if rid in self.waiting:
+                self.waiting.remove(rid)
+                self.running.append(rid)
+            sched.append((rid, "prefill", n))
+            budget -= n
+        return sched
+
+    # ------------------------------------------------------------------ metadata
+    def _tensor(self, x, dtype=torch.int32):
+        a = np.ascontiguousarray(np.asarray(x))
+        self.stats["h2d_bytes"] = self.stats.get("h2d_bytes", 0) + a.nbytes
+        return torch.as_tensor(a, dtype=dtype).to(self.dev, non_blocking=True)
+
+    def _upload(self, arrays: dict) -> dict:
+        """Pack int32 host arrays into one pinned buffer and upload them with one copy."""
+        flat = [np.ascontiguousarray(np.asarray(v, dtype=np.int32)).reshape(-1) for v in arrays.values()]
+        n = sum(f.size for f in flat)
+        if self.dev.type != "cuda":
+            out, off = {}, 0
+            for (k, v), f in zip(arrays.items(), flat):
+                out[k] = torch.from_numpy(f.copy()).view(np.asarray(v).shape) if f.size else torch.zeros(np.asarray(v).shape, dtype=torch.int32)
+            return out
+        if getattr(self, "_pin", None) is None or self._pin.numel() < n:
+            self._pin = torch.empty(max(n, 1 << 16), dtype=torch.int32, pin_memory=True)
+            self._dbuf = torch.empty(max(n, 1 << 16), dtype=torch.int32, device=self.dev)
+        # the previous step's copy must be finished before the pinned buffer is reused
+        if getattr(self, "_pin_event", None) is not None:
+            self._pin_event.synchronize()
+        host = self._pin.numpy()
+        off = 0
+        spans = []
+        for f in flat:
+            host[off:off + f.size] = f
+            spans.append((off, f.size))
+            off += f.size
+        dbuf = torch.empty(n, dtype=torch.int32, device=self.dev)
+        dbuf.copy_(self._pin[:n], non_blocking=True)
+        self._pin_event = torch.cuda.Event()
+        self._pin_event.record()
+        self.stats["h2d_bytes"] = self.stats.get("h2d_bytes", 0) + 4 * n
+        out = {}
+        for (k, v), (o, sz) in zip(arrays.items(), spans):
+            out[k] = dbuf[o:o + sz].view(np.asarray(v).shape)
+        return out
+
+    def _build(self, rows, logit_rows, commit_info, keep):
+        """rows: list of (rid, token, position); requests appear contiguously in order."""
+        toks, poss, slots, tok_req, q_start, seq_lens, bts = [], [], [], [], [0], [], []
+        req_slot, n_commit, keep_p, parity = [], [], [], []
+        order = []
+        for rid, tok, pos in rows:
+            if not order or order[-1] != rid:
+                order.append(rid)
+                q_start.append(q_start[-1])
+            q_start[-1] += 1
+            toks.append(tok)
+            poss.append(pos)
+            slots.append(self.bm.slot(rid, pos))
+            tok_req.append(len(order) - 1)
+        maxp = 1
+        for i, rid in enumerate(order):
+            b = q_start[i + 1]
+            seq_lens.append(poss[b - 1] + 1)
+            t = self.bm.table(rid)
+            bts.append(t)
+            maxp = max(maxp, len(t))
+            r = self.requests[rid]
+            req_slot.append(r.slot)
+            n_commit.append(commit_info.get(rid, 0))
+            keep_p.append(1 if keep.get(rid, False) else 0)
+            parity.append(self.slots.parity[r.slot])
+        bt = np.zeros((len(order), maxp), dtype=np.int32)
+        for i, t in enumerate(bts):
+            bt[i, :len(t)] = t
+        slots_np = np.asarray(slots, dtype=np.int64)
+        pos_np = np.asarray(poss, dtype=np.int64)
+        seq_np = np.asarray(seq_lens, dtype=np.int64)[np.asarray(tok_req, dtype=np.int64)]
+        stage_seat, owner_seat, owner_val = seat_plan(slots_np, pos_np, seq_np, self.stage_rows, self.sink,
+                                                      self.recent)
+        arrays = dict(tokens=toks, positions=poss, slots=slots, q_start=q_start, seq_lens=seq_lens, bt=bt,
+                      tok_req=tok_req, stage_seat=stage_seat, owner_seat=owner_seat, owner_val=owner_val,
+                      req_slot=req_slot, n_commit=n_commit, keep=keep_p, parity=parity, logit_rows=logit_rows)
+        plan_np = None
+        if self.dev.type == "cuda":
+            plan_np = A.plan_attention_host(q_start, seq_lens, self.g, self.Hk, self.sms)
+            arrays.update(work=plan_np[0], item_first=plan_np[1], item_count=plan_np[2])
+        d = self._upload(arrays)
+        plan = None
+        if plan_np is not None:
+            plan = A.AttnPlan(d["work"], d["item_first"], d["item_count"], plan_np[3], plan_np[4])
+        b = StepBatch(
+            tokens=d["tokens"], positions=d["positions"], slots=d["slots"], q_start=d["q_start"],
+            seq_lens=d["seq_lens"], block_tables=d["bt"], tok_req=d["tok_req"], q_start_l=q_start,
+            seq_lens_l=seq_lens, plan=plan,
+            stage_seat=d["stage_seat"] if self.stage_rows else None,
+            owner_seat=d["owner_seat"] if self.stage_rows else None,
+            owner_val=d["owner_val"] if self.stage_rows else None,
+            req_slot=d["req_slot"], n_commit=d["n_commit"], keep_pending=d["keep"], parity=d["parity"],
+            logit_rows=d["logit_rows"].long())
+        b.extra["order"] = order
+        return b
+
+    # ------------------------------------------------------------------ step
+    def step(self) -> dict:
+        sched = self._schedule()
+        if not sched:
+            return {}
+        rows, logit_rows, commit, keep = [], [], {}, {}
+        info = []
+        for rid, kind, n in sched:
+            r = self.requests[rid]
+            base = len(rows)
+            if kind == "verify":
+                toks = [r.last_token] + r.drafts
+                keep[rid] = True
+                logit_rows.extend(range(base, base + n))
+            else:
+                toks = r.prompt[r.num_computed:r.num_computed + n]
+                keep[rid] = False
+                if r.num_computed + n == len(r.prompt):
+                    logit_rows.append(base + n - 1)
+            commit[rid] = r.pending_commit
+            for i, t in enumerate(toks):
+                rows.append((rid, t, r.num_computed + i))
+            info.append((rid, kind, n, base))
+        b = self._build(rows, logit_rows, commit, keep)
+        with self._segment():
+            hid, tok = self.model.forward(b)
+        tok_h = tok.tolist()
+        self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * len(tok_h)
+        self.last = (hid, tok)
+        self._check_status()
+        # ---------------- verify / sample -----------------
+        now = self.timer()
+        li = 0
+        next_row_tok = [0] * len(rows)
+        draft_rows = []  # (rid, row index in step) rows whose MTP output starts drafting
+        for rid, kind, n, base in info:
+            r = self.requests[rid]
+            for i in range(n):
+                p = r.num_computed + i
+                next_row_tok[base + i] = r.prompt[p + 1] if p + 1 < len(r.prompt) else 0
+            if kind == "verify":
+                targets = tok_h[li:li + n]
+                li += n
+                d = r.drafts
+                if self.acceptance is not None:
+                    n_acc = min(self.acceptance(rid), len(d))
+                else:
+                    n_acc = 0
+                    while n_acc < len(d) and d[n_acc] == targets[n_acc]:
+                        n_acc += 1
+                emitted = d[:n_acc] + [targets[n_acc]]
+                for i in range(n):
+                    next_row_tok[base + i] = d[i] if i < n_acc else targets[i]
+                self.stats["drafts_proposed"] += len(d)
+                self.stats["drafts_accepted"] += n_acc
+                r.accepted.append(n_acc)
+                r.num_computed += n_acc + 1
+                r.pending_commit = n_acc + 1
+                self.slots.parity[r.slot] ^= 1
+                r.output.extend(emitted)
+                self.stats["tokens_out"] += len(emitted)
+                r.last_token = emitted[-1]
+                draft_rows.append((rid, base + n_acc))
+            else:
+                r.num_computed += n
+                r.pending_commit = 0
+                self.slots.parity[r.slot] ^= 1
+                if r.prefill_done:
+                    y = tok_h[li]
+                    li += 1
+                    next_row_tok[base + n - 1] = y
+                    r.output.append(y)
+                    self.stats["tokens_out"] += 1
+                    r.last_token = y
+                    r.first_token_time = now
+                    draft_rows.append((rid, base + n - 1))
+            if r.first_token_time is None and r.output:
+                r.first_token_time = now
+        # ---------------- MTP drafting -----------------
+        if self.num_spec > 0 and draft_rows:
+            self._draft(b, hid, rows, next_row_tok, draft_rows)
+        # ---------------- retire -----------------
+        for rid, kind, n, base in info:
+            r = self.requests[rid]
+            if r.finished:
+                r.finish_time = now
+                self.running.remove(rid)
+                self.finished.append(rid)
+                self.bm.free(rid)
+                self.slots.release(rid)
+        self.stats["steps"] += 1
+        return {"scheduled": sched}
+
+    def _draft(self, b: StepBatch, hid, rows, next_row_tok, draft_rows):
+        """MTP pass over the step's rows, then num_spec-1 chained single-token passes."""
+        m = self.model
+        up = self._upload({"tokens": next_row_tok, "rows": [ri for _, ri in draft_rows]})
+        b.tokens = up["tokens"]
+        b.logit_rows = up["rows"].long()
+        with self._segment():
+            h1, e = m.mtp.forward(b, hid)
+        drafts = {rid: [] for rid, _ in draft_rows}
+        e_h = e.tolist()
+        self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * len(e_h)
+        for (rid, _), t in zip(draft_rows, e_h):
+            drafts[rid].append(t)
+        h = h1[b.logit_rows]
+        for k in range(1, self.num_spec):
+            prow = []
+            for (rid, ri), t in zip(draft_rows, e_h):
+                # the MTP row after ``ri`` sits one position further
+                pos = rows[ri][2] + k
+                prow.append((rid, t, pos))
+            bk = self._build(prow, list(range(len(prow))), {}, {})
+            with self._segment():
+                    hk, e = m.mtp.forward(bk, h)
+            e_h = e.tolist()
+            self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * len(e_h)
+            for (rid, _), t in zip(draft_rows, e_h):
+                drafts[rid].append(t)
+            h = hk
+        for rid, d in drafts.items():
+            self.requests[rid].drafts = d
+
+    class _Seg:
+        def __init__(self, eng):
+            self.eng = eng
+
+        def __enter__(self):
+            if self.eng.record_device_time:
+                self.a = torch.cuda.Event(enable_timing=True)
+                self.a.record()
+
+        def __exit__(self, *exc):
+            if self.eng.record_device_time:
+                b = torch.cuda.Event(enable_timing=True)
+                b.record()
+                self.eng._events.append((self.a, b))
+
+    def _segment(self):
+        return LLMEngine._Seg(self)
+
+    def device_ms(self, reset: bool = True) -> float:
+        """Sum of recorded GPU segment durations (synchronises)."""
+        torch.cuda.synchronize()
+        t = sum(a.elapsed_time(b) for a, b in self._events)
+        if reset:
+            self._events = []
+        return t
+
+    def _check_status(self):
+        st = self.model.status
+        if st is not None:
+            v = int(st.item())
+            if v != 0:
+                raise RuntimeError(f"kernel reported status {v} (bounded wait expired or bad index)")

@@ -1,0 +1,459 @@
+"""Qwen3.5-shaped hybrid model on the oscar_b200 kernels (random init from a seed).
+
+Layer stack (``config.HybridConfig``): gated DeltaNet layers and, every
+``full_attention_interval`` layers, a gated full-attention layer whose KV cache is
+OSCAR INT2 (rotated, clipped, 2-bit per-vector codes in 128-token pages with an fp32
+sink/recent staging window).  All projections are W8A8 int8 GEMMs with per-channel
+weight scales and per-token dynamic activation scales; the residual stream is fp32.
+The MTP head (one full-attention layer with a BF16 KV "shadow" pool) drafts tokens
+for speculative decoding.
+
+Tensor parallelism: attention/GDN heads, the MLP intermediate dimension and the
+vocabulary are split across ranks; o_proj / out_proj / down_proj are row-parallel
+and their partial sums are all-reduced (NCCL baseline) before the fused
+residual-add + RMSNorm kernel.
+
+Reference parity: the OSCAR attention write/read semantics follow the reference
+backend (``oscar_ascend/backend.py:129-189, 239-415``); everything else is the host
+framework's model that the reference runs on (``delivery/serve_oscar.sh:76-99``).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from ..config import OscarConfig
+from ..kv import format as fmt
+from ..kv.oracle import staging_rows
+from ..kv.rotation import get_layer_rotation, random_orthogonal
+from ..ops import attention as A
+from ..ops import functional as F
+from ..ops.gdn import gdn_step
+from ..parallel.groups import TPGroup
+from .config import HybridConfig
+
+P_MAX = 4  # pending (uncommitted) tokens per GDN slot: 1 verified + 3 drafts
+
+
+@dataclass
+class QLinear:
+    q: torch.Tensor  # int8 [N, K]
+    s: torch.Tensor  # fp32 [N]
+
+    def to(self, device):
+        return QLinear(self.q.to(device), self.s.to(device))
+
+
+@dataclass
+class StepBatch:
+    """Device metadata of one engine step (built on the host, uploaded once)."""
+
+    tokens: torch.Tensor        # [T] int32
+    positions: torch.Tensor     # [T] int32
+    slots: torch.Tensor         # [T] int32 physical slot (block * 128 + offset), -1 = no write
+    q_start: torch.Tensor       # [R + 1] int32
+    seq_lens: torch.Tensor      # [R] int32 (including this step's tokens)
+    block_tables: torch.Tensor  # [R, max_pages] int32
+    tok_req: torch.Tensor       # [T] int32
+    q_start_l: list
+    seq_lens_l: list
+    plan: A.AttnPlan | None
+    stage_seat: torch.Tensor | None   # [T] int32
+    owner_seat: torch.Tensor | None   # [n] int32
+    owner_val: torch.Tensor | None    # [n] int32
+    req_slot: torch.Tensor            # [R] int32 (GDN state slot)
+    n_commit: torch.Tensor            # [R] int32
+    keep_pending: torch.Tensor        # [R] int32
+    parity: torch.Tensor              # [R] int32
+    logit_rows: torch.Tensor          # [n_sel] int64
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def T(self) -> int:
+        return int(self.tokens.shape[0])
+
+
+def _gen(seed: int, device) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def _rand_qlinear(N: int, K: int, seed: int, device) -> QLinear:
+    g = _gen(seed, device)
+    q = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g, device=device)
+    s = (torch.rand(N, generator=g, device=device) * 0.5 + 0.75) / (73.3 * math.sqrt(K))
+    return QLinear(q, s.float())
+
+
+def _rand_vec(n: int, seed: int, device, std: float = 0.02, mean: float = 0.0) -> torch.Tensor:
+    g = _gen(seed, device)
+    return (torch.randn(n, generator=g, device=device) * std + mean).float()
+
+
+class FullAttentionLayer:
+    """Gated full attention with OSCAR INT2 KV (or BF16 KV for the MTP draft layer)."""
+
+    def __init__(self, cfg: HybridConfig, tp: TPGroup, layer_id: int, seed: int, device, oscar: OscarConfig,
+                 kv_mode: str = "int2", rotation: str = "random"):
+        H, D = cfg.hidden_size, cfg.head_dim
+        self.layer_id = layer_id
+        self.D = D
+        self.Hq = cfg.num_attention_heads // tp.world
+        if cfg.num_key_value_heads >= tp.world:
+            self.Hk = cfg.num_key_value_heads // tp.world
+        else:
+            self.Hk = 1  # KV heads replicated across ranks (tp > num_key_value_heads)
+        self.kv_mode = 0 if kv_mode == "int2" else 1
+        self.scale = 1.0 / math.sqrt(D)
+        self.eps = cfg.rms_norm_eps
+        self.rot_dim = cfg.rot_dim
+        self.q_off = 0
+        self.q_head_stride = 2 * D  # per head: [query (D) | gate (D)]
+        self.k_off = self.Hq * 2 * D
+        self.v_off = self.k_off + self.Hk * D
+        self.n_qkv = self.v_off + self.Hk * D
+        base = seed * 1000 + layer_id * 17 + tp.rank * 100003
+        self.qkv = _rand_qlinear(self.n_qkv, H, base + 1, device)
+        self.o = _rand_qlinear(H, self.Hq * D, base + 2, device)
+        self.q_norm = _rand_vec(D, base + 3, device)
+        self.k_norm = _rand_vec(D, base + 4, device)
+        self.input_norm = _rand_vec(H, base + 5, device)
+        self.post_norm = _rand_vec(H, base + 6, device)
+        self.k_clip_idx = oscar.clip_index(oscar.k_clip_ratio) if (self.kv_mode == 0 and oscar.k_clip_ratio > 0) else -1
+        self.v_clip_idx = oscar.clip_index(oscar.v_clip_ratio) if (self.kv_mode == 0 and oscar.v_clip_ratio > 0) else -1
+        if self.kv_mode == 0:
+            if rotation == "identity":
+                self.Rk = self.Rv = self.RvT = None
+            elif rotation == "random":
+                self.Rk = random_orthogonal(D, seed * 7919 + layer_id * 2).to(device)
+                self.Rv = random_orthogonal(D, seed * 7919 + layer_id * 2 + 1).to(device)
+                self.RvT = self.Rv.t().contiguous()
+            else:  # checkpoint path (v2 oscar_rotations.pt)
+                self.Rk = get_layer_rotation(oscar.k_rotation_path or rotation, layer_id, D, device, mode="k",
+                                             strict=True)
+                self.Rv = get_layer_rotation(oscar.v_rotation_path or rotation, layer_id, D, device, mode="v",
+                                             strict=True)
+                self.RvT = self.Rv.t().contiguous()
+        else:
+            self.Rk = self.Rv = self.RvT = None
+        self.pool = self.kc = self.vc = None
+        self.stage_k = self.stage_v = None
+
+    def to(self, device):
+        for k, v in list(vars(self).items()):
+            if isinstance(v, torch.Tensor):
+                setattr(self, k, v.to(device))
+            elif isinstance(v, QLinear):
+                setattr(self, k, v.to(device))
+        return self
+
+    def allocate_cache(self, num_blocks: int, device, stage_rows: int = 0):
+        if self.kv_mode == 0:
+            self.pool = torch.zeros(num_blocks, self.Hk, fmt.page_head_bytes(self.D), dtype=torch.uint8,
+                                    device=device)
+            if stage_rows:
+                self.stage_k = torch.zeros(stage_rows * fmt.PAGE, self.Hk, self.D, dtype=torch.float32,
+                                           device=device)
+                self.stage_v = torch.zeros_like(self.stage_k)
+        else:
+            self.kc = torch.zeros(num_blocks, fmt.PAGE, self.Hk, self.D, dtype=torch.bfloat16, device=device)
+            self.vc = torch.zeros_like(self.kc)
+
+    def cache_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.pool, self.kc, self.vc, self.stage_k, self.stage_v)
+                   if t is not None)
+
+    def attention(self, xq, xs, b: StepBatch, rope, owner, stage_rows, write_owner: bool, status=None):
+        """qkv GEMM -> fused store -> paged attention -> merge. Returns (o_int8, o_scale)."""
+        T = xq.shape[0]
+        dev = xq.device
+        qkv = F.linear_i8(xq, xs, self.qkv.q, self.qkv.s, status=status)
+        q_out = torch.empty(T, self.Hq, self.D, dtype=torch.float16, device=dev)
+        k_fr = torch.empty(T, self.Hk, self.D, dtype=torch.float16, device=dev)
+        v_fr = torch.empty_like(k_fr)
+        staged = self.kv_mode == 0 and stage_rows > 0 and b.stage_seat is not None
+        A.kv_store(qkv, q_off=self.q_off, q_head_stride=self.q_head_stride, k_off=self.k_off, v_off=self.v_off,
+                   Hq=self.Hq, Hk=self.Hk, D=self.D, q_norm_w=self.q_norm, k_norm_w=self.k_norm, eps=self.eps,
+                   norm_offset=1.0, positions=b.positions, rope_cos=rope[0], rope_sin=rope[1], rot_dim=self.rot_dim,
+                   Rk=self.Rk, Rv=self.Rv, k_clip_idx=self.k_clip_idx, v_clip_idx=self.v_clip_idx, q_out=q_out,
+                   k_fresh=k_fr, v_fresh=v_fr, kv_mode=self.kv_mode, pool=self.pool, kc=self.kc, vc=self.vc,
+                   slots=b.slots, stage_k=self.stage_k if staged else None,
+                   stage_v=self.stage_v if staged else None, stage_seat=b.stage_seat if staged else None,
+                   owner=owner if staged else None,
+                   owner_seat=b.owner_seat if (staged and write_owner) else None,
+                   owner_val=b.owner_val if (staged and write_owner) else None, status=status)
+        stage = (self.stage_k, self.stage_v, owner, stage_rows) if staged else None
+        gate = qkv[:, self.D:]  # gate of head h at columns h * 2D + D ..
+        _, oq, os_ = A.attention(q_out, k_fr, v_fr, Hq=self.Hq, Hk=self.Hk, D=self.D, scale=self.scale,
+                                 kv_mode=self.kv_mode, pool=self.pool, kc=self.kc, vc=self.vc, stage=stage,
+                                 block_tables=b.block_tables, q_start_t=b.q_start, seq_lens_t=b.seq_lens,
+                                 q_start=b.q_start_l, seq_lens=b.seq_lens_l, plan=b.plan, tok_req=b.tok_req,
+                                 RvT=self.RvT, gate=gate, gate_ld=qkv.stride(0), gate_hstride=2 * self.D,
+                                 want_bf16=False, want_q=True, status=status)
+        return oq, os_
+
+
+class GDNLayer:
+    """Gated DeltaNet mixer (linear attention) with deferred speculative commit."""
+
+    def __init__(self, cfg: HybridConfig, tp: TPGroup, layer_id: int, seed: int, device):
+        H = cfg.hidden_size
+        self.layer_id = layer_id
+        self.Hk = cfg.linear_num_key_heads // tp.world
+        self.Hv = cfg.linear_num_value_heads // tp.world
+        self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        self.r = self.Hv // self.Hk
+        self.eps = cfg.rms_norm_eps
+        self.n_qkvz = self.Hk * (2 * self.dk + 2 * self.r * self.dv)
+        self.n_ba = 2 * self.Hv
+        self.conv_dim = 2 * self.Hk * self.dk + self.Hv * self.dv
+        base = seed * 1000 + layer_id * 17 + tp.rank * 100003
+        self.inp = _rand_qlinear(self.n_qkvz + self.n_ba, H, base + 1, device)
+        self.out = _rand_qlinear(H, self.Hv * self.dv, base + 2, device)
+        g = _gen(base + 3, device)
+        self.conv_w = (torch.randn(self.conv_dim, cfg.linear_conv_kernel_dim, generator=g, device=device) * 0.5).float()
+        self.A_log = torch.log(torch.rand(self.Hv, generator=g, device=device) * 15 + 1).float()
+        self.dt_bias = torch.ones(self.Hv, device=device).float()
+        self.norm_w = (1.0 + torch.randn(self.dv, generator=g, device=device) * 0.02).float()
+        self.input_norm = _rand_vec(H, base + 5, device)
+        self.post_norm = _rand_vec(H, base + 6, device)
+        self.state = self.conv_state = self.pend_x = self.pend_ba = None
+
+    def to(self, device):
+        for k, v in list(vars(self).items()):
+            if isinstance(v, torch.Tensor):
+                setattr(self, k, v.to(device))
+            elif isinstance(v, QLinear):
+                setattr(self, k, v.to(device))
+        return self
+
+    def allocate_cache(self, slots: int, device):
+        self.state = torch.zeros(slots, self.Hv, self.dk, self.dv, dtype=torch.bfloat16, device=device)
+        self.conv_state = torch.zeros(2, slots, self.conv_dim, 3, dtype=torch.bfloat16, device=device)
+        self.pend_x = torch.zeros(2, slots, P_MAX, self.conv_dim, dtype=torch.bfloat16, device=device)
+        self.pend_ba = torch.zeros(slots, P_MAX, 2 * self.Hv, dtype=torch.bfloat16, device=device)
+
+    def cache_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.state, self.conv_state, self.pend_x, self.pend_ba)
+                   if t is not None)
+
+    def mixer(self, xq, xs, b: StepBatch, status=None):
+        proj = F.linear_i8(xq, xs, self.inp.q, self.inp.s, status=status)
+        T = proj.shape[0]
+        o = torch.empty(T, self.Hv * self.dv, dtype=torch.bfloat16, device=proj.device)
+        gdn_step(proj[:, :self.n_qkvz], proj[:, self.n_qkvz:], Hk=self.Hk, Hv=self.Hv, dk=self.dk, dv=self.dv,
+                 conv_w=self.conv_w, A_log=self.A_log, dt_bias=self.dt_bias, norm_w=self.norm_w, eps=self.eps,
+                 state=self.state, conv_state=self.conv_state, pend_x=self.pend_x, pend_ba=self.pend_ba,
+                 parity=b.parity, req_slot=b.req_slot, q_start=b.q_start, n_commit=b.n_commit,
+                 keep_pending=b.keep_pending, out=o, smem_state=T > 64, status=status)
+        return F.act_quant(o)
+
+
+class MLP:
+    def __init__(self, cfg: HybridConfig, tp: TPGroup, layer_id: int, seed: int, device):
+        H = cfg.hidden_size
+        self.I = cfg.intermediate_size // tp.world
+        base = seed * 1000 + layer_id * 17 + tp.rank * 100003 + 50
+        self.gate_up = _rand_qlinear(2 * self.I, H, base + 1, device)
+        self.down = _rand_qlinear(H, self.I, base + 2, device)
+
+    def to(self, device):
+        self.gate_up = self.gate_up.to(device)
+        self.down = self.down.to(device)
+        return self
+
+
+class HybridModel:
+    """The full model of one tensor-parallel rank."""
+
+    def __init__(self, cfg: HybridConfig, tp: TPGroup | None = None, device="cpu", seed: int = 0,
+                 oscar: OscarConfig | None = None, kv_mode: str = "int2", rotation: str = "random",
+                 mtp: bool = True):
+        self.cfg = cfg
+        self.tp = tp or TPGroup()
+        self.device = torch.device(device)
+        self.oscar = oscar or OscarConfig().validate()
+        self.kv_mode = kv_mode
+        H = cfg.hidden_size
+        V = cfg.vocab_size
+        self.V_local = (V + self.tp.world - 1) // self.tp.world
+        self.vocab_begin = self.tp.rank * self.V_local
+        dev = self.device
+        base = seed * 1000 + self.tp.rank * 100003
+        g = _gen(base + 999, dev)
+        self.embed = (torch.randn(self.V_local, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        self.lm_head = _rand_qlinear(self.V_local, H, base + 998, dev)
+        self.final_norm = _rand_vec(H, base + 997, dev)
+        self.layers = []
+        for i, t in enumerate(cfg.layer_types):
+            mixer = (FullAttentionLayer(cfg, self.tp, i, seed, dev, self.oscar, kv_mode, rotation)
+                     if t == "full_attention" else GDNLayer(cfg, self.tp, i, seed, dev))
+            self.layers.append((mixer, MLP(cfg, self.tp, i, seed, dev)))
+        self.mtp = MTPHead(self, seed) if (mtp and cfg.num_mtp_layers > 0) else None
+        self.rope = F.rope_tables(cfg.max_position, cfg.rot_dim, cfg.rope_theta, dev)
+        self.stage_rows = 0
+        self.owner = None
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev) if dev.type == "cuda" else None
+
+    # ------------------------------------------------------------------ setup
+    def to(self, device):
+        self.device = torch.device(device)
+        self.embed = self.embed.to(device)
+        self.lm_head = self.lm_head.to(device)
+        self.final_norm = self.final_norm.to(device)
+        for mixer, mlp in self.layers:
+            mixer.to(device)
+            mlp.to(device)
+        if self.mtp is not None:
+            self.mtp.to(device)
+        self.rope = (self.rope[0].to(device), self.rope[1].to(device))
+        if self.owner is not None:
+            self.owner = self.owner.to(device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device) if self.device.type == "cuda" else None
+        return self
+
+    @property
+    def full_layers(self):
+        return [m for m, _ in self.layers if isinstance(m, FullAttentionLayer)]
+
+    @property
+    def gdn_layers(self):
+        return [m for m, _ in self.layers if isinstance(m, GDNLayer)]
+
+    def allocate_cache(self, num_blocks: int, max_slots: int):
+        o = self.oscar
+        self.stage_rows = staging_rows(o.sink_tokens, o.recent_tokens, o.staging_tokens) if (
+            o.window_enabled and self.kv_mode == "int2") else 0
+        if self.stage_rows:
+            self.owner = torch.full((self.stage_rows * fmt.PAGE,), -1, dtype=torch.int32, device=self.device)
+        for m in self.full_layers:
+            m.allocate_cache(num_blocks, self.device, self.stage_rows)
+        for m in self.gdn_layers:
+            m.allocate_cache(max_slots, self.device)
+        if self.mtp is not None:
+            self.mtp.layer.allocate_cache(num_blocks, self.device)
+
+    def cache_bytes(self) -> dict:
+        full = sum(m.cache_bytes() for m in self.full_layers)
+        gdn = sum(m.cache_bytes() for m in self.gdn_layers)
+        shadow = self.mtp.layer.cache_bytes() if self.mtp is not None else 0
+        return {"full_kv": full, "gdn_state": gdn, "mtp_shadow": shadow,
+                "owner": 0 if self.owner is None else self.owner.numel() * 4}
+
+    # ------------------------------------------------------------------ forward
+    def decoder(self, b: StepBatch, residual: torch.Tensor):
+        """All decoder layers; returns the pending MLP delta of the last layer."""
+        delta = torch.zeros_like(residual)
+        first_full = True
+        for i, (mixer, mlp) in enumerate(self.layers):
+            xq, xs, _ = F.rmsnorm_quant(residual, mixer.input_norm, self.cfg.rms_norm_eps,
+                                        delta=delta if i > 0 else None)
+            if isinstance(mixer, FullAttentionLayer):
+                oq, os_ = mixer.attention(xq, xs, b, self.rope, self.owner, self.stage_rows,
+                                          write_owner=first_full, status=self.status)
+                first_full = False
+                w_o = mixer.o
+            else:
+                oq, os_ = mixer.mixer(xq, xs, b, status=self.status)
+                w_o = mixer.out
+            delta.zero_()
+            F.linear_i8(oq, os_, w_o.q, w_o.s, out=delta, accumulate=True, status=self.status)
+            self.tp.all_reduce_(delta)
+            xq, xs, _ = F.rmsnorm_quant(residual, mixer.post_norm, self.cfg.rms_norm_eps, delta=delta)
+            gu = F.linear_i8(xq, xs, mlp.gate_up.q, mlp.gate_up.s, status=self.status)
+            hq, hs = F.swiglu_quant(gu, mlp.I)
+            delta.zero_()
+            F.linear_i8(hq, hs, mlp.down.q, mlp.down.s, out=delta, accumulate=True, status=self.status)
+            self.tp.all_reduce_(delta)
+        return delta
+
+    def forward(self, b: StepBatch):
+        """Main model on a step.  Returns ``(hidden_bf16 [T, H], next_tokens [n_sel])``."""
+        T = b.T
+        H = self.cfg.hidden_size
+        residual = torch.empty(T, H, dtype=torch.float32, device=self.device)
+        F.embed(b.tokens, self.embed, self.vocab_begin, residual)
+        self.tp.all_reduce_(residual)
+        delta = self.decoder(b, residual)
+        xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, self.cfg.rms_norm_eps, delta=delta,
+                                      want_bf16=True)
+        rows = b.logit_rows
+        tok = self.sample(xq[rows], xs[rows])
+        return hid, tok
+
+    def sample(self, xq, xs) -> torch.Tensor:
+        """Greedy sampling over the vocab-parallel lm_head (global argmax across ranks)."""
+        logits = F.linear_i8(xq, xs, self.lm_head.q, self.lm_head.s, status=self.status)
+        v, i = F.argmax(logits, self.vocab_begin)
+        if self.tp.world > 1:
+            vs = self.tp.all_gather(v.unsqueeze(0))      # [world, n]
+            ids = self.tp.all_gather(i.unsqueeze(0))
+            best = vs.argmax(dim=0)
+            i = ids.gather(0, best.unsqueeze(0)).squeeze(0)
+        return i
+
+
+class MTPHead:
+    """One-layer multi-token-prediction head (shares the embedding and lm_head)."""
+
+    def __init__(self, model: HybridModel, seed: int):
+        cfg = model.cfg
+        tp = model.tp
+        dev = model.device
+        H = cfg.hidden_size
+        lid = cfg.num_layers  # layer id after the main stack
+        base = seed * 1000 + lid * 17 + tp.rank * 100003 + 7
+        self.model = model
+        self.fc = _rand_qlinear(H, 2 * H, base + 1, dev)
+        self.norm_emb = _rand_vec(H, base + 2, dev)
+        self.norm_hid = _rand_vec(H, base + 3, dev)
+        self.final_norm = _rand_vec(H, base + 4, dev)
+        self.layer = FullAttentionLayer(cfg, tp, lid, seed, dev, model.oscar, kv_mode="bf16")
+        self.mlp = MLP(cfg, tp, lid, seed, dev)
+
+    def to(self, device):
+        for name in ("fc",):
+            setattr(self, name, getattr(self, name).to(device))
+        self.norm_emb = self.norm_emb.to(device)
+        self.norm_hid = self.norm_hid.to(device)
+        self.final_norm = self.final_norm.to(device)
+        self.layer.to(device)
+        self.mlp.to(device)
+        return self
+
+    def forward(self, b: StepBatch, hidden: torch.Tensor):
+        """Draft pass: ``hidden`` [T, H] bf16 (post-norm main or previous draft hidden),
+        ``b.tokens`` = the next token of every position.  Returns (hidden_bf16, next_tokens)."""
+        m = self.model
+        cfg = m.cfg
+        T, H = hidden.shape
+        eps = cfg.rms_norm_eps
+        e = torch.empty(T, H, dtype=torch.float32, device=m.device)
+        F.embed(b.tokens, m.embed, m.vocab_begin, e)
+        m.tp.all_reduce_(e)
+        _, _, e_n = F.rmsnorm_quant(e, self.norm_emb, eps, want_q=False, want_bf16=True)
+        hf = hidden.float().contiguous()
+        _, _, h_n = F.rmsnorm_quant(hf, self.norm_hid, eps, want_q=False, want_bf16=True)
+        cat = torch.cat([e_n, h_n], dim=1)
+        cq, cs = F.act_quant(cat)
+        residual = torch.zeros(T, H, dtype=torch.float32, device=m.device)
+        F.linear_i8(cq, cs, self.fc.q, self.fc.s, out=residual, accumulate=True, status=m.status)
+        m.tp.all_reduce_(residual) if False else None  # fc is replicated: no reduction needed
+        xq, xs, _ = F.rmsnorm_quant(residual, self.layer.input_norm, eps)
+        oq, os_ = self.layer.attention(xq, xs, b, m.rope, None, 0, write_owner=False, status=m.status)
+        delta = torch.zeros_like(residual)
+        F.linear_i8(oq, os_, self.layer.o.q, self.layer.o.s, out=delta, accumulate=True, status=m.status)
+        m.tp.all_reduce_(delta)
+        xq, xs, _ = F.rmsnorm_quant(residual, self.layer.post_norm, eps, delta=delta)
+        gu = F.linear_i8(xq, xs, self.mlp.gate_up.q, self.mlp.gate_up.s, status=m.status)
+        hq, hs = F.swiglu_quant(gu, self.mlp.I)
+        delta.zero_()
+        F.linear_i8(hq, hs, self.mlp.down.q, self.mlp.down.s, out=delta, accumulate=True, status=m.status)
+        m.tp.all_reduce_(delta)
+        xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, eps, delta=delta, want_bf16=True)
+        rows = b.logit_rows
+        tok = m.sample(xq[rows], xs[rows])
+        return hid, tok

@@ -1,0 +1,245 @@
+"""OSCAR FULL-attention ops: fused KV store, paged INT2/BF16 attention, split merge.
+
+GPU path (three launches per layer and step):
+
+1. ``kv_store``  - q/k RMSNorm + partial RoPE + fp32 rotation + clip + INT2 quantise +
+   page write + fp32 staging write (or a BF16 page write for the MTP draft layer);
+2. ``paged_attention`` - split-KV multi-query GQA attention over pages, staging and
+   the current chunk, tensor-core tiles, partial (O, LSE) per work item;
+3. ``attn_merge`` - split combine, ``o_rot @ R_vᵀ``, sigmoid output gate, int8 quant.
+
+The CPU path computes the same result with the torch oracle
+(:mod:`oscar_b200.kv.oracle`).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from ..kv import format as fmt
+from ._ext import ext
+from .functional import apply_rope_ref, head_rmsnorm_ref, quantize_rows_ref, _bf16_round
+
+ROWS = 64  # rows (query token x head-in-group) per attention work item
+
+
+@dataclass
+class AttnPlan:
+    """Host-built work decomposition of one step (shared by every FULL layer)."""
+
+    work: torch.Tensor        # [n_work, 4] int32: req, row0, kv_begin, kv_end
+    item_first: torch.Tensor  # [R * max_rb] int32
+    item_count: torch.Tensor  # [R * max_rb] int32
+    max_rb: int
+    n_work: int
+
+
+def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int, sms: int,
+                        min_chunk: int = 256, waves: int = 3):
+    """Work list as numpy arrays: ``(work [n,4], item_first, item_count, max_rb, n_work)``."""
+    R = len(seq_lens)
+    blocks = []  # (req, row0, kv_need)
+    max_rb = 1
+    for r in range(R):
+        n = q_start[r + 1] - q_start[r]
+        if n <= 0:
+            continue
+        prefix = seq_lens[r] - n
+        rows = n * g
+        rb = (rows + ROWS - 1) // ROWS
+        max_rb = max(max_rb, rb)
+        for b in range(rb):
+            last_row = min(rows, (b + 1) * ROWS) - 1
+            blocks.append((r, b * ROWS, prefix + last_row // g + 1))
+    total = sum(k for _, _, k in blocks)
+    target_items = max(1, (waves * sms) // max(Hk, 1))
+    chunk = max(min_chunk, int(math.ceil(total / target_items / 64.0)) * 64) if total else min_chunk
+    work = []
+    first = np.zeros(R * max_rb, dtype=np.int32)
+    count = np.zeros(R * max_rb, dtype=np.int32)
+    for r, row0, need in blocks:
+        rb = row0 // ROWS
+        first[r * max_rb + rb] = len(work)
+        splits = max(1, (need + chunk - 1) // chunk)
+        for s in range(splits):
+            work.append((r, row0, s * chunk, min(need, (s + 1) * chunk)))
+        count[r * max_rb + rb] = splits
+    n_work = len(work)
+    wt = np.asarray(work if work else [(0, 0, 0, 0)], dtype=np.int32).reshape(-1, 4)
+    return wt, first, count, max_rb, n_work
+
+
+def plan_attention(q_start: list[int], seq_lens: list[int], g: int, Hk: int, sms: int,
+                   device, min_chunk: int = 256, waves: int = 3) -> AttnPlan:
+    wt, first, count, max_rb, n_work = plan_attention_host(q_start, seq_lens, g, Hk, sms, min_chunk, waves)
+    return AttnPlan(torch.from_numpy(wt).to(device), torch.from_numpy(first).to(device),
+                    torch.from_numpy(count).to(device), max_rb, n_work)
+
+
+# ---------------------------------------------------------------------------
+# KV store
+# ---------------------------------------------------------------------------
+def clip_by_index(x: torch.Tensor, idx: int) -> torch.Tensor:
+    if idx < 0:
+        return x
+    thr = x.abs().sort(dim=-1).values[..., idx: idx + 1]
+    return torch.maximum(torch.minimum(x, thr), -thr)
+
+
+def kv_store(qkv, *, q_off, q_head_stride, k_off, v_off, Hq, Hk, D, q_norm_w, k_norm_w, eps, norm_offset,
+             positions, rope_cos, rope_sin, rot_dim, Rk, Rv, k_clip_idx, v_clip_idx, q_out, k_fresh, v_fresh,
+             kv_mode, pool, kc, vc, slots, stage_k=None, stage_v=None, stage_seat=None, owner=None,
+             owner_seat=None, owner_val=None, status=None):
+    """Fused write path of one FULL layer; see the module docstring."""
+    if qkv.is_cuda:
+        ext().kv_store(qkv, q_off, q_head_stride, k_off, v_off, Hq, Hk, D, q_norm_w, k_norm_w, float(eps),
+                       float(norm_offset), positions, rope_cos, rope_sin, rot_dim, Rk, Rv, k_clip_idx, v_clip_idx,
+                       q_out, k_fresh, v_fresh, kv_mode, pool, kc, vc, slots, stage_k, stage_v, stage_seat, owner,
+                       owner_seat, owner_val, status)
+        return
+    T = qkv.shape[0]
+    x = qkv.float()
+    q = torch.stack([x[:, q_off + h * q_head_stride: q_off + h * q_head_stride + D] for h in range(Hq)], 1)
+    k = x[:, k_off:k_off + Hk * D].reshape(T, Hk, D)
+    v = x[:, v_off:v_off + Hk * D].reshape(T, Hk, D)
+    if q_norm_w is not None:
+        q = head_rmsnorm_ref(q, q_norm_w, eps, norm_offset)
+    if k_norm_w is not None:
+        k = head_rmsnorm_ref(k, k_norm_w, eps, norm_offset)
+    if rope_cos is not None and rot_dim > 0:
+        q = apply_rope_ref(q, positions, rope_cos, rope_sin, rot_dim)
+        k = apply_rope_ref(k, positions, rope_cos, rope_sin, rot_dim)
+    qr = q @ Rk if Rk is not None else q
+    kr = k @ Rk if Rk is not None else k
+    vr = v @ Rv if Rv is not None else v
+    q_out.copy_(qr.half())
+    k_fresh.copy_(kr.half())
+    v_fresh.copy_(vr.half())
+    if owner_seat is not None and owner_seat.numel():
+        owner.view(-1)[owner_seat.long()] = owner_val.to(owner.dtype)
+    if stage_seat is not None:
+        sel = torch.nonzero(stage_seat >= 0, as_tuple=True)[0]
+        if sel.numel():
+            seats = stage_seat[sel].long()
+            stage_k.view(-1, Hk, D)[seats] = kr[sel]
+            stage_v.view(-1, Hk, D)[seats] = vr[sel]
+    valid = torch.nonzero(slots >= 0, as_tuple=True)[0]
+    if valid.numel() == 0:
+        return
+    s = slots[valid].long()
+    blk, off = s // fmt.PAGE, s % fmt.PAGE
+    if kv_mode == 1:
+        kc[blk, off] = kr[valid].to(torch.bfloat16)
+        vc[blk, off] = vr[valid].to(torch.bfloat16)
+        return
+    kcodes, vcodes, ks, kz, vs, vz = fmt.page_views(pool, D)
+    kp, kss, kzz = fmt.quantize(clip_by_index(kr[valid], k_clip_idx))
+    vp, vss, vzz = fmt.quantize(clip_by_index(vr[valid], v_clip_idx))
+    kcodes[blk, :, off] = kp
+    vcodes[blk, :, off] = vp
+    ks[blk, :, off] = kss.squeeze(-1).half()
+    kz[blk, :, off] = kzz.squeeze(-1).half()
+    vs[blk, :, off] = vss.squeeze(-1).half()
+    vz[blk, :, off] = vzz.squeeze(-1).half()
+
+
+# ---------------------------------------------------------------------------
+# attention + merge
+# ---------------------------------------------------------------------------
+def _history_fp16(kv_mode, pool, kc, vc, stage, bt_row, count, hk_idx, D):
+    """History K/V ``[count, D]`` of one KV head as the kernel sees it (fp16-rounded)."""
+    pos = torch.arange(count, device=bt_row.device)
+    blocks = bt_row[pos // fmt.PAGE].long()
+    offs = pos % fmt.PAGE
+    if kv_mode == 1:
+        k = kc[blocks, offs, hk_idx].float()
+        v = vc[blocks, offs, hk_idx].float()
+    else:
+        kk, vv = fmt.dequant_tokens(pool, blocks, offs, D)
+        k, v = kk[:, hk_idx], vv[:, hk_idx]
+    if stage is not None and count:
+        sk, sv, owner, rows = stage
+        r = blocks % rows
+        hit = (owner.view(rows, fmt.PAGE)[r, offs].long() == blocks).unsqueeze(-1)
+        k = torch.where(hit, sk.view(rows, fmt.PAGE, -1, D)[r, offs, hk_idx], k)
+        v = torch.where(hit, sv.view(rows, fmt.PAGE, -1, D)[r, offs, hk_idx], v)
+    return k.half().float(), v.half().float()
+
+
+def attention_ref(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, stage, block_tables,
+                  q_start: list[int], seq_lens: list[int]) -> torch.Tensor:
+    """Rotated-space attention output ``[T, Hq, D]`` (fp32) with the kernel's inputs."""
+    T = q.shape[0]
+    g = Hq // Hk
+    out = torch.zeros(T, Hq, D, dtype=torch.float32, device=q.device)
+    for r in range(len(seq_lens)):
+        a, b = q_start[r], q_start[r + 1]
+        if b <= a:
+            continue
+        n = b - a
+        prefix = seq_lens[r] - n
+        for h in range(Hk):
+            kh, vh = _history_fp16(kv_mode, pool, kc, vc, stage, block_tables[r], prefix, h, D)
+            kk = torch.cat([kh, k_fresh[a:b, h].float()])
+            vv = torch.cat([vh, v_fresh[a:b, h].float()])
+            qq = q[a:b, h * g:(h + 1) * g].float()  # [n, g, D]
+            s = torch.einsum("ngd,ld->ngl", qq, kk) * scale
+            kpos = torch.arange(prefix + n, device=q.device)
+            lim = prefix + torch.arange(n, device=q.device)
+            mask = kpos.view(1, 1, -1) <= lim.view(-1, 1, 1)
+            s = s.masked_fill(~mask, float("-inf"))
+            p = torch.softmax(s, dim=-1)
+            out[a:b, h * g:(h + 1) * g] = torch.einsum("ngl,ld->ngd", p, vv)
+    return out
+
+
+def merge_ref(o_rot: torch.Tensor, RvT, gate, want_bf16: bool, want_q: bool):
+    """``o = bf16(o_rot @ R_vᵀ * sigmoid(gate))`` -> (bf16 ``[T, Hq*D]``, int8, scale)."""
+    T, Hq, D = o_rot.shape
+    o = o_rot @ RvT if RvT is not None else o_rot
+    if gate is not None:
+        o = o * torch.sigmoid(gate.float())
+    o = _bf16_round(o).reshape(T, Hq * D)
+    q, s = quantize_rows_ref(o) if want_q else (None, None)
+    return (o.to(torch.bfloat16) if want_bf16 else None), q, s
+
+
+def attention(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, stage, block_tables,
+              q_start_t, seq_lens_t, q_start: list[int], seq_lens: list[int], plan: AttnPlan | None,
+              tok_req, RvT, gate, gate_ld, gate_hstride, want_bf16=False, want_q=True,
+              part_o=None, part_lse=None, status=None):
+    """Attention + merge.  Returns ``(o_bf16 | None, o_int8 | None, o_scale | None)``.
+
+    ``stage`` is ``(stage_k, stage_v, owner, rows)`` or ``None``; ``gate`` is the bf16
+    qkv buffer view whose ``[t, h*gate_hstride + d]`` element gates output ``(t, h, d)``.
+    """
+    T = q.shape[0]
+    if not q.is_cuda:
+        o_rot = attention_ref(q, k_fresh, v_fresh, Hq=Hq, Hk=Hk, D=D, scale=scale, kv_mode=kv_mode, pool=pool,
+                              kc=kc, vc=vc, stage=stage, block_tables=block_tables, q_start=q_start,
+                              seq_lens=seq_lens)
+        g = None
+        if gate is not None:
+            g = torch.stack([gate[:, h * gate_hstride: h * gate_hstride + D] for h in range(Hq)], 1)
+        return merge_ref(o_rot, RvT, g, want_bf16, want_q)
+    e = ext()
+    assert plan is not None
+    if part_o is None or part_o.numel() < plan.n_work * Hk * ROWS * D:
+        part_o = torch.empty(plan.n_work * Hk * ROWS * D, dtype=torch.float32, device=q.device)
+        part_lse = torch.empty(plan.n_work * Hk * ROWS, dtype=torch.float32, device=q.device)
+    sk = sv = own = None
+    rows = 0
+    if stage is not None:
+        sk, sv, own, rows = stage
+    e.paged_attention(q, k_fresh, v_fresh, Hq, Hk, D, float(scale), kv_mode, pool, kc, vc, sk, sv, own, rows,
+                      block_tables, q_start_t, seq_lens_t, plan.work, part_o, part_lse, status)
+    o_bf16 = torch.empty(T, Hq * D, dtype=torch.bfloat16, device=q.device) if want_bf16 else None
+    o_q = torch.empty(T, Hq * D, dtype=torch.int8, device=q.device) if want_q else None
+    o_s = torch.empty(T, dtype=torch.float32, device=q.device) if want_q else None
+    e.attn_merge(part_o, part_lse, plan.item_first, plan.item_count, plan.max_rb, tok_req, q_start_t, Hq, Hk, D,
+                 RvT, gate, gate_ld, gate_hstride, o_bf16, o_q, o_s, T)
+    return o_bf16, o_q, o_s

@@ -1,0 +1,229 @@
+"""Device-dispatching functional ops.
+
+CUDA tensors always run the hand-written sm_100a kernels of ``oscar_b200._C`` (the
+call raises if the extension is missing); CPU tensors run a pure-torch reference of
+the same computation with the same rounding points.  The references are the
+numerics oracle of the GPU tests.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..kv import format as fmt
+from ._ext import ext
+
+_NUM_SMS: dict[int, int] = {}
+
+
+def num_sms(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _NUM_SMS:
+        _NUM_SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _NUM_SMS[idx]
+
+
+def _bf16_round(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).float()
+
+
+# ---------------------------------------------------------------------------
+# activation quantisation
+# ---------------------------------------------------------------------------
+def quantize_rows_ref(v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row symmetric int8: ``q = rint(v * 127 / absmax)``, ``scale = absmax / 127``."""
+    v = v.float()
+    amax = v.abs().amax(dim=-1)
+    inv = torch.where(amax > 0, 127.0 / amax, torch.zeros_like(amax))
+    q = torch.clamp(torch.round(v * inv.unsqueeze(-1)), -127, 127).to(torch.int8)
+    scale = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax))
+    return q, scale
+
+
+def act_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 ``[T, K]`` -> (int8 ``[T, K]``, fp32 scale ``[T]``)."""
+    if x.is_cuda:
+        T, K = x.shape
+        q = torch.empty(T, K, dtype=torch.int8, device=x.device)
+        s = torch.empty(T, dtype=torch.float32, device=x.device)
+        ext().act_quant(x, q, s)
+        return q, s
+    return quantize_rows_ref(x.float())
+
+
+def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float = 1.0,
+                  delta: torch.Tensor | None = None, want_q: bool = True, want_bf16: bool = False,
+                  out_q=None, out_s=None, out_bf16=None):
+    """RMSNorm of the fp32 residual ``x`` (optionally ``x += delta`` first, in place).
+
+    ``y = bf16(x * rsqrt(mean(x^2) + eps) * (offset + w))``; returns
+    ``(q int8, scale, y_bf16)`` with the parts not requested set to ``None``.
+    """
+    T, H = x.shape
+    if x.is_cuda:
+        q = out_q if out_q is not None else (torch.empty(T, H, dtype=torch.int8, device=x.device) if want_q else None)
+        s = out_s if out_s is not None else (torch.empty(T, dtype=torch.float32, device=x.device) if want_q else None)
+        y = out_bf16 if out_bf16 is not None else (torch.empty(T, H, dtype=torch.bfloat16, device=x.device) if want_bf16 else None)
+        ext().rmsnorm_quant(x, delta, w, float(offset), float(eps), q, s, y)
+        return q, s, y
+    if delta is not None:
+        x += delta.float()
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    y = _bf16_round(xf * inv * (offset + w.float()))
+    q, s = quantize_rows_ref(y) if want_q else (None, None)
+    return q, s, (y.to(torch.bfloat16) if want_bf16 else None)
+
+
+def swiglu_quant(gu: torch.Tensor, I: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 ``[T, 2I]`` laid out ``[gate | up]`` -> int8 ``silu(gate) * up`` + scale."""
+    T = gu.shape[0]
+    if gu.is_cuda:
+        q = torch.empty(T, I, dtype=torch.int8, device=gu.device)
+        s = torch.empty(T, dtype=torch.float32, device=gu.device)
+        ext().swiglu_quant(gu, I, q, s)
+        return q, s
+    g = gu[:, :I].float()
+    u = gu[:, I:2 * I].float()
+    return quantize_rows_ref(_bf16_round(torch.nn.functional.silu(g) * u))
+
+
+# ---------------------------------------------------------------------------
+# W8A8 GEMM
+# ---------------------------------------------------------------------------
+@dataclass
+class GemmPlan:
+    swap: bool
+    bn: int
+    splits: int
+
+
+def plan_gemm(M: int, N: int, K: int, sms: int, allow_split: bool) -> GemmPlan:
+    """Tile plan for ``y[M,N] = x[M,K] W[N,K]^T`` on ``sms`` SMs."""
+    kblocks = max(1, (K + 127) // 128)
+    if M <= 256:
+        bn = 32 if M <= 32 else 64 if M <= 64 else 128 if M <= 128 else 256
+        tiles = (N + 127) // 128
+        swap = True
+    else:
+        bn = 256 if N >= 2048 else 128
+        tiles = ((M + 127) // 128) * ((N + bn - 1) // bn)
+        swap = False
+    splits = 1
+    if allow_split and tiles < sms:
+        splits = max(1, min(sms // max(tiles, 1), kblocks // 4, 16))
+    return GemmPlan(swap, bn, splits)
+
+
+def linear_i8(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+              out: torch.Tensor | None = None, accumulate: bool = False,
+              status: torch.Tensor | None = None) -> torch.Tensor:
+    """``out = (xq @ wq^T) * xs[:, None] * ws[None, :]``.
+
+    bf16 output by default.  With ``accumulate=True`` the result is *added* in fp32 to
+    ``out`` (the fp32 residual-delta buffer), which also enables split-K.
+    """
+    M, K = xq.shape
+    N = wq.shape[0]
+    if not xq.is_cuda:
+        y = (xq.double() @ wq.double().t()) * xs.double().unsqueeze(1) * ws.double().unsqueeze(0)
+        if accumulate:
+            assert out is not None
+            out += y.float()
+            return out
+        y = y.float().to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    e = ext()
+    plan = plan_gemm(M, N, K, num_sms(xq.device), allow_split=accumulate)
+    if accumulate:
+        assert out is not None and out.dtype == torch.float32
+        mode = 1
+    else:
+        if out is None:
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=xq.device)
+        mode = 0
+    if plan.swap:
+        e.gemm_i8(wq, xq, ws, xs, out, mode, 1, plan.bn, plan.splits if accumulate else 1, status)
+    else:
+        e.gemm_i8(xq, wq, xs, ws, out, mode, 0, plan.bn, plan.splits if accumulate else 1, status)
+    return out
+
+
+def quantize_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel symmetric int8 weight quantisation: ``w ~ q * s[:, None]``."""
+    amax = w.float().abs().amax(dim=1).clamp(min=1e-8)
+    s = amax / 127.0
+    q = torch.clamp(torch.round(w.float() / s.unsqueeze(1)), -127, 127).to(torch.int8)
+    return q, s.float()
+
+
+# ---------------------------------------------------------------------------
+# embedding / sampling
+# ---------------------------------------------------------------------------
+def embed(tokens: torch.Tensor, table: torch.Tensor, vocab_begin: int, out: torch.Tensor) -> torch.Tensor:
+    """fp32 rows of a (vocab-parallel) bf16 table; ids outside this shard give zeros."""
+    V = table.shape[0]
+    if tokens.is_cuda:
+        ext().embed(tokens, table, vocab_begin, vocab_begin + V, out)
+        return out
+    ids = tokens.long() - vocab_begin
+    mine = (ids >= 0) & (ids < V)
+    rows = table[ids.clamp(0, V - 1)].float()
+    out.copy_(torch.where(mine.unsqueeze(1), rows, torch.zeros_like(rows)))
+    return out
+
+
+def argmax(logits: torch.Tensor, index_offset: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Row-wise (max value, global index) of bf16 logits; ties -> lowest index."""
+    T = logits.shape[0]
+    if logits.is_cuda:
+        v = torch.empty(T, dtype=torch.float32, device=logits.device)
+        i = torch.empty(T, dtype=torch.int32, device=logits.device)
+        ext().argmax(logits, index_offset, v, i)
+        return v, i
+    v, i = logits.float().max(dim=-1)
+    return v, (i + index_offset).to(torch.int32)
+
+
+# ---------------------------------------------------------------------------
+# RoPE tables
+# ---------------------------------------------------------------------------
+def rope_tables(max_pos: int, rot_dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 ``cos/sin [max_pos, rot_dim/2]`` for rotate-half RoPE."""
+    inv = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.float64) / rot_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64).unsqueeze(1) * inv.unsqueeze(0)
+    return ang.cos().float().to(device), ang.sin().float().to(device)
+
+
+def apply_rope_ref(x: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, rot_dim: int):
+    """``x [T, H, D]`` fp32; rotate-half RoPE on the first ``rot_dim`` dims, bf16-rounded."""
+    half = rot_dim // 2
+    c = cos[pos.long()].unsqueeze(1)
+    s = sin[pos.long()].unsqueeze(1)
+    a = x[..., :half].clone()
+    b = x[..., half:rot_dim].clone()
+    out = x.clone()
+    out[..., :half] = _bf16_round(a * c - b * s)
+    out[..., half:rot_dim] = _bf16_round(b * c + a * s)
+    return out
+
+
+def head_rmsnorm_ref(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float) -> torch.Tensor:
+    inv = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+    return _bf16_round(x * inv * (offset + w.float()))
+
+
+def default_softmax_scale(D: int) -> float:
+    return 1.0 / math.sqrt(D)
+
+
+__all__ = [
+    "act_quant", "rmsnorm_quant", "swiglu_quant", "linear_i8", "plan_gemm", "quantize_weight",
+    "quantize_rows_ref", "embed", "argmax", "rope_tables", "apply_rope_ref", "head_rmsnorm_ref",
+    "num_sms", "fmt",
+]
