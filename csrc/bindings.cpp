@@ -44,6 +44,14 @@ T* ptr(const Tensor& t) {
 }
 template <typename T>
 T* optr(const optional<Tensor>& t) {
+  if (!(t.has_value() && t->defined())) return nullptr;
+  TORCH_CHECK(t->is_contiguous(), "oscar_b200: tensor operands must be contiguous (got strides ", t->strides(), ")");
+  TORCH_CHECK(t->is_cuda(), "oscar_b200: tensor operands must be CUDA tensors");
+  return reinterpret_cast<T*>(t->data_ptr());
+}
+// Same, for operands the kernels index row-wise with their own stride (views allowed).
+template <typename T>
+T* optr_view(const optional<Tensor>& t) {
   return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
 }
 
@@ -102,6 +110,11 @@ void kv_store(const Tensor& qkv, int64_t q_off, int64_t q_head_stride, int64_t k
   CHECK_DTYPE(k_fresh, at::kHalf);
   CHECK_DTYPE(slots, at::kInt);
   CHECK_DTYPE(positions, at::kInt);
+  CHECK_CONTIG(slots);
+  CHECK_CONTIG(positions);
+  CHECK_CONTIG(q_out);
+  CHECK_CONTIG(k_fresh);
+  CHECK_CONTIG(v_fresh);
   if (kv_mode == 0) {
     TORCH_CHECK(pool.has_value() && pool->scalar_type() == at::kByte && pool->is_contiguous(), "INT2 pool");
   } else {
@@ -166,6 +179,13 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
   CHECK_CONTIG(k_fresh);
   CHECK_CONTIG(v_fresh);
   CHECK_CONTIG(block_tables);
+  CHECK_CONTIG(work);
+  CHECK_CONTIG(q_start);
+  CHECK_CONTIG(seq_lens);
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(work.data_ptr()) % 16 == 0, "attention work list must be 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(k_fresh.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(v_fresh.data_ptr()) % 16 == 0,
+              "attention q / fresh k,v must be 16-byte aligned");
   oscar::AttnParams p{};
   p.q = ptr<__half>(q);
   p.k_fresh = ptr<__half>(k_fresh);
@@ -214,7 +234,7 @@ void attn_merge(const Tensor& part_o, const Tensor& part_lse, const Tensor& item
   p.Hk = Hk;
   p.D = D;
   p.RvT = optr<float>(RvT);
-  p.gate = optr<__nv_bfloat16>(gate);
+  p.gate = optr_view<__nv_bfloat16>(gate);
   p.gate_ld = gate_ld;
   p.gate_hstride = gate_hstride;
   p.out_bf16 = optr<__nv_bfloat16>(out_bf16);
@@ -234,6 +254,9 @@ void gdn_step(const Tensor& qkvz, const Tensor& ba, int64_t Hk, int64_t Hv, int6
   CHECK_DTYPE(state, at::kBFloat16);
   CHECK_DTYPE(conv_state, at::kBFloat16);
   TORCH_CHECK(qkvz.stride(1) == 1 && ba.stride(1) == 1, "gdn_step: rows must be contiguous");
+  for (const Tensor* t : {&conv_w, &A_log, &dt_bias, &norm_w, &state, &conv_state, &pend_x, &pend_ba, &parity,
+                          &req_slot, &q_start, &n_commit, &keep_pending, &out})
+    TORCH_CHECK(t->is_contiguous(), "gdn_step: state/metadata tensors must be contiguous");
   oscar::GdnParams p{};
   p.qkvz = ptr<__nv_bfloat16>(qkvz);
   p.ld_qkvz = qkvz.stride(0);

@@ -166,7 +166,7 @@ class LLMEngine:
     def _upload(self, arrays: dict) -> dict:
         """Pack int32 host arrays into one pinned buffer and upload them with one copy."""
         flat = [np.ascontiguousarray(np.asarray(v, dtype=np.int32)).reshape(-1) for v in arrays.values()]
-        n = sum(f.size for f in flat)
+        n = sum((f.size + 3) // 4 * 4 for f in flat)
         if self.dev.type != "cuda":
             out, off = {}, 0
             for (k, v), f in zip(arrays.items(), flat):
@@ -184,7 +184,7 @@ class LLMEngine:
         for f in flat:
             host[off:off + f.size] = f
             spans.append((off, f.size))
-            off += f.size
+            off += (f.size + 3) // 4 * 4  # keep every array 16-byte aligned (int4 loads)
         dbuf = torch.empty(n, dtype=torch.int32, device=self.dev)
         dbuf.copy_(self._pin[:n], non_blocking=True)
         self._pin_event = torch.cuda.Event()

@@ -117,13 +117,19 @@ def _qkv_layout(Hq, Hk, D):
 
 @pytest.mark.parametrize("rot", [False, True])
 def test_kv_store_matches_ref(rot):
+    """rot=False: no norm / RoPE / rotation, so the quantiser sees identical inputs and
+    codes, meta and staging must be bit-exact.  rot=True: the full fused pipeline; the
+    q/k norm and RoPE outputs may differ by one bf16 ulp (rsqrt rounding), so codes are
+    compared statistically."""
     torch.manual_seed(0)
     Hq, Hk, D, T = 6, 1, 256, 300
     q_off, qhs, k_off, v_off, N = _qkv_layout(Hq, Hk, D)
     qkv = (torch.randn(T, N) * 2).to(torch.bfloat16)
     pos = torch.arange(T, dtype=torch.int32) + 5
     cos, sin = F.rope_tables(1024, 64, 1e7, "cpu")
-    qn, kn = torch.randn(D) * 0.1, torch.randn(D) * 0.1
+    qn, kn = (torch.randn(D) * 0.1, torch.randn(D) * 0.1) if rot else (None, None)
+    if not rot:
+        cos = sin = None
     Rk = torch.linalg.qr(torch.randn(D, D)).Q if rot else None
     Rv = torch.linalg.qr(torch.randn(D, D)).Q if rot else None
     nb = 8
@@ -144,7 +150,7 @@ def test_kv_store_matches_ref(rot):
         vf = torch.empty_like(kf)
         A.kv_store(tens(qkv), q_off=q_off, q_head_stride=qhs, k_off=k_off, v_off=v_off, Hq=Hq, Hk=Hk, D=D,
                    q_norm_w=tens(qn), k_norm_w=tens(kn), eps=1e-6, norm_offset=1.0, positions=tens(pos),
-                   rope_cos=tens(cos), rope_sin=tens(sin), rot_dim=64, Rk=tens(Rk), Rv=tens(Rv), k_clip_idx=245,
+                   rope_cos=tens(cos), rope_sin=tens(sin), rot_dim=64 if rot else 0, Rk=tens(Rk), Rv=tens(Rv), k_clip_idx=245,
                    v_clip_idx=235, q_out=qo, k_fresh=kf, v_fresh=vf, kv_mode=0, pool=pool, kc=None, vc=None,
                    slots=tens(slots), stage_k=sk, stage_v=sv, stage_seat=tens(torch.from_numpy(ss)),
                    owner=owner, owner_seat=tens(torch.from_numpy(os_)), owner_val=tens(torch.from_numpy(ov)))
@@ -153,7 +159,7 @@ def test_kv_store_matches_ref(rot):
     assert _rel(g[0].float(), c[0].float()) < 2e-3
     assert _rel(g[1].float(), c[1].float()) < 2e-3
     assert torch.equal(g[6], c[6])
-    assert _rel(g[4], c[4]) < 1e-5
+    assert _rel(g[4], c[4]) < (1e-3 if rot else 1e-7)
     # INT2 codes and meta: exact without rotation; with rotation a tiny fraction of
     # codes may sit on the other side of a rounding boundary (fp32 summation order).
     kc_c, vc_c, *mc = fmt.page_views(c[3], D)
