@@ -254,7 +254,7 @@ void gdn_step(const Tensor& qkvz, const Tensor& ba, int64_t Hk, int64_t Hv, int6
   CHECK_DTYPE(state, at::kBFloat16);
   CHECK_DTYPE(conv_state, at::kBFloat16);
   TORCH_CHECK(qkvz.stride(1) == 1 && ba.stride(1) == 1, "gdn_step: rows must be contiguous");
-  for (const Tensor* t : {&conv_w, &A_log, &dt_bias, &norm_w, &state, &conv_state, &pend_x, &pend_ba, &parity,
+  for (const Tensor* t : std::initializer_list<const Tensor*>{&conv_w, &A_log, &dt_bias, &norm_w, &state, &conv_state, &pend_x, &pend_ba, &parity,
                           &req_slot, &q_start, &n_commit, &keep_pending, &out})
     TORCH_CHECK(t->is_contiguous(), "gdn_step: state/metadata tensors must be contiguous");
   oscar::GdnParams p{};
