@@ -45,8 +45,8 @@ T* ptr(const Tensor& t) {
 template <typename T>
 T* optr(const optional<Tensor>& t) {
   if (!(t.has_value() && t->defined())) return nullptr;
-  TORCH_CHECK(t->is_contiguous(), "oscar_b200: tensor operands must be contiguous (got strides ", t->strides(), ")");
   TORCH_CHECK(t->is_cuda(), "oscar_b200: tensor operands must be CUDA tensors");
+  TORCH_CHECK(t->is_contiguous(), "oscar_b200: tensor operands must be contiguous");
   return reinterpret_cast<T*>(t->data_ptr());
 }
 // Same, for operands the kernels index row-wise with their own stride (views allowed).

@@ -130,8 +130,8 @@ def test_kv_store_matches_ref(rot):
     qn, kn = (torch.randn(D) * 0.1, torch.randn(D) * 0.1) if rot else (None, None)
     if not rot:
         cos = sin = None
-    Rk = torch.linalg.qr(torch.randn(D, D)).Q if rot else None
-    Rv = torch.linalg.qr(torch.randn(D, D)).Q if rot else None
+    Rk = torch.linalg.qr(torch.randn(D, D)).Q.contiguous() if rot else None
+    Rv = torch.linalg.qr(torch.randn(D, D)).Q.contiguous() if rot else None
     nb = 8
     slots = torch.randperm(nb * fmt.PAGE)[:T].to(torch.int32)
     slots[7] = -1
