@@ -16,6 +16,8 @@
 #include "common.cuh"
 #include "params.h"
 
+#include <mutex>
+
 namespace oscar {
 
 
@@ -486,4 +488,86 @@ extern "C" int oscar_attn_merge(const oscar::MergeParams* params, cudaStream_t s
   }
   attn_merge_kernel<<<p.T, 256, smem, stream>>>(p);
   return (int)cudaGetLastError();
+}
+
+// ============================================================================
+// No-allocation entry point.
+//
+// This entry point has no counterpart in the reference (which has no CUDA code).
+// It serves callers that cannot allocate device memory at the time they launch
+// attention: code running inside a custom allocator or memory-pool callback,
+// embedders whose runtime forbids cudaMalloc on the serving path (it can
+// synchronise the device and stall other streams), and hosts that must run with
+// a fixed memory footprint decided at start-up.  Such callers pass their inputs
+// and outputs exactly as for oscar_paged_attention + oscar_attn_merge, but no
+// workspace: the split-KV partial results live in a fixed device array that is
+// part of this library's image.
+//
+// Limits and contract:
+//   * the scratch holds at most kNoAllocItems (work item x KV head) partials of
+//     64 rows x 256 dims in fp32 (16 MiB) plus their log-sum-exps (64 KiB); a call
+//     with n_work * Hk above that is rejected with -310 before anything launches;
+//   * every GPU that loads this library keeps those 16.06 MiB until the process
+//     exits;
+//   * every call on a device shares the same array and leaves its contents
+//     behind; each call overwrites every partial it later reads, so nothing needs
+//     to start at zero, but calls whose kernels overlap on the GPU (different
+//     streams without ordering between them) race on the array and must be
+//     serialised by the caller;
+//   * the first call on each device resolves the array's device address with
+//     cudaGetSymbolAddress while that device is current; make that first call
+//     before any stream capture;
+//   * the entry point itself calls no cudaMalloc, cudaFree or other allocating
+//     routine.
+// ============================================================================
+namespace oscar {
+namespace {
+constexpr int kNoAllocItems = 256;
+constexpr size_t kNoAllocPartO = (size_t)kNoAllocItems * kRows * kD;  // floats
+constexpr size_t kNoAllocPartL = (size_t)kNoAllocItems * kRows;       // floats
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocPartO + kNoAllocPartL];
+
+constexpr int kMaxDevices = 64;
+float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return -311;
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return (int)e;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+}  // namespace
+}  // namespace oscar
+
+// Same inputs and outputs as oscar_paged_attention followed by oscar_attn_merge;
+// the part_o / part_lse fields of both parameter blocks are ignored.
+extern "C" int oscar_paged_attention_noalloc(const oscar::AttnParams* attn, const oscar::MergeParams* merge,
+                                             cudaStream_t stream) {
+  using namespace oscar;
+  if (!attn || !merge) return -312;
+  if (attn->n_work <= 0 || merge->T <= 0) return 0;
+  if (attn->D != kD || merge->D != kD) return -300;
+  if ((long long)attn->n_work * attn->Hk > kNoAllocItems) return -310;
+  float* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  AttnParams a = *attn;
+  a.part_o = scratch;
+  a.part_lse = scratch + kNoAllocPartO;
+  MergeParams m = *merge;
+  m.part_o = a.part_o;
+  m.part_lse = a.part_lse;
+  rc = oscar_paged_attention(&a, stream);
+  if (rc) return rc;
+  return oscar_attn_merge(&m, stream);
 }
