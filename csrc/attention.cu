@@ -59,11 +59,12 @@ OSCAR_DEVICE uint32_t h2_u32(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Dequantise 16 INT2 codes (one 32-bit word, code k at bits 2k) into 16 fp16.
+// Dequantise 16 INT2 codes (one 32-bit word in pool bit order: dim 2m+e at bit
+// 16e+2m) into 16 fp16.
 OSCAR_DEVICE void dequant16(uint32_t w, float s, float z, uint4& lo, uint4& hi) {
   float v[16];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) v[k] = fmaf((float)((w >> (2 * k)) & 3u), s, z);
+  for (int k = 0; k < 16; ++k) v[k] = fmaf((float)((w >> (16 * (k & 1) + 2 * (k >> 1))) & 3u), s, z);
   lo.x = h2_u32(v[0], v[1]);
   lo.y = h2_u32(v[2], v[3]);
   lo.z = h2_u32(v[4], v[5]);
@@ -459,10 +460,13 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(MergeParams p) {
 }  // namespace
 }  // namespace oscar
 
+extern "C" int oscar_int2_attention(const oscar::AttnParams* params, cudaStream_t stream);
+
 extern "C" int oscar_paged_attention(const oscar::AttnParams* params, cudaStream_t stream) {
   using namespace oscar;
   const AttnParams& p = *params;
   if (p.n_work <= 0) return 0;
+  if (p.kv_mode == 0) return oscar_int2_attention(params, stream);  // pipelined code-domain kernel
   if (p.D != kD) return -300;
   const size_t smem = (kRows + 2 * kTile) * kRowBytes;
   static bool attr = false;

@@ -16,9 +16,16 @@ int oscar_num_sms();
 int oscar_kv_store(const oscar::StoreParams* p, cudaStream_t stream);
 int oscar_paged_attention(const oscar::AttnParams* p, cudaStream_t stream);
 int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
+int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi, const __nv_bfloat16* Rv_lo,
+                         cudaStream_t stream);
 int oscar_gdn_step(const oscar::GdnParams* p, int smem_state, cudaStream_t stream);
-int oscar_rmsnorm_quant(float* x, long long ldx, const float* delta, long long ldd, const float* w, float off,
-                        float eps, int T, int H, int8_t* out, float* scale, __nv_bfloat16* out_bf16, cudaStream_t s);
+int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long long ldd, const float* w, float off, float eps,
+                        int T, int H, int8_t* out, float* scale, __nv_bfloat16* out_bf16, const unsigned* signals,
+                        const int* epoch, int world, int zero_delta, int* status, cudaStream_t s);
+int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                     const float* scale_a, const float* scale_b, void* out, long long ldo, int mode, int trans, int bn,
+                     int splits, int* status, int* done_counter, int* epoch, unsigned** peer_signals, int rank,
+                     int world, cudaStream_t stream);
 int oscar_swiglu_quant(const __nv_bfloat16* gu, long long ld, int T, int I, int8_t* out, float* scale,
                        cudaStream_t s);
 int oscar_act_quant(const __nv_bfloat16* x, long long ld, int T, int K, int8_t* out, float* scale, cudaStream_t s);
@@ -92,6 +99,25 @@ void gemm_i8(const Tensor& A, const Tensor& B, const Tensor& scale_a, const Tens
            "gemm_i8");
 }
 
+// Row-parallel GEMM whose epilogue reduces into every rank's buffer through the NVLS
+// multicast address `mc_ptr` (raw device address from the symmetric-memory handle),
+// then publishes the completion epoch into every peer's signal pad.
+void gemm_i8_allreduce(const Tensor& A, const Tensor& B, const Tensor& scale_a, const Tensor& scale_b, int64_t mc_ptr,
+                       int64_t ldo, int64_t trans, int64_t bn, int64_t splits, Tensor& done_counter, Tensor& epoch,
+                       int64_t peer_signals_dev, int64_t rank, int64_t world, const optional<Tensor>& status) {
+  CHECK_DTYPE(A, at::kChar);
+  CHECK_DTYPE(B, at::kChar);
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_i8_allreduce: K must be contiguous");
+  TORCH_CHECK(mc_ptr != 0 && peer_signals_dev != 0, "gemm_i8_allreduce: multicast / signal pointers required");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_rc(oscar_gemm_i8_ex(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), M, N, K, ptr<float>(scale_a),
+                            ptr<float>(scale_b), reinterpret_cast<void*>(mc_ptr), ldo, 3, (int)trans, (int)bn,
+                            (int)splits, optr<int>(status), ptr<int>(done_counter), ptr<int>(epoch),
+                            reinterpret_cast<unsigned**>(peer_signals_dev), (int)rank, (int)world, stream()),
+           "gemm_i8_allreduce");
+}
+
 int64_t num_sms() { return oscar_num_sms(); }
 
 void kv_store(const Tensor& qkv, int64_t q_off, int64_t q_head_stride, int64_t k_off, int64_t v_off, int64_t Hq,
@@ -102,7 +128,9 @@ void kv_store(const Tensor& qkv, int64_t q_off, int64_t q_head_stride, int64_t k
               Tensor& v_fresh, int64_t kv_mode, const optional<Tensor>& pool, const optional<Tensor>& kc,
               const optional<Tensor>& vc, const Tensor& slots, const optional<Tensor>& stage_k,
               const optional<Tensor>& stage_v, const optional<Tensor>& stage_seat, const optional<Tensor>& owner,
-              const optional<Tensor>& owner_seat, const optional<Tensor>& owner_val, const optional<Tensor>& status) {
+              const optional<Tensor>& owner_seat, const optional<Tensor>& owner_val, const optional<Tensor>& status,
+              const optional<Tensor>& RkT_hi, const optional<Tensor>& RkT_lo, const optional<Tensor>& RvT_hi,
+              const optional<Tensor>& RvT_lo, Tensor& xbuf) {
   CHECK_CUDA(qkv);
   CHECK_DTYPE(qkv, at::kBFloat16);
   TORCH_CHECK(qkv.stride(1) == 1, "qkv rows must be contiguous");
@@ -140,6 +168,14 @@ void kv_store(const Tensor& qkv, int64_t q_off, int64_t q_head_stride, int64_t k
   p.rot_dim = rot_dim;
   p.Rk = optr<float>(Rk);
   p.Rv = optr<float>(Rv);
+  p.RkT_hi = optr<__nv_bfloat16>(RkT_hi);
+  p.RkT_lo = optr<__nv_bfloat16>(RkT_lo);
+  p.RvT_hi = optr<__nv_bfloat16>(RvT_hi);
+  p.RvT_lo = optr<__nv_bfloat16>(RvT_lo);
+  CHECK_DTYPE(xbuf, at::kBFloat16);
+  CHECK_CONTIG(xbuf);
+  TORCH_CHECK(xbuf.numel() >= qkv.size(0) * (Hq + 2 * Hk) * D, "kv_store: xbuf too small");
+  p.xbuf = ptr<__nv_bfloat16>(xbuf);
   p.k_clip_idx = k_clip_idx;
   p.v_clip_idx = v_clip_idx;
   p.q_out = ptr<__half>(q_out);
@@ -245,6 +281,35 @@ void attn_merge(const Tensor& part_o, const Tensor& part_lse, const Tensor& item
   check_rc(oscar_attn_merge(&p, stream()), "attn_merge");
 }
 
+void attn_merge_rot(const Tensor& part_o, const Tensor& part_lse, const Tensor& item_first,
+                    const Tensor& item_count, int64_t max_rb, const Tensor& tok_req, const Tensor& q_start, int64_t Hq,
+                    int64_t Hk, int64_t D, const optional<Tensor>& gate, int64_t gate_ld, int64_t gate_hstride,
+                    Tensor& out_bf16, int64_t T, const Tensor& Rv_hi, const Tensor& Rv_lo) {
+  CHECK_DTYPE(out_bf16, at::kBFloat16);
+  CHECK_CONTIG(out_bf16);
+  CHECK_DTYPE(Rv_hi, at::kBFloat16);
+  CHECK_CONTIG(Rv_hi);
+  CHECK_CONTIG(Rv_lo);
+  oscar::MergeParams p{};
+  p.part_o = ptr<float>(part_o);
+  p.part_lse = ptr<float>(part_lse);
+  p.item_first = ptr<int>(item_first);
+  p.item_count = ptr<int>(item_count);
+  p.max_rb = max_rb;
+  p.tok_req = ptr<int>(tok_req);
+  p.q_start = ptr<int>(q_start);
+  p.Hq = Hq;
+  p.Hk = Hk;
+  p.D = D;
+  p.gate = optr_view<__nv_bfloat16>(gate);
+  p.gate_ld = gate_ld;
+  p.gate_hstride = gate_hstride;
+  p.out_bf16 = ptr<__nv_bfloat16>(out_bf16);
+  p.T = T;
+  const c10::cuda::CUDAGuard guard(part_o.device());
+  check_rc(oscar_attn_merge_rot(&p, ptr<__nv_bfloat16>(Rv_hi), ptr<__nv_bfloat16>(Rv_lo), stream()), "attn_merge_rot");
+}
+
 void gdn_step(const Tensor& qkvz, const Tensor& ba, int64_t Hk, int64_t Hv, int64_t dk, int64_t dv,
               const Tensor& conv_w, const Tensor& A_log, const Tensor& dt_bias, const Tensor& norm_w, double eps,
               Tensor& state, Tensor& conv_state, Tensor& pend_x, Tensor& pend_ba, const Tensor& parity,
@@ -290,16 +355,19 @@ void gdn_step(const Tensor& qkvz, const Tensor& ba, int64_t Hk, int64_t Hv, int6
 }
 
 void rmsnorm_quant(Tensor& x, const optional<Tensor>& delta, const Tensor& w, double off, double eps,
-                   const optional<Tensor>& out, const optional<Tensor>& scale, const optional<Tensor>& out_bf16) {
+                   const optional<Tensor>& out, const optional<Tensor>& scale, const optional<Tensor>& out_bf16,
+                   int64_t signals_ptr, const optional<Tensor>& epoch, int64_t world, int64_t zero_delta,
+                   const optional<Tensor>& status) {
   CHECK_DTYPE(x, at::kFloat);
   CHECK_DTYPE(w, at::kFloat);
   TORCH_CHECK(x.stride(1) == 1, "rmsnorm_quant: rows must be contiguous");
   const bool has_d = delta.has_value() && delta->defined();
   if (has_d) TORCH_CHECK(delta->scalar_type() == at::kFloat && delta->stride(1) == 1, "delta must be fp32 rows");
   const c10::cuda::CUDAGuard guard(x.device());
-  check_rc(oscar_rmsnorm_quant(ptr<float>(x), x.stride(0), optr<float>(delta), has_d ? delta->stride(0) : 0,
+  check_rc(oscar_rmsnorm_quant(ptr<float>(x), x.stride(0), optr_view<float>(delta), has_d ? delta->stride(0) : 0,
                                ptr<float>(w), off, eps, x.size(0), x.size(1), optr<int8_t>(out), optr<float>(scale),
-                               optr<__nv_bfloat16>(out_bf16), stream()),
+                               optr<__nv_bfloat16>(out_bf16), reinterpret_cast<const unsigned*>(signals_ptr),
+                               optr<int>(epoch), (int)world, (int)zero_delta, optr<int>(status), stream()),
            "rmsnorm_quant");
 }
 
@@ -352,10 +420,12 @@ void f32_to_bf16(const Tensor& x, Tensor& y) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "oscar_b200 sm_100a kernels";
   m.def("gemm_i8", &gemm_i8);
+  m.def("gemm_i8_allreduce", &gemm_i8_allreduce);
   m.def("num_sms", &num_sms);
   m.def("kv_store", &kv_store);
   m.def("paged_attention", &paged_attention);
   m.def("attn_merge", &attn_merge);
+  m.def("attn_merge_rot", &attn_merge_rot);
   m.def("gdn_step", &gdn_step);
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("swiglu_quant", &swiglu_quant);

@@ -12,94 +12,190 @@
 namespace oscar {
 namespace {
 
-constexpr int kT = 256;  // threads per token-block
+constexpr int kT = 256;  // threads of the argmax kernel
 
-// Per-token symmetric int8 quantisation of `n` values held in registers.
-template <int PER>
-OSCAR_DEVICE void quant_store(const float (&v)[PER], int n_valid_base, int H, int8_t* out_row, float* scale_out,
-                              float* red) {
-  float amax = 0.f;
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int i = n_valid_base + e * kT;
-    if (i < H) amax = fmaxf(amax, fabsf(v[e]));
-  }
-  amax = block_max<kT / 32>(amax, red);
-  const float inv = amax > 0.f ? 127.f / amax : 0.f;
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int i = n_valid_base + e * kT;
-    if (i < H) out_row[i] = quant_i8(v[e], inv);
-  }
-  if (threadIdx.x == 0) *scale_out = amax > 0.f ? amax / 127.f : 1.f;
+// Vectorised row kernels: thread t owns vectors t, t + NT, ... of the row (4 fp32
+// or 8 bf16 per 16-byte vector), all loaded before any arithmetic.
+template <int NT>
+OSCAR_DEVICE float row_absmax(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = l < NT / 32 ? red[l] : 0.f;
+  return warp_max(t);
+}
+template <int NT>
+OSCAR_DEVICE float row_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = l < NT / 32 ? red[l] : 0.f;
+  return warp_sum(t);
 }
 
-template <int PER>
-__global__ void __launch_bounds__(kT) rmsnorm_quant_kernel(float* __restrict__ x, long long ldx,
-                                                         const float* __restrict__ delta, long long ldd,
+OSCAR_DEVICE uint32_t pack_i8x4(float a, float b, float c, float d, float inv) {
+  const uint32_t x0 = (uint8_t)quant_i8(a, inv), x1 = (uint8_t)quant_i8(b, inv);
+  const uint32_t x2 = (uint8_t)quant_i8(c, inv), x3 = (uint8_t)quant_i8(d, inv);
+  return x0 | (x1 << 8) | (x2 << 16) | (x3 << 24);
+}
+
+// RMSNorm of an fp32 row (with optional fused residual add) -> bf16-rounded -> int8.
+// Cross-rank completion of a fused GEMM + all-reduce: wait (bounded) until every
+// rank has published the current epoch into this rank's signal pad.
+struct RankWait {
+  const unsigned* signals;  // this rank's signal pad, slot q written by rank q
+  const int* epoch;         // local epoch counter, bumped by the producing GEMM
+  int world;
+  int* status;
+};
+
+OSCAR_DEVICE void wait_ranks(const RankWait& rw) {
+  if (!rw.signals || threadIdx.x != 0) return;
+  const unsigned e = (unsigned)*rw.epoch;
+  const uint64_t t0 = globaltimer_ns();
+  for (int q = 0; q < rw.world; ++q) {
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(rw.signals + q) : "memory");
+      if ((int)(v - e) >= 0) break;
+      if (globaltimer_ns() - t0 > 5000000000ull) {  // 5 s: report instead of hanging
+        record_status(rw.status, kTimeoutPeerFlag);
+        return;
+      }
+    }
+  }
+}
+
+template <int NT, int PV>
+__global__ void __launch_bounds__(NT) rmsnorm_quant_kernel(float* __restrict__ x, long long ldx,
+                                                         float* __restrict__ delta, long long ldd,
                                                          const float* __restrict__ w, float off, float eps, int H,
                                                          int8_t* __restrict__ out, float* __restrict__ scale,
-                                                         __nv_bfloat16* __restrict__ out_bf16) {
-  __shared__ float red[kT / 32];
+                                                         __nv_bfloat16* __restrict__ out_bf16, RankWait rw,
+                                                         int zero_delta) {
+  __shared__ float red[NT / 32];
   const int t = blockIdx.x;
-  float* xr = x + (long long)t * ldx;
-  float v[PER];
+  wait_ranks(rw);
+  __syncthreads();
+  const int nv = H / 4;
+  float4* xr = reinterpret_cast<float4*>(x + (long long)t * ldx);
+  float4* dr = delta ? reinterpret_cast<float4*>(delta + (long long)t * ldd) : nullptr;
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  float4 v[PV];
   float ss = 0.f;
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int i = threadIdx.x + e * kT;
-    v[e] = i < H ? xr[i] : 0.f;
-    if (delta && i < H) {
-      v[e] += delta[(long long)t * ldd + i];  // fused residual add
-      xr[i] = v[e];
+  for (int e = 0; e < PV; ++e) {
+    const int i = threadIdx.x + e * NT;
+    v[e] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (dr && i < nv) {
+      const float4 d = dr[i];
+      v[e].x += d.x; v[e].y += d.y; v[e].z += d.z; v[e].w += d.w;
+      xr[i] = v[e];  // fused residual add
+      if (zero_delta) dr[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // ready for the next reduction
     }
-    ss += v[e] * v[e];
+    ss += v[e].x * v[e].x + v[e].y * v[e].y + v[e].z * v[e].z + v[e].w * v[e].w;
   }
-  ss = block_sum<kT / 32>(ss, red);
+  ss = row_sum<NT>(ss, red);
   const float inv = rsqrtf(ss / (float)H + eps);
+  float amax = 0.f;
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int i = threadIdx.x + e * kT;
-    if (i < H) {
-      v[e] = __bfloat162float(__float2bfloat16(v[e] * inv * (off + w[i])));
-      if (out_bf16) out_bf16[(long long)t * H + i] = __float2bfloat16(v[e]);
+  for (int e = 0; e < PV; ++e) {
+    const int i = threadIdx.x + e * NT;
+    if (i < nv) {
+      const float4 ww = wr[i];
+      v[e].x = __bfloat162float(__float2bfloat16(v[e].x * inv * (off + ww.x)));
+      v[e].y = __bfloat162float(__float2bfloat16(v[e].y * inv * (off + ww.y)));
+      v[e].z = __bfloat162float(__float2bfloat16(v[e].z * inv * (off + ww.z)));
+      v[e].w = __bfloat162float(__float2bfloat16(v[e].w * inv * (off + ww.w)));
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[e].x), fabsf(v[e].y)), fmaxf(fabsf(v[e].z), fabsf(v[e].w))));
+      if (out_bf16) {
+        uint2 b;
+        b.x = pack_bf16x2(v[e].x, v[e].y);
+        b.y = pack_bf16x2(v[e].z, v[e].w);
+        reinterpret_cast<uint2*>(out_bf16 + (long long)t * H)[i] = b;
+      }
     }
   }
-  if (out) quant_store<PER>(v, threadIdx.x, H, out + (long long)t * H, scale + t, red);
-}
-
-template <int PER>
-__global__ void __launch_bounds__(kT) swiglu_quant_kernel(const __nv_bfloat16* __restrict__ gu, long long ld, int I,
-                                                        int8_t* __restrict__ out, float* __restrict__ scale) {
-  __shared__ float red[kT / 32];
-  const int t = blockIdx.x;
-  const __nv_bfloat16* r = gu + (long long)t * ld;
-  float v[PER];
+  if (!out) return;
+  amax = row_absmax<NT>(amax, red);
+  const float qi = amax > 0.f ? 127.f / amax : 0.f;
+  uint32_t* o = reinterpret_cast<uint32_t*>(out + (long long)t * H);
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int i = threadIdx.x + e * kT;
-    if (i < I) {
-      const float g = __bfloat162float(r[i]), u = __bfloat162float(r[I + i]);
-      v[e] = __bfloat162float(__float2bfloat16(silu(g) * u));
-    } else {
-      v[e] = 0.f;
-    }
+  for (int e = 0; e < PV; ++e) {
+    const int i = threadIdx.x + e * NT;
+    if (i < nv) o[i] = pack_i8x4(v[e].x, v[e].y, v[e].z, v[e].w, qi);
   }
-  quant_store<PER>(v, threadIdx.x, I, out + (long long)t * I, scale + t, red);
+  if (threadIdx.x == 0) scale[t] = amax > 0.f ? amax / 127.f : 1.f;
 }
 
-template <int PER>
-__global__ void __launch_bounds__(kT) act_quant_kernel(const __nv_bfloat16* __restrict__ x, long long ld, int K,
+OSCAR_DEVICE void unpack_bf16x8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 a = __bfloat1622float2(h[k]);
+    f[2 * k] = a.x;
+    f[2 * k + 1] = a.y;
+  }
+}
+
+// silu(gate) * up (bf16 [gate | up] row) -> bf16-rounded -> int8 (kMode 0), or plain
+// bf16 row -> int8 (kMode 1).
+template <int NT, int PV, int kMode>
+__global__ void __launch_bounds__(NT) row_quant_kernel(const __nv_bfloat16* __restrict__ in, long long ld, int I,
                                                      int8_t* __restrict__ out, float* __restrict__ scale) {
-  __shared__ float red[kT / 32];
+  __shared__ float red[NT / 32];
   const int t = blockIdx.x;
-  float v[PER];
+  const int nv = I / 8;
+  const uint4* g = reinterpret_cast<const uint4*>(in + (long long)t * ld);
+  const uint4* u = reinterpret_cast<const uint4*>(in + (long long)t * ld + I);
+  uint4 gr[PV], ur[PV];
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int i = threadIdx.x + e * kT;
-    v[e] = i < K ? __bfloat162float(x[(long long)t * ld + i]) : 0.f;
+  for (int e = 0; e < PV; ++e) {
+    const int i = threadIdx.x + e * NT;
+    if (i < nv) {
+      gr[e] = g[i];
+      if (kMode == 0) ur[e] = u[i];
+    }
   }
-  quant_store<PER>(v, threadIdx.x, K, out + (long long)t * K, scale + t, red);
+  float amax = 0.f;
+  float vals[PV][8];
+#pragma unroll
+  for (int e = 0; e < PV; ++e) {
+    const int i = threadIdx.x + e * NT;
+    if (i < nv) {
+      float a[8];
+      unpack_bf16x8(gr[e], a);
+      if (kMode == 0) {
+        float b[8];
+        unpack_bf16x8(ur[e], b);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a[k] = __bfloat162float(__float2bfloat16(silu(a[k]) * b[k]));
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        vals[e][k] = a[k];
+        amax = fmaxf(amax, fabsf(a[k]));
+      }
+    }
+  }
+  amax = row_absmax<NT>(amax, red);
+  const float qi = amax > 0.f ? 127.f / amax : 0.f;
+  uint2* o = reinterpret_cast<uint2*>(out + (long long)t * I);
+#pragma unroll
+  for (int e = 0; e < PV; ++e) {
+    const int i = threadIdx.x + e * NT;
+    if (i < nv) {
+      uint2 q;
+      q.x = pack_i8x4(vals[e][0], vals[e][1], vals[e][2], vals[e][3], qi);
+      q.y = pack_i8x4(vals[e][4], vals[e][5], vals[e][6], vals[e][7], qi);
+      o[i] = q;
+    }
+  }
+  if (threadIdx.x == 0) scale[t] = amax > 0.f ? amax / 127.f : 1.f;
 }
 
 __global__ void embed_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ table, int H,
@@ -175,37 +271,44 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, long long n, __n
 
 using namespace oscar;
 
-#define OSCAR_PER_DISPATCH(H, CALL) \
-  do {                              \
-    const int per = ((H) + kT - 1) / kT; \
-    if (per <= 4) { constexpr int PER = 4; CALL; } \
-    else if (per <= 8) { constexpr int PER = 8; CALL; } \
-    else if (per <= 16) { constexpr int PER = 16; CALL; } \
-    else if (per <= 24) { constexpr int PER = 24; CALL; } \
-    else if (per <= 40) { constexpr int PER = 40; CALL; } \
-    else if (per <= 72) { constexpr int PER = 72; CALL; } \
-    else return -400; \
+#define OSCAR_PV_DISPATCH(NV, NT, CALL)              \
+  do {                                                \
+    const int pv = ((NV) + (NT) - 1) / (NT);          \
+    if (pv <= 1) { constexpr int PV = 1; CALL; }      \
+    else if (pv <= 2) { constexpr int PV = 2; CALL; } \
+    else if (pv <= 3) { constexpr int PV = 3; CALL; } \
+    else if (pv <= 5) { constexpr int PV = 5; CALL; } \
+    else if (pv <= 8) { constexpr int PV = 8; CALL; } \
+    else return -400;                                 \
   } while (0)
 
-extern "C" int oscar_rmsnorm_quant(float* x, long long ldx, const float* delta, long long ldd, const float* w,
+extern "C" int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long long ldd, const float* w,
                                    float off, float eps, int T, int H, int8_t* out, float* scale,
-                                   __nv_bfloat16* out_bf16, cudaStream_t s) {
+                                   __nv_bfloat16* out_bf16, const unsigned* signals, const int* epoch, int world,
+                                   int zero_delta, int* status, cudaStream_t s) {
   if (T <= 0) return 0;
-  OSCAR_PER_DISPATCH(H, (rmsnorm_quant_kernel<PER><<<T, kT, 0, s>>>(x, ldx, delta, ldd, w, off, eps, H, out, scale, out_bf16)));
+  if (H % 4 || ldx % 4 || (delta && ldd % 4)) return -401;
+  constexpr int NT = 256;
+  RankWait rw{signals, epoch, world, status};
+  OSCAR_PV_DISPATCH(H / 4, NT, (rmsnorm_quant_kernel<NT, PV><<<T, NT, 0, s>>>(x, ldx, delta, ldd, w, off, eps, H, out, scale, out_bf16, rw, zero_delta)));
   return (int)cudaGetLastError();
 }
 
 extern "C" int oscar_swiglu_quant(const __nv_bfloat16* gu, long long ld, int T, int I, int8_t* out, float* scale,
                                   cudaStream_t s) {
   if (T <= 0) return 0;
-  OSCAR_PER_DISPATCH(I, (swiglu_quant_kernel<PER><<<T, kT, 0, s>>>(gu, ld, I, out, scale)));
+  if (I % 8 || ld % 8) return -401;
+  constexpr int NT = 512;
+  OSCAR_PV_DISPATCH(I / 8, NT, (row_quant_kernel<NT, PV, 0><<<T, NT, 0, s>>>(gu, ld, I, out, scale)));
   return (int)cudaGetLastError();
 }
 
 extern "C" int oscar_act_quant(const __nv_bfloat16* x, long long ld, int T, int K, int8_t* out, float* scale,
                                cudaStream_t s) {
   if (T <= 0) return 0;
-  OSCAR_PER_DISPATCH(K, (act_quant_kernel<PER><<<T, kT, 0, s>>>(x, ld, K, out, scale)));
+  if (K % 8 || ld % 8) return -401;
+  constexpr int NT = 256;
+  OSCAR_PV_DISPATCH(K / 8, NT, (row_quant_kernel<NT, PV, 1><<<T, NT, 0, s>>>(x, ld, K, out, scale)));
   return (int)cudaGetLastError();
 }
 

@@ -216,6 +216,18 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             v.w = pack_bf16x2((float)(int)r[j + 6] * sa * ep.scale_b[nb + j + 6], (float)(int)r[j + 7] * sa * ep.scale_b[nb + j + 7]);
             *reinterpret_cast<uint4*>(o + j) = v;
           }
+        } else if (ep.mode == 3 && !ep.trans && nb + 32 <= N && (ep.ldo % 4) == 0) {
+          // prefill-shaped tile: 16-byte in-switch reductions along the row
+          float* o = reinterpret_cast<float*>(ep.out) + (long long)m * ep.ldo + nb;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(o + j),
+                         "f"((float)(int)r[j + 0] * sa * ep.scale_b[nb + j + 0]),
+                         "f"((float)(int)r[j + 1] * sa * ep.scale_b[nb + j + 1]),
+                         "f"((float)(int)r[j + 2] * sa * ep.scale_b[nb + j + 2]),
+                         "f"((float)(int)r[j + 3] * sa * ep.scale_b[nb + j + 3])
+                         : "memory");
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -227,6 +239,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               reinterpret_cast<__nv_bfloat16*>(ep.out)[idx] = __float2bfloat16(v);
             } else if (ep.mode == 1) {
               atomicAdd(reinterpret_cast<float*>(ep.out) + idx, v);
+            } else if (ep.mode == 3) {
+              // in-switch reduction: adds v into this element of every rank's buffer
+              asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(
+                               reinterpret_cast<float*>(ep.out) + idx),
+                           "f"(v)
+                           : "memory");
             } else {
               reinterpret_cast<float*>(ep.out)[idx] = v;
             }
@@ -239,11 +257,27 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   }
 
+  if (ep.mode == 3) __threadfence_system();  // this thread's reductions before the CTA's done count
   sm100::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if (ep.mode == 3 && threadIdx.x == 0) {
+    // every CTA's reductions are issued; the last CTA publishes the epoch to all ranks
+    __threadfence_system();
+    const int done = atomicAdd(ep.done_counter, 1) + 1;
+    if (done == (int)gridDim.x) {
+      __threadfence_system();
+      *ep.done_counter = 0;
+      const int e = *ep.epoch + 1;
+      *ep.epoch = e;
+      for (int q = 0; q < ep.world; ++q) {
+        unsigned* slot = ep.peer_signals[q] + ep.rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slot), "r"((unsigned)e) : "memory");
+      }
+    }
   }
 }
 
@@ -341,20 +375,35 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmEpi& ep, int 
 
 // A: [M, K] int8 (row stride lda bytes), B: [N, K] int8 (row stride ldb bytes).
 // bn must be 32, 64, 128 or 256.  Returns 0 or an error code.
+extern "C" int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                                const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
+                                int trans, int bn, int splits, int* status, int* done_counter, int* epoch,
+                                unsigned** peer_signals, int rank, int world, cudaStream_t stream);
+
 extern "C" int oscar_gemm_i8(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                              const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
                              int trans, int bn, int splits, int* status, cudaStream_t stream) {
+  if (mode == 3) return -105;  // the multimem mode needs the completion state: use oscar_gemm_i8_ex
+  return oscar_gemm_i8_ex(A, lda, B, ldb, M, N, K, scale_a, scale_b, out, ldo, mode, trans, bn, splits, status,
+                          nullptr, nullptr, nullptr, 0, 1, stream);
+}
+
+extern "C" int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                                const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
+                                int trans, int bn, int splits, int* status, int* done_counter, int* epoch,
+                                unsigned** peer_signals, int rank, int world, cudaStream_t stream) {
   using namespace oscar;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 16) || (lda % 16) || (ldb % 16)) return -102;
   if (splits < 1) splits = 1;
-  if (splits > 1 && mode != 1) return -104;  // split-K partial sums must be accumulated
+  if (splits > 1 && mode != 1 && mode != 3) return -104;  // split-K partial sums must be accumulated
+  if (mode == 3 && (!done_counter || !epoch || !peer_signals || world < 1)) return -106;
   CUtensorMap ta, tb;
   int rc = make_map(&ta, A, M, K, lda, BM);
   if (rc) return rc;
   rc = make_map(&tb, B, N, K, ldb, bn);
   if (rc) return rc;
-  GemmEpi ep{scale_a, scale_b, out, ldo, mode, trans};
+  GemmEpi ep{scale_a, scale_b, out, ldo, mode, trans, done_counter, epoch, peer_signals, rank, world};
   switch (bn) {
     case 32: return launch<32>(ta, tb, ep, M, N, K, splits, status, stream);
     case 64: return launch<64>(ta, tb, ep, M, N, K, splits, status, stream);

@@ -9,10 +9,16 @@ namespace oscar {
 struct GemmEpi {
   const float* scale_a;  // [M]
   const float* scale_b;  // [N]
-  void* out;
+  void* out;             // mode 3: NVLS multicast address of the fp32 reduction buffer
   long long ldo;         // elements between consecutive output rows
-  int mode;              // 0: bf16 store, 1: fp32 atomic add, 2: fp32 store
+  int mode;              // 0: bf16 store, 1: fp32 atomic add, 2: fp32 store, 3: fp32 multimem add
   int trans;             // 0: out[m * ldo + n], 1: out[n * ldo + m]
+  // mode 3 completion: the last CTA bumps *epoch and stores it into slot `rank` of
+  // every peer's signal pad (peer_signals[q] + rank) with release semantics.
+  int* done_counter;
+  int* epoch;
+  unsigned** peer_signals;
+  int rank, world;
 };
 
 struct StoreParams {
@@ -30,6 +36,13 @@ struct StoreParams {
   int rot_dim;
   const float* Rk;  // [D, D] or nullptr (identity)
   const float* Rv;
+  // Rotation split for the tensor-core path: R^T as bf16 hi + lo parts,
+  // [D(n)][D(k)] each (nullptr -> SIMT fp32 path with Rk/Rv above).
+  const __nv_bfloat16* RkT_hi;
+  const __nv_bfloat16* RkT_lo;
+  const __nv_bfloat16* RvT_hi;
+  const __nv_bfloat16* RvT_lo;
+  __nv_bfloat16* xbuf;  // scratch [T * (Hq + 2 Hk), D] normalised / roped rows
   int k_clip_idx, v_clip_idx;  // ascending-sort index of the clip threshold, -1 = no clip
   __half* q_out;    // [T, Hq, D]
   __half* k_fresh;  // [T, Hk, D]

@@ -31,6 +31,7 @@ from ..ops import attention as A
 from ..ops.functional import num_sms
 from .block_manager import BlockManager, SlotManager
 from .staging import seat_plan
+from ..utils import launches as _launches
 
 
 @dataclass
@@ -93,9 +94,17 @@ class LLMEngine:
         # device-busy time of the model work (CUDA events around every GPU segment)
         self.record_device_time = False
         self._events: list = []
+        # CUDA graphs of the pure-decode (verify + drafting) steps
+        self.use_graphs = model.device.type == "cuda"
+        self._graphs: dict = {}
+        self._seen: dict = {}
+        self._graph_pool = torch.cuda.graph_pool_handle() if self.use_graphs else None
+        self._hid_static = None
         model.allocate_cache(num_blocks, max_slots)
+        model.setup_row_reduce(max_batched_tokens + max_slots * (1 + self.num_spec))
         cfg = model.oscar
         self.stage_rows = model.stage_rows
+        self._owner_host = np.full(max(1, self.stage_rows) * 128, -1, dtype=np.int32)
         self.sink, self.recent = cfg.sink_tokens, cfg.recent_tokens
         self.g = model.full_layers[0].Hq // model.full_layers[0].Hk if model.full_layers else 1
         self.Hk = model.full_layers[0].Hk if model.full_layers else 1
@@ -195,8 +204,13 @@ class LLMEngine:
             out[k] = dbuf[o:o + sz].view(np.asarray(v).shape)
         return out
 
-    def _build(self, rows, logit_rows, commit_info, keep):
-        """rows: list of (rid, token, position); requests appear contiguously in order."""
+    def _arrays(self, rows, logit_rows, commit_info, keep, static: bool = False):
+        """Host metadata of one batch: ``(arrays, meta)``.
+
+        ``static=True`` makes every array shape depend only on the batch shape (bucketed
+        block-table width, fixed attention splits, owner updates padded to one per token),
+        the form a captured CUDA graph can replay.
+        """
         toks, poss, slots, tok_req, q_start, seq_lens, bts = [], [], [], [], [0], [], []
         req_slot, n_commit, keep_p, parity = [], [], [], []
         order = []
@@ -221,6 +235,8 @@ class LLMEngine:
             n_commit.append(commit_info.get(rid, 0))
             keep_p.append(1 if keep.get(rid, False) else 0)
             parity.append(self.slots.parity[r.slot])
+        if static:
+            maxp = 1 << (maxp - 1).bit_length()
         bt = np.zeros((len(order), maxp), dtype=np.int32)
         for i, t in enumerate(bts):
             bt[i, :len(t)] = t
@@ -229,28 +245,113 @@ class LLMEngine:
         seq_np = np.asarray(seq_lens, dtype=np.int64)[np.asarray(tok_req, dtype=np.int64)]
         stage_seat, owner_seat, owner_val = seat_plan(slots_np, pos_np, seq_np, self.stage_rows, self.sink,
                                                       self.recent)
+        if self.stage_rows:
+            self._owner_host[owner_seat] = owner_val
+            if static:  # pad to one update per token with idempotent rewrites
+                pad = len(rows) - owner_seat.shape[0]
+                if pad > 0:
+                    fill = owner_seat[:1] if owner_seat.shape[0] else np.zeros(1, np.int32)
+                    owner_seat = np.concatenate([owner_seat, np.repeat(fill, pad)]).astype(np.int32)
+                    owner_val = self._owner_host[owner_seat].astype(np.int32)
         arrays = dict(tokens=toks, positions=poss, slots=slots, q_start=q_start, seq_lens=seq_lens, bt=bt,
                       tok_req=tok_req, stage_seat=stage_seat, owner_seat=owner_seat, owner_val=owner_val,
                       req_slot=req_slot, n_commit=n_commit, keep=keep_p, parity=parity, logit_rows=logit_rows)
-        plan_np = None
+        meta = {"q_start": q_start, "seq_lens": seq_lens, "order": order,
+                "max_qlen": max((q_start[i + 1] - q_start[i] for i in range(len(order))), default=0)}
         if self.dev.type == "cuda":
-            plan_np = A.plan_attention_host(q_start, seq_lens, self.g, self.Hk, self.sms)
+            fixed = 0
+            if static:
+                n_blocks = sum((q_start[i + 1] - q_start[i]) * self.g // A.ROWS + 1 for i in range(len(order)))
+                fixed = max(1, (3 * self.sms) // max(1, self.Hk * n_blocks))
+            plan_np = A.plan_attention_host(q_start, seq_lens, self.g, self.Hk, self.sms, fixed_splits=fixed)
             arrays.update(work=plan_np[0], item_first=plan_np[1], item_count=plan_np[2])
-        d = self._upload(arrays)
+            meta["max_rb"], meta["n_work"] = plan_np[3], plan_np[4]
+        return arrays, meta
+
+    def _batch(self, d: dict, meta: dict) -> StepBatch:
         plan = None
-        if plan_np is not None:
-            plan = A.AttnPlan(d["work"], d["item_first"], d["item_count"], plan_np[3], plan_np[4])
+        if "work" in d:
+            plan = A.AttnPlan(d["work"], d["item_first"], d["item_count"], meta["max_rb"], meta["n_work"])
         b = StepBatch(
             tokens=d["tokens"], positions=d["positions"], slots=d["slots"], q_start=d["q_start"],
-            seq_lens=d["seq_lens"], block_tables=d["bt"], tok_req=d["tok_req"], q_start_l=q_start,
-            seq_lens_l=seq_lens, plan=plan,
+            seq_lens=d["seq_lens"], block_tables=d["bt"], tok_req=d["tok_req"], q_start_l=meta["q_start"],
+            seq_lens_l=meta["seq_lens"], plan=plan,
             stage_seat=d["stage_seat"] if self.stage_rows else None,
             owner_seat=d["owner_seat"] if self.stage_rows else None,
             owner_val=d["owner_val"] if self.stage_rows else None,
             req_slot=d["req_slot"], n_commit=d["n_commit"], keep_pending=d["keep"], parity=d["parity"],
             logit_rows=d["logit_rows"].long())
-        b.extra["order"] = order
+        b.extra["order"] = meta["order"]
+        b.extra["max_qlen"] = meta["max_qlen"]
         return b
+
+    def _build(self, rows, logit_rows, commit_info, keep):
+        """Eager batch: host metadata uploaded with one copy."""
+        arrays, meta = self._arrays(rows, logit_rows, commit_info, keep)
+        return self._batch(self._upload(arrays), meta)
+
+    # ------------------------------------------------------------------ CUDA graphs
+    def _run_phase(self, name: str, specs: list, fn):
+        """Run ``fn(batches)`` for host metadata ``specs = [(arrays, meta), ...]``.
+
+        With graphs enabled, the second occurrence of a metadata shape is captured into
+        a CUDA graph whose metadata lives in a static device buffer; later occurrences
+        copy the new metadata into that buffer (one pinned host-to-device copy) and replay.
+        """
+        if not self.use_graphs or self.dev.type != "cuda":
+            return fn([self._batch(self._upload(a), m) for a, m in specs])
+        sig = (name,) + tuple(tuple((k, np.shape(v)) for k, v in a.items()) + (m.get("max_rb"), m.get("n_work"))
+                              for a, m in specs)
+        ent = self._graphs.get(sig)
+        if ent is not None:
+            self._fill_static(ent, specs)
+            ent["graph"].replay()
+            _launches.add(ent["launches"])
+            return ent["out"]
+        self._seen[sig] = self._seen.get(sig, 0) + 1
+        if self._seen[sig] < 2:
+            return fn([self._batch(self._upload(a), m) for a, m in specs])
+        # capture (kernel attributes and tensor maps were initialised by the eager run)
+        layout, n = [], 0
+        for a, _ in specs:
+            lay = {}
+            for k, v in a.items():
+                sz = int(np.prod(np.shape(v))) if np.ndim(v) else 1
+                lay[k] = (n, np.shape(v))
+                n += (sz + 3) // 4 * 4
+            layout.append(lay)
+        ent = {"layout": layout, "n": n, "dbuf": torch.zeros(max(n, 4), dtype=torch.int32, device=self.dev),
+               "pin": torch.empty(max(n, 4), dtype=torch.int32, pin_memory=True), "event": None}
+        self._fill_static(ent, specs)
+        batches = []
+        for (a, m), lay in zip(specs, layout):
+            d = {k: ent["dbuf"][o:o + int(np.prod(shp))].view(shp) for k, (o, shp) in lay.items()}
+            batches.append(self._batch(d, m))
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        n0 = _launches.count()
+        with torch.cuda.graph(g, pool=self._graph_pool):
+            out = fn(batches)
+        ent["launches"] = _launches.count() - n0  # kernels of this package inside the graph
+        ent["graph"], ent["out"] = g, out
+        self._graphs[sig] = ent
+        g.replay()
+        return out
+
+    def _fill_static(self, ent, specs):
+        if ent["event"] is not None:
+            ent["event"].synchronize()
+        host = ent["pin"].numpy()
+        for (a, _), lay in zip(specs, ent["layout"]):
+            for k, v in a.items():
+                o, shp = lay[k]
+                f = np.asarray(v, dtype=np.int32).reshape(-1)
+                host[o:o + f.size] = f
+        ent["dbuf"].copy_(ent["pin"][:ent["dbuf"].numel()], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        ent["event"] = ev
+        self.stats["h2d_bytes"] = self.stats.get("h2d_bytes", 0) + 4 * ent["n"]
 
     # ------------------------------------------------------------------ step
     def step(self) -> dict:
@@ -275,9 +376,16 @@ class LLMEngine:
             for i, t in enumerate(toks):
                 rows.append((rid, t, r.num_computed + i))
             info.append((rid, kind, n, base))
-        b = self._build(rows, logit_rows, commit, keep)
-        with self._segment():
-            hid, tok = self.model.forward(b)
+        static = self.use_graphs and all(kind == "verify" for _, kind, _, _ in info)
+        if static:
+            arrays, meta = self._arrays(rows, logit_rows, commit, keep, static=True)
+            b = (arrays, meta)
+            with self._segment():
+                hid, tok = self._run_phase("main", [(arrays, meta)], lambda bs: self._main_fn(bs[0]))
+        else:
+            b = self._build(rows, logit_rows, commit, keep)
+            with self._segment():
+                hid, tok = self._main_fn(b)
         tok_h = tok.tolist()
         self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * len(tok_h)
         self.last = (hid, tok)
@@ -345,36 +453,63 @@ class LLMEngine:
         self.stats["steps"] += 1
         return {"scheduled": sched}
 
-    def _draft(self, b: StepBatch, hid, rows, next_row_tok, draft_rows):
-        """MTP pass over the step's rows, then num_spec-1 chained single-token passes."""
+    def _main_fn(self, b: StepBatch):
+        """Main model; the hidden states land in a persistent buffer so that a captured
+        drafting graph always reads them from the same address."""
+        hid, tok = self.model.forward(b)
+        T, H = hid.shape
+        if self._hid_static is None or self._hid_static.shape[0] < T:
+            self._graphs = {k: v for k, v in self._graphs.items() if k[0] != "mtp"}  # their input moved
+            self._hid_static = torch.empty(max(T, self.max_batched_tokens), H, dtype=hid.dtype, device=hid.device)
+        self._hid_static[:T].copy_(hid)
+        return self._hid_static[:T], tok
+
+    def _draft(self, b, hid, rows, next_row_tok, draft_rows):
+        """MTP pass over the step's rows, then num_spec-1 chained single-token passes.
+
+        All passes run back to back on the device: the draft tokens of pass k are the
+        input tokens of pass k+1 without a host round trip; the host reads every draft
+        once at the end.
+        """
         m = self.model
-        up = self._upload({"tokens": next_row_tok, "rows": [ri for _, ri in draft_rows]})
-        b.tokens = up["tokens"]
-        b.logit_rows = up["rows"].long()
-        with self._segment():
-            h1, e = m.mtp.forward(b, hid)
-        drafts = {rid: [] for rid, _ in draft_rows}
-        e_h = e.tolist()
-        self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * len(e_h)
-        for (rid, _), t in zip(draft_rows, e_h):
-            drafts[rid].append(t)
-        h = h1[b.logit_rows]
-        for k in range(1, self.num_spec):
-            prow = []
-            for (rid, ri), t in zip(draft_rows, e_h):
-                # the MTP row after ``ri`` sits one position further
-                pos = rows[ri][2] + k
-                prow.append((rid, t, pos))
-            bk = self._build(prow, list(range(len(prow))), {}, {})
+        rows_sel = [ri for _, ri in draft_rows]
+
+        def chain(batches):
+            b1, later = batches[0], batches[1:]
+            h1, e = m.mtp.forward(b1, hid)
+            outs = [e]
+            h = h1[b1.logit_rows]
+            for bk in later:
+                h, e = m.mtp.forward(bk, h, tokens=e)
+                outs.append(e)
+            return torch.stack(outs, 1)
+
+        if isinstance(b, tuple):  # static (graph) metadata of a pure decode step
+            arrays, meta = b
+            a1 = dict(arrays)
+            a1["tokens"] = next_row_tok
+            a1["logit_rows"] = rows_sel
+            specs = [(a1, meta)]
+            for k in range(1, self.num_spec):
+                # the MTP row after ``ri`` sits one position further; tokens come from the device
+                prow = [(rid, 0, rows[ri][2] + k) for rid, ri in draft_rows]
+                specs.append(self._arrays(prow, list(range(len(prow))), {}, {}, static=True))
             with self._segment():
-                    hk, e = m.mtp.forward(bk, h)
-            e_h = e.tolist()
-            self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * len(e_h)
-            for (rid, _), t in zip(draft_rows, e_h):
-                drafts[rid].append(t)
-            h = hk
-        for rid, d in drafts.items():
-            self.requests[rid].drafts = d
+                drafts_t = self._run_phase("mtp", specs, chain)
+        else:
+            up = self._upload({"tokens": next_row_tok, "rows": rows_sel})
+            b.tokens = up["tokens"]
+            b.logit_rows = up["rows"].long()
+            later = []
+            for k in range(1, self.num_spec):
+                prow = [(rid, 0, rows[ri][2] + k) for rid, ri in draft_rows]
+                later.append(self._build(prow, list(range(len(prow))), {}, {}))
+            with self._segment():
+                drafts_t = chain([b] + later)
+        d = drafts_t.tolist()
+        self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * drafts_t.numel()
+        for (rid, _), row in zip(draft_rows, d):
+            self.requests[rid].drafts = [int(x) for x in row]
 
     class _Seg:
         def __init__(self, eng):

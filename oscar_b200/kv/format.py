@@ -21,6 +21,12 @@ Physical layout (this framework): the pool is page-major structure-of-arrays.  O
     [K scale  PAGE fp16 ] [K zero  PAGE fp16 ] [V scale PAGE fp16] [V zero PAGE fp16]
 
 so an attention CTA fetches one page-head with a single 16-byte-aligned bulk copy.
+
+Bit order inside the pool differs from the exchange format: each little-endian
+32-bit word of a code row covers 16 consecutive dims, and dim ``16w + 2m + e`` sits at
+bit ``16e + 2m``.  Adjacent dims 2m, 2m+1 are then the two halves of
+``(word >> 2m) & 0x00030003``, which the attention kernel widens to an fp16 pair
+with one logic op.  ``pack_page``/``unpack_page`` convert.
 """
 from __future__ import annotations
 
@@ -102,6 +108,31 @@ def unpack(packed: torch.Tensor, D: int) -> torch.Tensor:
     p = packed.to(torch.int32)
     parts = [(p >> (2 * k)) & 3 for k in range(4)]
     return torch.stack(parts, dim=-1).reshape(*p.shape[:-1], D)
+
+
+def _page_bit_positions(D: int) -> torch.Tensor:
+    """Bit position (within the code row) of every dim in the pool's bit order."""
+    d = torch.arange(D)
+    w, j = d // 16, d % 16
+    return w * 32 + 16 * (j % 2) + 2 * (j // 2)
+
+
+def pack_page(q: torch.Tensor) -> torch.Tensor:
+    """Codes ``[..., D]`` -> pool-order bytes ``[..., D/4]``."""
+    D = q.shape[-1]
+    pos = _page_bit_positions(D).to(q.device)
+    byte, shift = pos // 8, pos % 8
+    out = torch.zeros(*q.shape[:-1], D // 4, dtype=torch.int32, device=q.device)
+    vals = (q.to(torch.int32) & 3) << shift.to(torch.int32)
+    out.index_add_(-1 if out.dim() == 1 else out.dim() - 1, byte, vals)
+    return out.to(torch.uint8)
+
+
+def unpack_page(b: torch.Tensor, D: int) -> torch.Tensor:
+    """Pool-order bytes ``[..., D/4]`` -> codes ``[..., D]`` (int32)."""
+    pos = _page_bit_positions(D).to(b.device)
+    byte, shift = pos // 8, pos % 8
+    return (b.to(torch.int32)[..., byte] >> shift) & 3
 
 
 def quantize(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
@@ -197,8 +228,8 @@ def pool_to_slots(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor, 
         lo, hi = f16_le(t[b, :, o].float().unsqueeze(-1))
         slot[..., 2 * i: 2 * i + 1] = lo
         slot[..., 2 * i + 1: 2 * i + 2] = hi
-    slot[..., K_IDX_OFF: K_IDX_OFF + cb] = kc[b, :, o]
-    slot[..., V_IDX_OFF: V_IDX_OFF + cb] = vc[b, :, o]
+    slot[..., K_IDX_OFF: K_IDX_OFF + cb] = pack(unpack_page(kc[b, :, o], D))
+    slot[..., V_IDX_OFF: V_IDX_OFF + cb] = pack(unpack_page(vc[b, :, o], D))
     return slot
 
 
@@ -206,9 +237,22 @@ def dequant_tokens(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor,
     """Dequantize tokens of a page-packed pool -> ``(k [T,Hk,D], v [T,Hk,D])`` fp32 (rotated space)."""
     kc, vc, ks, kz, vs, vz = page_views(pool, D)
     b, o = blocks.long(), offs.long()
-    k = dequant(kc[b, :, o], ks[b, :, o].float().unsqueeze(-1), kz[b, :, o].float().unsqueeze(-1), D)
-    v = dequant(vc[b, :, o], vs[b, :, o].float().unsqueeze(-1), vz[b, :, o].float().unsqueeze(-1), D)
+    k = unpack_page(kc[b, :, o], D).float() * ks[b, :, o].float().unsqueeze(-1) + kz[b, :, o].float().unsqueeze(-1)
+    v = unpack_page(vc[b, :, o], D).float() * vs[b, :, o].float().unsqueeze(-1) + vz[b, :, o].float().unsqueeze(-1)
     return k, v
+
+
+def write_tokens(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor, k_c: torch.Tensor,
+                 v_c: torch.Tensor) -> None:
+    """Quantize clipped rotated ``k_c/v_c [T,Hk,D]`` into the pool at ``(blocks, offs)``."""
+    D = k_c.shape[-1]
+    kc, vc, ks, kz, vs, vz = page_views(pool, D)
+    b, o = blocks.long(), offs.long()
+    for x, codes_v, sv, zv in ((k_c, kc, ks, kz), (v_c, vc, vs, vz)):
+        scale, zero = vector_scales(x)
+        codes_v[b, :, o] = pack_page(codes(x, scale, zero))
+        sv[b, :, o] = scale.squeeze(-1).half()
+        zv[b, :, o] = zero.squeeze(-1).half()
 
 
 def rotate(x: torch.Tensor, R: torch.Tensor) -> torch.Tensor:

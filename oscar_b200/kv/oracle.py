@@ -46,14 +46,7 @@ def store_ref(k: torch.Tensor, v: torch.Tensor, pool: torch.Tensor, slots: torch
     valid = slots >= 0
     if valid.any():
         s = slots[valid].long()
-        blk, off = s // fmt.PAGE, s % fmt.PAGE
-        kc, vc, ks, kz, vs, vz = fmt.page_views(pool, D)
-        kp, kss, kzz = fmt.quantize(k_c[valid])
-        vp, vss, vzz = fmt.quantize(v_c[valid])
-        for src, dst in ((kp, kc), (vp, vc)):
-            dst[blk, :, off] = src
-        for src, dst in ((kss, ks), (kzz, kz), (vss, vs), (vzz, vz)):
-            dst[blk, :, off] = src.squeeze(-1).half()
+        fmt.write_tokens(pool, s // fmt.PAGE, s % fmt.PAGE, k_c[valid], v_c[valid])
     return k_rot, v_rot
 
 

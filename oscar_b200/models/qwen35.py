@@ -31,6 +31,7 @@ from ..kv.rotation import get_layer_rotation, random_orthogonal
 from ..ops import attention as A
 from ..ops import functional as F
 from ..ops.gdn import gdn_step
+from ..parallel.fused import NcclRowReduce, make_row_reduce
 from ..parallel.groups import TPGroup
 from .config import HybridConfig
 
@@ -81,16 +82,29 @@ def _gen(seed: int, device) -> torch.Generator:
     return g
 
 
-def _rand_qlinear(N: int, K: int, seed: int, device) -> QLinear:
+def _rand_qlinear(N: int, K: int, seed: int, device, rows=None, cols=None) -> QLinear:
+    """Random int8 weight of the LOGICAL (unsharded) ``[N, K]`` matrix, then this rank's
+    part: ``rows`` = list of ``(begin, end)`` row ranges (column-parallel) or ``cols`` =
+    one ``(begin, end)`` column range (row-parallel; the per-row scale stays whole).  Every
+    tensor-parallel size therefore holds slices of the same model."""
     g = _gen(seed, device)
     q = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g, device=device)
-    s = (torch.rand(N, generator=g, device=device) * 0.5 + 0.75) / (73.3 * math.sqrt(K))
-    return QLinear(q, s.float())
+    s = ((torch.rand(N, generator=g, device=device) * 0.5 + 0.75) / (73.3 * math.sqrt(K))).float()
+    if rows is not None:
+        q = torch.cat([q[a:b] for a, b in rows]).contiguous()
+        s = torch.cat([s[a:b] for a, b in rows]).contiguous()
+    if cols is not None:
+        q = q[:, cols[0]:cols[1]].contiguous()
+    return QLinear(q, s)
 
 
 def _rand_vec(n: int, seed: int, device, std: float = 0.02, mean: float = 0.0) -> torch.Tensor:
     g = _gen(seed, device)
     return (torch.randn(n, generator=g, device=device) * std + mean).float()
+
+
+def _blocks(begin: int, end: int, width: int, offset: int = 0) -> tuple[int, int]:
+    return offset + begin * width, offset + end * width
 
 
 class FullAttentionLayer:
@@ -115,9 +129,15 @@ class FullAttentionLayer:
         self.k_off = self.Hq * 2 * D
         self.v_off = self.k_off + self.Hk * D
         self.n_qkv = self.v_off + self.Hk * D
-        base = seed * 1000 + layer_id * 17 + tp.rank * 100003
-        self.qkv = _rand_qlinear(self.n_qkv, H, base + 1, device)
-        self.o = _rand_qlinear(H, self.Hq * D, base + 2, device)
+        base = seed * 1000 + layer_id * 17
+        nq, nk = cfg.num_attention_heads, cfg.num_key_value_heads
+        h0 = tp.rank * self.Hq
+        k0 = (tp.rank * nk) // tp.world if nk < tp.world else tp.rank * self.Hk
+        kv_base = nq * 2 * D
+        self.qkv = _rand_qlinear(nq * 2 * D + 2 * nk * D, H, base + 1, device, rows=[
+            _blocks(h0, h0 + self.Hq, 2 * D), _blocks(k0, k0 + self.Hk, D, kv_base),
+            _blocks(k0, k0 + self.Hk, D, kv_base + nk * D)])
+        self.o = _rand_qlinear(H, nq * D, base + 2, device, cols=_blocks(h0, h0 + self.Hq, D))
         self.q_norm = _rand_vec(D, base + 3, device)
         self.k_norm = _rand_vec(D, base + 4, device)
         self.input_norm = _rand_vec(H, base + 5, device)
@@ -139,8 +159,14 @@ class FullAttentionLayer:
                 self.RvT = self.Rv.t().contiguous()
         else:
             self.Rk = self.Rv = self.RvT = None
+        self._split_rotations()
         self.pool = self.kc = self.vc = None
         self.stage_k = self.stage_v = None
+
+    def _split_rotations(self):
+        self.rk_split = A.split_rotation(self.Rk)
+        self.rv_split = A.split_rotation(self.Rv)
+        self.rv_merge_split = A.split_rotation(self.RvT)
 
     def to(self, device):
         for k, v in list(vars(self).items()):
@@ -148,6 +174,7 @@ class FullAttentionLayer:
                 setattr(self, k, v.to(device))
             elif isinstance(v, QLinear):
                 setattr(self, k, v.to(device))
+        self._split_rotations()
         return self
 
     def allocate_cache(self, num_blocks: int, device, stage_rows: int = 0):
@@ -184,7 +211,8 @@ class FullAttentionLayer:
                    stage_v=self.stage_v if staged else None, stage_seat=b.stage_seat if staged else None,
                    owner=owner if staged else None,
                    owner_seat=b.owner_seat if (staged and write_owner) else None,
-                   owner_val=b.owner_val if (staged and write_owner) else None, status=status)
+                   owner_val=b.owner_val if (staged and write_owner) else None, status=status,
+                   rk_split=self.rk_split, rv_split=self.rv_split)
         stage = (self.stage_k, self.stage_v, owner, stage_rows) if staged else None
         gate = qkv[:, self.D:]  # gate of head h at columns h * 2D + D ..
         _, oq, os_ = A.attention(q_out, k_fr, v_fr, Hq=self.Hq, Hk=self.Hk, D=self.D, scale=self.scale,
@@ -192,7 +220,8 @@ class FullAttentionLayer:
                                  block_tables=b.block_tables, q_start_t=b.q_start, seq_lens_t=b.seq_lens,
                                  q_start=b.q_start_l, seq_lens=b.seq_lens_l, plan=b.plan, tok_req=b.tok_req,
                                  RvT=self.RvT, gate=gate, gate_ld=qkv.stride(0), gate_hstride=2 * self.D,
-                                 want_bf16=False, want_q=True, status=status)
+                                 want_bf16=False, want_q=True, status=status,
+                                 rv_merge_split=self.rv_merge_split)
         return oq, os_
 
 
@@ -210,12 +239,22 @@ class GDNLayer:
         self.n_qkvz = self.Hk * (2 * self.dk + 2 * self.r * self.dv)
         self.n_ba = 2 * self.Hv
         self.conv_dim = 2 * self.Hk * self.dk + self.Hv * self.dv
-        base = seed * 1000 + layer_id * 17 + tp.rank * 100003
-        self.inp = _rand_qlinear(self.n_qkvz + self.n_ba, H, base + 1, device)
-        self.out = _rand_qlinear(H, self.Hv * self.dv, base + 2, device)
+        base = seed * 1000 + layer_id * 17
+        nk, nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        k0, v0 = tp.rank * self.Hk, tp.rank * self.Hv
+        grp = 2 * self.dk + 2 * self.r * self.dv
+        # logical rows: [qkvz grouped per key head | ba grouped per key head]
+        self.inp = _rand_qlinear(nk * grp + 2 * nv, H, base + 1, device, rows=[
+            _blocks(k0, k0 + self.Hk, grp), _blocks(k0, k0 + self.Hk, 2 * self.r, nk * grp)])
+        self.out = _rand_qlinear(H, nv * self.dv, base + 2, device, cols=_blocks(v0, v0 + self.Hv, self.dv))
         g = _gen(base + 3, device)
-        self.conv_w = (torch.randn(self.conv_dim, cfg.linear_conv_kernel_dim, generator=g, device=device) * 0.5).float()
-        self.A_log = torch.log(torch.rand(self.Hv, generator=g, device=device) * 15 + 1).float()
+        Kd = nk * self.dk
+        conv_full = torch.randn(2 * Kd + nv * self.dv, cfg.linear_conv_kernel_dim, generator=g, device=device) * 0.5
+        # conv channels: [q heads | k heads | v heads]
+        self.conv_w = torch.cat([conv_full[k0 * self.dk:(k0 + self.Hk) * self.dk],
+                                 conv_full[Kd + k0 * self.dk:Kd + (k0 + self.Hk) * self.dk],
+                                 conv_full[2 * Kd + v0 * self.dv:2 * Kd + (v0 + self.Hv) * self.dv]]).float().contiguous()
+        self.A_log = torch.log(torch.rand(nv, generator=g, device=device) * 15 + 1)[v0:v0 + self.Hv].float().contiguous()
         self.dt_bias = torch.ones(self.Hv, device=device).float()
         self.norm_w = (1.0 + torch.randn(self.dv, generator=g, device=device) * 0.02).float()
         self.input_norm = _rand_vec(H, base + 5, device)
@@ -248,7 +287,7 @@ class GDNLayer:
                  conv_w=self.conv_w, A_log=self.A_log, dt_bias=self.dt_bias, norm_w=self.norm_w, eps=self.eps,
                  state=self.state, conv_state=self.conv_state, pend_x=self.pend_x, pend_ba=self.pend_ba,
                  parity=b.parity, req_slot=b.req_slot, q_start=b.q_start, n_commit=b.n_commit,
-                 keep_pending=b.keep_pending, out=o, smem_state=T > 64, status=status)
+                 keep_pending=b.keep_pending, out=o, smem_state=b.extra.get("max_qlen", T) > 4, status=status)
         return F.act_quant(o)
 
 
@@ -256,9 +295,12 @@ class MLP:
     def __init__(self, cfg: HybridConfig, tp: TPGroup, layer_id: int, seed: int, device):
         H = cfg.hidden_size
         self.I = cfg.intermediate_size // tp.world
-        base = seed * 1000 + layer_id * 17 + tp.rank * 100003 + 50
-        self.gate_up = _rand_qlinear(2 * self.I, H, base + 1, device)
-        self.down = _rand_qlinear(H, self.I, base + 2, device)
+        base = seed * 1000 + layer_id * 17 + 50
+        I_full = cfg.intermediate_size
+        i0 = tp.rank * self.I
+        self.gate_up = _rand_qlinear(2 * I_full, H, base + 1, device, rows=[
+            (i0, i0 + self.I), (I_full + i0, I_full + i0 + self.I)])
+        self.down = _rand_qlinear(H, I_full, base + 2, device, cols=(i0, i0 + self.I))
 
     def to(self, device):
         self.gate_up = self.gate_up.to(device)
@@ -282,10 +324,13 @@ class HybridModel:
         self.V_local = (V + self.tp.world - 1) // self.tp.world
         self.vocab_begin = self.tp.rank * self.V_local
         dev = self.device
-        base = seed * 1000 + self.tp.rank * 100003
+        base = seed * 1000
         g = _gen(base + 999, dev)
-        self.embed = (torch.randn(self.V_local, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        self.lm_head = _rand_qlinear(self.V_local, H, base + 998, dev)
+        v0, v1 = self.vocab_begin, min(V, self.vocab_begin + self.V_local)
+        emb = torch.zeros(self.V_local, H, dtype=torch.bfloat16, device=dev)
+        emb[:v1 - v0] = (torch.randn(V, H, generator=g, device=dev) * 0.02)[v0:v1].to(torch.bfloat16)
+        self.embed = emb
+        self.lm_head = _rand_qlinear(V, H, base + 998, dev, rows=[(v0, v1)])  # only real vocab rows
         self.final_norm = _rand_vec(H, base + 997, dev)
         self.layers = []
         for i, t in enumerate(cfg.layer_types):
@@ -344,13 +389,28 @@ class HybridModel:
                 "owner": 0 if self.owner is None else self.owner.numel() * 4}
 
     # ------------------------------------------------------------------ forward
-    def decoder(self, b: StepBatch, residual: torch.Tensor):
-        """All decoder layers; returns the pending MLP delta of the last layer."""
-        delta = torch.zeros_like(residual)
+    def setup_row_reduce(self, max_rows: int) -> None:
+        """Choose the row-parallel reduction: fused GEMM + NVLS all-reduce on CUDA TP
+        groups that support multicast, else GEMM + NCCL all-reduce."""
+        self.row_reduce = make_row_reduce(self.tp, max_rows, self.cfg.hidden_size, self.device)
+
+    def _reducer(self):
+        if getattr(self, "row_reduce", None) is None:
+            self.row_reduce = NcclRowReduce(self.tp)
+        return self.row_reduce
+
+    def decoder(self, b: StepBatch, residual: torch.Tensor) -> dict:
+        """All decoder layers; returns the pending (all-reduced) MLP delta of the last
+        layer as the keyword arguments of the RMSNorm that consumes it."""
+        red = self._reducer()
+        T, H = residual.shape
+        red.begin(T, H, residual.device)
+        eps = self.cfg.rms_norm_eps
+        pending: dict = {}
         first_full = True
-        for i, (mixer, mlp) in enumerate(self.layers):
-            xq, xs, _ = F.rmsnorm_quant(residual, mixer.input_norm, self.cfg.rms_norm_eps,
-                                        delta=delta if i > 0 else None)
+        k = 0
+        for mixer, mlp in self.layers:
+            xq, xs, _ = F.rmsnorm_quant(residual, mixer.input_norm, eps, status=self.status, **pending)
             if isinstance(mixer, FullAttentionLayer):
                 oq, os_ = mixer.attention(xq, xs, b, self.rope, self.owner, self.stage_rows,
                                           write_owner=first_full, status=self.status)
@@ -359,16 +419,13 @@ class HybridModel:
             else:
                 oq, os_ = mixer.mixer(xq, xs, b, status=self.status)
                 w_o = mixer.out
-            delta.zero_()
-            F.linear_i8(oq, os_, w_o.q, w_o.s, out=delta, accumulate=True, status=self.status)
-            self.tp.all_reduce_(delta)
-            xq, xs, _ = F.rmsnorm_quant(residual, mixer.post_norm, self.cfg.rms_norm_eps, delta=delta)
+            pending = red.gemm(oq, os_, w_o, k, status=self.status)
+            xq, xs, _ = F.rmsnorm_quant(residual, mixer.post_norm, eps, status=self.status, **pending)
             gu = F.linear_i8(xq, xs, mlp.gate_up.q, mlp.gate_up.s, status=self.status)
             hq, hs = F.swiglu_quant(gu, mlp.I)
-            delta.zero_()
-            F.linear_i8(hq, hs, mlp.down.q, mlp.down.s, out=delta, accumulate=True, status=self.status)
-            self.tp.all_reduce_(delta)
-        return delta
+            pending = red.gemm(hq, hs, mlp.down, k + 1, status=self.status)
+            k += 2
+        return pending
 
     def forward(self, b: StepBatch):
         """Main model on a step.  Returns ``(hidden_bf16 [T, H], next_tokens [n_sel])``."""
@@ -377,9 +434,9 @@ class HybridModel:
         residual = torch.empty(T, H, dtype=torch.float32, device=self.device)
         F.embed(b.tokens, self.embed, self.vocab_begin, residual)
         self.tp.all_reduce_(residual)
-        delta = self.decoder(b, residual)
-        xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, self.cfg.rms_norm_eps, delta=delta,
-                                      want_bf16=True)
+        pending = self.decoder(b, residual)
+        xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, self.cfg.rms_norm_eps, want_bf16=True,
+                                      status=self.status, **pending)
         rows = b.logit_rows
         tok = self.sample(xq[rows], xs[rows])
         return hid, tok
@@ -405,9 +462,9 @@ class MTPHead:
         dev = model.device
         H = cfg.hidden_size
         lid = cfg.num_layers  # layer id after the main stack
-        base = seed * 1000 + lid * 17 + tp.rank * 100003 + 7
+        base = seed * 1000 + lid * 17 + 7
         self.model = model
-        self.fc = _rand_qlinear(H, 2 * H, base + 1, dev)
+        self.fc = _rand_qlinear(H, 2 * H, base + 1, dev)  # replicated (small)
         self.norm_emb = _rand_vec(H, base + 2, dev)
         self.norm_hid = _rand_vec(H, base + 3, dev)
         self.final_norm = _rand_vec(H, base + 4, dev)
@@ -424,15 +481,16 @@ class MTPHead:
         self.mlp.to(device)
         return self
 
-    def forward(self, b: StepBatch, hidden: torch.Tensor):
+    def forward(self, b: StepBatch, hidden: torch.Tensor, tokens: torch.Tensor | None = None):
         """Draft pass: ``hidden`` [T, H] bf16 (post-norm main or previous draft hidden),
-        ``b.tokens`` = the next token of every position.  Returns (hidden_bf16, next_tokens)."""
+        ``tokens`` (default ``b.tokens``) = the next token of every position, may be a
+        device tensor produced by the previous pass.  Returns (hidden_bf16, next_tokens)."""
         m = self.model
         cfg = m.cfg
         T, H = hidden.shape
         eps = cfg.rms_norm_eps
         e = torch.empty(T, H, dtype=torch.float32, device=m.device)
-        F.embed(b.tokens, m.embed, m.vocab_begin, e)
+        F.embed(b.tokens if tokens is None else tokens, m.embed, m.vocab_begin, e)
         m.tp.all_reduce_(e)
         _, _, e_n = F.rmsnorm_quant(e, self.norm_emb, eps, want_q=False, want_bf16=True)
         hf = hidden.float().contiguous()
@@ -441,19 +499,16 @@ class MTPHead:
         cq, cs = F.act_quant(cat)
         residual = torch.zeros(T, H, dtype=torch.float32, device=m.device)
         F.linear_i8(cq, cs, self.fc.q, self.fc.s, out=residual, accumulate=True, status=m.status)
-        m.tp.all_reduce_(residual) if False else None  # fc is replicated: no reduction needed
         xq, xs, _ = F.rmsnorm_quant(residual, self.layer.input_norm, eps)
         oq, os_ = self.layer.attention(xq, xs, b, m.rope, None, 0, write_owner=False, status=m.status)
-        delta = torch.zeros_like(residual)
-        F.linear_i8(oq, os_, self.layer.o.q, self.layer.o.s, out=delta, accumulate=True, status=m.status)
-        m.tp.all_reduce_(delta)
-        xq, xs, _ = F.rmsnorm_quant(residual, self.layer.post_norm, eps, delta=delta)
+        red = m._reducer()
+        red.begin(T, H, residual.device)
+        pending = red.gemm(oq, os_, self.layer.o, 0, status=m.status)
+        xq, xs, _ = F.rmsnorm_quant(residual, self.layer.post_norm, eps, status=m.status, **pending)
         gu = F.linear_i8(xq, xs, self.mlp.gate_up.q, self.mlp.gate_up.s, status=m.status)
         hq, hs = F.swiglu_quant(gu, self.mlp.I)
-        delta.zero_()
-        F.linear_i8(hq, hs, self.mlp.down.q, self.mlp.down.s, out=delta, accumulate=True, status=m.status)
-        m.tp.all_reduce_(delta)
-        xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, eps, delta=delta, want_bf16=True)
+        pending = red.gemm(hq, hs, self.mlp.down, 1, status=m.status)
+        xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, eps, want_bf16=True, status=m.status, **pending)
         rows = b.logit_rows
         tok = m.sample(xq[rows], xs[rows])
         return hid, tok

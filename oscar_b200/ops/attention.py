@@ -39,8 +39,13 @@ class AttnPlan:
 
 
 def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int, sms: int,
-                        min_chunk: int = 256, waves: int = 3):
-    """Work list as numpy arrays: ``(work [n,4], item_first, item_count, max_rb, n_work)``."""
+                        min_chunk: int = 256, waves: int = 3, fixed_splits: int = 0):
+    """Work list as numpy arrays: ``(work [n,4], item_first, item_count, max_rb, n_work)``.
+
+    ``fixed_splits > 0`` gives every row block exactly that many page-aligned splits
+    (some may be empty), so the work-list shape depends only on the batch shape - the
+    form a captured CUDA graph replays.
+    """
     R = len(seq_lens)
     blocks = []  # (req, row0, kv_need)
     max_rb = 1
@@ -57,16 +62,24 @@ def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int
             blocks.append((r, b * ROWS, prefix + last_row // g + 1))
     total = sum(k for _, _, k in blocks)
     target_items = max(1, (waves * sms) // max(Hk, 1))
-    chunk = max(min_chunk, int(math.ceil(total / target_items / 64.0)) * 64) if total else min_chunk
+    # page-aligned (128-token) split ranges: every split streams whole pages
+    chunk = max(min_chunk, int(math.ceil(total / target_items / 128.0)) * 128) if total else min_chunk
     work = []
     first = np.zeros(R * max_rb, dtype=np.int32)
     count = np.zeros(R * max_rb, dtype=np.int32)
     for r, row0, need in blocks:
         rb = row0 // ROWS
         first[r * max_rb + rb] = len(work)
-        splits = max(1, (need + chunk - 1) // chunk)
-        for s in range(splits):
-            work.append((r, row0, s * chunk, min(need, (s + 1) * chunk)))
+        if fixed_splits > 0:
+            splits = fixed_splits
+            per = max(128, int(math.ceil(need / splits / 128.0)) * 128)
+            for s in range(splits):
+                b0 = min(need, s * per)
+                work.append((r, row0, b0, min(need, b0 + per)))
+        else:
+            splits = max(1, (need + chunk - 1) // chunk)
+            for s in range(splits):
+                work.append((r, row0, s * chunk, min(need, (s + 1) * chunk)))
         count[r * max_rb + rb] = splits
     n_work = len(work)
     wt = np.asarray(work if work else [(0, 0, 0, 0)], dtype=np.int32).reshape(-1, 4)
@@ -90,16 +103,34 @@ def clip_by_index(x: torch.Tensor, idx: int) -> torch.Tensor:
     return torch.maximum(torch.minimum(x, thr), -thr)
 
 
+def split_rotation(R: torch.Tensor | None):
+    """``R^T`` as bf16 hi + lo parts (``R^T ~ hi + lo`` to ~2^-16) for the tensor-core rotation."""
+    if R is None:
+        return None, None
+    RT = R.t().contiguous().float()
+    hi = RT.to(torch.bfloat16)
+    lo = (RT - hi.float()).to(torch.bfloat16)
+    return hi.contiguous(), lo.contiguous()
+
+
 def kv_store(qkv, *, q_off, q_head_stride, k_off, v_off, Hq, Hk, D, q_norm_w, k_norm_w, eps, norm_offset,
              positions, rope_cos, rope_sin, rot_dim, Rk, Rv, k_clip_idx, v_clip_idx, q_out, k_fresh, v_fresh,
              kv_mode, pool, kc, vc, slots, stage_k=None, stage_v=None, stage_seat=None, owner=None,
-             owner_seat=None, owner_val=None, status=None):
-    """Fused write path of one FULL layer; see the module docstring."""
+             owner_seat=None, owner_val=None, status=None, rk_split=None, rv_split=None):
+    """Fused write path of one FULL layer; see the module docstring.
+
+    ``rk_split``/``rv_split`` are the precomputed :func:`split_rotation` of ``Rk``/``Rv``.
+    """
     if qkv.is_cuda:
+        if rk_split is None:
+            rk_split = split_rotation(Rk)
+        if rv_split is None:
+            rv_split = split_rotation(Rv)
+        xbuf = torch.empty(qkv.shape[0] * (Hq + 2 * Hk) * D, dtype=torch.bfloat16, device=qkv.device)
         ext().kv_store(qkv, q_off, q_head_stride, k_off, v_off, Hq, Hk, D, q_norm_w, k_norm_w, float(eps),
                        float(norm_offset), positions, rope_cos, rope_sin, rot_dim, Rk, Rv, k_clip_idx, v_clip_idx,
                        q_out, k_fresh, v_fresh, kv_mode, pool, kc, vc, slots, stage_k, stage_v, stage_seat, owner,
-                       owner_seat, owner_val, status)
+                       owner_seat, owner_val, status, rk_split[0], rk_split[1], rv_split[0], rv_split[1], xbuf)
         return
     T = qkv.shape[0]
     x = qkv.float()
@@ -136,15 +167,7 @@ def kv_store(qkv, *, q_off, q_head_stride, k_off, v_off, Hq, Hk, D, q_norm_w, k_
         kc[blk, off] = kr[valid].to(torch.bfloat16)
         vc[blk, off] = vr[valid].to(torch.bfloat16)
         return
-    kcodes, vcodes, ks, kz, vs, vz = fmt.page_views(pool, D)
-    kp, kss, kzz = fmt.quantize(clip_by_index(kr[valid], k_clip_idx))
-    vp, vss, vzz = fmt.quantize(clip_by_index(vr[valid], v_clip_idx))
-    kcodes[blk, :, off] = kp
-    vcodes[blk, :, off] = vp
-    ks[blk, :, off] = kss.squeeze(-1).half()
-    kz[blk, :, off] = kzz.squeeze(-1).half()
-    vs[blk, :, off] = vss.squeeze(-1).half()
-    vz[blk, :, off] = vzz.squeeze(-1).half()
+    fmt.write_tokens(pool, blk, off, clip_by_index(kr[valid], k_clip_idx), clip_by_index(vr[valid], v_clip_idx))
 
 
 # ---------------------------------------------------------------------------
@@ -211,7 +234,7 @@ def merge_ref(o_rot: torch.Tensor, RvT, gate, want_bf16: bool, want_q: bool):
 def attention(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, stage, block_tables,
               q_start_t, seq_lens_t, q_start: list[int], seq_lens: list[int], plan: AttnPlan | None,
               tok_req, RvT, gate, gate_ld, gate_hstride, want_bf16=False, want_q=True,
-              part_o=None, part_lse=None, status=None):
+              part_o=None, part_lse=None, status=None, rv_merge_split=None):
     """Attention + merge.  Returns ``(o_bf16 | None, o_int8 | None, o_scale | None)``.
 
     ``stage`` is ``(stage_k, stage_v, owner, rows)`` or ``None``; ``gate`` is the bf16
@@ -237,6 +260,18 @@ def attention(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, s
         sk, sv, own, rows = stage
     e.paged_attention(q, k_fresh, v_fresh, Hq, Hk, D, float(scale), kv_mode, pool, kc, vc, sk, sv, own, rows,
                       block_tables, q_start_t, seq_lens_t, plan.work, part_o, part_lse, status)
+    if RvT is not None:
+        # tensor-core merge + rotation + gate, then the vectorised row quantiser
+        if rv_merge_split is None:
+            rv_merge_split = split_rotation(RvT)
+        o_bf16 = torch.empty(T, Hq * D, dtype=torch.bfloat16, device=q.device)
+        e.attn_merge_rot(part_o, part_lse, plan.item_first, plan.item_count, plan.max_rb, tok_req, q_start_t, Hq,
+                         Hk, D, gate, gate_ld, gate_hstride, o_bf16, T, rv_merge_split[0], rv_merge_split[1])
+        o_q = o_s = None
+        if want_q:
+            from .functional import act_quant
+            o_q, o_s = act_quant(o_bf16)
+        return (o_bf16 if want_bf16 else None), o_q, o_s
     o_bf16 = torch.empty(T, Hq * D, dtype=torch.bfloat16, device=q.device) if want_bf16 else None
     o_q = torch.empty(T, Hq * D, dtype=torch.int8, device=q.device) if want_q else None
     o_s = torch.empty(T, dtype=torch.float32, device=q.device) if want_q else None

@@ -55,21 +55,28 @@ def act_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float = 1.0,
                   delta: torch.Tensor | None = None, want_q: bool = True, want_bf16: bool = False,
-                  out_q=None, out_s=None, out_bf16=None):
+                  out_q=None, out_s=None, out_bf16=None, wait=None, zero_delta: bool = False, status=None):
     """RMSNorm of the fp32 residual ``x`` (optionally ``x += delta`` first, in place).
 
     ``y = bf16(x * rsqrt(mean(x^2) + eps) * (offset + w))``; returns
-    ``(q int8, scale, y_bf16)`` with the parts not requested set to ``None``.
+    ``(q int8, scale, y_bf16)`` with the parts not requested set to ``None``.  ``wait =
+    (signal_pad_ptr, epoch_tensor, world)`` first waits for every rank's completion flag
+    of a fused GEMM + all-reduce producing ``delta``; ``zero_delta`` clears ``delta``
+    after reading it.
     """
     T, H = x.shape
     if x.is_cuda:
         q = out_q if out_q is not None else (torch.empty(T, H, dtype=torch.int8, device=x.device) if want_q else None)
         s = out_s if out_s is not None else (torch.empty(T, dtype=torch.float32, device=x.device) if want_q else None)
         y = out_bf16 if out_bf16 is not None else (torch.empty(T, H, dtype=torch.bfloat16, device=x.device) if want_bf16 else None)
-        ext().rmsnorm_quant(x, delta, w, float(offset), float(eps), q, s, y)
+        sig, ep, world = wait if wait is not None else (0, None, 0)
+        ext().rmsnorm_quant(x, delta, w, float(offset), float(eps), q, s, y, int(sig), ep, int(world),
+                            int(zero_delta), status)
         return q, s, y
     if delta is not None:
         x += delta.float()
+        if zero_delta:
+            delta.zero_()
     xf = x.float()
     inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     y = _bf16_round(xf * inv * (offset + w.float()))

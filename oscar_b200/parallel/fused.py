@@ -1,0 +1,126 @@
+"""Row-parallel projection + all-reduce, fused into one GEMM over NVSwitch.
+
+Every row-parallel projection of the decoder (attention ``o_proj``, GDN ``out_proj``,
+MLP ``down_proj``) produces a partial sum that the tensor-parallel ranks must add
+before the next RMSNorm.  The reference issues a GEMM followed by a separate
+all-reduce collective per projection (vLLM's row-parallel linear under
+``oscar/vllm_plugin`` serving).  Here the two are one kernel:
+
+* the residual-delta buffers live in symmetric memory (``torch`` ``_symmetric_memory``
+  is only the allocator/rendezvous: it gives each rank's unicast pointer, the NVLS
+  multicast address of the whole allocation and per-rank signal pads);
+* the int8 tcgen05 GEMM epilogue writes its fp32 tile with
+  ``multimem.red.add`` to the multicast address, so the switch adds it into the same
+  element of every rank's buffer while the next tiles are still on the tensor cores;
+* the last CTA of the GEMM bumps a device-resident epoch and stores it with release
+  semantics into every peer's signal pad slot ``[rank]``;
+* the consuming RMSNorm kernel waits (bounded, acquire) until all ``world`` slots of its
+  own pad reach its epoch, adds the buffer into the fp32 residual and zeroes the
+  buffer for the reduction after next.
+
+Two buffers alternate: a rank can only start reduction ``i+2`` after it consumed
+reduction ``i+1``, which needs every peer's GEMM ``i+1`` done, which in each peer's
+stream order follows that peer's read-and-zero of reduction ``i``.  Every forward
+starts on buffer 0 and issues an even number of fused reductions, so captured CUDA
+graphs keep the alternation on replay.
+
+This path needs NVLS multicast (``has_multicast_support``); without it
+:class:`NcclRowReduce` (GEMM into a local delta + ``dist.all_reduce``) is used.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..ops import functional as F
+from ..ops._ext import ext
+from .groups import TPGroup
+
+
+class NcclRowReduce:
+    """Baseline: local fp32 delta, GEMM accumulate, NCCL all-reduce."""
+
+    fused = False
+
+    def __init__(self, tp: TPGroup):
+        self.tp = tp
+        self.delta = None
+
+    def begin(self, T: int, H: int, device) -> None:
+        if self.delta is None or self.delta.shape[0] < T or self.delta.shape[1] != H or self.delta.device != device:
+            self.delta = torch.zeros(max(T, 1), H, dtype=torch.float32, device=device)
+        self._T = T
+
+    def gemm(self, xq, xs, w, k: int, status=None) -> dict:
+        """``delta = all_reduce(xq @ w^T)``; returns the kwargs of the consuming RMSNorm."""
+        d = self.delta[:self._T]
+        d.zero_()
+        F.linear_i8(xq, xs, w.q, w.s, out=d, accumulate=True, status=status)
+        self.tp.all_reduce_(d)
+        return {"delta": d}
+
+
+class FusedRowReduce:
+    """GEMM epilogue reduces through NVLS multicast; the RMSNorm waits on peer flags."""
+
+    fused = True
+
+    def __init__(self, tp: TPGroup, max_rows: int, H: int, device):
+        import torch.distributed._symmetric_memory as symm
+
+        self.tp = tp
+        self.H = H
+        self.max_rows = max_rows
+        group = tp.group if tp.group is not None else dist.group.WORLD
+        self.bufs = symm.empty((2, max_rows, H), dtype=torch.float32, device=device)
+        self.hdl = symm.rendezvous(self.bufs, group)
+        if not self.hdl.has_multicast_support():
+            raise RuntimeError("NVLS multicast is not available for this group")
+        self.bufs.zero_()
+        self.mc = int(self.hdl.multicast_ptr)
+        self.peer_signals = int(self.hdl.signal_pad_ptrs_dev)
+        self.my_signals = int(self.hdl.signal_pad_ptrs[self.hdl.rank])
+        # zero our own signal slots (others' stores only ever raise them)
+        pad = self.hdl.get_signal_pad(self.hdl.rank, (tp.world,), dtype=torch.int32)
+        pad.zero_()
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+        self._T = 0
+
+    def begin(self, T: int, H: int, device) -> None:
+        if T > self.max_rows or H != self.H:
+            raise ValueError(f"fused all-reduce buffer holds {self.max_rows}x{self.H}, step needs {T}x{H}")
+        self._T = T
+
+    def gemm(self, xq, xs, w, k: int, status=None) -> dict:
+        M, K = xq.shape
+        N = w.q.shape[0]
+        plan = F.plan_gemm(M, N, K, F.num_sms(xq.device), allow_split=True)
+        b = k & 1
+        mc = self.mc + b * self.max_rows * self.H * 4
+        if plan.swap:
+            ext().gemm_i8_allreduce(w.q, xq, w.s, xs, mc, self.H, 1, plan.bn, plan.splits, self.done, self.epoch,
+                                    self.peer_signals, self.tp.rank, self.tp.world, status)
+        else:
+            ext().gemm_i8_allreduce(xq, w.q, xs, w.s, mc, self.H, 0, plan.bn, plan.splits, self.done, self.epoch,
+                                    self.peer_signals, self.tp.rank, self.tp.world, status)
+        return {"delta": self.bufs[b, :self._T], "wait": (self.my_signals, self.epoch, self.tp.world),
+                "zero_delta": True}
+
+
+def make_row_reduce(tp: TPGroup, max_rows: int, H: int, device):
+    """The fused path on CUDA TP groups with NVLS (``OSCAR_FUSED_AR=0`` forces NCCL)."""
+    want = os.environ.get("OSCAR_FUSED_AR", "1") != "0"
+    dev = torch.device(device)
+    if tp.world > 1 and want and dev.type == "cuda":
+        try:
+            return FusedRowReduce(tp, max_rows, H, dev)
+        except (RuntimeError, ImportError) as exc:  # no NVLS on this system
+            if os.environ.get("OSCAR_FUSED_AR") == "1":
+                raise
+            print(f"[oscar_b200] fused all-reduce unavailable ({exc}); using NCCL all-reduce")
+    return NcclRowReduce(tp)
