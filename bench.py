@@ -184,6 +184,7 @@ def main():
             "init_s": round(t_init, 1),
         }
         print(json.dumps(line), flush=True)
+    eng.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -1,6 +1,6 @@
-// Paged multi-query GQA attention over INT2 (or BF16) KV pages, plus the
-// split-KV merge that also rotates the output back (o_rot @ R_v^T), applies the
-// sigmoid output gate and quantises the result per token for the o_proj GEMM.
+// Paged multi-query GQA attention over BF16 KV pages (the MTP draft layer's shadow
+// cache), the dispatch of INT2 pages to the code-domain kernels, and the SIMT
+// split-KV merge used when no output rotation is needed.
 //
 // Work decomposition: one CTA per (work item, KV head).  A work item is
 // (request, 64-row block, KV token range); the 64 rows of a block are
@@ -9,7 +9,7 @@
 // shared memory as fp16 by the whole CTA from its source:
 //   * position >= prefix                  -> unquantised k/v of the current chunk
 //   * staged (owner tag == physical block) -> fp32 sink/recent staging
-//   * otherwise                            -> INT2 codes * scale + zero  (or BF16 page)
+//   * otherwise                            -> BF16 page
 // which reproduces the reference read semantics (paged_attention.py:136-260).
 // Scores and P.V run on the tensor cores (m16n8k16, fp32 accumulate) with an
 // online softmax; each CTA writes a normalised partial output and its LSE.
@@ -59,32 +59,14 @@ OSCAR_DEVICE uint32_t h2_u32(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Dequantise 16 INT2 codes (one 32-bit word in pool bit order: dim 2m+e at bit
-// 16e+2m) into 16 fp16.
-OSCAR_DEVICE void dequant16(uint32_t w, float s, float z, uint4& lo, uint4& hi) {
-  float v[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) v[k] = fmaf((float)((w >> (16 * (k & 1) + 2 * (k >> 1))) & 3u), s, z);
-  lo.x = h2_u32(v[0], v[1]);
-  lo.y = h2_u32(v[2], v[3]);
-  lo.z = h2_u32(v[4], v[5]);
-  lo.w = h2_u32(v[6], v[7]);
-  hi.x = h2_u32(v[8], v[9]);
-  hi.y = h2_u32(v[10], v[11]);
-  hi.z = h2_u32(v[12], v[13]);
-  hi.w = h2_u32(v[14], v[15]);
-}
-
 struct TileCtx {
   int req, hk, prefix, q0, kv_end;
   const int* bt;
 };
 
-// Raw INT2 data of one (token, half) owned by a thread: 32 code bytes of K and of V.
+// Source of one (token, half) owned by a thread.
 struct RawInt2 {
-  uint4 k0, k1, v0, v1;
-  float ks, kz, vs, vz;
-  int kind;  // 0 invalid, 1 int2, 2 fresh, 3 staged, 4 bf16
+  int kind;  // 0 invalid, 2 fresh, 3 staged, 4 bf16
   int blk, off, srow;
 };
 
@@ -107,24 +89,7 @@ OSCAR_DEVICE void load_raw(const AttnParams& p, const TileCtx& c, int pos, int h
       return;
     }
   }
-  if (p.kv_mode == 1) {
-    r.kind = 4;
-    return;
-  }
-  r.kind = 1;
-  const uint8_t* pg = p.pool + ((long long)blk * p.Hk + c.hk) * p.page_bytes;
-  const int cb = p.D / 4;  // 64
-  const uint4* kp = reinterpret_cast<const uint4*>(pg + off * cb + half * (cb / 2));
-  const uint4* vp = reinterpret_cast<const uint4*>(pg + kPage * cb + off * cb + half * (cb / 2));
-  r.k0 = __ldg(kp);
-  r.k1 = __ldg(kp + 1);
-  r.v0 = __ldg(vp);
-  r.v1 = __ldg(vp + 1);
-  const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * cb);
-  r.ks = __half2float(meta[off]);
-  r.kz = __half2float(meta[kPage + off]);
-  r.vs = __half2float(meta[2 * kPage + off]);
-  r.vz = __half2float(meta[3 * kPage + off]);
+  r.kind = 4;  // BF16 page (INT2 pages are read by the code-domain kernel)
 }
 
 // Write one thread's (token, half) = 128 dims of K and V into the fp16 tiles.
@@ -132,21 +97,6 @@ OSCAR_DEVICE void store_tile(const AttnParams& p, const TileCtx& c, int tok, int
                              const RawInt2& r, uint8_t* ks, uint8_t* vs) {
   const int d0 = half * 128;
   const int chunk0 = d0 / 8;
-  if (r.kind == 1) {
-    const uint32_t kw[8] = {r.k0.x, r.k0.y, r.k0.z, r.k0.w, r.k1.x, r.k1.y, r.k1.z, r.k1.w};
-    const uint32_t vw[8] = {r.v0.x, r.v0.y, r.v0.z, r.v0.w, r.v1.x, r.v1.y, r.v1.z, r.v1.w};
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      uint4 lo, hi;
-      dequant16(kw[w], r.ks, r.kz, lo, hi);
-      *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + 2 * w)) = lo;
-      *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + 2 * w + 1)) = hi;
-      dequant16(vw[w], r.vs, r.vz, lo, hi);
-      *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + 2 * w)) = lo;
-      *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + 2 * w + 1)) = hi;
-    }
-    return;
-  }
   if (r.kind == 0) {
     const uint4 zero = make_uint4(0, 0, 0, 0);
 #pragma unroll

@@ -55,6 +55,9 @@ __host__ __device__ inline Smem smem_layout(int page_bytes) {
   return s;
 }
 
+// V^T tile: 256 dim rows of 64 tokens (128 B), 16 B chunks XOR-swizzled by row.
+OSCAR_DEVICE uint32_t swz_vt(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
+
 // One warp's share of a 64-token tile: S = Q C^T for its 16 rows and TOK tokens,
 // online softmax, O += P' C_v.  Columns of the tile are tokens tok0 .. tok0+TOK-1.
 template <int TOK>
@@ -150,8 +153,8 @@ OSCAR_DEVICE void warp_tile(const uint32_t qs_a, const uint32_t ks_a, const uint
 #pragma unroll
     for (int dp = 0; dp < 16; ++dp) {
       uint32_t b0, b1, b2, b3;
-      mma::ldsm_x4_t(vs_a + mma::swz(tok0 + sg * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, 2 * dp + (lane >> 4)), b0, b1,
-                     b2, b3);
+      mma::ldsm_x4(vs_a + swz_vt(dp * 16 + (lane & 7) + (lane >> 4) * 8, ((tok0 + sg * 16) >> 3) + ((lane >> 3) & 1)),
+                   b0, b1, b2, b3);
       mma::mma_f16(o[2 * dp], a0, a1, a2, a3, b0, b1);
       mma::mma_f16(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
     }
@@ -275,42 +278,33 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_kernel(AttnParams 
         const int d0 = my_q * 64;
         const int c0 = d0 / 8;
         float4 par = make_float4(0.f, 0.f, 0.f, 0.f);
+        bool value_tok = false;
         if (pos >= kv_stop || pos < kv_begin) {
           const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            *reinterpret_cast<uint4*>(ks + mma::swz(my_tok, c0 + c)) = z;
-            *reinterpret_cast<uint4*>(vs + mma::swz(my_tok, c0 + c)) = z;
-          }
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(ks + mma::swz(my_tok, c0 + c)) = z;
         } else if (pos >= prefix) {  // current chunk: unquantised fp16
           const long long t = q0 + (pos - prefix);
           const uint4* kf = reinterpret_cast<const uint4*>(p.k_fresh + (t * p.Hk + hk) * kD + d0);
-          const uint4* vf = reinterpret_cast<const uint4*>(p.v_fresh + (t * p.Hk + hk) * kD + d0);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            *reinterpret_cast<uint4*>(ks + mma::swz(my_tok, c0 + c)) = __ldg(kf + c);
-            *reinterpret_cast<uint4*>(vs + mma::swz(my_tok, c0 + c)) = __ldg(vf + c);
-          }
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(ks + mma::swz(my_tok, c0 + c)) = __ldg(kf + c);
           par = make_float4(1.f, 0.f, 1.f, 0.f);
+          value_tok = true;
         } else if (staging && own[j] == blk) {  // staged sink/recent token: fp32 values
           const long long base = ((long long)((blk % p.stage_rows) * kPage + j) * p.Hk + hk) * kD + d0;
           const float4* kf = reinterpret_cast<const float4*>(p.stage_k + base);
-          const float4* vf = reinterpret_cast<const float4*>(p.stage_v + base);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float4 a = __ldg(kf + 2 * c), b = __ldg(kf + 2 * c + 1);
             *reinterpret_cast<uint4*>(ks + mma::swz(my_tok, c0 + c)) =
                 make_uint4(mma::h2_u32(a.x, a.y), mma::h2_u32(a.z, a.w), mma::h2_u32(b.x, b.y), mma::h2_u32(b.z, b.w));
-            const float4 e = __ldg(vf + 2 * c), f = __ldg(vf + 2 * c + 1);
-            *reinterpret_cast<uint4*>(vs + mma::swz(my_tok, c0 + c)) =
-                make_uint4(mma::h2_u32(e.x, e.y), mma::h2_u32(e.z, e.w), mma::h2_u32(f.x, f.y), mma::h2_u32(f.z, f.w));
           }
           par = make_float4(1.f, 0.f, 1.f, 0.f);
-        } else {  // INT2 codes: 64 dims = 16 bytes of K codes and of V codes
+          value_tok = true;
+        } else {  // INT2 K codes: 64 dims = 16 bytes
           const int cb = kD / 4;
           const uint4 kw = *reinterpret_cast<const uint4*>(pg + j * cb + my_q * 16);
-          const uint4 vw = *reinterpret_cast<const uint4*>(pg + kPage * cb + j * cb + my_q * 16);
-          const uint32_t kk[4] = {kw.x, kw.y, kw.z, kw.w}, vv[4] = {vw.x, vw.y, vw.z, vw.w};
+          const uint32_t kk[4] = {kw.x, kw.y, kw.z, kw.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t h0[4], h1[4];
@@ -318,10 +312,6 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_kernel(AttnParams 
             mma::codes8_to_h2(kk[q] >> 8, h1);
             *reinterpret_cast<uint4*>(ks + mma::swz(my_tok, c0 + 2 * q)) = make_uint4(h0[0], h0[1], h0[2], h0[3]);
             *reinterpret_cast<uint4*>(ks + mma::swz(my_tok, c0 + 2 * q + 1)) = make_uint4(h1[0], h1[1], h1[2], h1[3]);
-            mma::codes8_to_h2(vv[q], h0);
-            mma::codes8_to_h2(vv[q] >> 8, h1);
-            *reinterpret_cast<uint4*>(vs + mma::swz(my_tok, c0 + 2 * q)) = make_uint4(h0[0], h0[1], h0[2], h0[3]);
-            *reinterpret_cast<uint4*>(vs + mma::swz(my_tok, c0 + 2 * q + 1)) = make_uint4(h1[0], h1[1], h1[2], h1[3]);
           }
           if (my_q == 0) {
             const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * cb);
@@ -330,6 +320,37 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_kernel(AttnParams 
           }
         }
         if (my_q == 0) tokp[my_tok] = par;
+        // V^T tile: thread = dim, 64 tokens of codes (16 bytes of the dim-major V rows)
+        {
+          const int d = tid;
+          const uint4 vw = *reinterpret_cast<const uint4*>(pg + kPage * (kD / 4) + d * (kPage / 4) + half * 16);
+          const uint32_t vv[4] = {vw.x, vw.y, vw.z, vw.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t h0[4], h1[4];
+            mma::codes8_to_h2(vv[q], h0);
+            mma::codes8_to_h2(vv[q] >> 8, h1);
+            *reinterpret_cast<uint4*>(vs + swz_vt(d, 2 * q)) = make_uint4(h0[0], h0[1], h0[2], h0[3]);
+            *reinterpret_cast<uint4*>(vs + swz_vt(d, 2 * q + 1)) = make_uint4(h1[0], h1[1], h1[2], h1[3]);
+          }
+        }
+        // tokens that carry values instead of codes: overwrite their V^T columns
+        if (__syncthreads_or(value_tok)) {
+          const int d = tid;
+          for (int jj = 0; jj < kTile; ++jj) {
+            const int jp = half * kTile + jj, ps = page_pos + jp;
+            if (ps >= kv_stop || ps < kv_begin) continue;
+            float v;
+            if (ps >= prefix) {
+              v = __half2float(p.v_fresh[((long long)(q0 + ps - prefix) * p.Hk + hk) * kD + d]);
+            } else if (staging && own[jp] == blk) {
+              v = __ldg(p.stage_v + ((long long)((blk % p.stage_rows) * kPage + jp) * p.Hk + hk) * kD + d);
+            } else {
+              continue;
+            }
+            *reinterpret_cast<__half*>(vs + swz_vt(d, jj >> 3) + (jj & 7) * 2) = __float2half_rn(v);
+          }
+        }
       }
       __syncthreads();
       // the ring slot is consumed once both tiles of the page are built

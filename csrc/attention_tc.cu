@@ -1,0 +1,740 @@
+// INT2 paged attention on the 5th-generation tensor cores (tcgen05 + TMEM), for
+// work items of at most 32 query rows: decode (q_len 1, rows = g) and MTP verify
+// (q_len 4, rows = 4 g = 24 for the 6:1 GQA of the target model).
+//
+// One CTA per (work item, KV head), 12 warps with fixed roles:
+//   warp 0      streams whole page-heads (17,408 B + 512 B of staging owner tags)
+//               into a 4-deep shared-memory ring with plain bulk copies, and owns
+//               the TMEM allocation (512 columns);
+//   warp 1      one thread issues every tcgen05.mma;
+//   warps 4-7   "converters": TMEM lane t.  For page i they widen the 2-bit codes
+//               to exact fp16 (0..3) straight into tensor memory - K codes of
+//               token t (A operand of S^T = K Q^T, M = 128 tokens, K = 256 dims)
+//               and the dim-major V codes of dims t and t+128 (A operand of
+//               O^T += V^T P'^T, M = 128 dims, K = 128 tokens);
+//   warps 8-11  "softmax": TMEM lane t = token t of the page.  They read the
+//               page's N scores of token t from TMEM, apply the per-token INT2
+//               scale/zero (q.k = s (q.c) + z sum(q)), keep per-row running
+//               maxima, and write P' = p * s_v as fp16 into shared memory in the
+//               MN-major layout of the B operand of the P.V product.
+// Operand placement keeps shared-memory traffic small: codes never go through
+// shared memory as fp16, only the 2-bit page (bulk copy), Q (once) and P' do.
+//
+// TMEM columns: [0,128) K codes, [128,384) two V^T buffers (2 halves x 64),
+// [384,384+2N) two S^T buffers, [448,448+2N) the O^T accumulator (2 halves).
+//
+// Softmax bookkeeping.  A row's running max only moves when some score of the
+// page exceeds it by more than 2^8 (the probabilities stay <= 256, well inside
+// fp16 after scaling by s_v); then the four softmax warps agree on the new maxima
+// and rescale O^T in TMEM (after the previous P.V finished) and their partial
+// sums.  Each softmax thread keeps per-row partial sums over the tokens it owns:
+// l = sum p and C = sum p z_v; they are reduced across threads once at the end:
+//     out[r, d] = (O^T[d, r] + C_r) / l_r,   lse_r = m_r + log2 l_r  (log2 units).
+// Tokens that are not INT2 (the current chunk's unquantised k/v and staged
+// sink/recent tokens) carry their fp16 values with s = 1, z = 0, which gives the
+// reference read semantics (paged_attention.py:136-260) in the same pass.
+//
+// Every wait is bounded: an expired wait sets a CTA abort flag and a status code;
+// the roles that synchronise with named barriers agree on aborting through
+// bar.red.or so that none is left waiting, in-flight MMAs and bulk copies are
+// drained (bounded) and TMEM is freed before the CTA exits.
+#include "common.cuh"
+#include "mma.cuh"
+#include "params.h"
+#include "sm100.cuh"
+
+namespace oscar {
+namespace {
+
+constexpr int kD = 256;
+constexpr int kPage = 128;
+constexpr int kPartRows = 64;  // row stride of the split-KV partials (shared with the merge)
+constexpr int kRing = 4;
+constexpr int kThreads = 384;
+constexpr int kPageBytes = 17408;
+constexpr int kSlot = kPageBytes + kPage * 4;  // page + owner tags
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kSlack = 8.f;
+constexpr uint64_t kBudgetNs = 2000000000ull;
+constexpr uint32_t kColK = 0, kColV = 128, kColS = 384, kColO = 448, kTmemCols = 512;
+constexpr int kBarConv = 2, kBarSoft = 1, kBarStats = 3;
+
+template <int N>
+struct TcLayout {
+  static constexpr int kQOff = kRing * kSlot;  // 71,680: 1024-aligned
+  static constexpr int kQBytes = N * 512;       // 4 chunks of 64 dims x N rows x 128 B
+  static constexpr int kPOff = kQOff + kQBytes;
+  static constexpr int kPBytes = kPage * N * 2;  // one P' buffer: 128 tokens x N fp16
+  static constexpr int kMisc = kPOff + 2 * kPBytes;
+  static constexpr int kSq = kMisc;                  // N floats: sum(q) per row
+  static constexpr int kLim = kSq + N * 4;           // N ints: last visible key position per row
+  static constexpr int kMsm = kLim + N * 4;          // N floats: running row maxima (log2 units)
+  static constexpr int kRed = kMsm + N * 4;          // N x 4 floats: per-warp page maxima
+  static constexpr int kAlpha = kRed + N * 16;       // 2 x N floats: rescale factor of a page
+  static constexpr int kFin = kAlpha + 2 * N * 4;    // groups x 2N floats: partial l, C
+  static constexpr int kCoef = kFin + 1024;          // 2 x 128 float2: (1/s_v, z_v/s_v)
+  static constexpr int kVmask = kCoef + 2 * kPage * 8;  // 2 x 4 u32
+  static constexpr int kUpd = kVmask + 32;           // 2 ints + resc flag
+  static constexpr int kSlotBlk = kUpd + 16;         // kRing ints
+  static constexpr int kTmemSlot = kSlotBlk + kRing * 4;
+  static constexpr int kAbort = kTmemSlot + 4;
+  static constexpr int kBars = (kAbort + 4 + 7) / 8 * 8;
+  static constexpr int kNumBars = 2 * kRing + 2 + 2 * 6 + 2;
+  static constexpr int kTotal = kBars + kNumBars * 8;
+  // at least half the SM's shared memory: one CTA per SM (it holds all 512 TMEM columns)
+  static constexpr int kAlloc = (kTotal > 120 * 1024 ? kTotal : 120 * 1024) + 1024;  // + base alignment
+};
+
+struct Bars {
+  uint64_t* raw_full;   // [kRing]
+  uint64_t* raw_empty;  // [kRing]
+  uint64_t* k_full;
+  uint64_t* k_empty;
+  uint64_t* v_full;   // [2]
+  uint64_t* v_empty;  // [2]
+  uint64_t* s_full;   // [2]
+  uint64_t* s_empty;  // [2]
+  uint64_t* p_full;   // [2]
+  uint64_t* p_empty;  // [2]
+  uint64_t* mma_done;
+  uint64_t* stats_done;
+};
+
+// Transposed butterfly: on return lane r holds the reduction of row r (N = 32) or
+// of row r % 16 (N = 16) over the 32 lanes; v[] is clobbered.
+template <int N, bool kMax>
+OSCAR_DEVICE float rows_reduce(float (&v)[N]) {
+  const int lane = threadIdx.x & 31;
+  auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
+  if constexpr (N == 16) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = op(v[k], __shfl_xor_sync(0xffffffffu, v[k], 16));
+  }
+  constexpr int kFirst = N == 32 ? 16 : 8;
+#pragma unroll
+  for (int o = kFirst; o >= 1; o >>= 1) {
+    const bool up = lane & o;
+#pragma unroll
+    for (int k = 0; k < o; ++k) {
+      const float send = up ? v[k] : v[k + o];
+      const float keep = up ? v[k + o] : v[k];
+      v[k] = op(keep, __shfl_xor_sync(0xffffffffu, send, o));
+    }
+  }
+  return v[0];
+}
+
+template <int N>
+__global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnParams p) {
+  using L = TcLayout<N>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // swizzled operand tiles need 1024-byte aligned shared addresses
+  uint8_t* smem = smem_raw + ((1024u - (sm100::smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint8_t* ring = smem;
+  uint8_t* qs = smem + L::kQOff;
+  uint8_t* ps = smem + L::kPOff;
+  float* sq = reinterpret_cast<float*>(smem + L::kSq);
+  int* lim = reinterpret_cast<int*>(smem + L::kLim);
+  float* msm = reinterpret_cast<float*>(smem + L::kMsm);
+  float* red = reinterpret_cast<float*>(smem + L::kRed);
+  float* alpha = reinterpret_cast<float*>(smem + L::kAlpha);
+  float* fin = reinterpret_cast<float*>(smem + L::kFin);
+  float2* coef = reinterpret_cast<float2*>(smem + L::kCoef);
+  uint32_t* vmask = reinterpret_cast<uint32_t*>(smem + L::kVmask);
+  volatile int* upd = reinterpret_cast<volatile int*>(smem + L::kUpd);
+  volatile int* resc_flag = reinterpret_cast<volatile int*>(smem + L::kUpd + 8);
+  int* slot_blk = reinterpret_cast<int*>(smem + L::kSlotBlk);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kBars);
+  Bars B{bar, bar + kRing, bar + 2 * kRing, bar + 2 * kRing + 1, bar + 2 * kRing + 2, bar + 2 * kRing + 4,
+         bar + 2 * kRing + 6, bar + 2 * kRing + 8, bar + 2 * kRing + 10, bar + 2 * kRing + 12, bar + 2 * kRing + 14,
+         bar + 2 * kRing + 15};
+
+  const int item = blockIdx.x, hk = blockIdx.y;
+  const int4 w = p.work[item];
+  const int req = w.x, row0 = w.y, kv_begin = w.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = p.Hq / p.Hk;
+  const int q0 = p.q_start[req];
+  const int qlen = p.q_start[req + 1] - q0;
+  const int prefix = p.seq_lens[req] - qlen;
+  const int* bt = p.block_tables + (long long)req * p.bt_stride;
+  const int nrows = max(0, min(N, qlen * g - row0));
+  const int kv_stop = min(w.w, nrows > 0 ? prefix + (row0 + nrows - 1) / g + 1 : 0);
+  const bool staging = p.stage_rows > 0;
+  const int p_first = kv_begin / kPage;
+  const int n_pages = kv_stop > kv_begin ? (kv_stop - 1) / kPage - p_first + 1 : 0;
+
+  // ---------------------------------------------------------------- setup
+  if (warp == 0) {
+    sm100::tmem_alloc(tmem_slot, kTmemCols);
+    sm100::tmem_relinquish();
+  }
+  if (tid == 32) {
+    for (int i = 0; i < L::kNumBars; ++i) sm100::mbar_init(&bar[i], 1);
+    for (int s = 0; s < kRing; ++s) sm100::mbar_init(&B.raw_empty[s], 10);  // 4 converter, 4 softmax, 2 stats warps
+    for (int b = 0; b < 2; ++b) sm100::mbar_init(&B.p_empty[b], 3);       // P.V commit + 2 stats warps
+    sm100::mbar_init(B.stats_done, 2);
+    sm100::mbar_init(B.k_full, 4);
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&B.v_full[b], 4);
+      sm100::mbar_init(&B.s_empty[b], 4);
+      sm100::mbar_init(&B.p_full[b], 4);
+    }
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  // Q tile, K-major with the 128-byte swizzle: [dim chunk of 64][row][128 B]
+  for (int idx = tid; idx < N * 32; idx += kThreads) {
+    const int r = idx >> 5, ch = idx & 31;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nrows) {
+      const int gr = row0 + r, t = gr / g, h = gr % g;
+      v = __ldg(reinterpret_cast<const uint4*>(p.q + ((long long)(q0 + t) * p.Hq + hk * g + h) * kD) + ch);
+    }
+    *reinterpret_cast<uint4*>(qs + (ch >> 3) * (N * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4)) = v;
+  }
+  __syncthreads();
+  if (tid < N) {
+    float acc = 0.f;
+    for (int ch = 0; ch < 32; ++ch) {
+      const uint4 v = *reinterpret_cast<const uint4*>(qs + (ch >> 3) * (N * 128) + tid * 128 + (((ch & 7) ^ (tid & 7)) << 4));
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(h[k]);
+        acc += f.x + f.y;
+      }
+    }
+    sq[tid] = acc;
+    lim[tid] = tid < nrows ? prefix + (row0 + tid) / g : -1;
+    msm[tid] = -INFINITY;
+  }
+  sm100::fence_proxy_async();  // Q tile: generic writes -> tensor-core reads
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ page producer
+    if (lane == 0) {
+      const uint32_t tx = kPageBytes + (staging ? kPage * 4 : 0);
+      int issued = 0;
+      for (int i = 0; i < n_pages; ++i) {
+        const int s = i % kRing;
+        if (i >= kRing && !sm100::mbar_wait(&B.raw_empty[s], ((i / kRing) - 1) & 1, abort_flag, p.status,
+                                            kTimeoutSlotEmpty, kBudgetNs))
+          break;
+        const int blk = bt[p_first + i];
+        slot_blk[s] = blk;
+        uint8_t* dst = ring + s * kSlot;
+        sm100::mbar_arrive_expect_tx(&B.raw_full[s], tx);
+        sm100::bulk_load(dst, p.pool + ((long long)blk * p.Hk + hk) * kPageBytes, kPageBytes, &B.raw_full[s]);
+        if (staging)
+          sm100::bulk_load(dst + kPageBytes, p.owner + (long long)(blk % p.stage_rows) * kPage, kPage * 4,
+                           &B.raw_full[s]);
+        issued = i + 1;
+      }
+      if (*abort_flag) {  // copies in flight must land before the CTA exits
+        const uint64_t t0 = globaltimer_ns();
+        for (int i = max(0, issued - kRing); i < issued; ++i)
+          while (!sm100::mbar_try_wait(&B.raw_full[i % kRing], (i / kRing) & 1))
+            if (globaltimer_ns() - t0 > 200000000ull) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idq = sm100::idesc_f16(128, N, false, false);
+      const uint32_t idp = sm100::idesc_f16(128, N, false, true);
+      const uint32_t qa = sm100::smem_addr(qs), pa = sm100::smem_addr(ps);
+      constexpr uint32_t kPLayout = N == 32 ? 4u : 6u;  // P' rows of N fp16: 64 B / 32 B swizzle
+      constexpr uint32_t kPAtom = 8 * N * 2;           // 8 tokens
+      auto pv = [&](int j) -> bool {
+        if (!sm100::mbar_wait(&B.v_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs))
+          return false;
+        if (!sm100::mbar_wait(&B.p_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs))
+          return false;
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t bd =
+                sm100::smem_desc(pa + (j & 1) * L::kPBytes + ks * 2 * kPAtom, 16, kPAtom, kPLayout);
+            sm100::umma_f16_tmem_a(tbase + kColO + h * N, tbase + kColV + (j & 1) * 128 + h * 64 + ks * 8, bd, idp,
+                                   (j > 0 || ks > 0) ? 1u : 0u);
+          }
+        sm100::umma_commit(&B.v_empty[j & 1]);
+        sm100::umma_commit(&B.p_empty[j & 1]);
+        return true;
+      };
+      bool ok = true;
+      for (int i = 0; i < n_pages && ok; ++i) {
+        if (!sm100::mbar_wait(B.k_full, i & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs)) {
+          ok = false;
+          break;
+        }
+        if (i >= 2 && !sm100::mbar_wait(&B.s_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
+                                        kTimeoutAccEmpty, kBudgetNs)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+          const uint64_t qd = sm100::smem_desc(qa + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024, 2);
+          sm100::umma_f16_tmem_a(tbase + kColS + (i & 1) * N, tbase + kColK + kk * 8, qd, idq, kk > 0 ? 1u : 0u);
+        }
+        sm100::umma_commit(&B.s_full[i & 1]);
+        sm100::umma_commit(B.k_empty);
+        if (i >= 1) ok = pv(i - 1);
+      }
+      if (ok && n_pages > 0) pv(n_pages - 1);
+      // nothing may still write TMEM when it is freed
+      sm100::umma_commit(B.mma_done);
+      const uint64_t t0 = globaltimer_ns();
+      while (!sm100::mbar_try_wait(B.mma_done, 0))
+        if (globaltimer_ns() - t0 > 200000000ull) break;
+    }
+    __syncwarp();
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ converters
+    const int ct = tid - 128;  // TMEM lane
+    const uint32_t lrow = (uint32_t)(ct & ~31) << 16;
+    bool dead = false;
+    for (int i = 0; i < n_pages; ++i) {
+      const int s = i % kRing;
+      bool ok = !dead && sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull,
+                                          kBudgetNs);
+      if (ok && i >= 1)
+        ok = sm100::mbar_wait(B.k_empty, (i - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
+      const uint8_t* pg = ring + s * kSlot;
+      const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
+      const int blk = ok ? slot_blk[s] : 0;
+      const int page_pos = (p_first + i) * kPage;
+      bool val_tok = false;
+      if (ok) {
+        sm100::tc_fence_after();
+        // K codes of token ct -> 128 columns of fp16 pairs
+        const int j = ct, pos = page_pos + j;
+        const bool in = pos >= kv_begin && pos < kv_stop;
+        const int kind = !in ? 0 : pos >= prefix ? 1 : (staging && own[j] == blk) ? 2 : 3;
+        val_tok = kind == 1 || kind == 2;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          if (kind == 3) {
+            const uint4 cw = *reinterpret_cast<const uint4*>(pg + j * 64 + c * 16);
+            const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t a[4], b[4];
+              mma::codes8_to_h2(wd[q], a);
+              mma::codes8_to_h2(wd[q] >> 8, b);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                r[8 * q + e] = a[e];
+                r[8 * q + 4 + e] = b[e];
+              }
+            }
+          } else if (kind == 1) {
+            const uint4* src = reinterpret_cast<const uint4*>(
+                p.k_fresh + ((long long)(q0 + pos - prefix) * p.Hk + hk) * kD + 64 * c);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint4 v = __ldg(src + q);
+              r[4 * q] = v.x;
+              r[4 * q + 1] = v.y;
+              r[4 * q + 2] = v.z;
+              r[4 * q + 3] = v.w;
+            }
+          } else if (kind == 2) {
+            const float4* src = reinterpret_cast<const float4*>(
+                p.stage_k + ((long long)((blk % p.stage_rows) * kPage + j) * p.Hk + hk) * kD + 64 * c);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const float4 v = __ldg(src + q);
+              r[2 * q] = mma::h2_u32(v.x, v.y);
+              r[2 * q + 1] = mma::h2_u32(v.z, v.w);
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) r[q] = 0u;
+          }
+          sm100::tmem_st_32x32b_x32(tbase + lrow + kColK + 32 * c, r);
+        }
+        sm100::tmem_st_wait();
+        sm100::tc_fence_before();
+      }
+      const uint32_t bal = __ballot_sync(0xffffffffu, val_tok);
+      if (lane == 0) vmask[(i & 1) * 4 + (ct >> 5)] = bal;
+      if (sm100::bar_red_or(kBarConv, 128, !ok)) break;
+      if (lane == 0) sm100::mbar_arrive(B.k_full);
+
+      // V^T of dims ct and ct + 128 -> 2 x 64 columns
+      ok = i < 2 || sm100::mbar_wait(&B.v_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
+                                     kTimeoutAccEmpty, kBudgetNs);
+      if (ok) {
+        sm100::tc_fence_after();
+        const uint32_t* msk = vmask + (i & 1) * 4;
+        const bool any_val = (msk[0] | msk[1] | msk[2] | msk[3]) != 0u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int d = ct + 128 * h;
+          const uint4* src = reinterpret_cast<const uint4*>(pg + kPage * 64 + d * 32);
+          const uint4 a4 = src[0], b4 = src[1];
+          const uint32_t wd[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t r[32];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t a[4], b[4];
+              mma::codes8_to_h2(wd[4 * hf + q], a);
+              mma::codes8_to_h2(wd[4 * hf + q] >> 8, b);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                r[8 * q + e] = a[e];
+                r[8 * q + 4 + e] = b[e];
+              }
+            }
+            if (any_val) {
+              // tokens carrying values: replace their halves of the fp16 pairs
+#pragma unroll 1
+              for (int k = 0; k < 32; ++k) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const int tj = hf * 64 + 2 * k + e;
+                  if (!((msk[tj >> 5] >> (tj & 31)) & 1u)) continue;
+                  const int ps_ = page_pos + tj;
+                  float v;
+                  if (ps_ >= prefix)
+                    v = __half2float(p.v_fresh[((long long)(q0 + ps_ - prefix) * p.Hk + hk) * kD + d]);
+                  else
+                    v = __ldg(p.stage_v + ((long long)((blk % p.stage_rows) * kPage + tj) * p.Hk + hk) * kD + d);
+                  const uint32_t hv = (uint32_t)__half_as_ushort(__float2half_rn(v));
+                  uint32_t cur = 0;
+#pragma unroll
+                  for (int kk = 0; kk < 32; ++kk) cur = kk == k ? r[kk] : cur;
+                  cur = e ? ((cur & 0x0000ffffu) | (hv << 16)) : ((cur & 0xffff0000u) | hv);
+#pragma unroll
+                  for (int kk = 0; kk < 32; ++kk) r[kk] = kk == k ? cur : r[kk];
+                }
+              }
+            }
+            sm100::tmem_st_32x32b_x32(tbase + lrow + kColV + (i & 1) * 128 + h * 64 + hf * 32, r);
+          }
+        }
+        sm100::tmem_st_wait();
+        sm100::tc_fence_before();
+      }
+      if (sm100::bar_red_or(kBarConv, 128, !ok)) break;
+      if (lane == 0) {
+        sm100::mbar_arrive(&B.v_full[i & 1]);
+        sm100::mbar_arrive(&B.raw_empty[s]);
+      }
+      dead = !ok;
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ row statistics
+    // l_r = sum_j p_jr and C_r = sum_j p_jr z_vj, read back from the fp16 P' tile the
+    // tensor cores consume (P' = p s_v), so they match the P.V product exactly.
+    const int tt = tid - 64;
+    constexpr int kPairs = N / 2;             // row pairs
+    constexpr int kGroups = 64 / kPairs;      // token groups
+    constexpr int kTok = kPage / kGroups;     // tokens per group
+    const int rp = tt % kPairs, grp = tt / kPairs;
+    float l0 = 0.f, l1 = 0.f, c0 = 0.f, c1 = 0.f;
+    bool dead = false, aborted = false;
+    for (int i = 0; i < n_pages; ++i) {
+      const int s = i % kRing, b = i & 1;
+      bool ok = !dead && sm100::mbar_wait(&B.p_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
+                                          kBudgetNs);
+      if (ok) {
+        // per-token coefficients (1/s_v, z_v/s_v) of this page
+        const uint8_t* pg = ring + s * kSlot;
+        const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
+        const int blk = slot_blk[s];
+        const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * 64);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = 2 * tt + e, pos = (p_first + i) * kPage + j;
+          float2 cf = make_float2(0.f, 0.f);
+          if (pos >= kv_begin && pos < kv_stop) {
+            if (pos >= prefix || (staging && own[j] == blk)) {
+              cf = make_float2(1.f, 0.f);
+            } else {
+              const float sv = __half2float(meta[2 * kPage + j]);
+              const float inv = 1.f / sv;
+              cf = make_float2(inv, __half2float(meta[3 * kPage + j]) * inv);
+            }
+          }
+          coef[b * kPage + j] = cf;
+        }
+      }
+      if (sm100::bar_red_or(kBarStats, 64, !ok)) {
+        aborted = true;
+        break;
+      }
+      if (upd[b]) {  // the row maxima moved on this page: rescale the running sums
+        const float a0 = alpha[b * N + 2 * rp], a1 = alpha[b * N + 2 * rp + 1];
+        l0 *= a0;
+        c0 *= a0;
+        l1 *= a1;
+        c1 *= a1;
+      }
+      const uint8_t* pt = ps + b * L::kPBytes;
+#pragma unroll 4
+      for (int k = 0; k < kTok; ++k) {
+        const int j = grp * kTok + k;
+        const int c = (2 * rp) >> 3;
+        const int sw = N == 32 ? (c ^ ((j >> 1) & 3)) : (c ^ ((j >> 2) & 1));
+        const uint32_t hv = *reinterpret_cast<const uint32_t*>(pt + j * (N * 2) + (sw << 4) + ((2 * rp) & 7) * 2);
+        const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&hv));
+        const float2 cf = coef[b * kPage + j];
+        l0 = fmaf(pf.x, cf.x, l0);
+        c0 = fmaf(pf.x, cf.y, c0);
+        l1 = fmaf(pf.y, cf.x, l1);
+        c1 = fmaf(pf.y, cf.y, c1);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        sm100::mbar_arrive(&B.p_empty[b]);
+        sm100::mbar_arrive(&B.raw_empty[s]);
+      }
+    }
+    if (!aborted) {
+      float* fs = fin + grp * 2 * N;  // [group][l (N) | C (N)]
+      fs[2 * rp] = l0;
+      fs[2 * rp + 1] = l1;
+      fs[N + 2 * rp] = c0;
+      fs[N + 2 * rp + 1] = c1;
+    }
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(B.stats_done);
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ softmax
+    const int st = tid - 256;  // TMEM lane = token of the page
+    const int swarp = st >> 5;
+    const uint32_t lrow = (uint32_t)(st & ~31) << 16;
+    const float sl2 = p.scale * kLog2e;
+    bool dead = false, aborted = false;
+    for (int i = 0; i < n_pages; ++i) {
+      const int s = i % kRing, b = i & 1;
+      bool ok = !dead && sm100::mbar_wait(&B.s_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
+                                          kBudgetNs);
+      float sc[N];
+      if (ok) {
+        uint32_t raw[N];
+        sm100::tc_fence_after();
+        if constexpr (N == 32)
+          sm100::tmem_ld_32x32b_x32(tbase + lrow + kColS + b * N, raw);
+        else
+          sm100::tmem_ld_32x32b_x16(tbase + lrow + kColS + b * N, raw);
+        sm100::tmem_ld_wait();
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&B.s_empty[b]);
+#pragma unroll
+        for (int r = 0; r < N; ++r) sc[r] = __uint_as_float(raw[r]);
+        ok = sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs);
+      }
+      float vs = 0.f;
+      bool need = false;
+      if (ok) {
+        const uint8_t* pg = ring + s * kSlot;
+        const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
+        const int blk = slot_blk[s];
+        const int j = st, pos = (p_first + i) * kPage + j;
+        const bool in = pos >= kv_begin && pos < kv_stop;
+        float ks = 0.f, kz = 0.f;
+        if (in) {
+          if (pos >= prefix || (staging && own[j] == blk)) {
+            ks = 1.f;
+            vs = 1.f;
+          } else {
+            const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * 64);
+            ks = __half2float(meta[j]);
+            kz = __half2float(meta[kPage + j]);
+            vs = __half2float(meta[2 * kPage + j]);
+          }
+        }
+        const bool hist = pos < prefix;
+#pragma unroll
+        for (int r = 0; r < N; ++r) {
+          const bool vis = in && (hist || pos <= lim[r]);
+          sc[r] = vis ? fmaf(ks, sc[r], kz * sq[r]) * sl2 : -INFINITY;
+          need |= sc[r] > msm[r] + kSlack;
+        }
+      }
+      // P' buffer b (and alpha/upd slot b) are free once P.V(i-2) and the stats of page i-2 are done
+      if (ok && i >= 2)
+        ok = sm100::mbar_wait(&B.p_empty[b], ((i >> 1) - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
+      if (sm100::bar_red_or(kBarSoft, 128, !ok)) {
+        aborted = true;
+        break;
+      }
+      const bool upd_now = sm100::bar_red_or(kBarSoft, 128, need);
+      if (upd_now) {
+        // agree on the new row maxima
+        {
+          float t[N];
+#pragma unroll
+          for (int r = 0; r < N; ++r) t[r] = sc[r];
+          const float wm = rows_reduce<N, true>(t);
+          if (lane < N) red[lane * 4 + swarp] = wm;
+        }
+        if (st == 0) *resc_flag = 0;
+        sm100::bar_sync(kBarSoft, 128);
+        if (st < N) {
+          const float4 q4 = *reinterpret_cast<const float4*>(red + st * 4);
+          const float pm = fmaxf(fmaxf(q4.x, q4.y), fmaxf(q4.z, q4.w));
+          const float mo = msm[st];
+          const float mn = fmaxf(mo, pm);
+          const float a = (mn == mo) ? 1.f : (mo == -INFINITY ? 0.f : exp2f(mo - mn));
+          alpha[b * N + st] = a;
+          msm[st] = mn;
+          if (a != 1.f) *resc_flag = 1;
+        }
+        sm100::bar_sync(kBarSoft, 128);
+        if (*resc_flag && i > 0) {  // O^T holds pages < i: rescale its columns once P.V(i-1) is done
+          bool ok2 = sm100::mbar_wait(&B.p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, p.status,
+                                      kTimeoutAccFull, kBudgetNs);
+          if (ok2) {
+            sm100::tc_fence_after();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t o[N];
+              if constexpr (N == 32)
+                sm100::tmem_ld_32x32b_x32(tbase + lrow + kColO + h * N, o);
+              else
+                sm100::tmem_ld_32x32b_x16(tbase + lrow + kColO + h * N, o);
+              sm100::tmem_ld_wait();
+#pragma unroll
+              for (int r = 0; r < N; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[b * N + r]);
+              if constexpr (N == 32)
+                sm100::tmem_st_32x32b_x32(tbase + lrow + kColO + h * N, o);
+              else
+                sm100::tmem_st_32x32b_x16(tbase + lrow + kColO + h * N, o);
+            }
+            sm100::tmem_st_wait();
+            sm100::tc_fence_before();
+          }
+          ok = ok2;
+        }
+      }
+      if (st == 0) upd[b] = upd_now ? 1 : 0;
+      if (ok) {
+        uint32_t pk[N / 2];
+#pragma unroll
+        for (int r = 0; r < N; r += 2) {
+          const float m0 = msm[r], m1 = msm[r + 1];
+          const float p0 = exp2f(sc[r] - (m0 == -INFINITY ? 0.f : m0));
+          const float p1 = exp2f(sc[r + 1] - (m1 == -INFINITY ? 0.f : m1));
+          pk[r / 2] = mma::h2_u32(p0 * vs, p1 * vs);
+        }
+        // P' row of token st: N fp16 = N/8 chunks of 16 B, MN-major swizzled (64 B / 32 B rows)
+        uint8_t* prow = ps + b * L::kPBytes + st * (N * 2);
+#pragma unroll
+        for (int c = 0; c < N / 8; ++c) {
+          const int sw = N == 32 ? (c ^ ((st >> 1) & 3)) : (c ^ ((st >> 2) & 1));
+          *reinterpret_cast<uint4*>(prow + (sw << 4)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        }
+        sm100::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          sm100::mbar_arrive(&B.p_full[b]);
+          sm100::mbar_arrive(&B.raw_empty[s]);
+        }
+      }
+      dead = !ok;
+    }
+    if (!aborted) aborted = sm100::bar_red_or(kBarSoft, 128, dead);  // every softmax warp agrees
+    if (!aborted) {
+      // ---- output: out[r, d] = (O^T[d, r] + C_r) / l_r
+      bool ok = sm100::mbar_wait(B.stats_done, 0, abort_flag, p.status, kTimeoutAccFull, kBudgetNs);
+      if (ok && n_pages > 0)
+        ok = sm100::mbar_wait(&B.p_empty[(n_pages - 1) & 1], ((n_pages - 1) >> 1) & 1, abort_flag, p.status,
+                              kTimeoutAccFull, kBudgetNs);
+      if (ok) {
+        constexpr int kGroups = 64 / (N / 2);
+        sm100::tc_fence_after();
+        float* po = p.part_o + ((long long)item * p.Hk + hk) * kPartRows * kD;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t o[N];
+          if (n_pages > 0) {
+            if constexpr (N == 32)
+              sm100::tmem_ld_32x32b_x32(tbase + lrow + kColO + h * N, o);
+            else
+              sm100::tmem_ld_32x32b_x16(tbase + lrow + kColO + h * N, o);
+            sm100::tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int r = 0; r < N; ++r) o[r] = 0u;
+          }
+          const int d = st + 128 * h;
+#pragma unroll
+          for (int r = 0; r < N; ++r) {
+            if (r >= nrows) break;
+            float Lr = 0.f, Cr = 0.f;
+#pragma unroll
+            for (int q = 0; q < kGroups; ++q) {
+              Lr += fin[q * 2 * N + r];
+              Cr += fin[q * 2 * N + N + r];
+            }
+            po[r * kD + d] = Lr > 0.f ? (__uint_as_float(o[r]) + Cr) / Lr : 0.f;
+          }
+        }
+        if (st < nrows) {
+          float Lr = 0.f;
+#pragma unroll
+          for (int q = 0; q < kGroups; ++q) Lr += fin[q * 2 * N + st];
+          p.part_lse[((long long)item * p.Hk + hk) * kPartRows + st] =
+              Lr > 0.f ? (msm[st] + log2f(Lr)) / kLog2e : -INFINITY;
+        }
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+template <int N>
+int launch_tc(const AttnParams& p, cudaStream_t stream) {
+  using L = TcLayout<N>;
+  static int attr = 0;
+  if (!attr) {
+    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(int2_attention_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          L::kAlloc));
+    attr = 1;
+  }
+  dim3 grid(p.n_work, p.Hk);
+  int2_attention_tc_kernel<N><<<grid, kThreads, L::kAlloc, stream>>>(p);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace oscar
+
+// rows_per_item: the largest q_len * g - row0 of any work item (<= 32).
+extern "C" int oscar_int2_attention_tc(const oscar::AttnParams* params, int rows_per_item, cudaStream_t stream) {
+  using namespace oscar;
+  const AttnParams& p = *params;
+  if (p.n_work <= 0) return 0;
+  if (p.D != kD || p.kv_mode != 0) return -330;
+  if (p.page_bytes != kPageBytes) return -331;
+  if (rows_per_item <= 16) return launch_tc<16>(p, stream);
+  if (rows_per_item <= 32) return launch_tc<32>(p, stream);
+  return -332;
+}

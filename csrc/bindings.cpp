@@ -15,6 +15,7 @@ int oscar_gemm_i8(const void* A, long long lda, const void* B, long long ldb, in
 int oscar_num_sms();
 int oscar_kv_store(const oscar::StoreParams* p, cudaStream_t stream);
 int oscar_paged_attention(const oscar::AttnParams* p, cudaStream_t stream);
+int oscar_int2_attention_tc(const oscar::AttnParams* p, int rows_per_item, cudaStream_t stream);
 int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
 int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi, const __nv_bfloat16* Rv_lo,
                          cudaStream_t stream);
@@ -25,7 +26,7 @@ int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long long ldd, co
 int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                      const float* scale_a, const float* scale_b, void* out, long long ldo, int mode, int trans, int bn,
                      int splits, int* status, int* done_counter, int* epoch, unsigned** peer_signals, int rank,
-                     int world, cudaStream_t stream);
+                     int world, float* ws, int* tile_cnt, cudaStream_t stream);
 int oscar_swiglu_quant(const __nv_bfloat16* gu, long long ld, int T, int I, int8_t* out, float* scale,
                        cudaStream_t s);
 int oscar_act_quant(const __nv_bfloat16* x, long long ld, int T, int K, int8_t* out, float* scale, cudaStream_t s);
@@ -104,7 +105,8 @@ void gemm_i8(const Tensor& A, const Tensor& B, const Tensor& scale_a, const Tens
 // then publishes the completion epoch into every peer's signal pad.
 void gemm_i8_allreduce(const Tensor& A, const Tensor& B, const Tensor& scale_a, const Tensor& scale_b, int64_t mc_ptr,
                        int64_t ldo, int64_t trans, int64_t bn, int64_t splits, Tensor& done_counter, Tensor& epoch,
-                       int64_t peer_signals_dev, int64_t rank, int64_t world, const optional<Tensor>& status) {
+                       int64_t peer_signals_dev, int64_t rank, int64_t world, Tensor& ws, Tensor& tile_cnt,
+                       const optional<Tensor>& status) {
   CHECK_DTYPE(A, at::kChar);
   CHECK_DTYPE(B, at::kChar);
   TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_i8_allreduce: K must be contiguous");
@@ -114,7 +116,8 @@ void gemm_i8_allreduce(const Tensor& A, const Tensor& B, const Tensor& scale_a, 
   check_rc(oscar_gemm_i8_ex(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), M, N, K, ptr<float>(scale_a),
                             ptr<float>(scale_b), reinterpret_cast<void*>(mc_ptr), ldo, 3, (int)trans, (int)bn,
                             (int)splits, optr<int>(status), ptr<int>(done_counter), ptr<int>(epoch),
-                            reinterpret_cast<unsigned**>(peer_signals_dev), (int)rank, (int)world, stream()),
+                            reinterpret_cast<unsigned**>(peer_signals_dev), (int)rank, (int)world, ptr<float>(ws),
+                            ptr<int>(tile_cnt), stream()),
            "gemm_i8_allreduce");
 }
 
@@ -205,7 +208,7 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
                      const optional<Tensor>& vc, const optional<Tensor>& stage_k, const optional<Tensor>& stage_v,
                      const optional<Tensor>& owner, int64_t stage_rows, const Tensor& block_tables,
                      const Tensor& q_start, const Tensor& seq_lens, const Tensor& work, Tensor& part_o,
-                     Tensor& part_lse, const optional<Tensor>& status) {
+                     Tensor& part_lse, const optional<Tensor>& status, int64_t rows_per_item) {
   CHECK_CUDA(q);
   CHECK_DTYPE(q, at::kHalf);
   CHECK_DTYPE(k_fresh, at::kHalf);
@@ -250,7 +253,11 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
   p.status = optr<int>(status);
   TORCH_CHECK(part_o.numel() >= (int64_t)p.n_work * Hk * 64 * D, "part_o too small");
   const c10::cuda::CUDAGuard guard(q.device());
-  check_rc(oscar_paged_attention(&p, stream()), "paged_attention");
+  // INT2 items of <= 32 rows (decode / MTP verify) run on the tcgen05 kernel
+  if (kv_mode == 0 && rows_per_item > 0 && rows_per_item <= 32)
+    check_rc(oscar_int2_attention_tc(&p, (int)rows_per_item, stream()), "paged_attention(tcgen05)");
+  else
+    check_rc(oscar_paged_attention(&p, stream()), "paged_attention");
 }
 
 void attn_merge(const Tensor& part_o, const Tensor& part_lse, const Tensor& item_first, const Tensor& item_count,

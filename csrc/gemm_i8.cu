@@ -216,7 +216,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             v.w = pack_bf16x2((float)(int)r[j + 6] * sa * ep.scale_b[nb + j + 6], (float)(int)r[j + 7] * sa * ep.scale_b[nb + j + 7]);
             *reinterpret_cast<uint4*>(o + j) = v;
           }
-        } else if (ep.mode == 3 && !ep.trans && nb + 32 <= N && (ep.ldo % 4) == 0) {
+        } else if (ep.mode == 3 && splits == 1 && !ep.trans && nb + 32 <= N && (ep.ldo % 4) == 0) {
           // prefill-shaped tile: 16-byte in-switch reductions along the row
           float* o = reinterpret_cast<float*>(ep.out) + (long long)m * ep.ldo + nb;
 #pragma unroll
@@ -240,11 +240,15 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             } else if (ep.mode == 1) {
               atomicAdd(reinterpret_cast<float*>(ep.out) + idx, v);
             } else if (ep.mode == 3) {
-              // in-switch reduction: adds v into this element of every rank's buffer
-              asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(
-                               reinterpret_cast<float*>(ep.out) + idx),
-                           "f"(v)
-                           : "memory");
+              if (splits > 1) {
+                atomicAdd(ep.ws + idx, v);  // split-K partial: local workspace first
+              } else {
+                // in-switch reduction: adds v into this element of every rank's buffer
+                asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(
+                                 reinterpret_cast<float*>(ep.out) + idx),
+                             "f"(v)
+                             : "memory");
+              }
             } else {
               reinterpret_cast<float*>(ep.out)[idx] = v;
             }
@@ -254,6 +258,36 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&acc_empty[acc]);
+      if (ep.mode == 3 && splits > 1) {
+        // Split-K fix-up, per (tile, row quarter): every split adds its partial rows
+        // into the local workspace and counts itself in; the last one reads the sums
+        // back from L2, reduces them into every rank through the switch and clears
+        // the workspace for the next call.  NVLink then carries each element once.
+        __threadfence();
+        __syncwarp();
+        const int slot = (t / splits) * 4 + quarter;
+        int prev = 0;
+        if (lane == 0) prev = atomicAdd(ep.tile_cnt + slot, 1);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == splits - 1) {
+          __threadfence();
+          if (row_ok) {
+            for (int j = 0; j < BN; ++j) {
+              const int n = n0 + j;
+              if (n >= N) break;
+              const long long idx = ep.trans ? (long long)n * ep.ldo + m : (long long)m * ep.ldo + n;
+              const float v = __ldcg(ep.ws + idx);
+              asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(
+                               reinterpret_cast<float*>(ep.out) + idx),
+                           "f"(v)
+                           : "memory");
+              ep.ws[idx] = 0.f;
+            }
+          }
+          __syncwarp();
+          if (lane == 0) ep.tile_cnt[slot] = 0;
+        }
+      }
     }
   }
 
@@ -378,32 +412,35 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmEpi& ep, int 
 extern "C" int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                                 const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
                                 int trans, int bn, int splits, int* status, int* done_counter, int* epoch,
-                                unsigned** peer_signals, int rank, int world, cudaStream_t stream);
+                                unsigned** peer_signals, int rank, int world, float* ws, int* tile_cnt,
+                                cudaStream_t stream);
 
 extern "C" int oscar_gemm_i8(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                              const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
                              int trans, int bn, int splits, int* status, cudaStream_t stream) {
   if (mode == 3) return -105;  // the multimem mode needs the completion state: use oscar_gemm_i8_ex
   return oscar_gemm_i8_ex(A, lda, B, ldb, M, N, K, scale_a, scale_b, out, ldo, mode, trans, bn, splits, status,
-                          nullptr, nullptr, nullptr, 0, 1, stream);
+                          nullptr, nullptr, nullptr, 0, 1, nullptr, nullptr, stream);
 }
 
 extern "C" int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                                 const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
                                 int trans, int bn, int splits, int* status, int* done_counter, int* epoch,
-                                unsigned** peer_signals, int rank, int world, cudaStream_t stream) {
+                                unsigned** peer_signals, int rank, int world, float* ws, int* tile_cnt,
+                                cudaStream_t stream) {
   using namespace oscar;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 16) || (lda % 16) || (ldb % 16)) return -102;
   if (splits < 1) splits = 1;
   if (splits > 1 && mode != 1 && mode != 3) return -104;  // split-K partial sums must be accumulated
   if (mode == 3 && (!done_counter || !epoch || !peer_signals || world < 1)) return -106;
+  if (mode == 3 && splits > 1 && (!ws || !tile_cnt)) return -107;
   CUtensorMap ta, tb;
   int rc = make_map(&ta, A, M, K, lda, BM);
   if (rc) return rc;
   rc = make_map(&tb, B, N, K, ldb, bn);
   if (rc) return rc;
-  GemmEpi ep{scale_a, scale_b, out, ldo, mode, trans, done_counter, epoch, peer_signals, rank, world};
+  GemmEpi ep{scale_a, scale_b, out, ldo, mode, trans, done_counter, epoch, peer_signals, rank, world, ws, tile_cnt};
   switch (bn) {
     case 32: return launch<32>(ta, tb, ep, M, N, K, splits, status, stream);
     case 64: return launch<64>(ta, tb, ep, M, N, K, splits, status, stream);

@@ -48,8 +48,12 @@ __device__ __forceinline__ float kth_largest_abs(const float (&x)[8], int n, int
 }
 
 // One warp quantises one (token, head) vector of D = 32 * n elements.
+// codes_row: token-major code row (K), or nullptr with vt_words/tok set: V is stored
+// dim-major ("transposed") - dim d of the page owns kPage/16 words, and token tok sits
+// in word d * kPage/16 + tok/16 at bit 16*(tok&1) + 2*((tok&15)>>1).  Tokens of one
+// step share words, so the 2-bit fields are cleared and set with atomic reductions.
 __device__ void quantize_vector(float (&x)[8], int n, int clip_idx, int D, uint8_t* codes_row,
-                                __half* scale_dst, __half* zero_dst) {
+                                __half* scale_dst, __half* zero_dst, uint32_t* vt_words = nullptr, int tok = 0) {
   const int lane = threadIdx.x & 31;
   if (clip_idx >= 0) {
     const float thr = kth_largest_abs(x, n, D - clip_idx);
@@ -79,17 +83,26 @@ __device__ void quantize_vector(float (&x)[8], int n, int clip_idx, int D, uint8
   // 32-bit word holds dims 16w..16w+15 with dim 16w+2m+e at bit 16e+2m; the lanes
   // sharing a word OR their parts together and the first of them stores it.
   uint32_t part = 0;
+  const int tbit = 16 * (tok & 1) + 2 * ((tok & 15) >> 1);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     if (e < n) {
       float q = floorf(__fadd_rn(__fdiv_rn(__fsub_rn(x[e], zf), sf), 0.5f));
       q = fminf(fmaxf(q, 0.f), 3.f);
-      const int j = (lane * n + e) & 15;
-      part |= ((uint32_t)q) << (16 * (j & 1) + 2 * (j >> 1));
+      if (vt_words) {
+        uint32_t* w = vt_words + (lane * n + e) * (kPage / 16) + (tok >> 4);
+        atomicAnd(w, ~(3u << tbit));
+        atomicOr(w, ((uint32_t)q) << tbit);
+      } else {
+        const int j = (lane * n + e) & 15;
+        part |= ((uint32_t)q) << (16 * (j & 1) + 2 * (j >> 1));
+      }
     }
   }
-  for (int o = 1; o < 16 / n; o <<= 1) part |= __shfl_xor_sync(0xffffffffu, part, o);
-  if (((lane * n) & 15) == 0) reinterpret_cast<uint32_t*>(codes_row)[(lane * n) >> 4] = part;
+  if (!vt_words) {
+    for (int o = 1; o < 16 / n; o <<= 1) part |= __shfl_xor_sync(0xffffffffu, part, o);
+    if (((lane * n) & 15) == 0) reinterpret_cast<uint32_t*>(codes_row)[(lane * n) >> 4] = part;
+  }
   if (lane == 0) {
     *scale_dst = sh;
     *zero_dst = zh;
@@ -304,10 +317,12 @@ __global__ void __launch_bounds__(kThreads, 2) kv_rotate_kernel(StoreParams p, i
     }
     uint8_t* page = p.pool + ((long long)blk * Hk + h) * p.page_bytes;
     const int cb = D / 4;
-    uint8_t* codes = page + (is_v ? kPage * cb : 0) + off * cb;
     __half* meta = reinterpret_cast<__half*>(page + 2 * kPage * cb);
-    quantize_vector(x, n, is_v ? p.v_clip_idx : p.k_clip_idx, D, codes, meta + (is_v ? 2 : 0) * kPage + off,
-                    meta + (is_v ? 3 : 1) * kPage + off);
+    if (is_v)
+      quantize_vector(x, n, p.v_clip_idx, D, nullptr, meta + 2 * kPage + off, meta + 3 * kPage + off,
+                      reinterpret_cast<uint32_t*>(page + kPage * cb), off);
+    else
+      quantize_vector(x, n, p.k_clip_idx, D, page + off * cb, meta + off, meta + kPage + off);
   }
 }
 

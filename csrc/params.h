@@ -19,6 +19,12 @@ struct GemmEpi {
   int* epoch;
   unsigned** peer_signals;
   int rank, world;
+  // mode 3 with split-K: partial tiles are summed in this rank's fp32 workspace
+  // (same indexing as out, all zero between calls); the last split of a (tile, row
+  // quarter) - counted in tile_cnt - sends the reduced rows through the switch and
+  // re-zeroes them.
+  float* ws;
+  int* tile_cnt;
 };
 
 struct StoreParams {

@@ -111,6 +111,14 @@ class LLMEngine:
         self.sms = num_sms(self.dev) if self.dev.type == "cuda" else 148
 
     # ------------------------------------------------------------------ API
+    def close(self) -> None:
+        """Release the captured CUDA graphs (they may hold NCCL work: drop them before
+        the process group is destroyed)."""
+        if self.use_graphs:
+            torch.cuda.synchronize(self.dev)
+        self._graphs.clear()
+        self._seen.clear()
+
     def add_request(self, prompt, max_new_tokens: int) -> int:
         rid = next(self._ids)
         self.requests[rid] = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer())

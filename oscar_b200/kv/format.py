@@ -205,21 +205,53 @@ def parse_slot_bytes(slot: torch.Tensor, D: int) -> tuple[torch.Tensor, torch.Te
 def page_views(pool: torch.Tensor, D: int, page: int = PAGE):
     """Split a ``[blocks, Hk, page_head_bytes]`` uint8 pool into typed views.
 
-    Returns ``(k_codes [B,Hk,page,D/4], v_codes, k_scale [B,Hk,page] fp16, k_zero, v_scale, v_zero)``.
+    Returns ``(k_codes [B,Hk,page,D/4], v_codes_t [B,Hk,D,page/4], k_scale [B,Hk,page]
+    fp16, k_zero, v_scale, v_zero)``.  K codes are token-major (one row of ``D/4`` bytes
+    per token, dims in the pool bit order); V codes are dim-major (one row of
+    ``page/4`` bytes per dim, tokens in the same bit order), which is the operand
+    layout of the P.V product in the attention kernels.
     """
     nb, hk, pb = pool.shape
     off = page_offsets(D, page)
     assert pb == off["total"], f"pool page size {pb} != {off['total']}"
     cb = code_bytes(D)
     kc = pool[:, :, off["k"]: off["v"]].view(nb, hk, page, cb)
-    vc = pool[:, :, off["v"]: off["k_scale"]].view(nb, hk, page, cb)
+    vt = pool[:, :, off["v"]: off["k_scale"]].view(nb, hk, D, page // 4)
     meta = pool.view(torch.float16)[:, :, off["k_scale"] // 2: off["total"] // 2].view(nb, hk, 4, page)
-    return kc, vc, meta[:, :, 0], meta[:, :, 1], meta[:, :, 2], meta[:, :, 3]
+    return kc, vt, meta[:, :, 0], meta[:, :, 1], meta[:, :, 2], meta[:, :, 3]
+
+
+def _token_byte_shift(offs: torch.Tensor, page: int = PAGE):
+    pos = _page_bit_positions(page).to(offs.device)[offs.long()]
+    return pos // 8, pos % 8
+
+
+def read_v_codes(vt: torch.Tensor, b: torch.Tensor, o: torch.Tensor) -> torch.Tensor:
+    """Codes ``[T, Hk, D]`` of tokens ``(b, o)`` from the dim-major V view."""
+    byte, shift = _token_byte_shift(o, vt.shape[-1] * 4)
+    raw = vt[b.long(), :, :, byte].to(torch.int32)  # [T, Hk, D]
+    return (raw >> shift.view(-1, 1, 1).to(torch.int32)) & 3
+
+
+def write_v_codes(vt: torch.Tensor, b: torch.Tensor, o: torch.Tensor, q: torch.Tensor) -> None:
+    """Store codes ``q [T, Hk, D]`` of tokens ``(b, o)`` into the dim-major V view.  Four
+    tokens share a byte, so the writes go in four passes of non-colliding tokens."""
+    page = vt.shape[-1] * 4
+    byte, shift = _token_byte_shift(o, page)
+    lane = ((o.long() % 16) // 2) % 4  # tokens of one byte differ here
+    for p in range(4):
+        sel = torch.nonzero(lane == p, as_tuple=True)[0]
+        if sel.numel() == 0:
+            continue
+        bb, by, sh = b[sel].long(), byte[sel], shift[sel].view(-1, 1, 1).to(torch.int32)
+        cur = vt[bb, :, :, by].to(torch.int32)
+        new = (cur & ~(3 << sh)) | ((q[sel].to(torch.int32) & 3) << sh)
+        vt[bb, :, :, by] = new.to(torch.uint8)
 
 
 def pool_to_slots(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor, D: int) -> torch.Tensor:
     """Read tokens ``(blocks[i], offs[i])`` of a page-packed pool as ``[T, Hk, 160]`` slots."""
-    kc, vc, ks, kz, vs, vz = page_views(pool, D)
+    kc, vt, ks, kz, vs, vz = page_views(pool, D)
     b, o = blocks.long(), offs.long()
     T, hk = b.numel(), pool.shape[1]
     cb = code_bytes(D)
@@ -229,16 +261,16 @@ def pool_to_slots(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor, 
         slot[..., 2 * i: 2 * i + 1] = lo
         slot[..., 2 * i + 1: 2 * i + 2] = hi
     slot[..., K_IDX_OFF: K_IDX_OFF + cb] = pack(unpack_page(kc[b, :, o], D))
-    slot[..., V_IDX_OFF: V_IDX_OFF + cb] = pack(unpack_page(vc[b, :, o], D))
+    slot[..., V_IDX_OFF: V_IDX_OFF + cb] = pack(read_v_codes(vt, b, o))
     return slot
 
 
 def dequant_tokens(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor, D: int):
     """Dequantize tokens of a page-packed pool -> ``(k [T,Hk,D], v [T,Hk,D])`` fp32 (rotated space)."""
-    kc, vc, ks, kz, vs, vz = page_views(pool, D)
+    kc, vt, ks, kz, vs, vz = page_views(pool, D)
     b, o = blocks.long(), offs.long()
     k = unpack_page(kc[b, :, o], D).float() * ks[b, :, o].float().unsqueeze(-1) + kz[b, :, o].float().unsqueeze(-1)
-    v = unpack_page(vc[b, :, o], D).float() * vs[b, :, o].float().unsqueeze(-1) + vz[b, :, o].float().unsqueeze(-1)
+    v = read_v_codes(vt, b, o).float() * vs[b, :, o].float().unsqueeze(-1) + vz[b, :, o].float().unsqueeze(-1)
     return k, v
 
 
@@ -246,11 +278,15 @@ def write_tokens(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor, k
                  v_c: torch.Tensor) -> None:
     """Quantize clipped rotated ``k_c/v_c [T,Hk,D]`` into the pool at ``(blocks, offs)``."""
     D = k_c.shape[-1]
-    kc, vc, ks, kz, vs, vz = page_views(pool, D)
+    kc, vt, ks, kz, vs, vz = page_views(pool, D)
     b, o = blocks.long(), offs.long()
-    for x, codes_v, sv, zv in ((k_c, kc, ks, kz), (v_c, vc, vs, vz)):
+    for is_v, x, sv, zv in ((False, k_c, ks, kz), (True, v_c, vs, vz)):
         scale, zero = vector_scales(x)
-        codes_v[b, :, o] = pack_page(codes(x, scale, zero))
+        q = codes(x, scale, zero)
+        if is_v:
+            write_v_codes(vt, b, o, q)
+        else:
+            kc[b, :, o] = pack_page(q)
         sv[b, :, o] = scale.squeeze(-1).half()
         zv[b, :, o] = zero.squeeze(-1).half()
 

@@ -34,6 +34,7 @@ from ..ops.gdn import gdn_step
 from ..parallel.fused import NcclRowReduce, make_row_reduce
 from ..parallel.groups import TPGroup
 from .config import HybridConfig
+from .selection import AttentionSpec, beat, should_oscar
 
 P_MAX = 4  # pending (uncommitted) tokens per GDN slot: 1 verified + 3 drafts
 
@@ -196,6 +197,8 @@ class FullAttentionLayer:
     def attention(self, xq, xs, b: StepBatch, rope, owner, stage_rows, write_owner: bool, status=None):
         """qkv GEMM -> fused store -> paged attention -> merge. Returns (o_int8, o_scale)."""
         T = xq.shape[0]
+        if self.kv_mode == 0:
+            beat()
         dev = xq.device
         qkv = F.linear_i8(xq, xs, self.qkv.q, self.qkv.s, status=status)
         q_out = torch.empty(T, self.Hq, self.D, dtype=torch.float16, device=dev)
@@ -334,8 +337,11 @@ class HybridModel:
         self.final_norm = _rand_vec(H, base + 997, dev)
         self.layers = []
         for i, t in enumerate(cfg.layer_types):
-            mixer = (FullAttentionLayer(cfg, self.tp, i, seed, dev, self.oscar, kv_mode, rotation)
-                     if t == "full_attention" else GDNLayer(cfg, self.tp, i, seed, dev))
+            if t == "full_attention":
+                lkv = kv_mode if should_oscar(AttentionSpec(i), cfg) else "bf16"
+                mixer = FullAttentionLayer(cfg, self.tp, i, seed, dev, self.oscar, lkv, rotation)
+            else:
+                mixer = GDNLayer(cfg, self.tp, i, seed, dev)
             self.layers.append((mixer, MLP(cfg, self.tp, i, seed, dev)))
         self.mtp = MTPHead(self, seed) if (mtp and cfg.num_mtp_layers > 0) else None
         self.rope = F.rope_tables(cfg.max_position, cfg.rot_dim, cfg.rope_theta, dev)
@@ -370,8 +376,9 @@ class HybridModel:
 
     def allocate_cache(self, num_blocks: int, max_slots: int):
         o = self.oscar
+        int2 = any(m.kv_mode == 0 for m in self.full_layers)
         self.stage_rows = staging_rows(o.sink_tokens, o.recent_tokens, o.staging_tokens) if (
-            o.window_enabled and self.kv_mode == "int2") else 0
+            o.window_enabled and int2) else 0
         if self.stage_rows:
             self.owner = torch.full((self.stage_rows * fmt.PAGE,), -1, dtype=torch.int32, device=self.device)
         for m in self.full_layers:

@@ -14,6 +14,7 @@ The CPU path computes the same result with the torch oracle
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -25,6 +26,15 @@ from ._ext import ext
 from .functional import apply_rope_ref, head_rmsnorm_ref, quantize_rows_ref, _bf16_round
 
 ROWS = 64  # rows (query token x head-in-group) per attention work item
+# INT2 work items of <= 32 rows run on the tcgen05/TMEM kernel (OSCAR_ATTN_TC=0 keeps
+# every item on the warp-level mma.sync kernel, for A/B comparisons)
+USE_TC = os.environ.get("OSCAR_ATTN_TC", "1") != "0"
+
+
+def rows_per_item(q_start: list[int], g: int) -> int:
+    """Largest number of query rows (q_len x g, capped at ROWS) of any work item."""
+    n = max((q_start[i + 1] - q_start[i] for i in range(len(q_start) - 1)), default=0)
+    return min(ROWS, n * g)
 
 
 @dataclass
@@ -259,7 +269,8 @@ def attention(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, s
     if stage is not None:
         sk, sv, own, rows = stage
     e.paged_attention(q, k_fresh, v_fresh, Hq, Hk, D, float(scale), kv_mode, pool, kc, vc, sk, sv, own, rows,
-                      block_tables, q_start_t, seq_lens_t, plan.work, part_o, part_lse, status)
+                      block_tables, q_start_t, seq_lens_t, plan.work, part_o, part_lse, status,
+                      rows_per_item(q_start, Hq // Hk) if USE_TC else 0)
     if RvT is not None:
         # tensor-core merge + rotation + gate, then the vectorised row quantiser
         if rv_merge_split is None:

@@ -74,9 +74,12 @@ class FusedRowReduce:
         self.H = H
         self.max_rows = max_rows
         group = tp.group if tp.group is not None else dist.group.WORLD
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        if not symm._SymmetricMemory.has_multicast_support(symm.DeviceType.CUDA, idx):
+            raise RuntimeError("NVLS multicast is not supported on this device")
         self.bufs = symm.empty((2, max_rows, H), dtype=torch.float32, device=device)
         self.hdl = symm.rendezvous(self.bufs, group)
-        if not self.hdl.has_multicast_support():
+        if not int(self.hdl.multicast_ptr):
             raise RuntimeError("NVLS multicast is not available for this group")
         self.bufs.zero_()
         self.mc = int(self.hdl.multicast_ptr)
@@ -87,6 +90,9 @@ class FusedRowReduce:
         pad.zero_()
         self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
         self.done = torch.zeros(1, dtype=torch.int32, device=device)
+        # split-K partials are summed locally first (one NVLink crossing per element)
+        self.ws = torch.zeros(max_rows, H, dtype=torch.float32, device=device)
+        self.tile_cnt = torch.zeros(1 << 16, dtype=torch.int32, device=device)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
         self._T = 0
@@ -104,10 +110,10 @@ class FusedRowReduce:
         mc = self.mc + b * self.max_rows * self.H * 4
         if plan.swap:
             ext().gemm_i8_allreduce(w.q, xq, w.s, xs, mc, self.H, 1, plan.bn, plan.splits, self.done, self.epoch,
-                                    self.peer_signals, self.tp.rank, self.tp.world, status)
+                                    self.peer_signals, self.tp.rank, self.tp.world, self.ws, self.tile_cnt, status)
         else:
             ext().gemm_i8_allreduce(xq, w.q, xs, w.s, mc, self.H, 0, plan.bn, plan.splits, self.done, self.epoch,
-                                    self.peer_signals, self.tp.rank, self.tp.world, status)
+                                    self.peer_signals, self.tp.rank, self.tp.world, self.ws, self.tile_cnt, status)
         return {"delta": self.bufs[b, :self._T], "wait": (self.my_signals, self.epoch, self.tp.world),
                 "zero_delta": True}
 

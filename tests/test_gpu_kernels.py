@@ -164,8 +164,9 @@ def test_kv_store_matches_ref(rot):
     # codes may sit on the other side of a rounding boundary (fp32 summation order).
     kc_c, vc_c, *mc = fmt.page_views(c[3], D)
     kc_g, vc_g, *mg = fmt.page_views(g[3], D)
-    codes_c = torch.cat([fmt.unpack(kc_c, D).flatten(), fmt.unpack(vc_c, D).flatten()])
-    codes_g = torch.cat([fmt.unpack(kc_g, D).flatten(), fmt.unpack(vc_g, D).flatten()])
+    # 2-bit fields compared position by position (K token-major rows, V dim-major rows)
+    codes_c = torch.cat([fmt.unpack(x, x.shape[-1] * 4).flatten() for x in (kc_c, vc_c)])
+    codes_g = torch.cat([fmt.unpack(x, x.shape[-1] * 4).flatten() for x in (kc_g, vc_g)])
     diff = (codes_c != codes_g).float().mean().item()
     if rot:
         assert diff < 2e-3
@@ -212,8 +213,12 @@ def _build_cache(dev, Hk, D, seqs, qlens, seed, stage_rows=0, kv_mode=0):
     return nb, bt
 
 
-@pytest.mark.parametrize("case", ["decode", "mtp", "mixed", "bf16"])
-def test_paged_attention_matches_ref(case):
+@pytest.mark.parametrize("use_tc", [True, False], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("case", ["decode", "mtp", "mixed", "bf16", "long"])
+def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
+    if not use_tc and case in ("mixed", "bf16"):
+        pytest.skip("same kernel as the tcgen05 run")
+    monkeypatch.setattr(A, "USE_TC", use_tc)
     torch.manual_seed(1)
     Hq, Hk, D = 6, 1, 256
     g = Hq // Hk
@@ -223,6 +228,8 @@ def test_paged_attention_matches_ref(case):
         seqs, qlens = [2000, 513, 4100], [4, 4, 4]
     elif case == "mixed":
         seqs, qlens = [300, 1000], [300, 37]
+    elif case == "long":
+        seqs, qlens = [16384, 9000, 24579], [4, 4, 4]
     else:
         seqs, qlens = [900, 260], [4, 4]
     kv_mode = 1 if case == "bf16" else 0
