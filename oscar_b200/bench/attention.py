@@ -1,0 +1,180 @@
+"""Single-GPU attention sweep (reference tool:
+``tools/benchmark_attention.py:25-205``).
+
+Head geometry of one TP4 rank of the target model: Hq = 6, Hk = 1, head_dim 256,
+128-token pages.  Paged decode / MTP-verify attention over INT2 pages at history
+lengths 1024 / 8192 / 32768, batch 1-32, 1-4 query tokens, plus a prefill
+continuation of 9256 new tokens over a 15360-token INT2 history.  Variants:
+
+* ``int2_tc``   - the tcgen05/TMEM kernel (work items of <= 32 rows),
+* ``int2_mma``  - the warp-level mma.sync kernel,
+* ``bf16``      - the same attention over a BF16 KV cache (the uncompressed baseline).
+
+Each variant is checked against the first one on the merged output (rtol 1e-2),
+then the attention kernel alone is timed with CUDA events, L2 flushed before every
+sample, median of warm samples.  Reported: microseconds, bytes of KV the kernel must
+read, achieved GB/s and its fraction of the measured HBM copy bandwidth.
+
+    python -m oscar_b200.bench.attention [--hist 1024,8192,32768] [--batch 1,8,32] [--qlen 1,4]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import numpy as np
+import torch
+
+from ..kv import format as fmt
+from ..ops import attention as A
+from ..ops import functional as F
+from ..ops._ext import ext
+from .harness import compare_calls
+
+
+def _peak_gbs() -> float:
+    here = os.path.dirname(os.path.abspath(__file__))
+    for p in (os.path.join(here, "..", "..", "MEASURED_PEAKS.json"),):
+        try:
+            with open(p) as f:
+                return float(json.load(f)["hbm_gbs"])
+        except (OSError, KeyError, ValueError):
+            pass
+    return 6650.0  # earlier measurement on this pool when the file is absent
+
+
+def build_case(hist: int, batch: int, qlen: int, hq: int = 6, hk: int = 1, D: int = 256, seed: int = 0,
+               staging: bool = True, device="cuda"):
+    """Random INT2 + BF16 caches holding ``hist`` tokens of history per request."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    seqs = [hist + qlen] * batch
+    pages = [(s + 127) // 128 for s in seqs]
+    nb = sum(pages) + 4
+    perm = torch.randperm(nb, generator=g)
+    bt = torch.zeros(batch, max(pages), dtype=torch.int32)
+    k = 0
+    for r in range(batch):
+        bt[r, :pages[r]] = perm[k:k + pages[r]]
+        k += pages[r]
+    dev = torch.device(device)
+    pool = torch.randint(0, 256, (nb, hk, fmt.page_head_bytes(D)), dtype=torch.uint8, generator=g)
+    _, _, ks, kz, vs, vz = fmt.page_views(pool, D)
+    ks.copy_((torch.rand(ks.shape, generator=g) * 0.5 + 0.2).half())
+    vs.copy_((torch.rand(vs.shape, generator=g) * 0.5 + 0.2).half())
+    kz.copy_((-torch.rand(kz.shape, generator=g) - 0.3).half())
+    vz.copy_((-torch.rand(vz.shape, generator=g) - 0.3).half())
+    kc = torch.randn(nb, 128, hk, D, generator=g).to(torch.bfloat16)
+    vc = torch.randn(nb, 128, hk, D, generator=g).to(torch.bfloat16)
+    T = batch * qlen
+    q = torch.randn(T, hq, D, generator=g).half()
+    kf = torch.randn(T, hk, D, generator=g).half()
+    vf = torch.randn(T, hk, D, generator=g).half()
+    q_start = [0] + list(np.cumsum([qlen] * batch))
+    stage = None
+    if staging:
+        rows = 64
+        sk = torch.randn(rows * 128, hk, D, generator=g)
+        sv = torch.randn(rows * 128, hk, D, generator=g)
+        owner = torch.full((rows * 128,), -1, dtype=torch.int32)
+        for r in range(batch):  # sink page and the last two pages of every request
+            for p in {0, pages[r] - 2, pages[r] - 1}:
+                if p >= 0:
+                    b = int(bt[r, p])
+                    owner.view(rows, 128)[b % rows] = b
+        stage = (sk.to(dev), sv.to(dev), owner.to(dev), rows)
+    d = lambda t: t.to(dev)  # noqa: E731
+    tok_req = torch.repeat_interleave(torch.arange(batch), torch.tensor([qlen] * batch)).to(torch.int32)
+    plan = A.plan_attention(q_start, seqs, hq // hk, hk, F.num_sms(dev), dev)
+    return dict(q=d(q), kf=d(kf), vf=d(vf), pool=d(pool), kc=d(kc), vc=d(vc), bt=d(bt), stage=stage,
+                q_start=q_start, seqs=seqs, q_start_t=d(torch.tensor(q_start, dtype=torch.int32)),
+                seq_lens_t=d(torch.tensor(seqs, dtype=torch.int32)), tok_req=d(tok_req), plan=plan, hq=hq, hk=hk,
+                D=D, pages=sum(pages), T=T)
+
+
+def _attention(c, kv_mode: int, use_tc: bool):
+    A.USE_TC = use_tc
+    out, _, _ = A.attention(c["q"], c["kf"], c["vf"], Hq=c["hq"], Hk=c["hk"], D=c["D"], scale=1 / 16,
+                            kv_mode=kv_mode, pool=c["pool"], kc=c["kc"], vc=c["vc"],
+                            stage=c["stage"] if kv_mode == 0 else None, block_tables=c["bt"],
+                            q_start_t=c["q_start_t"], seq_lens_t=c["seq_lens_t"], q_start=c["q_start"],
+                            seq_lens=c["seqs"], plan=c["plan"], tok_req=c["tok_req"], RvT=None, gate=None,
+                            gate_ld=0, gate_hstride=0, want_bf16=True, want_q=False)
+    return out
+
+
+def _kernel_only(c, kv_mode: int, use_tc: bool):
+    plan = c["plan"]
+    po = torch.empty(plan.n_work * c["hk"] * A.ROWS * c["D"], dtype=torch.float32, device=c["q"].device)
+    pl = torch.empty(plan.n_work * c["hk"] * A.ROWS, dtype=torch.float32, device=c["q"].device)
+    sk, sv, own, rows = c["stage"] if (kv_mode == 0 and c["stage"] is not None) else (None, None, None, 0)
+    rpi = A.rows_per_item(c["q_start"], c["hq"] // c["hk"]) if use_tc else 0
+    e = ext()
+
+    def run():
+        e.paged_attention(c["q"], c["kf"], c["vf"], c["hq"], c["hk"], c["D"], 1 / 16, kv_mode, c["pool"], c["kc"],
+                          c["vc"], sk, sv, own, rows, c["bt"], c["q_start_t"], c["seq_lens_t"], plan.work, po, pl,
+                          None, rpi)
+        return None
+
+    return run
+
+
+def kv_bytes(c, kv_mode: int) -> int:
+    D = c["D"]
+    per_page = fmt.page_head_bytes(D) + 512 if kv_mode == 0 else 2 * 128 * D * 2
+    return c["pages"] * c["hk"] * per_page
+
+
+def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16")):
+    c = build_case(hist, batch, qlen)
+    rows = qlen * c["hq"] // c["hk"]
+    vs = [v for v in variants if not (v == "int2_tc" and rows > 32)]
+    # numerics: merged outputs against the first variant
+    outs = {}
+    for v in vs:
+        outs[v] = _attention(c, 0 if v.startswith("int2") else 1, v == "int2_tc").float()
+    ref = outs[vs[0]]
+    errs = {v: float((outs[v] - ref).norm() / ref.norm()) for v in vs}
+    # the INT2 variants read the same cache and must agree; BF16 reads another cache
+    for v in vs:
+        if v.startswith("int2") and vs[0].startswith("int2"):
+            assert errs[v] < 1e-2, f"{v} disagrees with {vs[0]}: {errs[v]:.3e}"
+    fns = {v: _kernel_only(c, 0 if v.startswith("int2") else 1, v == "int2_tc") for v in vs}
+    tim = compare_calls(fns, iters=iters, flush=True)
+    peak = _peak_gbs()
+    res = []
+    for v in vs:
+        kvm = 0 if v.startswith("int2") else 1
+        by = kv_bytes(c, kvm)
+        us = tim[v].median_ms * 1e3
+        gbs = by / (us * 1e-6) / 1e9
+        res.append({"variant": v, "hist": hist, "batch": batch, "qlen": qlen, "us": round(us, 2),
+                    "kv_bytes": by, "gbs": round(gbs, 1), "frac_hbm_of_measured": round(gbs / peak, 3),
+                    "n_work": c["plan"].n_work, "rel_err_vs_first": round(errs[v], 5)})
+    A.USE_TC = os.environ.get("OSCAR_ATTN_TC", "1") != "0"
+    return res
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--hist", default="1024,8192,32768")
+    ap.add_argument("--batch", default="1,8,32")
+    ap.add_argument("--qlen", default="1,4")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--prefill", action="store_true", help="also run the 9256-over-15360 continuation")
+    args = ap.parse_args(argv)
+    torch.cuda.init()
+    for hist in map(int, args.hist.split(",")):
+        for batch in map(int, args.batch.split(",")):
+            for qlen in map(int, args.qlen.split(",")):
+                for r in run_case(hist, batch, qlen, args.iters):
+                    print(json.dumps(r), flush=True)
+    if args.prefill:
+        for r in run_case(15360, 1, 9256, max(3, args.iters // 3), variants=("int2_mma", "bf16")):
+            print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -119,6 +119,15 @@ class LLMEngine:
         self._graphs.clear()
         self._seen.clear()
 
+    def release(self, rid: int) -> None:
+        """Forget a finished request (its cache blocks and slot were freed when it finished)."""
+        r = self.requests.get(rid)
+        if r is None or not r.finished:
+            return
+        del self.requests[rid]
+        if rid in self.finished:
+            self.finished.remove(rid)
+
     def add_request(self, prompt, max_new_tokens: int) -> int:
         rid = next(self._ids)
         self.requests[rid] = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer())

@@ -161,6 +161,7 @@ class FullAttentionLayer:
         else:
             self.Rk = self.Rv = self.RvT = None
         self._split_rotations()
+        self.calib = None  # CalibrationCapture while calibrating rotations
         self.pool = self.kc = self.vc = None
         self.stage_k = self.stage_v = None
 
@@ -216,6 +217,9 @@ class FullAttentionLayer:
                    owner_seat=b.owner_seat if (staged and write_owner) else None,
                    owner_val=b.owner_val if (staged and write_owner) else None, status=status,
                    rk_split=self.rk_split, rv_split=self.rv_split)
+        if self.calib is not None:  # rotation calibration: unquantised q / k / v of this layer
+            self.calib.record(f"model.layers.{self.layer_id}.self_attn.attn", q_out, k_fr, v_fr, self.Hq, self.Hk,
+                              self.D)
         stage = (self.stage_k, self.stage_v, owner, stage_rows) if staged else None
         gate = qkv[:, self.D:]  # gate of head h at columns h * 2D + D ..
         _, oq, os_ = A.attention(q_out, k_fr, v_fr, Hq=self.Hq, Hk=self.Hk, D=self.D, scale=self.scale,

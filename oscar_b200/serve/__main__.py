@@ -1,0 +1,121 @@
+"""Serve CLI: ``python -m oscar_b200.serve`` (one process per GPU; torchrun for TP).
+
+    torchrun --nproc-per-node 4 --master-addr 127.0.0.1 -m oscar_b200.serve \\
+        --model qwen35-27b --port 8000
+
+Equivalent of the reference's serve script (``delivery/serve_oscar.sh:64-99``):
+TP over all ranks of the launch, 15,360 batched tokens per step, up to 128
+concurrent sequences, MTP with 3 draft tokens, OSCAR INT2 KV for the FULL layers
+(rotations from ``OSCAR_ASCEND_K_ROTATION_PATH`` / ``V_ROTATION_PATH`` when set, else
+seeded random orthogonal), the cache sized from free memory by the budget seam.
+Every rank prints its READY manifest; rank 0 serves HTTP, the others follow it in
+lockstep.  Weights are random (seeded) - this framework ships no checkpoint loader
+for the target model's real weights.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+
+def parse(argv=None):
+    ap = argparse.ArgumentParser(prog="python -m oscar_b200.serve")
+    ap.add_argument("--model", default="qwen35-27b")
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--max-num-seqs", type=int, default=128)
+    ap.add_argument("--max-batched-tokens", type=int,
+                    default=int(os.environ.get("OSCAR_ASCEND_BATCHED_TOKENS", "15360") or 15360))
+    ap.add_argument("--num-spec", type=int, default=3)
+    ap.add_argument("--kv", choices=["int2", "bf16"], default="int2")
+    ap.add_argument("--gpu-memory-utilization", type=float, default=0.9)
+    ap.add_argument("--num-blocks", type=int, default=None, help="fixed block count (testing)")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--tokenizer", default=None, help="local HF tokenizer directory (optional)")
+    ap.add_argument("--device", default=None, help="cpu runs the torch reference path (testing)")
+    return ap.parse_args(argv)
+
+
+def build(args):
+    from ..config import OscarConfig
+    from ..engine import budget as B
+    from ..engine.engine import LLMEngine
+    from ..models.config import CONFIGS
+    from ..models.qwen35 import HybridModel
+    from ..parallel.groups import init_distributed, make_groups
+
+    rank, world, local = init_distributed(backend="gloo" if args.device == "cpu" else None)
+    dev = torch.device(args.device) if args.device == "cpu" else torch.device("cuda", local)
+    if dev.type == "cuda":
+        torch.cuda.set_device(dev)
+    tp = make_groups(tp=world)
+    cfg = CONFIGS[args.model](**({} if args.layers is None else {"num_layers": args.layers}))
+    oscar = OscarConfig.from_env(head_dim=cfg.head_dim)
+    rot = "random"
+    if oscar.k_rotation_path:
+        rot = oscar.k_rotation_path
+    model = HybridModel(cfg, tp, device=dev, seed=args.seed, oscar=oscar, kv_mode=args.kv, rotation=rot)
+    if args.num_blocks is not None:
+        blocks, budget = args.num_blocks, None
+    else:
+        geo = B.geometry_of(model, max_slots=args.max_num_seqs)
+        avail = B.available_memory(dev, args.gpu_memory_utilization)
+        budget = B.memory_budget(avail, geo)
+        blocks = budget.blocks
+        if world > 1:  # every rank uses the smallest budget
+            t = torch.tensor([blocks], device=dev if dev.type == "cuda" else "cpu")
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            blocks = int(t.item())
+    eng = LLMEngine(model, num_blocks=blocks, max_slots=args.max_num_seqs,
+                    max_batched_tokens=args.max_batched_tokens, num_spec=args.num_spec)
+    B.verify_layers(cfg.full_layer_ids, [m.layer_id for m in model.full_layers])
+    man = B.ready_manifest(model, rank, world, budget)
+    print(man.line(), flush=True)
+    mans = [None] * world
+    if world > 1:
+        dist.all_gather_object(mans, json.loads(man.line().split("READY ", 1)[1]))
+        B.validate(mans, world_size=world)
+    else:
+        mans = [json.loads(man.line().split("READY ", 1)[1])]
+    return rank, world, model, eng, mans
+
+
+def main(argv=None) -> int:
+    args = parse(argv)
+    rank, world, model, eng, mans = build(args)
+    from .worker import ControlChannel, EngineWorker, follower_loop
+
+    control = ControlChannel.create(list(range(world))) if world > 1 else None
+    if rank != 0:
+        follower_loop(eng, control)
+        eng.close()
+        dist.destroy_process_group()
+        return 0
+    import uvicorn
+
+    from .server import create_app
+
+    tok = None
+    if args.tokenizer:
+        from transformers import AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(args.tokenizer, local_files_only=True)
+    worker = EngineWorker(eng, control).start()
+    app = create_app(worker, tok, mans, model_name=model.cfg.name, vocab_size=model.cfg.vocab_size)
+    try:
+        uvicorn.run(app, host=args.host, port=args.port, log_level="info")
+    finally:
+        worker.stop()
+        eng.close()
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

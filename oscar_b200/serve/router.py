@@ -1,0 +1,93 @@
+"""Data-parallel request router: one HTTP endpoint in front of several engine replicas.
+
+BASELINE config 5 runs DP2 x TP4 on 8 GPUs; the reference rejects DP != 1
+(``oscar_ascend/integration.py:75-76``).  Here every DP replica is an independent
+TP serve group (``python -m oscar_b200.serve`` on its own port) and this router
+forwards each completion to the replica with the least outstanding work: prompt +
+requested tokens of the requests it has sent there and not yet seen answered, ties
+broken by replica index (deterministic, so a replayed trace lands identically).
+
+    python -m oscar_b200.serve.router --backends http://127.0.0.1:8000,http://127.0.0.1:8001 --port 9000
+"""
+from __future__ import annotations
+
+import argparse
+import threading
+
+import httpx
+from fastapi import FastAPI, HTTPException, Request
+
+
+class DPRouter:
+    """Least-outstanding-tokens assignment over ``n`` replicas."""
+
+    def __init__(self, n: int):
+        if n < 1:
+            raise ValueError("need at least one replica")
+        self.load = [0] * n
+        self.sent = [0] * n
+        self._lock = threading.Lock()
+
+    def acquire(self, cost: int) -> int:
+        with self._lock:
+            i = min(range(len(self.load)), key=lambda j: (self.load[j], j))
+            self.load[i] += cost
+            self.sent[i] += 1
+            return i
+
+    def release(self, i: int, cost: int) -> None:
+        with self._lock:
+            self.load[i] -= cost
+
+
+def request_cost(body: dict) -> int:
+    p = body.get("prompt", [])
+    n = len(p) if isinstance(p, list) else len(str(p).encode())
+    return n + int(body.get("max_tokens", 16))
+
+
+def create_router_app(backends: list[str], transport: httpx.AsyncBaseTransport | None = None,
+                      timeout_s: float = 3600.0) -> FastAPI:
+    app = FastAPI(title="oscar-b200 router")
+    router = DPRouter(len(backends))
+    client = httpx.AsyncClient(transport=transport, timeout=timeout_s)
+
+    @app.get("/health")
+    async def health():
+        return {"ok": True, "replicas": len(backends), "load": router.load, "sent": router.sent}
+
+    @app.post("/v1/completions")
+    async def completions(req: Request):
+        body = await req.json()
+        cost = request_cost(body)
+        i = router.acquire(cost)
+        try:
+            r = await client.post(backends[i].rstrip("/") + "/v1/completions", json=body)
+        except httpx.HTTPError as e:
+            raise HTTPException(502, f"replica {i} unreachable: {e!r}") from e
+        finally:
+            router.release(i, cost)
+        if r.status_code != 200:
+            raise HTTPException(r.status_code, r.text)
+        out = r.json()
+        out["replica"] = i
+        return out
+
+    app.state.router = router
+    return app
+
+
+def main(argv=None) -> int:
+    import uvicorn
+
+    ap = argparse.ArgumentParser(prog="python -m oscar_b200.serve.router")
+    ap.add_argument("--backends", required=True)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=9000)
+    args = ap.parse_args(argv)
+    uvicorn.run(create_router_app(args.backends.split(",")), host=args.host, port=args.port)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -3,9 +3,12 @@
 Produces ``oscar_b200/_C*.so``.  Every CUDA source is compiled for
 ``compute_100a``/``sm_100a`` only; there is no other architecture.
 """
+import json
 import os
+import subprocess
 from pathlib import Path
 
+import torch
 from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
@@ -24,6 +27,24 @@ sources = ["csrc/bindings.cpp"] + sorted(str(p.relative_to(ROOT)) for p in CSRC.
 
 os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 4))
 
+
+def _nvcc_version() -> str:
+    try:
+        out = subprocess.run(["nvcc", "--version"], capture_output=True, text=True).stdout
+        return out.strip().splitlines()[-1]
+    except OSError:
+        return "unknown"
+
+
+class Build(BuildExtension.with_options(use_ninja=True)):
+    """Also records what the extension was built against (read by the runtime guard)."""
+
+    def run(self):
+        super().run()
+        meta = {"torch": torch.__version__, "cuda": torch.version.cuda, "nvcc": _nvcc_version(),
+                "nvcc_flags": NVCC_FLAGS, "sources": sources}
+        (ROOT / "oscar_b200" / "_C_build.json").write_text(json.dumps(meta, indent=1))
+
 setup(
     name="oscar_b200",
     version="0.1.0",
@@ -36,5 +57,5 @@ setup(
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
         )
     ],
-    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    cmdclass={"build_ext": Build},
 )
