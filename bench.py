@@ -50,9 +50,22 @@ def parse():
 
 
 def reference_arm(args):
-    msg = ("reference is a vLLM-Ascend plugin (oscar-ascend 0.2.0) that hard-requires torch_npu and "
-           "vllm_ascend on Ascend NPUs; it has no CUDA serving path to run on B200")
-    print(json.dumps({"impl": "reference", "unavailable": msg, "metric": METRIC, "n_gpus": args.gpus}))
+    """The reference is installed unmodified in baseline/_ref (pip --no-deps; its
+    declared dependencies vllm==0.23.0 and vllm-ascend are not in the offline
+    wheelhouse).  Its only public entry point is the vLLM general plugin
+    ``oscar_ascend.plugin:load_plugin``, which forces the Ascend NPU platform and
+    imports vllm_ascend / torch_npu on the serving path; none of that exists for CUDA,
+    so the reference's own stock path cannot produce this metric on a B200."""
+    import importlib.util
+    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    missing = [m for m in ("vllm_ascend", "torch_npu") if importlib.util.find_spec(m) is None]
+    if not os.path.isdir(os.path.join(ref, "oscar_ascend")):
+        why = "reference not installed in baseline/_ref (offline pip install failed)"
+    else:
+        why = ("reference (oscar-ascend 0.2.0, installed in baseline/_ref) is a vLLM-Ascend plugin whose serving "
+               f"path needs {', '.join(missing) or 'an Ascend NPU'} on Ascend NPUs; it has no CUDA path to run on B200")
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why, "metric": METRIC, "n_gpus": args.gpus}))
     return 0
 
 
@@ -103,9 +116,14 @@ def main():
     tp0 = time.perf_counter()
     for r in eng.requests.values():
         r.arrival = tp0
+    prof_prefill = os.environ.get("OSCAR_PROFILE_RANGE") == "prefill"
+    if prof_prefill:
+        torch.cuda.cudart().cudaProfilerStart()
     while any(not eng.requests[i].output for i in ids):
         eng.step()
     barrier_sync()
+    if prof_prefill:
+        torch.cuda.cudart().cudaProfilerStop()
     t_prefill = time.perf_counter() - tp0
     ttft = [eng.requests[i].first_token_time - eng.requests[i].arrival for i in ids]
 

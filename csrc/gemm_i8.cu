@@ -216,18 +216,6 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             v.w = pack_bf16x2((float)(int)r[j + 6] * sa * ep.scale_b[nb + j + 6], (float)(int)r[j + 7] * sa * ep.scale_b[nb + j + 7]);
             *reinterpret_cast<uint4*>(o + j) = v;
           }
-        } else if (ep.mode == 3 && splits == 1 && !ep.trans && nb + 32 <= N && (ep.ldo % 4) == 0) {
-          // prefill-shaped tile: 16-byte in-switch reductions along the row
-          float* o = reinterpret_cast<float*>(ep.out) + (long long)m * ep.ldo + nb;
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(o + j),
-                         "f"((float)(int)r[j + 0] * sa * ep.scale_b[nb + j + 0]),
-                         "f"((float)(int)r[j + 1] * sa * ep.scale_b[nb + j + 1]),
-                         "f"((float)(int)r[j + 2] * sa * ep.scale_b[nb + j + 2]),
-                         "f"((float)(int)r[j + 3] * sa * ep.scale_b[nb + j + 3])
-                         : "memory");
-          }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -240,15 +228,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             } else if (ep.mode == 1) {
               atomicAdd(reinterpret_cast<float*>(ep.out) + idx, v);
             } else if (ep.mode == 3) {
-              if (splits > 1) {
-                atomicAdd(ep.ws + idx, v);  // split-K partial: local workspace first
-              } else {
-                // in-switch reduction: adds v into this element of every rank's buffer
-                asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(
-                                 reinterpret_cast<float*>(ep.out) + idx),
-                             "f"(v)
-                             : "memory");
-              }
+              // stage in the local workspace; the reduction through the switch is issued
+              // below with 16-byte transactions
+              if (splits > 1)
+                atomicAdd(ep.ws + idx, v);
+              else
+                ep.ws[idx] = v;
             } else {
               reinterpret_cast<float*>(ep.out)[idx] = v;
             }
@@ -258,34 +243,71 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&acc_empty[acc]);
-      if (ep.mode == 3 && splits > 1) {
-        // Split-K fix-up, per (tile, row quarter): every split adds its partial rows
-        // into the local workspace and counts itself in; the last one reads the sums
-        // back from L2, reduces them into every rank through the switch and clears
-        // the workspace for the next call.  NVLink then carries each element once.
+      if (ep.mode == 3) {
+        // The rows of this (tile, row quarter) are complete in the workspace once every
+        // split has added its part (split-K: counted in tile_cnt; else this warp alone).
+        // The last contributor reads them back from L2 and reduces them into every rank
+        // through the switch, 16 bytes per multimem.red, then clears the workspace.
+        bool last = true;
         __threadfence();
         __syncwarp();
         const int slot = (t / splits) * 4 + quarter;
-        int prev = 0;
-        if (lane == 0) prev = atomicAdd(ep.tile_cnt + slot, 1);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == splits - 1) {
-          __threadfence();
-          if (row_ok) {
-            for (int j = 0; j < BN; ++j) {
+        if (splits > 1) {
+          int prev = 0;
+          if (lane == 0) prev = atomicAdd(ep.tile_cnt + slot, 1);
+          prev = __shfl_sync(0xffffffffu, prev, 0);
+          last = prev == splits - 1;
+          if (last) __threadfence();
+        }
+        if (last) {
+          float* out = reinterpret_cast<float*>(ep.out);
+          const int mq = m0 + quarter * 32;  // first row of this warp
+          if (ep.trans) {
+            // element (m, n) at n * ldo + m: lanes cover 8 x 4 consecutive rows of 4 columns
+            const int m4 = mq + 4 * (lane & 7);
+            for (int jj = lane >> 3; jj < BN; jj += 4) {
+              const int n = n0 + jj;
+              if (n >= N) break;
+              const long long base = (long long)n * ep.ldo + m4;
+              if (m4 + 3 < M) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(ep.ws + base));
+                asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(out + base),
+                             "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                             : "memory");
+                *reinterpret_cast<float4*>(ep.ws + base) = make_float4(0.f, 0.f, 0.f, 0.f);
+              } else {
+                for (int e = 0; e < 4 && m4 + e < M; ++e) {
+                  const float v = __ldcg(ep.ws + base + e);
+                  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(out + base + e), "f"(v)
+                               : "memory");
+                  ep.ws[base + e] = 0.f;
+                }
+              }
+            }
+          } else if (row_ok) {
+            // element (m, n) at m * ldo + n: each thread owns a row
+            for (int j = 0; j < BN; j += 4) {
               const int n = n0 + j;
               if (n >= N) break;
-              const long long idx = ep.trans ? (long long)n * ep.ldo + m : (long long)m * ep.ldo + n;
-              const float v = __ldcg(ep.ws + idx);
-              asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(
-                               reinterpret_cast<float*>(ep.out) + idx),
-                           "f"(v)
-                           : "memory");
-              ep.ws[idx] = 0.f;
+              const long long base = (long long)m * ep.ldo + n;
+              if (n + 3 < N) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(ep.ws + base));
+                asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(out + base),
+                             "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                             : "memory");
+                *reinterpret_cast<float4*>(ep.ws + base) = make_float4(0.f, 0.f, 0.f, 0.f);
+              } else {
+                for (int e = 0; n + e < N; ++e) {
+                  const float v = __ldcg(ep.ws + base + e);
+                  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(out + base + e), "f"(v)
+                               : "memory");
+                  ep.ws[base + e] = 0.f;
+                }
+              }
             }
           }
           __syncwarp();
-          if (lane == 0) ep.tile_cnt[slot] = 0;
+          if (splits > 1 && lane == 0) ep.tile_cnt[slot] = 0;
         }
       }
     }
@@ -434,7 +456,9 @@ extern "C" int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, lon
   if (splits < 1) splits = 1;
   if (splits > 1 && mode != 1 && mode != 3) return -104;  // split-K partial sums must be accumulated
   if (mode == 3 && (!done_counter || !epoch || !peer_signals || world < 1)) return -106;
-  if (mode == 3 && splits > 1 && (!ws || !tile_cnt)) return -107;
+  if (mode == 3 && (!ws || !tile_cnt)) return -107;
+  if (mode == 3 && (ldo % 4 || (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(ws) & 15)))
+    return -108;  // 16-byte reductions need 16-byte aligned rows
   CUtensorMap ta, tb;
   int rc = make_map(&ta, A, M, K, lda, BM);
   if (rc) return rc;

@@ -26,6 +26,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from ..kv.offload import HostKVStore
 from ..models.qwen35 import HybridModel, StepBatch
 from ..ops import attention as A
 from ..ops.functional import num_sms
@@ -75,7 +76,7 @@ class SeededAcceptance:
 class LLMEngine:
     def __init__(self, model: HybridModel, num_blocks: int, max_slots: int, max_batched_tokens: int = 15360,
                  num_spec: int = 3, acceptance: SeededAcceptance | None = None, prefill_policy: str = "fcfs",
-                 timer=time.perf_counter):
+                 timer=time.perf_counter, offload: bool = False):
         self.model = model
         self.dev = model.device
         self.num_spec = num_spec if model.mtp is not None else 0
@@ -109,6 +110,9 @@ class LLMEngine:
         self.g = model.full_layers[0].Hq // model.full_layers[0].Hk if model.full_layers else 1
         self.Hk = model.full_layers[0].Hk if model.full_layers else 1
         self.sms = num_sms(self.dev) if self.dev.type == "cuda" else 148
+        # preemption by swapping to pinned host memory (off: requests wait for blocks)
+        self.offload = HostKVStore(model) if offload else None
+        self.swapped_q: list[int] = []
 
     # ------------------------------------------------------------------ API
     def close(self) -> None:
@@ -135,7 +139,48 @@ class LLMEngine:
         return rid
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self.swapped_q)
+
+    # ------------------------------------------------------------------ preemption
+    def _swap_out(self, rid: int) -> None:
+        r = self.requests[rid]
+        off = self.offload
+        sw = off.swap_out(rid, list(self.bm.table(rid)), r.slot, self.slots.parity[r.slot],
+                          on_freed=lambda: (self.bm.free(rid), self.slots.release(rid)))
+        if sw.owner_cleared is not None and len(sw.owner_cleared):
+            self._owner_host[sw.owner_cleared] = -1
+        off.drain()  # blocks and slot are reusable in this very step
+        r.slot = -1
+        self.running.remove(rid)
+        self.swapped_q.append(rid)
+        self.stats["preempted"] = self.stats.get("preempted", 0) + 1
+
+    def _swap_in_ready(self) -> None:
+        while self.swapped_q:
+            rid = self.swapped_q[0]
+            n = self.offload.swapped[rid].n_blocks
+            if n > self.bm.free_blocks or not self.slots.free_slots:
+                return
+            self.swapped_q.pop(0)
+            blocks = self.bm.ensure(rid, n * self.bm.page)
+            r = self.requests[rid]
+            r.slot = self.slots.acquire(rid)
+            parity, seats, tags = self.offload.swap_in(rid, list(blocks), r.slot)
+            self.slots.parity[r.slot] = parity
+            if seats is not None:
+                self._owner_host[seats] = tags
+            self.running.append(rid)
+
+    def _preempt_for(self, rid: int, tokens: int, scheduled: set) -> bool:
+        """Swap out the newest running requests not in this step until ``rid`` fits."""
+        if self.offload is None:
+            return False
+        while not self.bm.can_allocate(rid, tokens):
+            victims = [v for v in reversed(self.running) if v != rid and v not in scheduled]
+            if not victims:
+                return False
+            self._swap_out(victims[0])
+        return True
 
     def generate(self, prompts, max_new_tokens: int) -> list[list[int]]:
         ids = [self.add_request(p, max_new_tokens) for p in prompts]
@@ -148,16 +193,24 @@ class LLMEngine:
         """Returns a list of (rid, kind, n_tokens) with kind in {"verify", "prefill"}."""
         sched = []
         budget = self.max_batched_tokens
-        for rid in self.running:
+        if self.offload is not None:
+            self.offload.poll()
+            self._swap_in_ready()
+        scheduled: set = set()
+        for rid in list(self.running):
+            if rid not in self.running:  # swapped out for an earlier request of this step
+                continue
             r = self.requests[rid]
             if not r.prefill_done:
                 continue
             n = 1 + len(r.drafts)
             extra = 2 * self.num_spec + 2
-            if not self.bm.can_allocate(rid, r.num_computed + n + extra):
-                continue  # no space this step (preemption is not needed for fixed-size batches)
+            if not self.bm.can_allocate(rid, r.num_computed + n + extra) and not self._preempt_for(
+                    rid, r.num_computed + n + extra, scheduled):
+                continue  # no space this step and nothing to preempt
             self.bm.ensure(rid, r.num_computed + n + extra)
             sched.append((rid, "verify", n))
+            scheduled.add(rid)
             budget -= n
         candidates = [rid for rid in self.running if not self.requests[rid].prefill_done] + list(self.waiting)
         if self.prefill_policy == "wide" and candidates:

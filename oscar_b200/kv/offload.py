@@ -1,0 +1,249 @@
+"""Host KV offload: swap a request's cache out to pinned host memory and back.
+
+The reference does not offload KV (``README.md:111``); BASELINE config 5 asks for host
+offload of cold INT2 pages.  At the target shapes the INT2 cache of every running
+request fits in HBM, so offload serves preemption: when the block pool runs dry the
+scheduler swaps the most recently admitted request out - every FULL layer's INT2 pages,
+the MTP layer's BF16 shadow pages, the request's staged sink/recent values and its GDN
+recurrent state - frees its blocks and slot, and swaps it back in (new physical blocks,
+new slot) when room returns.  Outputs are identical to an uninterrupted run.
+
+The request's pages are gathered (``index_select``) on the compute stream, and the
+copies to pinned host memory run on a side stream; the blocks return to the free list
+once the copies' event has completed (:meth:`HostKVStore.poll` / ``drain``).  Swap-in
+copies host -> device on the side stream, the compute stream waits on its event and
+scatters the pages into the new blocks.  Staging owner tags change with the blocks, so
+both directions report the tag updates for the engine's host mirror of the table.  On
+the CPU reference path the same code runs without streams.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+PAGE = 128
+
+
+@dataclass
+class Swapped:
+    """Host copy of one request's device state."""
+
+    rid: int
+    n_blocks: int
+    pages: list            # per FULL layer: [n_blocks, Hk, page_bytes] uint8 (host)
+    shadow: tuple | None   # MTP layer (kc, vc): [n_blocks, 128, Hk, D] bf16 (host)
+    staged_mask: torch.Tensor | None   # [n_blocks, 128] bool: seat held this block's token
+    staged: list           # per FULL layer: (k, v) [n_staged, Hk, D] fp32 (host)
+    gdn: list              # per GDN layer: tuple of host tensors
+    parity: int = 0
+    event: object = None   # completion of the device->host copies
+    nbytes: int = 0
+    owner_cleared: object = None  # staging seats whose tags were reset (numpy)
+
+
+@dataclass
+class OffloadStats:
+    swapped_out: int = 0
+    swapped_in: int = 0
+    bytes_out: int = 0
+    bytes_in: int = 0
+    host_bytes_peak: int = 0
+    _host_now: int = 0
+
+
+class HostKVStore:
+    def __init__(self, model, pin: bool | None = None):
+        self.model = model
+        dev = model.device
+        self.cuda = dev.type == "cuda"
+        self.pin = self.cuda if pin is None else pin
+        self.stream = torch.cuda.Stream(device=dev) if self.cuda else None
+        self.swapped: dict[int, Swapped] = {}
+        self.stats = OffloadStats()
+        self._pending_free: list = []  # (event, callback)
+
+    # ------------------------------------------------------------ helpers
+    def _to_host(self, dev_tensors: list) -> list:
+        """Device temporaries -> pinned host copies on the side stream."""
+        if not self.cuda:
+            return [t.clone() for t in dev_tensors]
+        main = torch.cuda.current_stream(self.model.device)
+        self.stream.wait_stream(main)
+        out = []
+        with torch.cuda.stream(self.stream):
+            for t in dev_tensors:
+                h = torch.empty(t.shape, dtype=t.dtype, pin_memory=self.pin)
+                h.copy_(t, non_blocking=True)
+                t.record_stream(self.stream)
+                out.append(h)
+        return out
+
+    def _to_device(self, host_tensors: list) -> list:
+        if not self.cuda:
+            return list(host_tensors)
+        dev = self.model.device
+        out = []
+        with torch.cuda.stream(self.stream):
+            for h in host_tensors:
+                out.append(h.to(dev, non_blocking=True))
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        main = torch.cuda.current_stream(dev)
+        main.wait_event(ev)
+        for t in out:
+            t.record_stream(main)
+        ev.synchronize()  # the pinned sources may be released after this
+        return out
+
+    def poll(self) -> None:
+        """Run the deferred frees whose device->host copies have completed."""
+        keep = []
+        for ev, cb in self._pending_free:
+            if ev is None or ev.query():
+                cb()
+            else:
+                keep.append((ev, cb))
+        self._pending_free = keep
+
+    def drain(self) -> None:
+        for ev, cb in self._pending_free:
+            if ev is not None:
+                ev.synchronize()
+            cb()
+        self._pending_free = []
+
+    # ------------------------------------------------------------ layout
+    def _gdn_views(self, g):
+        return ((g.state, 0), (g.conv_state, 1), (g.pend_x, 1), (g.pend_ba, 0))
+
+    # ------------------------------------------------------------ swap out
+    def swap_out(self, rid: int, blocks: list[int], slot: int, parity: int, on_freed) -> Swapped:
+        """Gather on the compute stream, copy to host on the side stream; ``on_freed`` runs
+        (from :meth:`poll`) once the copies are done and the blocks may be reused."""
+        m = self.model
+        dev = m.device
+        idx = torch.tensor(blocks, dtype=torch.long, device=dev)
+        dev_t, kinds = [], []
+        for layer in m.full_layers:
+            if layer.pool is not None:
+                dev_t.append(layer.pool.index_select(0, idx))
+                kinds.append(("pool", 1))
+            else:
+                dev_t += [layer.kc.index_select(0, idx), layer.vc.index_select(0, idx)]
+                kinds.append(("bf16", 2))
+        n_shadow = 0
+        if getattr(m, "mtp", None) is not None and m.mtp.layer.kc is not None:
+            L = m.mtp.layer
+            dev_t += [L.kc.index_select(0, idx), L.vc.index_select(0, idx)]
+            n_shadow = 2
+        maskd = None
+        n_staged = 0
+        owner_cleared = None
+        if m.stage_rows:
+            rows = m.stage_rows
+            seats = ((idx % rows) * PAGE).unsqueeze(1) + torch.arange(PAGE, device=dev)  # [nb, 128]
+            own = m.owner[seats.view(-1)].view(len(blocks), PAGE)
+            maskd = own == idx.unsqueeze(1).to(own.dtype)
+            sel = seats[maskd]
+            for layer in m.full_layers:
+                if layer.stage_k is not None:
+                    dev_t += [layer.stage_k.index_select(0, sel), layer.stage_v.index_select(0, sel)]
+                    n_staged += 1
+            m.owner[sel] = -1  # these seats stop belonging to blocks that are about to be reused
+            dev_t.append(maskd)
+            owner_cleared = sel
+        s = torch.tensor([slot], dtype=torch.long, device=dev)
+        for g in m.gdn_layers:
+            dev_t += [t.index_select(dim, s) for t, dim in self._gdn_views(g)]
+        host = self._to_host(dev_t)
+        ev = None
+        if self.cuda:
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        # unpack
+        it = iter(host)
+        pages = [next(it) if k == "pool" else (next(it), next(it)) for k, _ in kinds]
+        shadow = (next(it), next(it)) if n_shadow else None
+        staged = [(next(it), next(it)) for _ in range(n_staged)]
+        mask = next(it) if maskd is not None else None
+        gdn = [tuple(next(it) for _ in range(4)) for _ in m.gdn_layers]
+        nbytes = sum(t.numel() * t.element_size() for t in host)
+        sw = Swapped(rid, len(blocks), pages, shadow, mask, staged, gdn, parity, ev, nbytes)
+        sw.owner_cleared = owner_cleared.cpu().numpy() if owner_cleared is not None else None
+        self.swapped[rid] = sw
+        self._pending_free.append((ev, on_freed))
+        st = self.stats
+        st.swapped_out += 1
+        st.bytes_out += nbytes
+        st._host_now += nbytes
+        st.host_bytes_peak = max(st.host_bytes_peak, st._host_now)
+        return sw
+
+    # ------------------------------------------------------------ swap in
+    def swap_in(self, rid: int, blocks: list[int], slot: int):
+        """Restore ``rid`` into new ``blocks`` / ``slot``.  Returns ``(parity, seats, tags)``:
+        the saved slot parity and the staging owner-tag updates (numpy, or None)."""
+        m = self.model
+        sw = self.swapped.pop(rid)
+        if sw.event is not None:
+            sw.event.synchronize()  # the host copy is complete before it is read back
+        dev = m.device
+        assert len(blocks) == sw.n_blocks
+        idx = torch.tensor(blocks, dtype=torch.long, device=dev)
+        flat = list(_tensors(sw.pages, sw.shadow, sw.staged, []))
+        if sw.staged_mask is not None:
+            flat.append(sw.staged_mask)
+        for g in sw.gdn:
+            flat += list(g)
+        d = iter(self._to_device(flat))
+        for layer, hp in zip(m.full_layers, sw.pages):
+            if layer.pool is not None:
+                layer.pool.index_copy_(0, idx, next(d))
+            else:
+                layer.kc.index_copy_(0, idx, next(d))
+                layer.vc.index_copy_(0, idx, next(d))
+        if sw.shadow is not None:
+            L = m.mtp.layer
+            L.kc.index_copy_(0, idx, next(d))
+            L.vc.index_copy_(0, idx, next(d))
+        staged = [(next(d), next(d)) for _ in sw.staged]
+        owner_upd = (None, None)
+        if sw.staged_mask is not None:
+            maskd = next(d)
+            rows = m.stage_rows
+            seats = ((idx % rows) * PAGE).unsqueeze(1) + torch.arange(PAGE, device=dev)
+            # no stale tag may claim the new blocks; restored tokens get their tags back
+            tags = torch.where(maskd, idx.unsqueeze(1), torch.full_like(seats, -1)).view(-1).to(m.owner.dtype)
+            m.owner[seats.view(-1)] = tags
+            owner_upd = (seats.view(-1).cpu().numpy(), tags.cpu().numpy())
+            sel = seats[maskd]
+            it = iter(staged)
+            for layer in m.full_layers:
+                if layer.stage_k is not None:
+                    k, v = next(it)
+                    layer.stage_k.index_copy_(0, sel, k)
+                    layer.stage_v.index_copy_(0, sel, v)
+        s = torch.tensor([slot], dtype=torch.long, device=dev)
+        for g in m.gdn_layers:
+            for t, dim in self._gdn_views(g):
+                t.index_copy_(dim, s, next(d))
+        st = self.stats
+        st.swapped_in += 1
+        st.bytes_in += sw.nbytes
+        st._host_now -= sw.nbytes
+        return sw.parity, owner_upd[0], owner_upd[1]
+
+
+def _tensors(pages, shadow, staged, gdn):
+    for p in pages:
+        if isinstance(p, tuple):
+            yield from p
+        else:
+            yield p
+    if shadow is not None:
+        yield from shadow
+    for kv in staged:
+        yield from kv
+    for g in gdn:
+        yield from g
