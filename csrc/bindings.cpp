@@ -22,7 +22,8 @@ int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi
 int oscar_gdn_step(const oscar::GdnParams* p, int smem_state, cudaStream_t stream);
 int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long long ldd, const float* w, float off, float eps,
                         int T, int H, int8_t* out, float* scale, __nv_bfloat16* out_bf16, const unsigned* signals,
-                        const int* epoch, int world, int zero_delta, int* status, cudaStream_t s);
+                        const int* epoch, int world, int zero_delta, int* status, long long wait_budget_ns,
+                        cudaStream_t s);
 int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                      const float* scale_a, const float* scale_b, void* out, long long ldo, int mode, int trans, int bn,
                      int splits, int* status, int* done_counter, int* epoch, unsigned** peer_signals, int rank,
@@ -364,7 +365,7 @@ void gdn_step(const Tensor& qkvz, const Tensor& ba, int64_t Hk, int64_t Hv, int6
 void rmsnorm_quant(Tensor& x, const optional<Tensor>& delta, const Tensor& w, double off, double eps,
                    const optional<Tensor>& out, const optional<Tensor>& scale, const optional<Tensor>& out_bf16,
                    int64_t signals_ptr, const optional<Tensor>& epoch, int64_t world, int64_t zero_delta,
-                   const optional<Tensor>& status) {
+                   const optional<Tensor>& status, int64_t wait_budget_ns) {
   CHECK_DTYPE(x, at::kFloat);
   CHECK_DTYPE(w, at::kFloat);
   TORCH_CHECK(x.stride(1) == 1, "rmsnorm_quant: rows must be contiguous");
@@ -374,7 +375,8 @@ void rmsnorm_quant(Tensor& x, const optional<Tensor>& delta, const Tensor& w, do
   check_rc(oscar_rmsnorm_quant(ptr<float>(x), x.stride(0), optr_view<float>(delta), has_d ? delta->stride(0) : 0,
                                ptr<float>(w), off, eps, x.size(0), x.size(1), optr<int8_t>(out), optr<float>(scale),
                                optr<__nv_bfloat16>(out_bf16), reinterpret_cast<const unsigned*>(signals_ptr),
-                               optr<int>(epoch), (int)world, (int)zero_delta, optr<int>(status), stream()),
+                               optr<int>(epoch), (int)world, (int)zero_delta, optr<int>(status),
+                               (long long)wait_budget_ns, stream()),
            "rmsnorm_quant");
 }
 

@@ -51,6 +51,7 @@ struct RankWait {
   const int* epoch;         // local epoch counter, bumped by the producing GEMM
   int world;
   int* status;
+  uint64_t budget_ns;  // give up (status kTimeoutPeerFlag) after this long
 };
 
 OSCAR_DEVICE void wait_ranks(const RankWait& rw) {
@@ -62,7 +63,7 @@ OSCAR_DEVICE void wait_ranks(const RankWait& rw) {
       unsigned v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(rw.signals + q) : "memory");
       if ((int)(v - e) >= 0) break;
-      if (globaltimer_ns() - t0 > 5000000000ull) {  // 5 s: report instead of hanging
+      if (globaltimer_ns() - t0 > rw.budget_ns) {  // report instead of hanging
         record_status(rw.status, kTimeoutPeerFlag);
         return;
       }
@@ -285,11 +286,11 @@ using namespace oscar;
 extern "C" int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long long ldd, const float* w,
                                    float off, float eps, int T, int H, int8_t* out, float* scale,
                                    __nv_bfloat16* out_bf16, const unsigned* signals, const int* epoch, int world,
-                                   int zero_delta, int* status, cudaStream_t s) {
+                                   int zero_delta, int* status, long long wait_budget_ns, cudaStream_t s) {
   if (T <= 0) return 0;
   if (H % 4 || ldx % 4 || (delta && ldd % 4)) return -401;
   constexpr int NT = 256;
-  RankWait rw{signals, epoch, world, status};
+  RankWait rw{signals, epoch, world, status, (uint64_t)(wait_budget_ns > 0 ? wait_budget_ns : 5000000000ll)};
   OSCAR_PV_DISPATCH(H / 4, NT, (rmsnorm_quant_kernel<NT, PV><<<T, NT, 0, s>>>(x, ldx, delta, ldd, w, off, eps, H, out, scale, out_bf16, rw, zero_delta)));
   return (int)cudaGetLastError();
 }

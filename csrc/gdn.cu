@@ -355,6 +355,365 @@ __global__ void __launch_bounds__(kThreads) gdn_chunk_kernel(GdnParams p) {
   if (!conv_saved) save_conv();
 }
 
+// ---------------------------------------------------------------------------
+// Decode / MTP-verify variant (<= 8 tokens per request and value head, 4 warps).
+// Same algebra as above with the two products on the tensor cores:
+//   pass 1:  [k_1..k_8 ; q_1..q_8] (16 x dk) . S0 (dk x dv)   -> S0^T k_t, S0^T q_t
+//   pass 2:  S_w = G_w S0 + [k_1..k_8] (dk x 8) . C (8 x dv),  C_s = (G_w / G_s) d_s
+// (mma.sync m16n8k16, bf16 in, fp32 accumulate).  The state lives in shared memory
+// as bf16 in an XOR-swizzled layout and crosses global memory once each way with
+// 16-byte accesses; thread j owns value column j for the per-column recurrence.
+constexpr int kDecC = 8;
+constexpr int kDecThreads = 128;
+
+OSCAR_DEVICE uint32_t sw16(int row, int chunk) {  // [row][128 bf16]: 16 chunks of 16 B per row
+  return (uint32_t)(row * 256 + ((chunk ^ (row & 7)) << 4));
+}
+OSCAR_DEVICE void ldsm4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+OSCAR_DEVICE void ldsm4t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+OSCAR_DEVICE void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                 uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
+  __shared__ __align__(128) uint8_t sS[kD * 256];   // state, bf16 [dk][dv] swizzled
+  __shared__ __align__(128) uint8_t sA[16 * 256];   // rows 0-7: k_t, 8-15: q_t (bf16 [tok][dk])
+  // one region, three lives: normalised k/q columns (fp32) -> pass-1 result -> pass-2 B operand
+  __shared__ __align__(128) uint8_t sU[2 * kD * (kDecC + 1) * 4];
+  float (*kT)[kDecC + 1] = reinterpret_cast<float (*)[kDecC + 1]>(sU);
+  float (*qT)[kDecC + 1] = reinterpret_cast<float (*)[kDecC + 1]>(sU + kD * (kDecC + 1) * 4);
+  float (*kvq)[kD] = reinterpret_cast<float (*)[kD]>(sU);  // rows t: S^T k_t, 8 + t: S^T q_t
+  uint8_t* sC = sU;                                        // rows 0-7: C_s (bf16 [s][dv]), 8-15 zero
+  __shared__ float KK[kDecC][kDecC], KQ[kDecC][kDecC];
+  __shared__ float Lg[kDecC], Bt[kDecC];
+  __shared__ float red[kDecC][2][4];
+  __shared__ float pb_b[16], pb_a[16];
+
+  const int req = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int j = tid;
+  const int t0 = p.q_start[req], T = p.q_start[req + 1] - t0;
+  const int a = p.n_commit[req];
+  const int n = a + T;
+  if (n <= 0) return;
+  const bool keep = p.keep_pending[req] != 0;
+  const int w_last = keep ? a - 1 : n - 1;  // last token included in the stored state
+  const int slot = p.req_slot[req];
+  const int r = p.Hv / p.Hk;
+  const int gk = h / r, hh = h % r;
+  const int Kd = p.Hk * p.dk;
+  const int conv_dim = 2 * Kd + p.Hv * p.dv;
+  const int cq = gk * p.dk + j, ck = Kd + gk * p.dk + j, cv = 2 * Kd + h * p.dv + j;
+  const long long grp = (long long)gk * (2 * p.dk + 2 * r * p.dv);
+  const int par = p.parity[req];
+  const __nv_bfloat16* cs = p.conv_state + ((long long)par * p.slots + slot) * conv_dim * 3;
+  __nv_bfloat16* cs_out = p.conv_state + ((long long)(1 - par) * p.slots + slot) * conv_dim * 3;
+  const __nv_bfloat16* px = p.pend_x + ((long long)par * p.slots + slot) * p.P * conv_dim;
+  __nv_bfloat16* px_out = p.pend_x + ((long long)(1 - par) * p.slots + slot) * p.P * conv_dim;
+  __nv_bfloat16* pb = p.pend_ba + (long long)slot * p.P * 2 * p.Hv;
+  __nv_bfloat16* st = p.state + ((long long)slot * p.Hv + h) * p.dk * p.dv;
+  if (n > kDecC || a > p.P || (keep && T > p.P)) {
+    if (tid == 0) record_status(p.status, kBadShape);
+    return;
+  }
+  const uint32_t sS_a = smem_u32(sS), sA_a = smem_u32(sA), sC_a = smem_u32(sC);
+
+  // state -> shared memory (16-byte loads, swizzled chunks)
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(st);
+#pragma unroll 4
+    for (int v = tid; v < kD * 16; v += kDecThreads) {
+      const int row = v >> 4, ch = v & 15;
+      *reinterpret_cast<uint4*>(sS + sw16(row, ch)) = __ldg(src + v);
+    }
+  }
+  if (tid < a) {
+    pb_b[tid] = __bfloat162float(pb[tid * 2 * p.Hv + h]);
+    pb_a[tid] = __bfloat162float(pb[tid * 2 * p.Hv + p.Hv + h]);
+  }
+  __syncthreads();
+
+  // ---- conv + SiLU of channel j for every token ----
+  float wq[3], wk[3], wv[3], cwq[4], cwk[4], cwv[4];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    wq[i] = __bfloat162float(cs[cq * 3 + i]);
+    wk[i] = __bfloat162float(cs[ck * 3 + i]);
+    wv[i] = __bfloat162float(cs[cv * 3 + i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    cwq[i] = p.conv_w[cq * 4 + i];
+    cwk[i] = p.conv_w[ck * 4 + i];
+    cwv[i] = p.conv_w[cv * 4 + i];
+  }
+  auto save_conv = [&]() {
+    if (hh == 0)
+      for (int i = 0; i < 3; ++i) {
+        cs_out[cq * 3 + i] = __float2bfloat16(wq[i]);
+        cs_out[ck * 3 + i] = __float2bfloat16(wk[i]);
+      }
+    for (int i = 0; i < 3; ++i) cs_out[cv * 3 + i] = __float2bfloat16(wv[i]);
+  };
+  bool conv_saved = false;
+  if (keep && a == 0) {
+    save_conv();
+    conv_saved = true;
+  }
+  const float A = -__expf(p.A_log[h]);
+  const float dtb = p.dt_bias[h];
+  float vv[kDecC], zz[kDecC], qv[kDecC], kv[kDecC];
+  float sq_part[kDecC], sk_part[kDecC];
+#pragma unroll
+  for (int u = 0; u < kDecC; ++u) {
+    vv[u] = zz[u] = qv[u] = kv[u] = 0.f;
+    if (u < n) {
+      float xq, xk, xv, braw, araw;
+      if (u < a) {
+        const __nv_bfloat16* prow = px + (long long)u * conv_dim;
+        xq = __bfloat162float(prow[cq]);
+        xk = __bfloat162float(prow[ck]);
+        xv = __bfloat162float(prow[cv]);
+        braw = pb_b[u];
+        araw = pb_a[u];
+      } else {
+        const int t = u - a;
+        const __nv_bfloat16* row = p.qkvz + (long long)(t0 + t) * p.ld_qkvz + grp;
+        const __nv_bfloat16* barow = p.ba + (long long)(t0 + t) * p.ld_ba + (long long)gk * 2 * r;
+        const __nv_bfloat16 bq = row[j], bk = row[p.dk + j], bv = row[2 * p.dk + hh * p.dv + j];
+        const __nv_bfloat16 bb = barow[hh], baa = barow[r + hh];
+        xq = __bfloat162float(bq);
+        xk = __bfloat162float(bk);
+        xv = __bfloat162float(bv);
+        braw = __bfloat162float(bb);
+        araw = __bfloat162float(baa);
+        zz[u] = __bfloat162float(row[2 * p.dk + r * p.dv + hh * p.dv + j]);
+        if (keep) {
+          __nv_bfloat16* pw = px_out + (long long)t * conv_dim;
+          if (hh == 0) {
+            pw[cq] = bq;
+            pw[ck] = bk;
+          }
+          pw[cv] = bv;
+          if (j == 0) {
+            pb[t * 2 * p.Hv + h] = bb;
+            pb[t * 2 * p.Hv + p.Hv + h] = baa;
+          }
+        }
+      }
+      float q = cwq[3] * xq, k = cwk[3] * xk, v = cwv[3] * xv;
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        q = fmaf(cwq[i], wq[i], q);
+        k = fmaf(cwk[i], wk[i], k);
+        v = fmaf(cwv[i], wv[i], v);
+      }
+      wq[0] = wq[1]; wq[1] = wq[2]; wq[2] = xq;
+      wk[0] = wk[1]; wk[1] = wk[2]; wk[2] = xk;
+      wv[0] = wv[1]; wv[1] = wv[2]; wv[2] = xv;
+      if (keep && u == a - 1) {
+        save_conv();
+        conv_saved = true;
+      }
+      qv[u] = silu(q);
+      kv[u] = silu(k);
+      vv[u] = silu(v);
+      if (tid == 0) {
+        Bt[u] = sigmoidf_(braw);
+        Lg[u] = A * softplusf(araw + dtb);
+      }
+    }
+    sq_part[u] = warp_sum(qv[u] * qv[u]);
+    sk_part[u] = warp_sum(kv[u] * kv[u]);
+  }
+  if (!conv_saved) save_conv();
+  if (lane == 0)
+#pragma unroll
+    for (int u = 0; u < kDecC; ++u) {
+      red[u][0][warp] = sq_part[u];
+      red[u][1][warp] = sk_part[u];
+    }
+  __syncthreads();
+  // ---- L2-normalised q (times 1/sqrt(dk)) and k: fp32 columns and bf16 MMA rows ----
+  const float qscale = rsqrtf((float)p.dk);
+#pragma unroll
+  for (int u = 0; u < kDecC; ++u) {
+    const float sq = red[u][0][0] + red[u][0][1] + red[u][0][2] + red[u][0][3];
+    const float sk = red[u][1][0] + red[u][1][1] + red[u][1][2] + red[u][1][3];
+    const float qn = u < n ? qv[u] * rsqrtf(sq + 1e-6f) * qscale : 0.f;
+    const float kn = u < n ? kv[u] * rsqrtf(sk + 1e-6f) : 0.f;
+    qT[j][u] = qn;
+    kT[j][u] = kn;
+    *reinterpret_cast<__nv_bfloat16*>(sA + sw16(u, j >> 3) + (j & 7) * 2) = __float2bfloat16(kn);
+    *reinterpret_cast<__nv_bfloat16*>(sA + sw16(8 + u, j >> 3) + (j & 7) * 2) = __float2bfloat16(qn);
+  }
+  if (tid == 0)
+    for (int u = 1; u < n; ++u) Lg[u] += Lg[u - 1];  // cumulative log decay
+  __syncthreads();
+  // ---- pairwise k_s.k_t and k_s.q_t (fp32) ----
+  for (int pr = warp; pr < n * n; pr += kDecThreads / 32) {
+    const int s_ = pr / n, t_ = pr % n;
+    if (s_ > t_) continue;
+    float kk = 0.f, kq = 0.f;
+    for (int i = lane; i < kD; i += 32) {
+      kk = fmaf(kT[i][s_], kT[i][t_], kk);
+      kq = fmaf(kT[i][s_], qT[i][t_], kq);
+    }
+    kk = warp_sum(kk);
+    kq = warp_sum(kq);
+    if (lane == 0) {
+      KK[s_][t_] = kk;
+      KQ[s_][t_] = kq;
+    }
+  }
+  // ---- pass 1 (tensor cores): rows 0-7 S0^T k_t, rows 8-15 S0^T q_t; warp w: columns 32w.. ----
+  {
+    float acc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < kD / 16; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldsm4(sA_a + sw16(lane & 15, 2 * ks + (lane >> 4)), a0, a1, a2, a3);
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr) {
+        uint32_t b0, b1, b2, b3;
+        const int krow = 16 * ks + (lane & 7) + ((lane >> 3) & 1) * 8;
+        ldsm4t(sS_a + sw16(krow, (32 * warp + 16 * pr) / 8 + (lane >> 4)), b0, b1, b2, b3);
+        mma_bf16_16816(acc[2 * pr], a0, a1, a2, a3, b0, b1);
+        mma_bf16_16816(acc[2 * pr + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncthreads();  // every warp is done with the k/q columns that kvq overwrites
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int col = 32 * warp + 8 * nt + 2 * (lane & 3);
+      *reinterpret_cast<float2*>(&kvq[lane >> 2][col]) = make_float2(acc[nt][0], acc[nt][1]);
+      *reinterpret_cast<float2*>(&kvq[(lane >> 2) + 8][col]) = make_float2(acc[nt][2], acc[nt][3]);
+    }
+  }
+  __syncthreads();
+  // ---- per column: triangular solve for d_t, outputs o_t ----
+  float dd[kDecC], ov[kDecC];
+#pragma unroll
+  for (int t = 0; t < kDecC; ++t) {
+    dd[t] = 0.f;
+    if (t < n) {
+      float acc = vv[t] - __expf(Lg[t]) * kvq[t][j];
+#pragma unroll
+      for (int s_ = 0; s_ < kDecC; ++s_)
+        if (s_ < t) acc -= __expf(Lg[t] - Lg[s_]) * KK[s_][t] * dd[s_];
+      dd[t] = Bt[t] * acc;
+    }
+  }
+  float os[kDecC];
+#pragma unroll
+  for (int u = 0; u < kDecC; ++u) {
+    float o = 0.f;
+    if (u < n && u >= a) {
+      o = __expf(Lg[u]) * kvq[8 + u][j];
+#pragma unroll
+      for (int s_ = 0; s_ < kDecC; ++s_)
+        if (s_ <= u) o += __expf(Lg[u] - Lg[s_]) * KQ[s_][u] * dd[s_];
+    }
+    ov[u] = o;
+    os[u] = warp_sum(o * o);
+  }
+  // C_s = (G_w / G_s) d_s as the B operand of pass 2 (rows 8-15 stay zero)
+  const int w = w_last;
+  float Gw = 0.f;
+  __syncthreads();  // every column has read its pass-1 values: sC may overwrite them
+  if (w >= 0) {
+    Gw = __expf(Lg[w]);
+#pragma unroll
+    for (int s_ = 0; s_ < 16; ++s_) {
+      const float c = (s_ < kDecC && s_ <= w) ? __expf(Lg[w] - Lg[s_]) * dd[s_ < kDecC ? s_ : 0] : 0.f;
+      *reinterpret_cast<__nv_bfloat16*>(sC + sw16(s_, j >> 3) + (j & 7) * 2) = __float2bfloat16(c);
+    }
+  }
+  __syncthreads();  // red (pass 1 values consumed) may be reused; sC complete
+  if (lane == 0)
+#pragma unroll
+    for (int u = 0; u < kDecC; ++u) red[u][0][warp] = os[u];
+  __syncthreads();
+  // ---- gated RMSNorm over dv and output ----
+  const float nw = p.norm_w[j];
+#pragma unroll
+  for (int u = 0; u < kDecC; ++u) {
+    if (u < n && u >= a) {
+      const float ss = red[u][0][0] + red[u][0][1] + red[u][0][2] + red[u][0][3];
+      float o = ov[u] * rsqrtf(ss / (float)p.dv + p.eps);
+      o = __bfloat162float(__float2bfloat16(o)) * nw;
+      o = o * silu(zz[u]);
+      p.out[(long long)(t0 + u - a) * p.Hv * p.dv + h * p.dv + j] = __float2bfloat16(o);
+    }
+  }
+  // ---- pass 2 (tensor cores): S_w = G_w S0 + K C; warp w: state rows 32w .. 32w+31 ----
+  if (w >= 0) {
+#pragma unroll 1
+    for (int cb = 0; cb < 4; ++cb) {  // 32-column blocks
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const int i0 = 32 * warp + 16 * mt;
+        uint32_t a0, a1, a2, a3;  // A[i][s] = k_s[i] (transposed read of the k rows of sA)
+        {
+          const int mi = lane >> 3;
+          const int srow = (mi >> 1) * 8 + (lane & 7);
+          ldsm4t(sA_a + sw16(srow, (i0 + (mi & 1) * 8) >> 3), a0, a1, a2, a3);
+        }
+        float acc[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int col = 32 * cb + 8 * nt + 2 * (lane & 3);
+          const int ra = i0 + (lane >> 2), rb = ra + 8;
+          const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(sS + sw16(ra, col >> 3) + (col & 7) * 2);
+          const __nv_bfloat162 y = *reinterpret_cast<const __nv_bfloat162*>(sS + sw16(rb, col >> 3) + (col & 7) * 2);
+          const float2 fx = __bfloat1622float2(x), fy = __bfloat1622float2(y);
+          acc[nt][0] = Gw * fx.x;
+          acc[nt][1] = Gw * fx.y;
+          acc[nt][2] = Gw * fy.x;
+          acc[nt][3] = Gw * fy.y;
+        }
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          uint32_t b0, b1, b2, b3;
+          const int krow = (lane & 7) + ((lane >> 3) & 1) * 8;
+          ldsm4t(sC_a + sw16(krow, (32 * cb + 16 * pr) / 8 + (lane >> 4)), b0, b1, b2, b3);
+          mma_bf16_16816(acc[2 * pr], a0, a1, a2, a3, b0, b1);
+          mma_bf16_16816(acc[2 * pr + 1], a0, a1, a2, a3, b2, b3);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int col = 32 * cb + 8 * nt + 2 * (lane & 3);
+          const int ra = i0 + (lane >> 2), rb = ra + 8;
+          *reinterpret_cast<__nv_bfloat162*>(sS + sw16(ra, col >> 3) + (col & 7) * 2) =
+              __floats2bfloat162_rn(acc[nt][0], acc[nt][1]);
+          *reinterpret_cast<__nv_bfloat162*>(sS + sw16(rb, col >> 3) + (col & 7) * 2) =
+              __floats2bfloat162_rn(acc[nt][2], acc[nt][3]);
+        }
+      }
+    }
+    __syncthreads();
+    uint4* dst = reinterpret_cast<uint4*>(st);
+#pragma unroll 4
+    for (int v = tid; v < kD * 16; v += kDecThreads) {
+      const int row = v >> 4, ch = v & 15;
+      dst[v] = *reinterpret_cast<const uint4*>(sS + sw16(row, ch));
+    }
+  }
+}
+
 }  // namespace
 }  // namespace oscar
 
@@ -373,8 +732,10 @@ extern "C" int oscar_gdn_step(const oscar::GdnParams* params, int smem_state, cu
       attr = true;
     }
     gdn_chunk_kernel<16, true><<<grid, kThreads, smem, stream>>>(p);
+  } else if (smem_state == 0 && p.P <= kDecC) {
+    // decode / verify: <= 8 tokens per request (commits + new) on the tensor cores
+    gdn_decode_kernel<<<grid, kDecThreads, 0, stream>>>(p);
   } else {
-    // decode / verify: one chunk of <= 8 tokens per request (commits + new), bf16 staging
     const int smem = kD * kD * sizeof(__nv_bfloat16);
     gdn_chunk_kernel<8, false><<<grid, kThreads, smem, stream>>>(p);
   }

@@ -60,18 +60,19 @@ def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float = 
 
     ``y = bf16(x * rsqrt(mean(x^2) + eps) * (offset + w))``; returns
     ``(q int8, scale, y_bf16)`` with the parts not requested set to ``None``.  ``wait =
-    (signal_pad_ptr, epoch_tensor, world)`` first waits for every rank's completion flag
-    of a fused GEMM + all-reduce producing ``delta``; ``zero_delta`` clears ``delta``
-    after reading it.
+    (signal_pad_ptr, epoch_tensor, world[, budget_ms])`` first waits for every rank's
+    completion flag of a fused GEMM + all-reduce producing ``delta`` (bounded: after
+    ``budget_ms``, default 5000, the kernel records a timeout in ``status`` and goes on);
+    ``zero_delta`` clears ``delta`` after reading it.
     """
     T, H = x.shape
     if x.is_cuda:
         q = out_q if out_q is not None else (torch.empty(T, H, dtype=torch.int8, device=x.device) if want_q else None)
         s = out_s if out_s is not None else (torch.empty(T, dtype=torch.float32, device=x.device) if want_q else None)
         y = out_bf16 if out_bf16 is not None else (torch.empty(T, H, dtype=torch.bfloat16, device=x.device) if want_bf16 else None)
-        sig, ep, world = wait if wait is not None else (0, None, 0)
+        sig, ep, world, budget_ms = (tuple(wait) + (5000,))[:4] if wait is not None else (0, None, 0, 5000)
         ext().rmsnorm_quant(x, delta, w, float(offset), float(eps), q, s, y, int(sig), ep, int(world),
-                            int(zero_delta), status)
+                            int(zero_delta), status, int(budget_ms * 1e6))
         return q, s, y
     if delta is not None:
         x += delta.float()

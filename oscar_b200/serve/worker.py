@@ -80,7 +80,18 @@ class EngineWorker:
             raise RuntimeError(f"engine worker failed: {self.error!r}")
         fut: Future = Future()
         self.q.put((list(map(int, prompt)), int(max_tokens), fut))
+        if self.error is not None:  # the loop died while this was being queued
+            self._fail_queued(self.error)
         return fut
+
+    def _fail_queued(self, err: BaseException) -> None:
+        while True:
+            try:
+                _, _, fut = self.q.get_nowait()
+            except queue.Empty:
+                return
+            if not fut.done():
+                fut.set_exception(err)
 
     def start(self) -> "EngineWorker":
         self._thread = threading.Thread(target=self._run, name="oscar-engine", daemon=True)
@@ -105,6 +116,7 @@ class EngineWorker:
 
     def _run(self) -> None:
         eng = self.engine
+        new: list = []
         try:
             while True:
                 stop = self._stop.is_set()
@@ -119,16 +131,17 @@ class EngineWorker:
                     rid = eng.add_request(p, m)
                     self.futures[rid] = fut
                     self.metrics.requests += 1
+                new = []
                 if eng.has_work():
                     eng.step()
                     self.metrics.steps += 1
                     self._resolve()
         except BaseException as e:  # noqa: BLE001 - surfaced to every pending request
             self.error = e
-            for fut in self.futures.values():
+            for fut in list(self.futures.values()) + [f for _, _, f in new]:
                 if not fut.done():
                     fut.set_exception(e)
-            raise
+            self._fail_queued(e)
 
     def _resolve(self) -> None:
         eng = self.engine

@@ -367,3 +367,20 @@ def test_gdn_step_matches_ref(mode):
     assert torch.equal(g[2], c[2])
     assert torch.equal(g[3], c[3])
     assert torch.equal(g[4], c[4])
+
+
+def test_peer_wait_times_out_into_status():
+    """Failure detection on the device without a fault: the consumer's wait on peer
+    completion flags that nobody sets gives up after its budget, records the timeout in
+    the status word and returns; the context stays usable."""
+    dev = torch.device(DEV)
+    x = torch.randn(4, 512, device=dev)
+    w = torch.zeros(512, device=dev)
+    flags = torch.zeros(8, dtype=torch.int32, device=dev)  # no rank ever publishes
+    epoch = torch.ones(1, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    F.rmsnorm_quant(x, w, 1e-6, wait=(flags.data_ptr(), epoch, 2, 200), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 5  # kTimeoutPeerFlag
+    y = (x * 2).sum()  # the device still works
+    assert torch.isfinite(y)
