@@ -403,26 +403,24 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
               }
             }
             if (any_val) {
-              // tokens carrying values: replace their halves of the fp16 pairs
-#pragma unroll 1
+              // tokens carrying values (current chunk / staged): their halves of the fp16
+              // pairs come from memory; every index is static so r stays in registers
+              const uint32_t mw0 = msk[2 * hf], mw1 = msk[2 * hf + 1];
+              const int sbase = staging ? (blk % p.stage_rows) * kPage : 0;
+#pragma unroll
               for (int k = 0; k < 32; ++k) {
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                  const int tj = hf * 64 + 2 * k + e;
-                  if (!((msk[tj >> 5] >> (tj & 31)) & 1u)) continue;
-                  const int ps_ = page_pos + tj;
-                  float v;
-                  if (ps_ >= prefix)
-                    v = __half2float(p.v_fresh[((long long)(q0 + ps_ - prefix) * p.Hk + hk) * kD + d]);
-                  else
-                    v = __ldg(p.stage_v + ((long long)((blk % p.stage_rows) * kPage + tj) * p.Hk + hk) * kD + d);
-                  const uint32_t hv = (uint32_t)__half_as_ushort(__float2half_rn(v));
-                  uint32_t cur = 0;
-#pragma unroll
-                  for (int kk = 0; kk < 32; ++kk) cur = kk == k ? r[kk] : cur;
-                  cur = e ? ((cur & 0x0000ffffu) | (hv << 16)) : ((cur & 0xffff0000u) | hv);
-#pragma unroll
-                  for (int kk = 0; kk < 32; ++kk) r[kk] = kk == k ? cur : r[kk];
+                  const int tl = 2 * k + e;  // token within this 64-token half
+                  const bool isval = ((tl < 32 ? mw0 >> tl : mw1 >> (tl - 32)) & 1u) != 0u;
+                  if (isval) {
+                    const int tj = hf * 64 + tl, ps_ = page_pos + tj;
+                    const float v = ps_ >= prefix
+                                        ? __half2float(p.v_fresh[((long long)(q0 + ps_ - prefix) * p.Hk + hk) * kD + d])
+                                        : __ldg(p.stage_v + ((long long)(sbase + tj) * p.Hk + hk) * kD + d);
+                    const uint32_t hv = (uint32_t)__half_as_ushort(__float2half_rn(v));
+                    r[k] = e ? ((r[k] & 0x0000ffffu) | (hv << 16)) : ((r[k] & 0xffff0000u) | hv);
+                  }
                 }
               }
             }

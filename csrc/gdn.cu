@@ -428,14 +428,16 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
   }
   const uint32_t sS_a = smem_u32(sS), sA_a = smem_u32(sA), sC_a = smem_u32(sC);
 
-  // state -> shared memory (16-byte loads, swizzled chunks)
+  // state -> shared memory with asynchronous 16-byte copies (swizzled chunks); they
+  // stream in while the conv / gate / norm work below runs
   {
     const uint4* src = reinterpret_cast<const uint4*>(st);
-#pragma unroll 4
+#pragma unroll
     for (int v = tid; v < kD * 16; v += kDecThreads) {
       const int row = v >> 4, ch = v & 15;
-      *reinterpret_cast<uint4*>(sS + sw16(row, ch)) = __ldg(src + v);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sS_a + sw16(row, ch)), "l"(src + v) : "memory");
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
   if (tid < a) {
     pb_b[tid] = __bfloat162float(pb[tid * 2 * p.Hv + h]);
@@ -576,6 +578,9 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
       KQ[s_][t_] = kq;
     }
   }
+  // the state copies have landed (this thread's), and every thread's (barrier)
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
   // ---- pass 1 (tensor cores): rows 0-7 S0^T k_t, rows 8-15 S0^T q_t; warp w: columns 32w.. ----
   {
     float acc[4][4];

@@ -10,7 +10,8 @@ Behaviour follows the reference's diagnostics (``oscar_ascend/diagnostics.py:36-
   meaning "no filter";
 * every hooked stage records inclusive, device-synchronised wall time: the time spent
   draining earlier GPU work before the stage (``wait_before_ms``), the first and the
-  largest duration and the sum;
+  largest duration and the sum; ``OSCAR_PROFILE_TIMER=events`` instead brackets each
+  stage with CUDA events and an NVTX range (no synchronisation inside the step);
 * a ``TorchDispatchMode`` counts ``aten::sort``/``argsort`` calls inside the step and
   keeps the Python stacks of integer-dtype sorts (the reference hunted host-visible
   integer sorts on the serving path);
@@ -104,13 +105,15 @@ class Diagnostics:
     _stages: dict | None = None
     _last_end: float = 0.0
     code_sha256: str | None = None
+    mode: str = "sync"  # "sync" | "events" (CUDA events + NVTX, no syncs in the step)
+    _pending: list = field(default_factory=list)
 
     @classmethod
     def from_env(cls, rank: int = 0, sink=None) -> "Diagnostics":
         return cls(steps=_env_int("OSCAR_ASCEND_PROFILE_STEPS"),
                    min_requests=_env_int("OSCAR_ASCEND_PROFILE_MIN_REQUESTS"),
                    max_tokens_per_request=_env_int("OSCAR_ASCEND_PROFILE_MAX_TOKENS_PER_REQUEST"),
-                   rank=rank, sink=sink)
+                   rank=rank, sink=sink, mode=os.environ.get("OSCAR_PROFILE_TIMER", "sync"))
 
     @property
     def enabled(self) -> bool:
@@ -134,9 +137,26 @@ class Diagnostics:
 
     @contextmanager
     def timed(self, name: str):
-        """Synchronised inclusive timing of a stage (no-op outside a captured step)."""
+        """Inclusive timing of a stage (no-op outside a captured step).
+
+        ``mode == "sync"`` (default, and always on the CPU): device-synchronised wall
+        time, with the time spent draining earlier work as ``wait_before_ms``.
+        ``mode == "events"`` on CUDA: CUDA events around the stage on the current stream
+        and an NVTX range, no synchronisation inside the step; resolved after the step.
+        """
         if self._stages is None:
             yield
+            return
+        if self.mode == "events" and torch.cuda.is_available() and torch.cuda.is_initialized():
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push(name)
+            s.record()
+            try:
+                yield
+            finally:
+                e.record()
+                torch.cuda.nvtx.range_pop()
+                self._pending.append((name, s, e))
             return
         t0 = time.perf_counter()
         self._sync()
@@ -178,6 +198,11 @@ class Diagnostics:
                 out = step_fn()
         finally:
             stages, self._stages = self._stages, None  # context always reset, also on exceptions
+            if self._pending:
+                torch.cuda.synchronize()
+                for name, s, e in self._pending:
+                    stages.setdefault(name, Record()).add(s.elapsed_time(e), 0.0)
+                self._pending = []
         self.captured += 1
         rec = {"step": self.seen, "shape": shape, "wall_ms": round((time.perf_counter() - t0) * 1e3, 4),
                "stages": {k: v.as_dict() for k, v in stages.items()},
