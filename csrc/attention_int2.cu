@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_kernel(AttnParams 
           value_tok = true;
         } else {  // INT2 K codes: 64 dims = 16 bytes
           const int cb = kD / 4;
-          const uint4 kw = *reinterpret_cast<const uint4*>(pg + j * cb + my_q * 16);
+          const uint4 kw = *reinterpret_cast<const uint4*>(pg + j * cb + ((my_q ^ ((j >> 1) & 3)) << 4));
           const uint32_t kk[4] = {kw.x, kw.y, kw.z, kw.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {

@@ -59,6 +59,14 @@ constexpr uint64_t kBudgetNs = 2000000000ull;
 constexpr uint32_t kColK = 0, kColV = 128, kColS = 384, kColO = 448, kTmemCols = 512;
 constexpr int kBarConv = 2, kBarSoft = 1, kBarStats = 3;
 
+// Optional per-CTA event timeline (globaltimer ns) for performance analysis; off
+// unless a buffer was installed with oscar_attn_tc_trace (slot layout: 64 u64 per CTA).
+__device__ unsigned long long* g_tc_trace = nullptr;
+OSCAR_DEVICE void trace(int ev) {
+  unsigned long long* t = g_tc_trace;
+  if (t != nullptr && ev < 64) t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * 64 + ev] = globaltimer_ns();
+}
+
 template <int N>
 struct TcLayout {
   static constexpr int kQOff = kRing * kSlot;  // 71,680: 1024-aligned
@@ -167,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   const int n_pages = kv_stop > kv_begin ? (kv_stop - 1) / kPage - p_first + 1 : 0;
 
   // ---------------------------------------------------------------- setup
+  if (tid == 0) trace(0);
   if (warp == 0) {
     sm100::tmem_alloc(tmem_slot, kTmemCols);
     sm100::tmem_relinquish();
@@ -216,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  if (tid == 0) trace(1);
 
   if (warp == 0) {
     // ------------------------------------------------------------ page producer
@@ -236,6 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           sm100::bulk_load(dst + kPageBytes, p.owner + (long long)(blk % p.stage_rows) * kPage, kPage * 4,
                            &B.raw_full[s]);
         issued = i + 1;
+        if (i < 8) trace(8 + i);
       }
       if (*abort_flag) {  // copies in flight must land before the CTA exits
         const uint64_t t0 = globaltimer_ns();
@@ -290,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           sm100::umma_f16_tmem_a(tbase + kColS + (i & 1) * N, tbase + kColK + kk * 8, qd, idq, kk > 0 ? 1u : 0u);
         }
         sm100::umma_commit(&B.s_full[i & 1]);
+        if (i < 8) trace(16 + i);
         sm100::umma_commit(B.k_empty);
         if (i >= 1) ok = pv(i - 1);
       }
@@ -305,40 +317,49 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     // ------------------------------------------------------------ converters
     const int ct = tid - 128;  // TMEM lane
     const uint32_t lrow = (uint32_t)(ct & ~31) << 16;
-    bool dead = false;
+    // No named barriers in this loop: every warp arrives on the mbarriers itself, so a
+    // warp whose bounded wait expires simply leaves (the others time out in turn).
     for (int i = 0; i < n_pages; ++i) {
       const int s = i % kRing;
-      bool ok = !dead && sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull,
-                                          kBudgetNs);
-      if (ok && i >= 1)
-        ok = sm100::mbar_wait(B.k_empty, (i - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
+      if (!sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs))
+        break;
+      if (i >= 1 && !sm100::mbar_wait(B.k_empty, (i - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs))
+        break;
       const uint8_t* pg = ring + s * kSlot;
       const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
-      const int blk = ok ? slot_blk[s] : 0;
+      const int blk = slot_blk[s];
       const int page_pos = (p_first + i) * kPage;
-      bool val_tok = false;
-      if (ok) {
-        sm100::tc_fence_after();
+      // value tokens (current chunk or staged) of the page, as a 128-bit mask computed by
+      // every warp for itself: lane l looks at tokens l, 32 + l, 64 + l, 96 + l
+      uint32_t vm[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int tj = 32 * q + lane, ps_ = page_pos + tj;
+        const bool in = ps_ >= kv_begin && ps_ < kv_stop;
+        vm[q] = __ballot_sync(0xffffffffu, in && (ps_ >= prefix || (staging && own[tj] == blk)));
+      }
+      const bool any_val = (vm[0] | vm[1] | vm[2] | vm[3]) != 0u;
+      sm100::tc_fence_after();
+      {
         // K codes of token ct -> 128 columns of fp16 pairs
         const int j = ct, pos = page_pos + j;
         const bool in = pos >= kv_begin && pos < kv_stop;
         const int kind = !in ? 0 : pos >= prefix ? 1 : (staging && own[j] == blk) ? 2 : 3;
-        val_tok = kind == 1 || kind == 2;
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
           if (kind == 3) {
-            const uint4 cw = *reinterpret_cast<const uint4*>(pg + j * 64 + c * 16);
+            const uint4 cw = *reinterpret_cast<const uint4*>(pg + j * 64 + ((c ^ ((j >> 1) & 3)) << 4));
             const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              uint32_t a[4], b[4];
-              mma::codes8_to_h2(wd[q], a);
-              mma::codes8_to_h2(wd[q] >> 8, b);
+              uint32_t a4[4], b4[4];
+              mma::codes8_to_h2(wd[q], a4);
+              mma::codes8_to_h2(wd[q] >> 8, b4);
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                r[8 * q + e] = a[e];
-                r[8 * q + 4 + e] = b[e];
+                r[8 * q + e] = a4[e];
+                r[8 * q + 4 + e] = b4[e];
               }
             }
           } else if (kind == 1) {
@@ -370,72 +391,76 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         sm100::tmem_st_wait();
         sm100::tc_fence_before();
       }
-      const uint32_t bal = __ballot_sync(0xffffffffu, val_tok);
-      if (lane == 0) vmask[(i & 1) * 4 + (ct >> 5)] = bal;
-      if (sm100::bar_red_or(kBarConv, 128, !ok)) break;
+      __syncwarp();
       if (lane == 0) sm100::mbar_arrive(B.k_full);
+      if (ct == 0 && i < 8) trace(24 + i);
 
       // V^T of dims ct and ct + 128 -> 2 x 64 columns
-      ok = i < 2 || sm100::mbar_wait(&B.v_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
-                                     kTimeoutAccEmpty, kBudgetNs);
-      if (ok) {
-        sm100::tc_fence_after();
-        const uint32_t* msk = vmask + (i & 1) * 4;
-        const bool any_val = (msk[0] | msk[1] | msk[2] | msk[3]) != 0u;
+      if (i >= 2 && !sm100::mbar_wait(&B.v_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
+                                      kTimeoutAccEmpty, kBudgetNs))
+        break;
+      sm100::tc_fence_after();
+      const int sbase = staging ? (blk % p.stage_rows) * kPage : 0;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        const int d = ct + 128 * h;
+        const uint4* src = reinterpret_cast<const uint4*>(pg + kPage * 64 + d * 32);
+        const uint4 a4 = src[0], b4 = src[1];
+        const uint32_t wd[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int d = ct + 128 * h;
-          const uint4* src = reinterpret_cast<const uint4*>(pg + kPage * 64 + d * 32);
-          const uint4 a4 = src[0], b4 = src[1];
-          const uint32_t wd[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t r[32];
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            uint32_t r[32];
+          for (int q = 0; q < 4; ++q) {
+            uint32_t x4[4], y4[4];
+            mma::codes8_to_h2(wd[4 * hf + q], x4);
+            mma::codes8_to_h2(wd[4 * hf + q] >> 8, y4);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t a[4], b[4];
-              mma::codes8_to_h2(wd[4 * hf + q], a);
-              mma::codes8_to_h2(wd[4 * hf + q] >> 8, b);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                r[8 * q + e] = a[e];
-                r[8 * q + 4 + e] = b[e];
-              }
+            for (int e = 0; e < 4; ++e) {
+              r[8 * q + e] = x4[e];
+              r[8 * q + 4 + e] = y4[e];
             }
-            if (any_val) {
-              // tokens carrying values (current chunk / staged): their halves of the fp16
-              // pairs come from memory; every index is static so r stays in registers
-              const uint32_t mw0 = msk[2 * hf], mw1 = msk[2 * hf + 1];
-              const int sbase = staging ? (blk % p.stage_rows) * kPage : 0;
-#pragma unroll
-              for (int k = 0; k < 32; ++k) {
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const int tl = 2 * k + e;  // token within this 64-token half
-                  const bool isval = ((tl < 32 ? mw0 >> tl : mw1 >> (tl - 32)) & 1u) != 0u;
-                  if (isval) {
-                    const int tj = hf * 64 + tl, ps_ = page_pos + tj;
-                    const float v = ps_ >= prefix
-                                        ? __half2float(p.v_fresh[((long long)(q0 + ps_ - prefix) * p.Hk + hk) * kD + d])
-                                        : __ldg(p.stage_v + ((long long)(sbase + tj) * p.Hk + hk) * kD + d);
-                    const uint32_t hv = (uint32_t)__half_as_ushort(__float2half_rn(v));
-                    r[k] = e ? ((r[k] & 0x0000ffffu) | (hv << 16)) : ((r[k] & 0xffff0000u) | hv);
-                  }
-                }
-              }
-            }
-            sm100::tmem_st_32x32b_x32(tbase + lrow + kColV + (i & 1) * 128 + h * 64 + hf * 32, r);
           }
+          if (any_val) {
+            // Value tokens: their halves of the fp16 pairs come from memory.  The loads are
+            // unconditional (a non-value token reads a harmless fixed element), so a batch
+            // of 8 is in flight at once; every register index is static.
+            const uint32_t mw0 = vm[2 * hf], mw1 = vm[2 * hf + 1];
+#pragma unroll
+            for (int g8 = 0; g8 < 8; ++g8) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int tl = 8 * g8 + e, tj = hf * 64 + tl, ps_ = page_pos + tj;
+                const bool isval = ((tl < 32 ? mw0 >> tl : mw1 >> (tl - 32)) & 1u) != 0u;
+                const bool fresh = ps_ >= prefix;
+                const long long fi = (isval && fresh) ? ((long long)(q0 + ps_ - prefix) * p.Hk + hk) * kD + d : 0;
+                const long long si = (isval && !fresh) ? ((long long)(sbase + tj) * p.Hk + hk) * kD + d : 0;
+                const float fv = __half2float(p.v_fresh[fi]);
+                const float sv = staging ? __ldg(p.stage_v + si) : 0.f;
+                v[e] = fresh ? fv : sv;
+              }
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int tl = 8 * g8 + e, k = tl >> 1;
+                const bool isval = ((tl < 32 ? mw0 >> tl : mw1 >> (tl - 32)) & 1u) != 0u;
+                const uint32_t hv = (uint32_t)__half_as_ushort(__float2half_rn(v[e]));
+                const uint32_t nv = (tl & 1) ? ((r[k] & 0x0000ffffu) | (hv << 16)) : ((r[k] & 0xffff0000u) | hv);
+                r[k] = isval ? nv : r[k];
+              }
+            }
+          }
+          sm100::tmem_st_32x32b_x32(tbase + lrow + kColV + (i & 1) * 128 + h * 64 + hf * 32, r);
         }
-        sm100::tmem_st_wait();
-        sm100::tc_fence_before();
       }
-      if (sm100::bar_red_or(kBarConv, 128, !ok)) break;
+      sm100::tmem_st_wait();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (ct == 0 && i < 8) trace(32 + i);
       if (lane == 0) {
         sm100::mbar_arrive(&B.v_full[i & 1]);
         sm100::mbar_arrive(&B.raw_empty[s]);
       }
-      dead = !ok;
     }
   } else if (warp == 2 || warp == 3) {
     // ------------------------------------------------------------ row statistics
@@ -646,6 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         __syncwarp();
         if (lane == 0) {
           sm100::mbar_arrive(&B.p_full[b]);
+          if (st == 0 && i < 8) trace(40 + i);
           sm100::mbar_arrive(&B.raw_empty[s]);
         }
       }
@@ -700,8 +726,10 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   }
 
   // ---------------------------------------------------------------- teardown
+  if (tid == 256) trace(2);  // softmax role done (outputs written)
   sm100::tc_fence_before();
   __syncthreads();
+  if (tid == 0) trace(3);
   if (warp == 0) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tbase, kTmemCols);
@@ -724,6 +752,11 @@ int launch_tc(const AttnParams& p, cudaStream_t stream) {
 
 }  // namespace
 }  // namespace oscar
+
+// Install (or, with nullptr, remove) the per-CTA timeline buffer of the tcgen05 kernel.
+extern "C" int oscar_attn_tc_trace(unsigned long long* buf) {
+  return (int)cudaMemcpyToSymbol(oscar::g_tc_trace, &buf, sizeof(buf));
+}
 
 // rows_per_item: the largest q_len * g - row0 of any work item (<= 32).
 extern "C" int oscar_int2_attention_tc(const oscar::AttnParams* params, int rows_per_item, cudaStream_t stream) {

@@ -16,6 +16,7 @@ int oscar_num_sms();
 int oscar_kv_store(const oscar::StoreParams* p, cudaStream_t stream);
 int oscar_paged_attention(const oscar::AttnParams* p, cudaStream_t stream);
 int oscar_int2_attention_tc(const oscar::AttnParams* p, int rows_per_item, cudaStream_t stream);
+int oscar_attn_tc_trace(unsigned long long* buf);
 int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
 int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi, const __nv_bfloat16* Rv_lo,
                          cudaStream_t stream);
@@ -121,6 +122,9 @@ void gemm_i8_allreduce(const Tensor& A, const Tensor& B, const Tensor& scale_a, 
                             ptr<int>(tile_cnt), stream()),
            "gemm_i8_allreduce");
 }
+
+// Install a per-CTA timeline buffer for the tcgen05 attention kernel (0 removes it).
+void attn_tc_trace(int64_t ptr) { check_rc(oscar_attn_tc_trace(reinterpret_cast<unsigned long long*>(ptr)), "attn_tc_trace"); }
 
 int64_t num_sms() { return oscar_num_sms(); }
 
@@ -429,6 +433,7 @@ void f32_to_bf16(const Tensor& x, Tensor& y) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "oscar_b200 sm_100a kernels";
   m.def("gemm_i8", &gemm_i8);
+  m.def("attn_tc_trace", &attn_tc_trace);
   m.def("gemm_i8_allreduce", &gemm_i8_allreduce);
   m.def("num_sms", &num_sms);
   m.def("kv_store", &kv_store);

@@ -48,7 +48,8 @@ __device__ __forceinline__ float kth_largest_abs(const float (&x)[8], int n, int
 }
 
 // One warp quantises one (token, head) vector of D = 32 * n elements.
-// codes_row: token-major code row (K), or nullptr with vt_words/tok set: V is stored
+// codes_row: token-major code row (K, 16-byte chunks swizzled by tok), or nullptr with
+// vt_words/tok set: V is stored
 // dim-major ("transposed") - dim d of the page owns kPage/16 words, and token tok sits
 // in word d * kPage/16 + tok/16 at bit 16*(tok&1) + 2*((tok&15)>>1).  Tokens of one
 // step share words, so the 2-bit fields are cleared and set with atomic reductions.
@@ -101,7 +102,13 @@ __device__ void quantize_vector(float (&x)[8], int n, int clip_idx, int D, uint8
   }
   if (!vt_words) {
     for (int o = 1; o < 16 / n; o <<= 1) part |= __shfl_xor_sync(0xffffffffu, part, o);
-    if (((lane * n) & 15) == 0) reinterpret_cast<uint32_t*>(codes_row)[(lane * n) >> 4] = part;
+    if (((lane * n) & 15) == 0) {
+      // 16-byte chunks of a K code row are XOR-swizzled by the token (tok >> 1), so that
+      // the attention kernels' per-token row reads hit distinct shared-memory banks
+      const int w = (lane * n) >> 4, nch = D / 64;
+      const int sw = (((w >> 2) ^ ((tok >> 1) & (nch - 1))) << 2) | (w & 3);
+      reinterpret_cast<uint32_t*>(codes_row)[sw] = part;
+    }
   }
   if (lane == 0) {
     *scale_dst = sh;
@@ -322,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 2) kv_rotate_kernel(StoreParams p, i
       quantize_vector(x, n, p.v_clip_idx, D, nullptr, meta + 2 * kPage + off, meta + 3 * kPage + off,
                       reinterpret_cast<uint32_t*>(page + kPage * cb), off);
     else
-      quantize_vector(x, n, p.k_clip_idx, D, page + off * cb, meta + off, meta + kPage + off);
+      quantize_vector(x, n, p.k_clip_idx, D, page + off * cb, meta + off, meta + kPage + off, nullptr, off);
   }
 }
 

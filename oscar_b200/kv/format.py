@@ -207,9 +207,10 @@ def page_views(pool: torch.Tensor, D: int, page: int = PAGE):
 
     Returns ``(k_codes [B,Hk,page,D/4], v_codes_t [B,Hk,D,page/4], k_scale [B,Hk,page]
     fp16, k_zero, v_scale, v_zero)``.  K codes are token-major (one row of ``D/4`` bytes
-    per token, dims in the pool bit order); V codes are dim-major (one row of
-    ``page/4`` bytes per dim, tokens in the same bit order), which is the operand
-    layout of the P.V product in the attention kernels.
+    per token, dims in the pool bit order, 16-byte chunks swizzled by the token, see
+    :func:`k_chunk_perm`); V codes are dim-major (one row of ``page/4`` bytes per dim,
+    tokens in the same bit order), which is the operand layout of the P.V product in
+    the attention kernels.
     """
     nb, hk, pb = pool.shape
     off = page_offsets(D, page)
@@ -219,6 +220,35 @@ def page_views(pool: torch.Tensor, D: int, page: int = PAGE):
     vt = pool[:, :, off["v"]: off["k_scale"]].view(nb, hk, D, page // 4)
     meta = pool.view(torch.float16)[:, :, off["k_scale"] // 2: off["total"] // 2].view(nb, hk, 4, page)
     return kc, vt, meta[:, :, 0], meta[:, :, 1], meta[:, :, 2], meta[:, :, 3]
+
+
+def k_chunk_perm(offs: torch.Tensor, D: int) -> torch.Tensor:
+    """Byte permutation of the K code rows of tokens ``offs``: the row's 16-byte chunk
+    ``c`` is stored at chunk ``c ^ ((off >> 1) & (D/64 - 1))`` (bank-conflict-free reads
+    of one row per thread in the attention kernels).  Returns ``[T, D/4]`` byte indices:
+    ``stored[:, idx[t]] == logical``."""
+    cb = code_bytes(D)
+    nch = cb // 16
+    b = torch.arange(cb, device=offs.device)
+    ch, within = b // 16, b % 16
+    sw = (ch.unsqueeze(0) ^ ((offs.long().unsqueeze(1) >> 1) & (nch - 1))) * 16 + within.unsqueeze(0)
+    return sw
+
+
+def read_k_codes(kc: torch.Tensor, b: torch.Tensor, o: torch.Tensor, D: int) -> torch.Tensor:
+    """Codes ``[T, Hk, D]`` of tokens ``(b, o)`` from the token-major K view."""
+    rows = kc[b.long(), :, o.long()]  # [T, Hk, D/4] stored order
+    idx = k_chunk_perm(o, D).unsqueeze(1).expand(-1, rows.shape[1], -1)
+    return unpack_page(torch.gather(rows, 2, idx), D)
+
+
+def write_k_codes(kc: torch.Tensor, b: torch.Tensor, o: torch.Tensor, q: torch.Tensor) -> None:
+    D = q.shape[-1]
+    logical = pack_page(q)  # [T, Hk, D/4]
+    idx = k_chunk_perm(o, D).unsqueeze(1).expand(-1, logical.shape[1], -1)
+    stored = torch.empty_like(logical)
+    stored.scatter_(2, idx, logical)
+    kc[b.long(), :, o.long()] = stored
 
 
 def _token_byte_shift(offs: torch.Tensor, page: int = PAGE):
@@ -260,7 +290,7 @@ def pool_to_slots(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor, 
         lo, hi = f16_le(t[b, :, o].float().unsqueeze(-1))
         slot[..., 2 * i: 2 * i + 1] = lo
         slot[..., 2 * i + 1: 2 * i + 2] = hi
-    slot[..., K_IDX_OFF: K_IDX_OFF + cb] = pack(unpack_page(kc[b, :, o], D))
+    slot[..., K_IDX_OFF: K_IDX_OFF + cb] = pack(read_k_codes(kc, b, o, D))
     slot[..., V_IDX_OFF: V_IDX_OFF + cb] = pack(read_v_codes(vt, b, o))
     return slot
 
@@ -269,7 +299,7 @@ def dequant_tokens(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor,
     """Dequantize tokens of a page-packed pool -> ``(k [T,Hk,D], v [T,Hk,D])`` fp32 (rotated space)."""
     kc, vt, ks, kz, vs, vz = page_views(pool, D)
     b, o = blocks.long(), offs.long()
-    k = unpack_page(kc[b, :, o], D).float() * ks[b, :, o].float().unsqueeze(-1) + kz[b, :, o].float().unsqueeze(-1)
+    k = read_k_codes(kc, b, o, D).float() * ks[b, :, o].float().unsqueeze(-1) + kz[b, :, o].float().unsqueeze(-1)
     v = read_v_codes(vt, b, o).float() * vs[b, :, o].float().unsqueeze(-1) + vz[b, :, o].float().unsqueeze(-1)
     return k, v
 
@@ -286,7 +316,7 @@ def write_tokens(pool: torch.Tensor, blocks: torch.Tensor, offs: torch.Tensor, k
         if is_v:
             write_v_codes(vt, b, o, q)
         else:
-            kc[b, :, o] = pack_page(q)
+            write_k_codes(kc, b, o, q)
         sv[b, :, o] = scale.squeeze(-1).half()
         zv[b, :, o] = zero.squeeze(-1).half()
 
