@@ -8,7 +8,6 @@
 // share a KV head read each KV tile once.  Each KV tile of 64 tokens is built in
 // shared memory as fp16 by the whole CTA from its source:
 //   * position >= prefix                  -> unquantised k/v of the current chunk
-//   * staged (owner tag == physical block) -> fp32 sink/recent staging
 //   * otherwise                            -> BF16 page
 // which reproduces the reference read semantics (paged_attention.py:136-260).
 // Scores and P.V run on the tensor cores (m16n8k16, fp32 accumulate) with an
@@ -66,7 +65,7 @@ struct TileCtx {
 
 // Source of one (token, half) owned by a thread.
 struct RawInt2 {
-  int kind;  // 0 invalid, 2 fresh, 3 staged, 4 bf16
+  int kind;  // 0 invalid, 2 fresh, 4 bf16
   int blk, off, srow;
 };
 
@@ -81,15 +80,7 @@ OSCAR_DEVICE void load_raw(const AttnParams& p, const TileCtx& c, int pos, int h
   const int blk = c.bt[page];
   r.blk = blk;
   r.off = off;
-  if (p.stage_rows > 0) {
-    const int row = blk % p.stage_rows;
-    if (p.owner[row * kPage + off] == blk) {
-      r.kind = 3;
-      r.srow = row;
-      return;
-    }
-  }
-  r.kind = 4;  // BF16 page (INT2 pages are read by the code-domain kernel)
+  r.kind = 4;  // BF16 page (INT2 pages and their staging are read by the code-domain kernels)
 }
 
 // Write one thread's (token, half) = 128 dims of K and V into the fp16 tiles.
@@ -114,21 +105,6 @@ OSCAR_DEVICE void store_tile(const AttnParams& p, const TileCtx& c, int tok, int
     for (int j = 0; j < 16; ++j) {
       *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + j)) = __ldg(kf + j);
       *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + j)) = __ldg(vf + j);
-    }
-    return;
-  }
-  if (r.kind == 3) {
-    const long long base = ((long long)(r.srow * kPage + r.off) * p.Hk + c.hk) * p.D + d0;
-    const float4* kf = reinterpret_cast<const float4*>(p.stage_k + base);
-    const float4* vf = reinterpret_cast<const float4*>(p.stage_v + base);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float4 a = __ldg(kf + 2 * j), b = __ldg(kf + 2 * j + 1);
-      *reinterpret_cast<uint4*>(ks + swz(tok, chunk0 + j)) =
-          make_uint4(h2_u32(a.x, a.y), h2_u32(a.z, a.w), h2_u32(b.x, b.y), h2_u32(b.z, b.w));
-      const float4 e = __ldg(vf + 2 * j), f = __ldg(vf + 2 * j + 1);
-      *reinterpret_cast<uint4*>(vs + swz(tok, chunk0 + j)) =
-          make_uint4(h2_u32(e.x, e.y), h2_u32(e.z, e.w), h2_u32(f.x, f.y), h2_u32(f.z, f.w));
     }
     return;
   }

@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_kernel(AttnParams 
             if (ps >= prefix) {
               v = __half2float(p.v_fresh[((long long)(q0 + ps - prefix) * p.Hk + hk) * kD + d]);
             } else if (staging && own[jp] == blk) {
-              v = __ldg(p.stage_v + ((long long)((blk % p.stage_rows) * kPage + jp) * p.Hk + hk) * kD + d);
+              v = __ldg(p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage + (long long)d * kPage + jp);
             } else {
               continue;
             }

@@ -329,22 +329,28 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
       const int blk = slot_blk[s];
       const int page_pos = (p_first + i) * kPage;
-      // value tokens (current chunk or staged) of the page, as a 128-bit mask computed by
-      // every warp for itself: lane l looks at tokens l, 32 + l, 64 + l, 96 + l
-      uint32_t vm[4];
+      // Tokens that carry values, as 128-bit masks computed by every warp for itself
+      // (lane l looks at tokens l, 32 + l, 64 + l, 96 + l): staged sink/recent tokens
+      // (owner tag == block, read from the staging arena; this includes current-chunk
+      // tokens that were staged in this step - the same values) and current-chunk
+      // tokens that are not staged (read from the fresh buffer).
+      uint32_t smk[4], fmk[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int tj = 32 * q + lane, ps_ = page_pos + tj;
         const bool in = ps_ >= kv_begin && ps_ < kv_stop;
-        vm[q] = __ballot_sync(0xffffffffu, in && (ps_ >= prefix || (staging && own[tj] == blk)));
+        const bool stg = in && staging && own[tj] == blk;
+        const bool frs = in && !stg && ps_ >= prefix;
+        smk[q] = __ballot_sync(0xffffffffu, stg);
+        fmk[q] = __ballot_sync(0xffffffffu, frs);
       }
-      const bool any_val = (vm[0] | vm[1] | vm[2] | vm[3]) != 0u;
       sm100::tc_fence_after();
       {
         // K codes of token ct -> 128 columns of fp16 pairs
         const int j = ct, pos = page_pos + j;
         const bool in = pos >= kv_begin && pos < kv_stop;
-        const int kind = !in ? 0 : pos >= prefix ? 1 : (staging && own[j] == blk) ? 2 : 3;
+        const bool stg_j = in && staging && own[j] == blk;
+        const int kind = !in ? 0 : stg_j ? 2 : pos >= prefix ? 1 : 3;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
@@ -421,32 +427,47 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
               r[8 * q + 4 + e] = y4[e];
             }
           }
-          if (any_val) {
-            // Value tokens: their halves of the fp16 pairs come from memory.  The loads are
-            // unconditional (a non-value token reads a harmless fixed element), so a batch
-            // of 8 is in flight at once; every register index is static.
-            const uint32_t mw0 = vm[2 * hf], mw1 = vm[2 * hf + 1];
+          const uint32_t sm0 = smk[2 * hf], sm1 = smk[2 * hf + 1];
+          if ((sm0 | sm1) != 0u) {
+            // staged tokens: this dim's 64 values of the page half are contiguous fp32 in
+            // the dim-major staging arena - 16 independent 16-byte loads
+            const float4* srow = reinterpret_cast<const float4*>(
+                p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage + (long long)d * kPage + hf * 64);
+            float4 sv4[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) sv4[q] = __ldg(srow + q);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const float2 f = (k & 1) ? make_float2(sv4[k >> 1].z, sv4[k >> 1].w) : make_float2(sv4[k >> 1].x, sv4[k >> 1].y);
+              const uint32_t hv = mma::h2_u32(f.x, f.y);
+              const int tl = 2 * k;
+              const uint32_t b0 = ((tl < 32 ? sm0 >> tl : sm1 >> (tl - 32)) & 1u);
+              const uint32_t b1 = ((tl + 1 < 32 ? sm0 >> (tl + 1) : sm1 >> (tl - 31)) & 1u);
+              const uint32_t keep = (b0 ? 0u : 0x0000ffffu) | (b1 ? 0u : 0xffff0000u);
+              r[k] = (r[k] & keep) | (hv & ~keep);
+            }
+          }
+          const uint32_t fm0 = fmk[2 * hf], fm1 = fmk[2 * hf + 1];
+          if ((fm0 | fm1) != 0u) {
+            // current-chunk tokens without a staging seat (staging off, or lost a seat
+            // collision): fp16 values from the fresh buffer, 8 loads in flight at a time
 #pragma unroll
             for (int g8 = 0; g8 < 8; ++g8) {
               float v[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const int tl = 8 * g8 + e, tj = hf * 64 + tl, ps_ = page_pos + tj;
-                const bool isval = ((tl < 32 ? mw0 >> tl : mw1 >> (tl - 32)) & 1u) != 0u;
-                const bool fresh = ps_ >= prefix;
-                const long long fi = (isval && fresh) ? ((long long)(q0 + ps_ - prefix) * p.Hk + hk) * kD + d : 0;
-                const long long si = (isval && !fresh) ? ((long long)(sbase + tj) * p.Hk + hk) * kD + d : 0;
-                const float fv = __half2float(p.v_fresh[fi]);
-                const float sv = staging ? __ldg(p.stage_v + si) : 0.f;
-                v[e] = fresh ? fv : sv;
+                const bool isf = ((tl < 32 ? fm0 >> tl : fm1 >> (tl - 32)) & 1u) != 0u;
+                const long long fi = isf ? ((long long)(q0 + ps_ - prefix) * p.Hk + hk) * kD + d : 0;
+                v[e] = __half2float(p.v_fresh[fi]);
               }
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const int tl = 8 * g8 + e, k = tl >> 1;
-                const bool isval = ((tl < 32 ? mw0 >> tl : mw1 >> (tl - 32)) & 1u) != 0u;
+                const bool isf = ((tl < 32 ? fm0 >> tl : fm1 >> (tl - 32)) & 1u) != 0u;
                 const uint32_t hv = (uint32_t)__half_as_ushort(__float2half_rn(v[e]));
                 const uint32_t nv = (tl & 1) ? ((r[k] & 0x0000ffffu) | (hv << 16)) : ((r[k] & 0xffff0000u) | hv);
-                r[k] = isval ? nv : r[k];
+                r[k] = isf ? nv : r[k];
               }
             }
           }
@@ -550,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       const int s = i % kRing, b = i & 1;
       bool ok = !dead && sm100::mbar_wait(&B.s_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
                                           kBudgetNs);
+      if (st == 0 && i < 4) trace(48 + 4 * i);
       float sc[N];
       if (ok) {
         uint32_t raw[N];
@@ -597,11 +619,13 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       // P' buffer b (and alpha/upd slot b) are free once P.V(i-2) and the stats of page i-2 are done
       if (ok && i >= 2)
         ok = sm100::mbar_wait(&B.p_empty[b], ((i >> 1) - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
+      if (st == 0 && i < 4) trace(49 + 4 * i);
       if (sm100::bar_red_or(kBarSoft, 128, !ok)) {
         aborted = true;
         break;
       }
       const bool upd_now = sm100::bar_red_or(kBarSoft, 128, need);
+      if (st == 0 && i < 4) trace(50 + 4 * i);
       if (upd_now) {
         // agree on the new row maxima
         {

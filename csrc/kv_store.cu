@@ -306,10 +306,17 @@ __global__ void __launch_bounds__(kThreads, 2) kv_rotate_kernel(StoreParams p, i
     if (p.stage_seat) {
       const int seat = p.stage_seat[t];
       if (seat >= 0) {
-        float* st = (is_v ? p.stage_v : p.stage_k) + ((long long)seat * Hk + h) * D + lane * n;
+        if (is_v) {  // dim-major per row: [row][Hk][D][128]
+          float* st = p.stage_v + ((long long)(seat / kPage) * Hk + h) * D * kPage + seat % kPage;
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (e < n) st[e] = x[e];
+          for (int e = 0; e < 8; ++e)
+            if (e < n) st[(long long)(lane * n + e) * kPage] = x[e];
+        } else {  // token-major: [row * 128 + off][Hk][D]
+          float* st = p.stage_k + ((long long)seat * Hk + h) * D + lane * n;
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e < n) st[e] = x[e];
+        }
       }
     }
     const int slot = p.slots[t];

@@ -60,7 +60,7 @@ struct StoreParams {
   __nv_bfloat16* vc;
   const int* slots;  // [T]
   float* stage_k;    // [rows * 128, Hk, D]
-  float* stage_v;
+  float* stage_v;  // [rows][Hk][D][128] (dim-major per row); stage_k: [rows * 128][Hk][D]
   const int* stage_seat;  // [T]: seat if this token is kept and wins its seat, else -1
   int* owner;             // [rows * 128]
   const int* owner_seat;  // [n_owner]
@@ -82,7 +82,7 @@ struct AttnParams {
   const __nv_bfloat16* kc;  // [blocks, 128, Hk, D]
   const __nv_bfloat16* vc;
   const float* stage_k;  // [rows * 128, Hk, D]
-  const float* stage_v;
+  const float* stage_v;  // [rows][Hk][D][128]
   const int* owner;  // [rows * 128]
   int stage_rows;    // 0: staging disabled
   const int* block_tables;

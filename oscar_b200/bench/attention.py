@@ -76,13 +76,21 @@ def build_case(hist: int, batch: int, qlen: int, hq: int = 6, hk: int = 1, D: in
     if staging:
         rows = 64
         sk = torch.randn(rows * 128, hk, D, generator=g)
-        sv = torch.randn(rows * 128, hk, D, generator=g)
+        sv = torch.randn(rows, hk, D, 128, generator=g)
         owner = torch.full((rows * 128,), -1, dtype=torch.int32)
         for r in range(batch):  # sink page and the last two pages of every request
             for p in {0, pages[r] - 2, pages[r] - 1}:
                 if p >= 0:
                     b = int(bt[r, p])
                     owner.view(rows, 128)[b % rows] = b
+            # the current chunk's tokens are staged with their own (fresh) values, as the
+            # store kernel does in serving
+            for i in range(qlen):
+                pos = hist + i
+                b, off = int(bt[r, pos // 128]), pos % 128
+                t = r * qlen + i
+                sk[(b % rows) * 128 + off] = kf[t].float()
+                sv[b % rows, :, :, off] = vf[t].float()
         stage = (sk.to(dev), sv.to(dev), owner.to(dev), rows)
     d = lambda t: t.to(dev)  # noqa: E731
     tok_req = torch.repeat_interleave(torch.arange(batch), torch.tensor([qlen] * batch)).to(torch.int32)

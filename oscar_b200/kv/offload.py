@@ -148,7 +148,9 @@ class HostKVStore:
             sel = seats[maskd]
             for layer in m.full_layers:
                 if layer.stage_k is not None:
-                    dev_t += [layer.stage_k.index_select(0, sel), layer.stage_v.index_select(0, sel)]
+                    # V staging is dim-major per row: gather [n, Hk, D] at (row, :, :, off)
+                    dev_t += [layer.stage_k.index_select(0, sel),
+                              layer.stage_v[sel // PAGE, :, :, sel % PAGE].contiguous()]
                     n_staged += 1
             m.owner[sel] = -1  # these seats stop belonging to blocks that are about to be reused
             dev_t.append(maskd)
@@ -223,7 +225,7 @@ class HostKVStore:
                 if layer.stage_k is not None:
                     k, v = next(it)
                     layer.stage_k.index_copy_(0, sel, k)
-                    layer.stage_v.index_copy_(0, sel, v)
+                    layer.stage_v[sel // PAGE, :, :, sel % PAGE] = v
         s = torch.tensor([slot], dtype=torch.long, device=dev)
         for g in m.gdn_layers:
             for t, dim in self._gdn_views(g):

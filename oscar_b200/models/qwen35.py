@@ -186,7 +186,10 @@ class FullAttentionLayer:
             if stage_rows:
                 self.stage_k = torch.zeros(stage_rows * fmt.PAGE, self.Hk, self.D, dtype=torch.float32,
                                            device=device)
-                self.stage_v = torch.zeros_like(self.stage_k)
+                # V staging is dim-major per row (the attention kernels read one dim's
+                # 128 tokens contiguously)
+                self.stage_v = torch.zeros(stage_rows, self.Hk, self.D, fmt.PAGE, dtype=torch.float32,
+                                           device=device)
         else:
             self.kc = torch.zeros(num_blocks, fmt.PAGE, self.Hk, self.D, dtype=torch.bfloat16, device=device)
             self.vc = torch.zeros_like(self.kc)

@@ -167,7 +167,7 @@ def kv_store(qkv, *, q_off, q_head_stride, k_off, v_off, Hq, Hk, D, q_norm_w, k_
         if sel.numel():
             seats = stage_seat[sel].long()
             stage_k.view(-1, Hk, D)[seats] = kr[sel]
-            stage_v.view(-1, Hk, D)[seats] = vr[sel]
+            stage_v.view(-1, Hk, D, fmt.PAGE)[seats // fmt.PAGE, :, :, seats % fmt.PAGE] = vr[sel]
     valid = torch.nonzero(slots >= 0, as_tuple=True)[0]
     if valid.numel() == 0:
         return
@@ -199,7 +199,7 @@ def _history_fp16(kv_mode, pool, kc, vc, stage, bt_row, count, hk_idx, D):
         r = blocks % rows
         hit = (owner.view(rows, fmt.PAGE)[r, offs].long() == blocks).unsqueeze(-1)
         k = torch.where(hit, sk.view(rows, fmt.PAGE, -1, D)[r, offs, hk_idx], k)
-        v = torch.where(hit, sv.view(rows, fmt.PAGE, -1, D)[r, offs, hk_idx], v)
+        v = torch.where(hit, sv.view(rows, -1, D, fmt.PAGE)[r, hk_idx, :, offs], v)
     return k.half().float(), v.half().float()
 
 
@@ -247,7 +247,8 @@ def attention(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, s
               part_o=None, part_lse=None, status=None, rv_merge_split=None):
     """Attention + merge.  Returns ``(o_bf16 | None, o_int8 | None, o_scale | None)``.
 
-    ``stage`` is ``(stage_k, stage_v, owner, rows)`` or ``None``; ``gate`` is the bf16
+    ``stage`` is ``(stage_k [rows*128, Hk, D], stage_v [rows, Hk, D, 128], owner, rows)`` or
+    ``None``; ``gate`` is the bf16
     qkv buffer view whose ``[t, h*gate_hstride + d]`` element gates output ``(t, h, d)``.
     """
     T = q.shape[0]

@@ -94,7 +94,7 @@ def _paged_case(seqs, qlens, hq, hk, seed, stage_pages=(), dev="cuda", use_tc=Tr
     pool = _random_pool(nb, hk, D, g)
     rows = 8
     sk = torch.randn(rows * 128, hk, D, generator=g)
-    sv = torch.randn(rows * 128, hk, D, generator=g)
+    sv = torch.randn(rows, hk, D, 128, generator=g)
     owner = torch.full((rows * 128,), -1, dtype=torch.int32)
     for r, p, cnt in stage_pages:  # staging hits on (request, page), first cnt tokens
         b = int(bt[r, p])
@@ -201,7 +201,7 @@ def _full_backend_case(window: bool, hist: int = 24579, qlen: int = 4) -> float:
     d = lambda t: t.to(dev)  # noqa: E731
     st = None
     if stage is not None:
-        st = (d(stage.k.view(rows * 128, hk, D)), d(stage.v.view(rows * 128, hk, D)),
+        st = (d(stage.k.view(rows * 128, hk, D)), d(stage.v.permute(0, 2, 3, 1).contiguous()),
               d(stage.owner.view(-1).to(torch.int32)), rows)
     qr, knr, vnr = (q @ Rk).half(), (kn @ Rk).half(), (vn @ Rv).half()
     plan_ = A.plan_attention([0, qlen], [hist + qlen], hq // hk, hk, F.num_sms(torch.device(dev)), dev)

@@ -143,7 +143,7 @@ def test_kv_store_matches_ref(rot):
         tens = lambda t: None if t is None else t.to(dev)  # noqa: E731
         pool = torch.zeros(nb, Hk, fmt.page_head_bytes(D), dtype=torch.uint8, device=dev)
         sk = torch.zeros(rows * 128, Hk, D, device=dev)
-        sv = torch.zeros_like(sk)
+        sv = torch.zeros(rows, Hk, D, 128, device=dev)
         owner = torch.full((rows * 128,), -1, dtype=torch.int32, device=dev)
         qo = torch.empty(T, Hq, D, dtype=torch.float16, device=dev)
         kf = torch.empty(T, Hk, D, dtype=torch.float16, device=dev)
@@ -248,7 +248,7 @@ def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
     vz.copy_((-torch.rand(vz.shape) - 0.3).half())
     rows = 4
     sk = torch.randn(rows * 128, Hk, D)
-    sv = torch.randn(rows * 128, Hk, D)
+    sv = torch.randn(rows, Hk, D, 128)
     owner = torch.full((rows * 128,), -1, dtype=torch.int32)
     # mark a few staged tokens for request 0: its first page and a later page
     b0 = int(bt[0, 0])
