@@ -17,6 +17,7 @@ int oscar_kv_store(const oscar::StoreParams* p, cudaStream_t stream);
 int oscar_paged_attention(const oscar::AttnParams* p, cudaStream_t stream);
 int oscar_int2_attention_tc(const oscar::AttnParams* p, int rows_per_item, cudaStream_t stream);
 int oscar_attn_tc_trace(unsigned long long* buf);
+int oscar_bf16_attention_tc(const oscar::AttnParams* p, long long num_blocks, int rows_per_item, cudaStream_t stream);
 int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
 int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi, const __nv_bfloat16* Rv_lo,
                          cudaStream_t stream);
@@ -261,6 +262,8 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
   // INT2 items of <= 32 rows (decode / MTP verify) run on the tcgen05 kernel
   if (kv_mode == 0 && rows_per_item > 0 && rows_per_item <= 32)
     check_rc(oscar_int2_attention_tc(&p, (int)rows_per_item, stream()), "paged_attention(tcgen05)");
+  else if (kv_mode == 1 && rows_per_item > 0 && rows_per_item <= 32)
+    check_rc(oscar_bf16_attention_tc(&p, kc->size(0), (int)rows_per_item, stream()), "paged_attention(bf16 tcgen05)");
   else
     check_rc(oscar_paged_attention(&p, stream()), "paged_attention");
 }

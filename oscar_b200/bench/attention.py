@@ -8,7 +8,9 @@ continuation of 9256 new tokens over a 15360-token INT2 history.  Variants:
 
 * ``int2_tc``   - the tcgen05/TMEM kernel (work items of <= 32 rows),
 * ``int2_mma``  - the warp-level mma.sync kernel,
-* ``bf16``      - the same attention over a BF16 KV cache (the uncompressed baseline).
+* ``bf16_tc``   - the same attention over a BF16 KV cache (the uncompressed baseline) on
+                  the tcgen05 BF16 kernel (TMA-fed, <= 32 rows per item),
+* ``bf16``      - BF16 KV on the warp-level mma.sync kernel.
 
 Each variant is checked against the first one on the merged output (rtol 1e-2),
 then the attention kernel alone is timed with CUDA events, L2 flushed before every
@@ -72,6 +74,11 @@ def build_case(hist: int, batch: int, qlen: int, hq: int = 6, hk: int = 1, D: in
     kf = torch.randn(T, hk, D, generator=g).half()
     vf = torch.randn(T, hk, D, generator=g).half()
     q_start = [0] + list(np.cumsum([qlen] * batch))
+    for r in range(batch):  # the store writes the current chunk into the BF16 cache first
+        for i in range(qlen):
+            pos = hist + i
+            kc[int(bt[r, pos // 128]), pos % 128] = kf[r * qlen + i].to(torch.bfloat16)
+            vc[int(bt[r, pos // 128]), pos % 128] = vf[r * qlen + i].to(torch.bfloat16)
     stage = None
     if staging:
         rows = 64
@@ -135,21 +142,23 @@ def kv_bytes(c, kv_mode: int) -> int:
     return c["pages"] * c["hk"] * per_page
 
 
-def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16")):
+def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16_tc", "bf16")):
     c = build_case(hist, batch, qlen)
     rows = qlen * c["hq"] // c["hk"]
-    vs = [v for v in variants if not (v == "int2_tc" and rows > 32)]
+    vs = [v for v in variants if not (v.endswith("_tc") and rows > 32)]
     # numerics: merged outputs against the first variant
     outs = {}
     for v in vs:
-        outs[v] = _attention(c, 0 if v.startswith("int2") else 1, v == "int2_tc").float()
+        outs[v] = _attention(c, 0 if v.startswith("int2") else 1, v.endswith("_tc")).float()
     ref = outs[vs[0]]
     errs = {v: float((outs[v] - ref).norm() / ref.norm()) for v in vs}
-    # the INT2 variants read the same cache and must agree; BF16 reads another cache
-    for v in vs:
-        if v.startswith("int2") and vs[0].startswith("int2"):
-            assert errs[v] < 1e-2, f"{v} disagrees with {vs[0]}: {errs[v]:.3e}"
-    fns = {v: _kernel_only(c, 0 if v.startswith("int2") else 1, v == "int2_tc") for v in vs}
+    # variants that read the same cache must agree (the BF16 cache is another cache)
+    for fam in ("int2", "bf16"):
+        fv = [v for v in vs if v.startswith(fam)]
+        for v in fv[1:]:
+            e = float((outs[v] - outs[fv[0]]).norm() / outs[fv[0]].norm())
+            assert e < 1e-2, f"{v} disagrees with {fv[0]}: {e:.3e}"
+    fns = {v: _kernel_only(c, 0 if v.startswith("int2") else 1, v.endswith("_tc")) for v in vs}
     tim = compare_calls(fns, iters=iters, flush=True)
     peak = _peak_gbs()
     res = []

@@ -216,7 +216,7 @@ def _build_cache(dev, Hk, D, seqs, qlens, seed, stage_rows=0, kv_mode=0):
 @pytest.mark.parametrize("use_tc", [True, False], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("case", ["decode", "mtp", "mixed", "bf16", "long"])
 def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
-    if not use_tc and case in ("mixed", "bf16"):
+    if not use_tc and case == "mixed":
         pytest.skip("same kernel as the tcgen05 run")
     monkeypatch.setattr(A, "USE_TC", use_tc)
     torch.manual_seed(1)
@@ -258,6 +258,13 @@ def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
     kf = torch.randn(T, Hk, D).half()
     vf = torch.randn(T, Hk, D).half()
     q_start = [0] + list(np.cumsum(qlens))
+    # the store writes the current chunk into the BF16 cache before attention reads it
+    for r in range(R):
+        for i in range(qlens[r]):
+            pos = seqs[r] - qlens[r] + i
+            b, o = int(bt[r, pos // 128]), pos % 128
+            kc[b, o] = kf[q_start[r] + i].to(torch.bfloat16)
+            vc[b, o] = vf[q_start[r] + i].to(torch.bfloat16)
     stage_cpu = (sk, sv, owner, rows) if kv_mode == 0 else None
     ref_b, ref_q, ref_s = A.attention(q, kf, vf, Hq=Hq, Hk=Hk, D=D, scale=1 / 16, kv_mode=kv_mode, pool=pool, kc=kc,
                                       vc=vc, stage=stage_cpu, block_tables=bt, q_start_t=None, seq_lens_t=None,
