@@ -60,11 +60,141 @@ constexpr uint32_t kColK = 0, kColV = 128, kColS = 384, kColO = 448, kTmemCols =
 constexpr int kBarConv = 2, kBarSoft = 1, kBarStats = 3;
 
 // Optional per-CTA event timeline (globaltimer ns) for performance analysis; off
-// unless a buffer was installed with oscar_attn_tc_trace (slot layout: 64 u64 per CTA).
+// unless a buffer was installed with oscar_attn_tc_trace (slot layout: 96 u64 per CTA).
 __device__ unsigned long long* g_tc_trace = nullptr;
+constexpr int kTraceSlots = 96;
 OSCAR_DEVICE void trace(int ev) {
   unsigned long long* t = g_tc_trace;
-  if (t != nullptr && ev < 64) t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * 64 + ev] = globaltimer_ns();
+  if (t != nullptr && ev < kTraceSlots)
+    t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * kTraceSlots + ev] = globaltimer_ns();
+}
+// Same, ordered after the computation of `dep` (the timer read consumes it).
+OSCAR_DEVICE void trace_dep(int ev, float dep) {
+  unsigned long long* t = g_tc_trace;
+  if (t != nullptr && ev < kTraceSlots) {
+    uint64_t v;
+    asm volatile("{\n\t.reg .f32 d;\n\tmov.f32 d, %1;\n\tmov.u64 %0, %%globaltimer;\n\t}" : "=l"(v) : "f"(dep));
+    t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * kTraceSlots + ev] = v;
+  }
+}
+
+// ---- out-of-line rare paths.  Pages holding value tokens (the current chunk, staged
+// sink/recent tokens) are a few per request; their merge code is kept out of the
+// per-page loop so the common path of every role stays resident in the
+// instruction cache (the whole kernel is larger than it).
+
+// 32 fp16 pairs of 64 K codes (one 16-byte chunk of a token's codes).
+OSCAR_DEVICE void k_chunk_codes(const uint8_t* pg, int j, int c, uint32_t (&r)[32]) {
+  const uint4 cw = *reinterpret_cast<const uint4*>(pg + j * 64 + ((c ^ ((j >> 1) & 3)) << 4));
+  const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t a4[4], b4[4];
+    mma::codes8_to_h2(wd[q], a4);
+    mma::codes8_to_h2(wd[q] >> 8, b4);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      r[8 * q + e] = a4[e];
+      r[8 * q + 4 + e] = b4[e];
+    }
+  }
+}
+
+// K row of a warp in which some token carries values: lane j writes fp16 values
+// (kind 1: fresh fp16 row `kf`, kind 2: staged fp32 row `sk`) or its codes.
+__device__ __noinline__ void k_row_mixed(uint32_t taddr, const uint8_t* pg, int j, int kind, const __half* kf,
+                                         const float* sk) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    if (kind == 1) {
+      const uint4* src = reinterpret_cast<const uint4*>(kf + 64 * c);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint4 v = __ldg(src + q);
+        r[4 * q] = v.x;
+        r[4 * q + 1] = v.y;
+        r[4 * q + 2] = v.z;
+        r[4 * q + 3] = v.w;
+      }
+    } else if (kind == 2) {
+      const float4* src = reinterpret_cast<const float4*>(sk + 64 * c);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const float4 v = __ldg(src + q);
+        r[2 * q] = mma::h2_u32(v.x, v.y);
+        r[2 * q + 1] = mma::h2_u32(v.z, v.w);
+      }
+    } else {
+      k_chunk_codes(pg, j, c, r);
+    }
+    sm100::tmem_st_32x32b_x32(taddr + 32 * c, r);
+  }
+}
+
+// 64 tokens of V^T row d (one page half) when some of them carry values: staged
+// tokens (mask sm, from the dim-major staging row `srow`, may be null when sm == 0)
+// and current-chunk tokens without a staging seat (mask fm, fp16 from the fresh
+// buffer: token tl at vf[fbase + tl * fstride]).  Codes elsewhere.
+__device__ __noinline__ void v_half_mixed(uint32_t taddr, uint4 cw, uint64_t sm, uint64_t fm, const float* srow,
+                                          const __half* vf, long long fbase, long long fstride) {
+  uint32_t r[32];
+  const uint32_t w4[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t x4[4], y4[4];
+    mma::codes8_to_h2(w4[q], x4);
+    mma::codes8_to_h2(w4[q] >> 8, y4);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      r[8 * q + e] = x4[e];
+      r[8 * q + 4 + e] = y4[e];
+    }
+  }
+  if (sm != 0ull) {
+    const float4* s4 = reinterpret_cast<const float4*>(srow);
+#pragma unroll 4
+    for (int q = 0; q < 16; ++q) {
+      const float4 v = __ldg(s4 + q);
+      const uint32_t lo = mma::h2_u32(v.x, v.y), hi = mma::h2_u32(v.z, v.w);
+      const uint32_t m = (uint32_t)(sm >> (4 * q)) & 15u;  // tokens 4q .. 4q + 3
+      const uint32_t k0 = ((m & 1u) ? 0u : 0x0000ffffu) | ((m & 2u) ? 0u : 0xffff0000u);
+      const uint32_t k1 = ((m & 4u) ? 0u : 0x0000ffffu) | ((m & 8u) ? 0u : 0xffff0000u);
+      r[2 * q] = (r[2 * q] & k0) | (lo & ~k0);
+      r[2 * q + 1] = (r[2 * q + 1] & k1) | (hi & ~k1);
+    }
+  }
+  while (fm != 0ull) {
+    const int tl = __ffsll((long long)fm) - 1;
+    fm &= fm - 1ull;
+    const uint32_t hv = (uint32_t)__half_as_ushort(vf[fbase + (long long)tl * fstride]);
+    const int k = tl >> 1;
+#pragma unroll
+    for (int kk = 0; kk < 32; ++kk)
+      if (kk == k) r[kk] = (tl & 1) ? ((r[kk] & 0x0000ffffu) | (hv << 16)) : ((r[kk] & 0xffff0000u) | hv);
+  }
+  sm100::tmem_st_32x32b_x32(taddr, r);
+}
+
+// O^T (both halves, N columns each) scaled by alpha[r] per row column r.
+template <int N>
+__device__ __noinline__ void rescale_o(uint32_t taddr, const float* alpha) {
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    uint32_t o[N];
+    if constexpr (N == 32)
+      sm100::tmem_ld_32x32b_x32(taddr + h * N, o);
+    else
+      sm100::tmem_ld_32x32b_x16(taddr + h * N, o);
+    sm100::tmem_ld_wait();
+#pragma unroll
+    for (int r = 0; r < N; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
+    if constexpr (N == 32)
+      sm100::tmem_st_32x32b_x32(taddr + h * N, o);
+    else
+      sm100::tmem_st_32x32b_x16(taddr + h * N, o);
+  }
+  sm100::tmem_st_wait();
 }
 
 template <int N>
@@ -351,48 +481,19 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         const bool in = pos >= kv_begin && pos < kv_stop;
         const bool stg_j = in && staging && own[j] == blk;
         const int kind = !in ? 0 : stg_j ? 2 : pos >= prefix ? 1 : 3;
+        if (__any_sync(0xffffffffu, kind == 1 || kind == 2)) {
+          const __half* kf = kind == 1 ? p.k_fresh + ((long long)(q0 + pos - prefix) * p.Hk + hk) * kD : nullptr;
+          const float* sk = kind == 2 ? p.stage_k + ((long long)((blk % p.stage_rows) * kPage + j) * p.Hk + hk) * kD
+                                      : nullptr;
+          k_row_mixed(tbase + lrow + kColK, pg, j, kind, kf, sk);
+        } else {
+          // out-of-range tokens keep their (finite) codes: their scores are masked
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          if (kind == 3) {
-            const uint4 cw = *reinterpret_cast<const uint4*>(pg + j * 64 + ((c ^ ((j >> 1) & 3)) << 4));
-            const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t a4[4], b4[4];
-              mma::codes8_to_h2(wd[q], a4);
-              mma::codes8_to_h2(wd[q] >> 8, b4);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                r[8 * q + e] = a4[e];
-                r[8 * q + 4 + e] = b4[e];
-              }
-            }
-          } else if (kind == 1) {
-            const uint4* src = reinterpret_cast<const uint4*>(
-                p.k_fresh + ((long long)(q0 + pos - prefix) * p.Hk + hk) * kD + 64 * c);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint4 v = __ldg(src + q);
-              r[4 * q] = v.x;
-              r[4 * q + 1] = v.y;
-              r[4 * q + 2] = v.z;
-              r[4 * q + 3] = v.w;
-            }
-          } else if (kind == 2) {
-            const float4* src = reinterpret_cast<const float4*>(
-                p.stage_k + ((long long)((blk % p.stage_rows) * kPage + j) * p.Hk + hk) * kD + 64 * c);
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const float4 v = __ldg(src + q);
-              r[2 * q] = mma::h2_u32(v.x, v.y);
-              r[2 * q + 1] = mma::h2_u32(v.z, v.w);
-            }
-          } else {
-#pragma unroll
-            for (int q = 0; q < 32; ++q) r[q] = 0u;
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            k_chunk_codes(pg, j, c, r);
+            sm100::tmem_st_32x32b_x32(tbase + lrow + kColK + 32 * c, r);
           }
-          sm100::tmem_st_32x32b_x32(tbase + lrow + kColK + 32 * c, r);
         }
         sm100::tmem_st_wait();
         sm100::tc_fence_before();
@@ -406,72 +507,40 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
                                       kTimeoutAccEmpty, kBudgetNs))
         break;
       sm100::tc_fence_after();
-      const int sbase = staging ? (blk % p.stage_rows) * kPage : 0;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         const int d = ct + 128 * h;
         const uint4* src = reinterpret_cast<const uint4*>(pg + kPage * 64 + d * 32);
-        const uint4 a4 = src[0], b4 = src[1];
-        const uint32_t wd[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
+#pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {
-          uint32_t r[32];
+          const uint4 cw = src[hf];
+          const uint32_t taddr = tbase + lrow + kColV + (i & 1) * 128 + h * 64 + hf * 32;
+          const uint64_t sm = hf ? ((uint64_t)smk[3] << 32) | smk[2] : ((uint64_t)smk[1] << 32) | smk[0];
+          const uint64_t fm = hf ? ((uint64_t)fmk[3] << 32) | fmk[2] : ((uint64_t)fmk[1] << 32) | fmk[0];
+          if ((sm | fm) != 0ull) {
+            // staged tokens: this dim's 64 values of the page half are contiguous fp32
+            // in the dim-major staging arena
+            const float* srow = sm != 0ull ? p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage +
+                                                 (long long)d * kPage + hf * 64
+                                           : nullptr;
+            const long long fbase = ((long long)(q0 + page_pos + hf * 64 - prefix) * p.Hk + hk) * kD + d;
+            v_half_mixed(taddr, cw, sm, fm, srow, p.v_fresh, fbase, (long long)p.Hk * kD);
+          } else {
+            uint32_t r[32];
+            const uint32_t w4[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t x4[4], y4[4];
-            mma::codes8_to_h2(wd[4 * hf + q], x4);
-            mma::codes8_to_h2(wd[4 * hf + q] >> 8, y4);
+            for (int q = 0; q < 4; ++q) {
+              uint32_t x4[4], y4[4];
+              mma::codes8_to_h2(w4[q], x4);
+              mma::codes8_to_h2(w4[q] >> 8, y4);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              r[8 * q + e] = x4[e];
-              r[8 * q + 4 + e] = y4[e];
-            }
-          }
-          const uint32_t sm0 = smk[2 * hf], sm1 = smk[2 * hf + 1];
-          if ((sm0 | sm1) != 0u) {
-            // staged tokens: this dim's 64 values of the page half are contiguous fp32 in
-            // the dim-major staging arena - 16 independent 16-byte loads
-            const float4* srow = reinterpret_cast<const float4*>(
-                p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage + (long long)d * kPage + hf * 64);
-            float4 sv4[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) sv4[q] = __ldg(srow + q);
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              const float2 f = (k & 1) ? make_float2(sv4[k >> 1].z, sv4[k >> 1].w) : make_float2(sv4[k >> 1].x, sv4[k >> 1].y);
-              const uint32_t hv = mma::h2_u32(f.x, f.y);
-              const int tl = 2 * k;
-              const uint32_t b0 = ((tl < 32 ? sm0 >> tl : sm1 >> (tl - 32)) & 1u);
-              const uint32_t b1 = ((tl + 1 < 32 ? sm0 >> (tl + 1) : sm1 >> (tl - 31)) & 1u);
-              const uint32_t keep = (b0 ? 0u : 0x0000ffffu) | (b1 ? 0u : 0xffff0000u);
-              r[k] = (r[k] & keep) | (hv & ~keep);
-            }
-          }
-          const uint32_t fm0 = fmk[2 * hf], fm1 = fmk[2 * hf + 1];
-          if ((fm0 | fm1) != 0u) {
-            // current-chunk tokens without a staging seat (staging off, or lost a seat
-            // collision): fp16 values from the fresh buffer, 8 loads in flight at a time
-#pragma unroll
-            for (int g8 = 0; g8 < 8; ++g8) {
-              float v[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const int tl = 8 * g8 + e, tj = hf * 64 + tl, ps_ = page_pos + tj;
-                const bool isf = ((tl < 32 ? fm0 >> tl : fm1 >> (tl - 32)) & 1u) != 0u;
-                const long long fi = isf ? ((long long)(q0 + ps_ - prefix) * p.Hk + hk) * kD + d : 0;
-                v[e] = __half2float(p.v_fresh[fi]);
-              }
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const int tl = 8 * g8 + e, k = tl >> 1;
-                const bool isf = ((tl < 32 ? fm0 >> tl : fm1 >> (tl - 32)) & 1u) != 0u;
-                const uint32_t hv = (uint32_t)__half_as_ushort(__float2half_rn(v[e]));
-                const uint32_t nv = (tl & 1) ? ((r[k] & 0x0000ffffu) | (hv << 16)) : ((r[k] & 0xffff0000u) | hv);
-                r[k] = isf ? nv : r[k];
+              for (int e = 0; e < 4; ++e) {
+                r[8 * q + e] = x4[e];
+                r[8 * q + 4 + e] = y4[e];
               }
             }
+            sm100::tmem_st_32x32b_x32(taddr, r);
           }
-          sm100::tmem_st_32x32b_x32(tbase + lrow + kColV + (i & 1) * 128 + h * 64 + hf * 32, r);
         }
       }
       sm100::tmem_st_wait();
@@ -588,6 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         for (int r = 0; r < N; ++r) sc[r] = __uint_as_float(raw[r]);
         ok = sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs);
       }
+      if (st == 0 && i < 4) trace(49 + 4 * i);
       float vs = 0.f;
       bool need = false;
       if (ok) {
@@ -609,23 +679,25 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           }
         }
         const bool hist = pos < prefix;
+        if (i < 4) trace_dep(st == 0 ? 64 + 4 * i : kTraceSlots, ks + kz + vs);
 #pragma unroll
         for (int r = 0; r < N; ++r) {
           const bool vis = in && (hist || pos <= lim[r]);
           sc[r] = vis ? fmaf(ks, sc[r], kz * sq[r]) * sl2 : -INFINITY;
           need |= sc[r] > msm[r] + kSlack;
         }
+        if (i < 4) trace_dep(st == 0 ? 65 + 4 * i : kTraceSlots, sc[N - 1] + (need ? 1.f : 0.f));
       }
       // P' buffer b (and alpha/upd slot b) are free once P.V(i-2) and the stats of page i-2 are done
       if (ok && i >= 2)
         ok = sm100::mbar_wait(&B.p_empty[b], ((i >> 1) - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
-      if (st == 0 && i < 4) trace(49 + 4 * i);
+      if (st == 0 && i < 4) trace(50 + 4 * i);
       if (sm100::bar_red_or(kBarSoft, 128, !ok)) {
         aborted = true;
         break;
       }
       const bool upd_now = sm100::bar_red_or(kBarSoft, 128, need);
-      if (st == 0 && i < 4) trace(50 + 4 * i);
+      if (st == 0 && i < 4) trace(51 + 4 * i);
       if (upd_now) {
         // agree on the new row maxima
         {
@@ -653,22 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
                                       kTimeoutAccFull, kBudgetNs);
           if (ok2) {
             sm100::tc_fence_after();
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              uint32_t o[N];
-              if constexpr (N == 32)
-                sm100::tmem_ld_32x32b_x32(tbase + lrow + kColO + h * N, o);
-              else
-                sm100::tmem_ld_32x32b_x16(tbase + lrow + kColO + h * N, o);
-              sm100::tmem_ld_wait();
-#pragma unroll
-              for (int r = 0; r < N; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[b * N + r]);
-              if constexpr (N == 32)
-                sm100::tmem_st_32x32b_x32(tbase + lrow + kColO + h * N, o);
-              else
-                sm100::tmem_st_32x32b_x16(tbase + lrow + kColO + h * N, o);
-            }
-            sm100::tmem_st_wait();
+            rescale_o<N>(tbase + lrow + kColO, alpha + b * N);
             sm100::tc_fence_before();
           }
           ok = ok2;
@@ -708,11 +765,29 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       if (ok && n_pages > 0)
         ok = sm100::mbar_wait(&B.p_empty[(n_pages - 1) & 1], ((n_pages - 1) >> 1) & 1, abort_flag, p.status,
                               kTimeoutAccFull, kBudgetNs);
-      if (ok) {
+      // every softmax warp agrees before the named barrier below
+      if (!sm100::bar_red_or(kBarSoft, 128, !ok)) {
         constexpr int kGroups = 64 / (N / 2);
+        // per-row totals (l_r, C_r) once, into the page-maxima scratch (N x 4 floats)
+        if (st < N) {
+          float Lr = 0.f, Cr = 0.f;
+#pragma unroll
+          for (int q = 0; q < kGroups; ++q) {
+            Lr += fin[q * 2 * N + st];
+            Cr += fin[q * 2 * N + N + st];
+          }
+          const float inv = Lr > 0.f ? 1.f / Lr : 0.f;
+          red[2 * st] = inv;
+          red[2 * st + 1] = Cr * inv;
+          if (st < nrows)
+            p.part_lse[((long long)item * p.Hk + hk) * kPartRows + st] =
+                Lr > 0.f ? (msm[st] + log2f(Lr)) / kLog2e : -INFINITY;
+        }
+        sm100::bar_sync(kBarSoft, 128);
         sm100::tc_fence_after();
         float* po = p.part_o + ((long long)item * p.Hk + hk) * kPartRows * kD;
-#pragma unroll
+        const float2* rc = reinterpret_cast<const float2*>(red);
+#pragma unroll 1
         for (int h = 0; h < 2; ++h) {
           uint32_t o[N];
           if (n_pages > 0) {
@@ -728,22 +803,9 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           const int d = st + 128 * h;
 #pragma unroll
           for (int r = 0; r < N; ++r) {
-            if (r >= nrows) break;
-            float Lr = 0.f, Cr = 0.f;
-#pragma unroll
-            for (int q = 0; q < kGroups; ++q) {
-              Lr += fin[q * 2 * N + r];
-              Cr += fin[q * 2 * N + N + r];
-            }
-            po[r * kD + d] = Lr > 0.f ? (__uint_as_float(o[r]) + Cr) / Lr : 0.f;
+            const float2 f = rc[r];  // (1 / l_r, C_r / l_r)
+            if (r < nrows) po[r * kD + d] = fmaf(__uint_as_float(o[r]), f.x, f.y);
           }
-        }
-        if (st < nrows) {
-          float Lr = 0.f;
-#pragma unroll
-          for (int q = 0; q < kGroups; ++q) Lr += fin[q * 2 * N + st];
-          p.part_lse[((long long)item * p.Hk + hk) * kPartRows + st] =
-              Lr > 0.f ? (msm[st] + log2f(Lr)) / kLog2e : -INFINITY;
         }
       }
     }
