@@ -3,6 +3,7 @@
 // launch error.  There is no CPU fallback here: the Python layer uses the
 // pure-torch oracle only for CPU tensors.
 #include <torch/extension.h>
+#include <cstdlib>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -22,6 +23,8 @@ int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
 int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi, const __nv_bfloat16* Rv_lo,
                          cudaStream_t stream);
 int oscar_gdn_step(const oscar::GdnParams* p, int smem_state, cudaStream_t stream);
+long long oscar_gdn_chunk_ws_bytes(int T, int Hk, int Hv, int max_chunks);
+int oscar_gdn_chunked(oscar::GdnParams* p, int T, void* ws, cudaStream_t stream);
 int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long long ldd, const float* w, float off, float eps,
                         int T, int H, int8_t* out, float* scale, __nv_bfloat16* out_bf16, const unsigned* signals,
                         const int* epoch, int world, int zero_delta, int* status, long long wait_budget_ns,
@@ -366,6 +369,22 @@ void gdn_step(const Tensor& qkvz, const Tensor& ba, int64_t Hk, int64_t Hv, int6
   p.R = req_slot.numel();
   p.status = optr<int>(status);
   const c10::cuda::CUDAGuard guard(qkvz.device());
+  // Prefill steps: requests of >= 16 new tokens (nothing to commit or keep) take the
+  // chunked tensor-core path; it reads qkvz rows with 16-byte loads.
+  const int T = (int)qkvz.size(0);
+  const bool aligned = (p.ld_qkvz % 8 == 0) && (reinterpret_cast<uintptr_t>(p.qkvz) % 16 == 0) && dk == 128 &&
+                       dv == 128;
+  static const bool chunked_on = [] {
+    const char* e = std::getenv("OSCAR_GDN_CHUNKED");
+    return !(e && e[0] == '0');
+  }();
+  if (smem_state && aligned && T >= 16 && chunked_on) {
+    p.long_min = 16;
+    p.max_chunks = T / 64 + p.R;
+    const long long bytes = oscar_gdn_chunk_ws_bytes(T, (int)Hk, (int)Hv, p.max_chunks);
+    Tensor ws = at::empty({bytes}, qkvz.options().dtype(at::kByte));
+    check_rc(oscar_gdn_chunked(&p, T, ws.data_ptr(), stream()), "gdn_chunked");
+  }
   check_rc(oscar_gdn_step(&p, (int)smem_state, stream()), "gdn_step");
 }
 

@@ -60,6 +60,8 @@ __global__ void __launch_bounds__(kThreads) gdn_chunk_kernel(GdnParams p) {
   const int n_all = a + T;
   if (n_all <= 0) return;
   const bool keep = p.keep_pending[req] != 0;
+  // long prefill requests run in the chunked tensor-core path (gdn_chunk.cu)
+  if (p.long_min > 0 && T >= p.long_min && a == 0 && !keep) return;
   const int write_after = keep ? a - 1 : n_all - 1;  // last token included in the stored state
   const int slot = p.req_slot[req];
   const int r = p.Hv / p.Hk;

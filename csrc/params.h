@@ -143,6 +143,19 @@ struct GdnParams {
   __nv_bfloat16* out;       // [T, Hv * dv]
   int R;
   int* status;
+  // Chunked (WY-form) prefill path for requests with long_min <= T tokens, nothing to
+  // commit and nothing kept pending; long_min == 0 disables it.  Workspaces:
+  int long_min;
+  int max_chunks;             // capacity of the per-chunk workspaces (64-token chunks)
+  __nv_bfloat16* ws_q;        // [T, Hk, dk]  conv + SiLU + L2-normalised q (times dk^-1/2)
+  __nv_bfloat16* ws_k;        // [T, Hk, dk]  conv + SiLU + L2-normalised k
+  __nv_bfloat16* ws_v;        // [T, Hv, dv]  conv + SiLU v
+  float* ws_beta;             // [T, Hv]      sigmoid(b)
+  float* ws_lg;               // [T, Hv]      log g
+  __nv_bfloat16* ws_w;        // [chunks, Hv, 64, dk]  W = T diag(beta G) K
+  __nv_bfloat16* ws_ut;       // [chunks, Hv, dv, 64]  U^T, U = T diag(beta) V
+  __nv_bfloat16* ws_p;        // [chunks, Hv, 64, 64]  (G_t / G_s) q_t.k_s for s <= t
+  float* ws_g;                // [chunks, Hv, 64]      cumulative log decay in the chunk
 };
 
 }  // namespace oscar

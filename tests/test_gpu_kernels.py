@@ -337,10 +337,12 @@ def _gdn_inputs(T, Hk, Hv, dk, dv, seed):
     return qkvz, ba, w, conv_dim
 
 
-@pytest.mark.parametrize("mode", ["prefill_long", "decode", "verify_commit"])
+@pytest.mark.parametrize("mode", ["prefill_long", "prefill_mixed", "decode", "verify_commit"])
 def test_gdn_step_matches_ref(mode):
+    """prefill_long / prefill_mixed exercise the chunked (WY) tensor-core path for
+    requests of >= 16 tokens, next to verify and short requests in the same step."""
     Hk, Hv, dk, dv = 2, 6, 128, 128
-    slots, P = 3, 4
+    slots, P = 4, 4
     conv_dim = 2 * Hk * dk + Hv * dv
     gen = torch.Generator().manual_seed(5)
     state0 = (torch.randn(slots, Hv, dk, dv, generator=gen) * 0.1).to(torch.bfloat16)
@@ -349,6 +351,8 @@ def test_gdn_step_matches_ref(mode):
     pb0 = torch.randn(slots, P, 2 * Hv, generator=gen).to(torch.bfloat16)
     if mode == "prefill_long":
         qlens, ncom, keep = [200, 37], [0, 0], [0, 0]
+    elif mode == "prefill_mixed":
+        qlens, ncom, keep = [150, 4, 3, 64], [0, 2, 0, 0], [0, 1, 0, 0]
     elif mode == "decode":
         qlens, ncom, keep = [1, 1, 1], [0, 0, 0], [0, 0, 0]
     else:
@@ -357,7 +361,7 @@ def test_gdn_step_matches_ref(mode):
     T = sum(qlens)
     qkvz, ba, w, _ = _gdn_inputs(T, Hk, Hv, dk, dv, 9)
     q_start = torch.tensor([0] + list(np.cumsum(qlens)), dtype=torch.int32)
-    meta = dict(parity=torch.tensor([0, 1, 0][:R], dtype=torch.int32), req_slot=torch.tensor([2, 0, 1][:R], dtype=torch.int32),
+    meta = dict(parity=torch.tensor([0, 1, 0, 1][:R], dtype=torch.int32), req_slot=torch.tensor([2, 0, 1, 3][:R], dtype=torch.int32),
                 q_start=q_start, n_commit=torch.tensor(ncom, dtype=torch.int32),
                 keep_pending=torch.tensor(keep, dtype=torch.int32))
     res = {}
@@ -365,7 +369,7 @@ def test_gdn_step_matches_ref(mode):
         st, cs, px, pb = (t.clone().to(dev) for t in (state0, conv0, px0, pb0))
         out = torch.zeros(T, Hv * dv, dtype=torch.bfloat16, device=dev)
         gdn_step(qkvz.to(dev), ba.to(dev), Hk=Hk, Hv=Hv, dk=dk, dv=dv, eps=1e-6, state=st, conv_state=cs, pend_x=px,
-                 pend_ba=pb, out=out, smem_state=(mode == "prefill_long"), **{k: v.to(dev) for k, v in w.items()},
+                 pend_ba=pb, out=out, smem_state=mode.startswith("prefill"), **{k: v.to(dev) for k, v in w.items()},
                  **{k: v.to(dev) for k, v in meta.items()})
         res[dev] = [t.cpu() for t in (out, st, cs, px, pb)]
     c, g = res["cpu"], res[DEV]
