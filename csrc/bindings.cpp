@@ -23,6 +23,8 @@ int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
 int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi, const __nv_bfloat16* Rv_lo,
                          cudaStream_t stream);
 int oscar_gdn_step(const oscar::GdnParams* p, int smem_state, cudaStream_t stream);
+int oscar_int2_prefill_tc(const oscar::AttnParams* p, const void* tiles, int n_tiles, long long fresh_rows,
+                          cudaStream_t stream);
 long long oscar_gdn_chunk_ws_bytes(int T, int Hk, int Hv, int max_chunks);
 int oscar_gdn_chunked(oscar::GdnParams* p, int T, void* ws, cudaStream_t stream);
 int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long long ldd, const float* w, float off, float eps,
@@ -217,7 +219,8 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
                      const optional<Tensor>& vc, const optional<Tensor>& stage_k, const optional<Tensor>& stage_v,
                      const optional<Tensor>& owner, int64_t stage_rows, const Tensor& block_tables,
                      const Tensor& q_start, const Tensor& seq_lens, const Tensor& work, Tensor& part_o,
-                     Tensor& part_lse, const optional<Tensor>& status, int64_t rows_per_item) {
+                     Tensor& part_lse, const optional<Tensor>& status, int64_t rows_per_item,
+                     const optional<Tensor>& tiles, int64_t n_tiles, int64_t n_short) {
   CHECK_CUDA(q);
   CHECK_DTYPE(q, at::kHalf);
   CHECK_DTYPE(k_fresh, at::kHalf);
@@ -262,6 +265,43 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
   p.status = optr<int>(status);
   TORCH_CHECK(part_o.numel() >= (int64_t)p.n_work * Hk * 64 * D, "part_o too small");
   const c10::cuda::CUDAGuard guard(q.device());
+  // Steps with prefill ("long") requests: the planner puts the short requests' items
+  // first (decode / verify, split over the KV range) and gives every 64-row block of a
+  // long request one item; INT2 long requests run on the tcgen05 prefill kernel in tiles
+  // of 128 rows, everything else on the warp-level kernel.
+  static const bool prefill_tc = [] {
+    const char* e = std::getenv("OSCAR_ATTN_PREFILL_TC");
+    return !(e && e[0] == '0');
+  }();
+  if (n_tiles > 0 && tiles.has_value() && tiles->defined()) {
+    CHECK_DTYPE((*tiles), at::kInt);
+    TORCH_CHECK(tiles->is_contiguous() && reinterpret_cast<uintptr_t>(tiles->data_ptr()) % 16 == 0,
+                "attention tiles must be contiguous and 16-byte aligned");
+    TORCH_CHECK(n_short >= 0 && n_short <= p.n_work && n_tiles <= tiles->size(0), "attention tiles: bad counts");
+    if (n_short > 0) {
+      oscar::AttnParams ps = p;
+      ps.n_work = (int)n_short;
+      if (kv_mode == 0 && rows_per_item > 0 && rows_per_item <= 32)
+        check_rc(oscar_int2_attention_tc(&ps, (int)rows_per_item, stream()), "paged_attention(tcgen05)");
+      else if (kv_mode == 1 && rows_per_item > 0 && rows_per_item <= 32)
+        check_rc(oscar_bf16_attention_tc(&ps, kc->size(0), (int)rows_per_item, stream()),
+                 "paged_attention(bf16 tcgen05)");
+      else
+        check_rc(oscar_paged_attention(&ps, stream()), "paged_attention");
+    }
+    if (kv_mode == 0 && prefill_tc) {
+      check_rc(oscar_int2_prefill_tc(&p, tiles->data_ptr(), (int)n_tiles, k_fresh.size(0), stream()),
+               "paged_attention(tcgen05 prefill)");
+    } else if (n_short < p.n_work) {
+      oscar::AttnParams pl = p;
+      pl.work = p.work + n_short;
+      pl.n_work = p.n_work - (int)n_short;
+      pl.part_o = p.part_o + n_short * Hk * 64 * D;
+      pl.part_lse = p.part_lse + n_short * Hk * 64;
+      check_rc(oscar_paged_attention(&pl, stream()), "paged_attention");
+    }
+    return;
+  }
   // INT2 items of <= 32 rows (decode / MTP verify) run on the tcgen05 kernel
   if (kv_mode == 0 && rows_per_item > 0 && rows_per_item <= 32)
     check_rc(oscar_int2_attention_tc(&p, (int)rows_per_item, stream()), "paged_attention(tcgen05)");

@@ -6,7 +6,8 @@ Head geometry of one TP4 rank of the target model: Hq = 6, Hk = 1, head_dim 256,
 lengths 1024 / 8192 / 32768, batch 1-32, 1-4 query tokens, plus a prefill
 continuation of 9256 new tokens over a 15360-token INT2 history.  Variants:
 
-* ``int2_tc``   - the tcgen05/TMEM kernel (work items of <= 32 rows),
+* ``int2_tc``   - the tcgen05/TMEM kernels (decode/verify items of <= 32 rows; prefill
+                  chunks in tiles of 128 rows),
 * ``int2_mma``  - the warp-level mma.sync kernel,
 * ``bf16_tc``   - the same attention over a BF16 KV cache (the uncompressed baseline) on
                   the tcgen05 BF16 kernel (TMA-fed, <= 32 rows per item),
@@ -124,13 +125,15 @@ def _kernel_only(c, kv_mode: int, use_tc: bool):
     po = torch.empty(plan.n_work * c["hk"] * A.ROWS * c["D"], dtype=torch.float32, device=c["q"].device)
     pl = torch.empty(plan.n_work * c["hk"] * A.ROWS, dtype=torch.float32, device=c["q"].device)
     sk, sv, own, rows = c["stage"] if (kv_mode == 0 and c["stage"] is not None) else (None, None, None, 0)
-    rpi = A.rows_per_item(c["q_start"], c["hq"] // c["hk"]) if use_tc else 0
+    A.USE_TC = use_tc
+    rpi = A._rpi(plan, c["q_start"], c["hq"] // c["hk"])
+    tiles = plan.tiles if (use_tc and plan.n_tiles > 0) else None
     e = ext()
 
     def run():
         e.paged_attention(c["q"], c["kf"], c["vf"], c["hq"], c["hk"], c["D"], 1 / 16, kv_mode, c["pool"], c["kc"],
                           c["vc"], sk, sv, own, rows, c["bt"], c["q_start_t"], c["seq_lens_t"], plan.work, po, pl,
-                          None, rpi)
+                          None, rpi, tiles, plan.n_tiles if tiles is not None else 0, plan.n_short)
         return None
 
     return run
@@ -145,7 +148,7 @@ def kv_bytes(c, kv_mode: int) -> int:
 def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16_tc", "bf16")):
     c = build_case(hist, batch, qlen)
     rows = qlen * c["hq"] // c["hk"]
-    vs = [v for v in variants if not (v.endswith("_tc") and rows > 32)]
+    vs = [v for v in variants if not (v == "bf16_tc" and rows > 32)]
     # numerics: merged outputs against the first variant
     outs = {}
     for v in vs:
@@ -189,7 +192,7 @@ def main(argv=None):
                 for r in run_case(hist, batch, qlen, args.iters):
                     print(json.dumps(r), flush=True)
     if args.prefill:
-        for r in run_case(15360, 1, 9256, max(3, args.iters // 3), variants=("int2_mma", "bf16")):
+        for r in run_case(15360, 1, 9256, max(3, args.iters // 3), variants=("int2_tc", "int2_mma", "bf16")):
             print(json.dumps(r), flush=True)
 
 

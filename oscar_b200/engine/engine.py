@@ -334,14 +334,17 @@ class LLMEngine:
                 n_blocks = sum((q_start[i + 1] - q_start[i]) * self.g // A.ROWS + 1 for i in range(len(order)))
                 fixed = max(1, (3 * self.sms) // max(1, self.Hk * n_blocks))
             plan_np = A.plan_attention_host(q_start, seq_lens, self.g, self.Hk, self.sms, fixed_splits=fixed)
-            arrays.update(work=plan_np[0], item_first=plan_np[1], item_count=plan_np[2])
+            arrays.update(work=plan_np[0], item_first=plan_np[1], item_count=plan_np[2], tiles=plan_np[5])
             meta["max_rb"], meta["n_work"] = plan_np[3], plan_np[4]
+            meta["n_short"], meta["rpi_short"] = plan_np[6], plan_np[7]
+            meta["n_tiles"] = int((plan_np[5][:, 2] >= 0).sum()) if plan_np[4] > plan_np[6] else 0
         return arrays, meta
 
     def _batch(self, d: dict, meta: dict) -> StepBatch:
         plan = None
         if "work" in d:
-            plan = A.AttnPlan(d["work"], d["item_first"], d["item_count"], meta["max_rb"], meta["n_work"])
+            plan = A.AttnPlan(d["work"], d["item_first"], d["item_count"], meta["max_rb"], meta["n_work"], d["tiles"],
+                              meta["n_tiles"], meta["n_short"], meta["rpi_short"])
         b = StepBatch(
             tokens=d["tokens"], positions=d["positions"], slots=d["slots"], q_start=d["q_start"],
             seq_lens=d["seq_lens"], block_tables=d["bt"], tok_req=d["tok_req"], q_start_l=meta["q_start"],

@@ -31,6 +31,18 @@ ROWS = 64  # rows (query token x head-in-group) per attention work item
 USE_TC = os.environ.get("OSCAR_ATTN_TC", "1") != "0"
 
 
+def _rpi(plan: "AttnPlan", q_start: list[int], g: int) -> int:
+    """Rows per item the decode/verify kernel is instantiated for (0: warp-level kernel)."""
+    if not USE_TC:
+        return 0
+    return plan.rpi_short if plan.n_tiles > 0 else rows_per_item(q_start, g)
+
+
+# INT2 prefill chunks run on the tcgen05 prefill kernel when USE_TC is set (the
+# OSCAR_ATTN_PREFILL_TC=0 environment switch of the extension keeps them on the
+# warp-level kernel for A/B comparisons).
+
+
 def rows_per_item(q_start: list[int], g: int) -> int:
     """Largest number of query rows (q_len x g, capped at ROWS) of any work item."""
     n = max((q_start[i + 1] - q_start[i] for i in range(len(q_start) - 1)), default=0)
@@ -46,18 +58,31 @@ class AttnPlan:
     item_count: torch.Tensor  # [R * max_rb] int32
     max_rb: int
     n_work: int
+    # prefill tiles of 128 rows for the INT2 tensor-core prefill kernel:
+    # [n_tiles, 4] int32 (req, row0, item of rows 0-63, item of rows 64-127 or -1)
+    tiles: torch.Tensor | None = None
+    n_tiles: int = 0
+    n_short: int = -1    # items of the short (decode / verify) requests come first
+    rpi_short: int = 0   # largest row count of a short request's item
+
+
+LONG_ROWS = 32  # requests with more query rows (q_len x g) are prefill ("long") requests
 
 
 def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int, sms: int,
-                        min_chunk: int = 256, waves: int = 3, fixed_splits: int = 0):
-    """Work list as numpy arrays: ``(work [n,4], item_first, item_count, max_rb, n_work)``.
+                        min_chunk: int = 256, waves: int = 3, fixed_splits: int = 0, long_rows: int = LONG_ROWS):
+    """Work list as numpy arrays:
+    ``(work [n,4], item_first, item_count, max_rb, n_work, tiles [n_tiles,4], n_short, rpi_short)``.
 
-    ``fixed_splits > 0`` gives every row block exactly that many page-aligned splits
-    (some may be empty), so the work-list shape depends only on the batch shape - the
-    form a captured CUDA graph replays.
+    Items of short requests (<= ``long_rows`` query rows) come first and are split over
+    the KV range for parallelism; ``fixed_splits > 0`` gives each of their row blocks
+    exactly that many page-aligned splits (some may be empty), so the work-list shape
+    depends only on the batch shape - the form a captured CUDA graph replays.  Long
+    (prefill) requests get one item per 64-row block covering their whole KV range,
+    paired into 128-row ``tiles`` for the tensor-core prefill kernel.
     """
     R = len(seq_lens)
-    blocks = []  # (req, row0, kv_need)
+    blocks = []  # (req, row0, kv_need, long)
     max_rb = 1
     for r in range(R):
         n = q_start[r + 1] - q_start[r]
@@ -69,16 +94,21 @@ def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int
         max_rb = max(max_rb, rb)
         for b in range(rb):
             last_row = min(rows, (b + 1) * ROWS) - 1
-            blocks.append((r, b * ROWS, prefix + last_row // g + 1))
-    total = sum(k for _, _, k in blocks)
+            blocks.append((r, b * ROWS, prefix + last_row // g + 1, rows > long_rows))
+    short = [bk for bk in blocks if not bk[3]]
+    longb = [bk for bk in blocks if bk[3]]
+    total = sum(k for _, _, k, _ in short)
     target_items = max(1, (waves * sms) // max(Hk, 1))
     # page-aligned (128-token) split ranges: every split streams whole pages
     chunk = max(min_chunk, int(math.ceil(total / target_items / 128.0)) * 128) if total else min_chunk
     work = []
     first = np.zeros(R * max_rb, dtype=np.int32)
     count = np.zeros(R * max_rb, dtype=np.int32)
-    for r, row0, need in blocks:
+    rpi_short = 0
+    for r, row0, need, _ in short:
         rb = row0 // ROWS
+        rows = (q_start[r + 1] - q_start[r]) * g
+        rpi_short = max(rpi_short, min(ROWS, rows - row0))
         first[r * max_rb + rb] = len(work)
         if fixed_splits > 0:
             splits = fixed_splits
@@ -91,16 +121,36 @@ def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int
             for s in range(splits):
                 work.append((r, row0, s * chunk, min(need, (s + 1) * chunk)))
         count[r * max_rb + rb] = splits
+    n_short = len(work)
+    for r, row0, need, _ in longb:
+        rb = row0 // ROWS
+        first[r * max_rb + rb] = len(work)
+        count[r * max_rb + rb] = 1
+        work.append((r, row0, 0, need))
+    tiles = []
+    for r, row0, need, _ in longb:
+        if row0 % (2 * ROWS):
+            continue
+        rb = row0 // ROWS
+        rows = (q_start[r + 1] - q_start[r]) * g
+        item_b = int(first[r * max_rb + rb + 1]) if row0 + ROWS < rows else -1
+        tiles.append((r, row0, int(first[r * max_rb + rb]), item_b))
+    # longest tiles (most keys) first
+    tiles.sort(key=lambda t: -(seq_lens[t[0]] - (q_start[t[0] + 1] - q_start[t[0]]) + t[1] // g))
     n_work = len(work)
     wt = np.asarray(work if work else [(0, 0, 0, 0)], dtype=np.int32).reshape(-1, 4)
-    return wt, first, count, max_rb, n_work
+    tt = np.asarray(tiles if tiles else [(0, 0, -1, -1)], dtype=np.int32).reshape(-1, 4)
+    return wt, first, count, max_rb, n_work, tt, n_short, rpi_short
 
 
 def plan_attention(q_start: list[int], seq_lens: list[int], g: int, Hk: int, sms: int,
                    device, min_chunk: int = 256, waves: int = 3) -> AttnPlan:
-    wt, first, count, max_rb, n_work = plan_attention_host(q_start, seq_lens, g, Hk, sms, min_chunk, waves)
+    wt, first, count, max_rb, n_work, tt, n_short, rpi_short = plan_attention_host(q_start, seq_lens, g, Hk, sms,
+                                                                                   min_chunk, waves)
+    n_tiles = int((tt[:, 2] >= 0).sum()) if n_work > n_short else 0
     return AttnPlan(torch.from_numpy(wt).to(device), torch.from_numpy(first).to(device),
-                    torch.from_numpy(count).to(device), max_rb, n_work)
+                    torch.from_numpy(count).to(device), max_rb, n_work, torch.from_numpy(tt).to(device), n_tiles,
+                    n_short, rpi_short)
 
 
 # ---------------------------------------------------------------------------
@@ -271,7 +321,8 @@ def attention(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, s
         sk, sv, own, rows = stage
     e.paged_attention(q, k_fresh, v_fresh, Hq, Hk, D, float(scale), kv_mode, pool, kc, vc, sk, sv, own, rows,
                       block_tables, q_start_t, seq_lens_t, plan.work, part_o, part_lse, status,
-                      rows_per_item(q_start, Hq // Hk) if USE_TC else 0)
+                      _rpi(plan, q_start, Hq // Hk), plan.tiles if (USE_TC and plan.n_tiles > 0) else None,
+                      plan.n_tiles if USE_TC else 0, plan.n_short if (USE_TC and plan.n_tiles > 0) else 0)
     if RvT is not None:
         # tensor-core merge + rotation + gate, then the vectorised row quantiser
         if rv_merge_split is None:

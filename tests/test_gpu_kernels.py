@@ -214,13 +214,16 @@ def _build_cache(dev, Hk, D, seqs, qlens, seed, stage_rows=0, kv_mode=0):
 
 
 @pytest.mark.parametrize("use_tc", [True, False], ids=["tcgen05", "mma_sync"])
-@pytest.mark.parametrize("case", ["decode", "mtp", "mixed", "bf16", "long"])
+@pytest.mark.parametrize("case", ["decode", "mtp", "mixed", "bf16", "long", "prefill", "bf16_prefill"])
 def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
-    if not use_tc and case == "mixed":
+    """``mixed`` / ``prefill`` run prefill chunks (tcgen05 prefill kernel: fresh-only and
+    INT2-history tiles, staged tokens, two KV heads) next to short verify/decode requests
+    in the same step; ``bf16_prefill`` the same plan over a BF16 cache."""
+    if not use_tc and case in ("mixed", "prefill"):
         pytest.skip("same kernel as the tcgen05 run")
     monkeypatch.setattr(A, "USE_TC", use_tc)
     torch.manual_seed(1)
-    Hq, Hk, D = 6, 1, 256
+    Hq, Hk, D = (12, 2, 256) if case == "prefill" else (6, 1, 256)
     g = Hq // Hk
     if case == "decode":
         seqs, qlens = [700, 1200, 129], [1, 1, 1]
@@ -230,9 +233,13 @@ def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
         seqs, qlens = [300, 1000], [300, 37]
     elif case == "long":
         seqs, qlens = [16384, 9000, 24579], [4, 4, 4]
+    elif case == "prefill":
+        seqs, qlens = [1500, 700, 1003], [200, 64, 3]
+    elif case == "bf16_prefill":
+        seqs, qlens = [1500, 403], [200, 3]
     else:
         seqs, qlens = [900, 260], [4, 4]
-    kv_mode = 1 if case == "bf16" else 0
+    kv_mode = 1 if case.startswith("bf16") else 0
     R = len(seqs)
     nb, bt = _build_cache("cpu", Hk, D, seqs, qlens, 3)
     pool = torch.zeros(nb, Hk, fmt.page_head_bytes(D), dtype=torch.uint8)
