@@ -308,11 +308,15 @@ bf16_attention_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_c
     const int swarp = st >> 5;
     const uint32_t lrow = (uint32_t)(st & ~31) << 16;
     const float sl2 = p.scale * kLog2e;
+    // per-row constants in registers (lane r holds row r), broadcast by shuffles
+    const int lim_l = lim[lane % N];
+    float m_l = msm[lane % N];
     bool dead = false, aborted = false;
     for (int i = 0; i < n_pages; ++i) {
       const int b = i & 1;
       bool ok = !dead && sm100::mbar_wait(&s_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
                                           kBudgetNs);
+      ok = __all_sync(0xffffffffu, ok);  // warp-uniform before the shuffles below
       float sc[N];
       bool need = false;
       if (ok) {
@@ -331,9 +335,12 @@ bf16_attention_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_c
         const bool hist = pos < prefix;
 #pragma unroll
         for (int r = 0; r < N; ++r) {
-          const bool vis = in && (hist || pos <= lim[r]);
+          // every lane takes part in both shuffles (no short-circuit around them)
+          const int lv = __shfl_sync(0xffffffffu, lim_l, r);
+          const float mv = __shfl_sync(0xffffffffu, m_l, r);
+          const bool vis = in && (hist || pos <= lv);
           sc[r] = vis ? __uint_as_float(raw[r]) * sl2 : -INFINITY;
-          need |= sc[r] > msm[r] + kSlack;
+          need |= sc[r] > mv + kSlack;
         }
       }
       if (ok && i >= 2)
@@ -364,6 +371,7 @@ bf16_attention_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_c
           if (a != 1.f) *resc_flag = 1;
         }
         sm100::bar_sync(kBarSoft, 128);
+        m_l = msm[lane % N];
         if (*resc_flag && i > 0) {
           const bool ok2 = sm100::mbar_wait(&p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, p.status,
                                             kTimeoutAccFull, kBudgetNs);
@@ -391,13 +399,14 @@ bf16_attention_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_c
         }
       }
       if (st == 0) upd[b] = upd_now ? 1 : 0;
+      ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         uint32_t pk[N / 2];
+        const float mref_l = m_l == -INFINITY ? 0.f : m_l;
 #pragma unroll
         for (int r = 0; r < N; r += 2) {
-          const float m0 = msm[r], m1 = msm[r + 1];
-          const float p0 = exp2f(sc[r] - (m0 == -INFINITY ? 0.f : m0));
-          const float p1 = exp2f(sc[r + 1] - (m1 == -INFINITY ? 0.f : m1));
+          const float p0 = exp2f(sc[r] - __shfl_sync(0xffffffffu, mref_l, r));
+          const float p1 = exp2f(sc[r + 1] - __shfl_sync(0xffffffffu, mref_l, r + 1));
           pk[r / 2] = pack_bf16x2(p0, p1);
         }
         uint8_t* prow = ps + b * L::kPBytes + st * (N * 2);

@@ -5,13 +5,11 @@
 //
 // Key tiles of 128 keys:
 //   history tiles  - one KV page each (positions < prefix).  The 2-bit page arrives by
-//                    bulk copy; converter warps widen K codes (token-major) and V codes
-//                    (dim-major) to exact fp16 0..3 in shared memory, in the K-major
-//                    128-byte-swizzled layouts of the B operands of S = Q K^T and
+//                    bulk copy; converter warps dequantise K codes (token-major) and V
+//                    codes (dim-major) to fp16 values s c + z in shared memory, in the
+//                    K-major 128-byte-swizzled layouts of the B operands of S = Q K^T and
 //                    O += P V; staged sink/recent tokens (owner tag == block) carry their
-//                    fp32 values instead.  Scores are corrected per key,
-//                    q.k = s_k (q.c) + z_k sum(q), and P' = p s_v feeds P.V, with
-//                    l += p and C += p z_v tracked per row:  out = (O + C) / l.
+//                    fp32 values instead.  The softmax then treats every tile alike.
 //   fresh tiles    - the chunk's own (unquantised) k / v, 128 tokens at a time, loaded by
 //                    TMA straight into the operand layouts (V MN-major).
 // Operand chunks (16 KB: 128 keys x 64 dims of K, or 64 dims x 128 keys of V) stream
@@ -55,8 +53,7 @@ constexpr int kThreads = 320;
 constexpr int kSlots = 6;      // operand ring (16 KB chunks)
 constexpr int kRaw = 3;        // raw page ring
 constexpr int kPageBytes = 17408;
-constexpr int kCoefOff = kPageBytes + kPage * 4;        // per-key coefficients after the owner tags
-constexpr int kRawSlot = kCoefOff + kPage * 24;         // + 128 x (float4 + float2)
+constexpr int kRawSlot = kPageBytes + kPage * 4;        // page + owner tags
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kSlack = 8.f;
 constexpr uint64_t kBudgetNs = 2000000000ull;
@@ -67,15 +64,13 @@ struct PfLayout {
   static constexpr int kQ = 0;                                   // 4 x [128 rows][128 B]
   static constexpr int kOps = 65536;                             // kSlots x 16 KB
   static constexpr int kRawOff = kOps + kSlots * 16384;          // kRaw x kRawSlot
-  static constexpr int kSq = kRawOff + kRaw * kRawSlot;          // 128 floats
-  static constexpr int kLim = kSq + 512;                         // 128 ints
+  static constexpr int kLim = kRawOff + kRaw * kRawSlot;         // 128 ints
   static constexpr int kSlotBlk = kLim + 512;                    // kRaw ints
   static constexpr int kTmemSlot = kSlotBlk + 16;
   static constexpr int kAbort = kTmemSlot + 16;
   static constexpr int kBars = kAbort + 16;
-  // full[kSlots], empty[kSlots], raw_full[kRaw], raw_empty[kRaw], cf_full[kRaw], s_full[2], s_free[2],
-  // p_full[2], drain
-  static constexpr int kNumBars = 2 * kSlots + 3 * kRaw + 7;
+  // full[kSlots], empty[kSlots], raw_full[kRaw], raw_empty[kRaw], s_full[2], s_free[2], p_full[2], drain
+  static constexpr int kNumBars = 2 * kSlots + 2 * kRaw + 7;
   static constexpr int kTotal = kBars + kNumBars * 8;
   static constexpr int kAlloc = kTotal + 1024;  // + base alignment
 };
@@ -109,25 +104,29 @@ OSCAR_DEVICE void store_row(uint8_t* base, int row, const uint32_t (&r)[32]) {
     *reinterpret_cast<uint4*>(p + ((q ^ (row & 7)) << 4)) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
 }
 
-// Rare paths (pages holding staged sink/recent tokens), kept out of line.
-// V row of 64 keys: codes, with the staged keys (bit set in m) taken from the
-// dim-major staging row `srow` (64 contiguous fp32).
-__device__ __noinline__ void v_row_staged(uint8_t* base, int row, uint4 cw, const float* srow, uint64_t m) {
-  uint32_t r[32];
-  widen16(cw, r);
+// Dequantise fp16 code pairs: r[k] = r[k] * s_k + z_k (fp16x2 lanes).
+OSCAR_DEVICE uint32_t hfma2_u32(uint32_t x, uint32_t s, uint32_t z) {
+  __half2 v = __hfma2(*reinterpret_cast<__half2*>(&x), *reinterpret_cast<__half2*>(&s),
+                      *reinterpret_cast<__half2*>(&z));
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Staged keys (bit set in m) of one 64-key V row take their values from the dim-major
+// staging row `srow` (64 contiguous fp32).
+OSCAR_DEVICE void merge_staged_v(uint32_t (&r)[32], const float* srow, uint64_t m) {
 #pragma unroll
   for (int q = 0; q < 16; ++q) {
+    const uint32_t b = (uint32_t)(m >> (4 * q)) & 15u;
+    if (b == 0u) continue;
     const float4 v = __ldg(reinterpret_cast<const float4*>(srow) + q);
     const uint32_t lo = mma::h2_u32(v.x, v.y), hi = mma::h2_u32(v.z, v.w);
-    const uint32_t b = (uint32_t)(m >> (4 * q)) & 15u;
     const uint32_t k0 = ((b & 1u) ? 0u : 0x0000ffffu) | ((b & 2u) ? 0u : 0xffff0000u);
     const uint32_t k1 = ((b & 4u) ? 0u : 0x0000ffffu) | ((b & 8u) ? 0u : 0xffff0000u);
     r[2 * q] = (r[2 * q] & k0) | (lo & ~k0);
     r[2 * q + 1] = (r[2 * q + 1] & k1) | (hi & ~k1);
   }
-  store_row(base, row, r);
 }
-// K row of a staged key: 64 fp32 values of the staging arena.
+// Rare path, kept out of line: K row of a staged key: 64 fp32 values of the staging arena.
 __device__ __noinline__ void k_row_staged(uint8_t* base, int row, const float* sk) {
   uint32_t r[32];
 #pragma unroll
@@ -149,7 +148,6 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
   uint8_t* qs = smem + L::kQ;
   uint8_t* ops = smem + L::kOps;
   uint8_t* raw = smem + L::kRawOff;
-  float* sq = reinterpret_cast<float*>(smem + L::kSq);
   int* lim = reinterpret_cast<int*>(smem + L::kLim);
   int* slot_blk = reinterpret_cast<int*>(smem + L::kSlotBlk);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
@@ -159,8 +157,7 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
   uint64_t* empty = full + kSlots;
   uint64_t* raw_full = empty + kSlots;
   uint64_t* raw_empty = raw_full + kRaw;
-  uint64_t* cf_full = raw_empty + kRaw;
-  uint64_t* s_full = cf_full + kRaw;
+  uint64_t* s_full = raw_empty + kRaw;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_full + 4;
   uint64_t* drain = s_full + 6;
@@ -187,7 +184,6 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
   }
   if (tid == 9 * 32) {
     for (int i = 0; i < L::kNumBars; ++i) sm100::mbar_init(&bar[i], 1);
-    for (int r = 0; r < kRaw; ++r) sm100::mbar_init(&raw_empty[r], 5);  // converter leader + 4 softmax warps
     for (int b = 0; b < 2; ++b) sm100::mbar_init(&p_full[b], 4);
     *abort_flag = 0;
     sm100::fence_mbar_init();
@@ -207,21 +203,7 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
     *reinterpret_cast<uint4*>(qs + (ch >> 3) * (kRows * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4)) = v;
   }
   __syncthreads();
-  if (tid < kRows) {
-    float acc = 0.f;
-    for (int ch = 0; ch < 32; ++ch) {
-      const uint4 v = *reinterpret_cast<const uint4*>(qs + (ch >> 3) * (kRows * 128) + tid * 128 +
-                                                      (((ch & 7) ^ (tid & 7)) << 4));
-      const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 f = __half22float2(h[k]);
-        acc += f.x + f.y;
-      }
-    }
-    sq[tid] = acc;
-    lim[tid] = tid < nrows ? prefix + (row0 + tid) / g : -1;
-  }
+  if (tid < kRows) lim[tid] = tid < nrows ? prefix + (row0 + tid) / g : -1;
   sm100::fence_proxy_async();  // Q tile: generic writes -> tensor-core reads
   sm100::tc_fence_before();
   __syncthreads();
@@ -346,6 +328,7 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
         const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
         if (hist && part == 0 && ok)
           ok = sm100::mbar_wait(&raw_full[rs], (ti / kRaw) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs);
+        ok = __all_sync(0xffffffffu, ok);
         const int blk = hist ? slot_blk[rs] : 0;
         const int nvalid = hist ? min(kPage, prefix - kPage * ti) : 0;
         // staged keys of this page, as 128-bit masks every warp computes for itself
@@ -357,27 +340,28 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
             smk[q] = __ballot_sync(0xffffffffu, ok && tj < nvalid && own[tj] == blk);
           }
         }
-        if (hist && part == 0 && ok) {
-          // per-key coefficients for the softmax: (s_k, z_k) scaled to log2 units, s_v, 1/s_v, z_v/s_v
-          const int j = ct;
-          const bool stg = (smk[j >> 5] >> (j & 31)) & 1u;
-          float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          float2 c2 = make_float2(0.f, 0.f);
-          if (j < nvalid) {
-            if (stg) {
-              c4 = make_float4(sl2, 0.f, 1.f, 1.f);
-            } else {
-              const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * 64);
-              const float ks = __half2float(meta[j]), kz = __half2float(meta[kPage + j]);
-              const float vs = __half2float(meta[2 * kPage + j]), vz = __half2float(meta[3 * kPage + j]);
-              const float inv = 1.f / vs;
-              c4 = make_float4(ks * sl2, kz * sl2, vs, inv);
-              c2 = make_float2(vz * inv, 0.f);
+        // dequantisation constants: K - this thread's key; V - lane l holds the fp16
+        // (scale, zero) pairs of keys 64 hf + 2 l, + 1 (broadcast by shuffles); keys past
+        // the history get zero scale and zero so stale meta cannot leak in
+        const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * 64);
+        uint32_t ks2 = 0u, kz2 = 0u, vsp = 0u, vzp = 0u;
+        if (hist && ok) {
+          if (part == 0) {
+            const int j = ct;
+            if (j < nvalid) {
+              const __half ks = meta[j], kz = meta[kPage + j];
+              const __half2 s2 = __halves2half2(ks, ks), z2 = __halves2half2(kz, kz);
+              ks2 = *reinterpret_cast<const uint32_t*>(&s2);
+              kz2 = *reinterpret_cast<const uint32_t*>(&z2);
             }
+          } else {
+            const int kb = 64 * (ct >> 6) + 2 * lane;
+            vsp = *reinterpret_cast<const uint32_t*>(meta + 2 * kPage + kb);
+            vzp = *reinterpret_cast<const uint32_t*>(meta + 3 * kPage + kb);
+            const uint32_t keep = (kb < nvalid ? 0x0000ffffu : 0u) | (kb + 1 < nvalid ? 0xffff0000u : 0u);
+            vsp &= keep;
+            vzp &= keep;
           }
-          uint8_t* cf = raw + rs * kRawSlot + kCoefOff;
-          *reinterpret_cast<float4*>(cf + 16 * j) = c4;
-          *reinterpret_cast<float2*>(cf + 16 * kPage + 8 * j) = c2;
         }
         for (int c = 0; c < 4; ++c) {
           const int u = part == 0 ? use_k(ti, c) : use_v(ti, c, n);
@@ -385,6 +369,7 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
           if (ok && u >= kSlots)
             ok = sm100::mbar_wait(&empty[s], ((u / kSlots) - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty,
                                   kBudgetNs);
+          ok = __all_sync(0xffffffffu, ok);  // warp-uniform before the shuffles below
           uint8_t* dst = ops + s * 16384;
           if (ok && !hist) {
             // fresh tile: one TMA box (128 tokens x 64 dims) of k or v
@@ -404,6 +389,8 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
                 const uint4 cw = *reinterpret_cast<const uint4*>(pg + j * 64 + ((c ^ ((j >> 1) & 3)) << 4));
                 uint32_t r[32];
                 widen16(cw, r);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) r[k] = hfma2_u32(r[k], ks2, kz2);
                 store_row(dst, j, r);
               }
             } else {
@@ -411,16 +398,16 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
               const int dl = ct & 63, hf = ct >> 6, d = 64 * c + dl;
               const uint4 cw = *reinterpret_cast<const uint4*>(pg + kPage * 64 + d * 32 + hf * 16);
               const uint64_t m = ((uint64_t)smk[2 * hf + 1] << 32) | smk[2 * hf];
-              if (m != 0ull) {
-                v_row_staged(dst + hf * 8192, dl, cw,
-                             p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage + (long long)d * kPage +
-                                 hf * 64,
-                             m);
-              } else {
-                uint32_t r[32];
-                widen16(cw, r);
-                store_row(dst + hf * 8192, dl, r);
-              }
+              uint32_t r[32];
+              widen16(cw, r);
+#pragma unroll
+              for (int k = 0; k < 32; ++k)
+                r[k] = hfma2_u32(r[k], __shfl_sync(0xffffffffu, vsp, k), __shfl_sync(0xffffffffu, vzp, k));
+              if (m != 0ull)  // warp-uniform: staged keys carry their own values
+                merge_staged_v(r, p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage +
+                                      (long long)d * kPage + hf * 64,
+                               m);
+              store_row(dst + hf * 8192, dl, r);
             }
             sm100::fence_proxy_async();  // generic writes -> tensor-core reads
           }
@@ -428,10 +415,7 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
             ok = false;
             break;
           }
-          if (ct == 0 && hist) {
-            if (part == 0 && c == 0) sm100::mbar_arrive(&cf_full[rs]);  // coefficients are in
-            sm100::mbar_arrive(&full[s]);
-          }
+          if (ct == 0 && hist) sm100::mbar_arrive(&full[s]);
         }
         if (!ok) break;
         if (part == 1 && hist && ct == 0) sm100::mbar_arrive(&raw_empty[rs]);
@@ -449,21 +433,15 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
     const int r = tid;  // TMEM lane = query row
     const uint32_t lrow = (uint32_t)(warp * 32) << 16;
     const int my_lim = lim[r];
-    const float sqr = sq[r];
-    float m = -INFINITY, l = 0.f, C = 0.f;
+    float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int i = 0; i < n && ok; ++i) {
       const int b = i & 1;
       const bool hist = i < nh;
-      const int rs = i % kRaw;
       ok = sm100::mbar_wait(&s_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull, kBudgetNs);
-      if (ok && hist)
-        ok = sm100::mbar_wait(&cf_full[rs], (i / kRaw) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       sm100::tc_fence_after();
-      const float4* c4 = reinterpret_cast<const float4*>(raw + rs * kRawSlot + kCoefOff);
-      const float2* c2 = reinterpret_cast<const float2*>(raw + rs * kRawSlot + kCoefOff + 16 * kPage);
       // visible keys of this tile for this row: j < jmax
       const int jmax = hist ? min(kPage, prefix - kPage * i) : max(0, min(kPage, my_lim - prefix - kPage * (i - nh) + 1));
       const uint32_t sb = tbase + lrow + kColS + b * 128;
@@ -477,23 +455,16 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int j = 32 * c + e;
-          float sc;
-          if (hist) {
-            const float4 k = c4[j];
-            sc = fmaf(k.x, __uint_as_float(raw32[e]), k.y * sqr);
-          } else {
-            sc = __uint_as_float(raw32[e]) * sl2;
-          }
-          pm = j < jmax ? fmaxf(pm, sc) : pm;
+          pm = j < jmax ? fmaxf(pm, __uint_as_float(raw32[e])) : pm;
         }
       }
+      pm *= sl2;  // log2 units
       // ---- running maximum: moves only when exceeded by more than 2^kSlack
       float alpha = 1.f;
       if (pm > m + kSlack) {
         alpha = m == -INFINITY ? 0.f : exp2f(m - pm);
         m = pm;
         l *= alpha;
-        C *= alpha;
       }
       if (__any_sync(0xffffffffu, alpha != 1.f) && i > 0) {
         // O holds tiles < i: rescale this warp's rows once P.V(i-1) is done
@@ -522,42 +493,22 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
         sm100::tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float ph[2];
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            const int j = 32 * c + e + x;
-            float sc, vs = 1.f;
-            if (hist) {
-              const float4 k = c4[j];
-              sc = fmaf(k.x, __uint_as_float(raw32[e + x]), k.y * sqr);
-              vs = k.z;
-            } else {
-              sc = __uint_as_float(raw32[e + x]) * sl2;
-            }
-            const float pv = j < jmax ? exp2f(sc - mref) * vs : 0.f;
-            const __half hv = __float2half_rn(pv);
-            ph[x] = __half2float(hv);
-            if (hist) {
-              const float4 k = c4[j];
-              l = fmaf(ph[x], k.w, l);
-              C = fmaf(ph[x], c2[j].x, C);
-            } else {
-              l += ph[x];
-            }
-          }
-          pk[e >> 1] = mma::h2_u32(ph[0], ph[1]);
+          const int j = 32 * c + e;
+          const float p0 = j < jmax ? exp2f(fmaf(__uint_as_float(raw32[e]), sl2, -mref)) : 0.f;
+          const float p1 = j + 1 < jmax ? exp2f(fmaf(__uint_as_float(raw32[e + 1]), sl2, -mref)) : 0.f;
+          const __half2 h = __floats2half2_rn(p0, p1);
+          const float2 hf = __half22float2(h);
+          l += hf.x + hf.y;  // the row sum of exactly the P the tensor cores read
+          pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h);
         }
         sm100::tmem_st_32x32b_x16(sb + 16 * c, pk);
       }
       sm100::tmem_st_wait();
       sm100::tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        sm100::mbar_arrive(&p_full[b]);
-        if (hist) sm100::mbar_arrive(&raw_empty[rs]);
-      }
+      if (lane == 0) sm100::mbar_arrive(&p_full[b]);
     }
-    // ---- output: out[r, d] = (O[r, d] + C_r) / l_r  into the 64-row partials
+    // ---- output: out[r, d] = O[r, d] / l_r  into the 64-row partials
     if (ok && n > 0)
       ok = sm100::mbar_wait(&s_free[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
                             kBudgetNs);
@@ -582,8 +533,8 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
             *reinterpret_cast<float4*>(po + 32 * c + e) =
-                make_float4((__uint_as_float(o[e]) + C) * inv, (__uint_as_float(o[e + 1]) + C) * inv,
-                            (__uint_as_float(o[e + 2]) + C) * inv, (__uint_as_float(o[e + 3]) + C) * inv);
+                make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
+                            __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
         }
       }
       if (write)

@@ -38,6 +38,8 @@
 // the roles that synchronise with named barriers agree on aborting through
 // bar.red.or so that none is left waiting, in-flight MMAs and bulk copies are
 // drained (bounded) and TMEM is freed before the CTA exits.
+#include <climits>
+
 #include "common.cuh"
 #include "mma.cuh"
 #include "params.h"
@@ -57,7 +59,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kSlack = 8.f;
 constexpr uint64_t kBudgetNs = 2000000000ull;
 constexpr uint32_t kColK = 0, kColV = 128, kColS = 384, kColO = 448, kTmemCols = 512;
-constexpr int kBarConv = 2, kBarSoft = 1, kBarStats = 3;
+constexpr int kBarSoft = 1, kBarStats = 3;
 
 // Optional per-CTA event timeline (globaltimer ns) for performance analysis; off
 // unless a buffer was installed with oscar_attn_tc_trace (slot layout: 96 u64 per CTA).
@@ -67,6 +69,16 @@ OSCAR_DEVICE void trace(int ev) {
   unsigned long long* t = g_tc_trace;
   if (t != nullptr && ev < kTraceSlots)
     t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * kTraceSlots + ev] = globaltimer_ns();
+}
+// Raw value into a trace slot (e.g. a clock64 difference).
+OSCAR_DEVICE void trace_val(int ev, unsigned long long v) {
+  unsigned long long* t = g_tc_trace;
+  if (t != nullptr && ev < kTraceSlots) t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * kTraceSlots + ev] = v;
+}
+OSCAR_DEVICE unsigned long long clock_dep(float dep) {
+  unsigned long long v;
+  asm volatile("{\n\t.reg .f32 d;\n\tmov.f32 d, %1;\n\tmov.u64 %0, %%clock64;\n\t}" : "=l"(v) : "f"(dep));
+  return v;
 }
 // Same, ordered after the computation of `dep` (the timer read consumes it).
 OSCAR_DEVICE void trace_dep(int ev, float dep) {
@@ -178,7 +190,7 @@ __device__ __noinline__ void v_half_mixed(uint32_t taddr, uint4 cw, uint64_t sm,
 
 // O^T (both halves, N columns each) scaled by alpha[r] per row column r.
 template <int N>
-__device__ __noinline__ void rescale_o(uint32_t taddr, const float* alpha) {
+OSCAR_DEVICE void rescale_o(uint32_t taddr, const float* alpha) {
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
     uint32_t o[N];
@@ -635,6 +647,11 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     const int swarp = st >> 5;
     const uint32_t lrow = (uint32_t)(st & ~31) << 16;
     const float sl2 = p.scale * kLog2e;
+    // per-row constants live in registers, lane r holding row r (broadcast by shuffles:
+    // a warp reading one shared-memory word per row is far slower here)
+    const float sq_l = sq[lane % N];
+    const int lim_l = lim[lane % N];
+    float m_l = msm[lane % N];
     bool dead = false, aborted = false;
     for (int i = 0; i < n_pages; ++i) {
       const int s = i % kRing, b = i & 1;
@@ -657,6 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         for (int r = 0; r < N; ++r) sc[r] = __uint_as_float(raw[r]);
         ok = sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs);
       }
+      ok = __all_sync(0xffffffffu, ok);  // warp-uniform before the shuffles below
       if (st == 0 && i < 4) trace(49 + 4 * i);
       float vs = 0.f;
       bool need = false;
@@ -680,13 +698,25 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         }
         const bool hist = pos < prefix;
         if (i < 4) trace_dep(st == 0 ? 64 + 4 * i : kTraceSlots, ks + kz + vs);
+        const unsigned long long cl0 = clock_dep(ks + kz + vs);
+        // per-row constants with 16-byte shared loads; the causal limits only matter on
+        // pages that reach the current chunk
+        const float kss = ks * sl2, kzs = kz * sl2;
+        const bool page_hist = (p_first + i + 1) * kPage <= prefix;
+        float dmax = -INFINITY;
 #pragma unroll
         for (int r = 0; r < N; ++r) {
-          const bool vis = in && (hist || pos <= lim[r]);
-          sc[r] = vis ? fmaf(ks, sc[r], kz * sq[r]) * sl2 : -INFINITY;
-          need |= sc[r] > msm[r] + kSlack;
+          const float qv = __shfl_sync(0xffffffffu, sq_l, r);
+          const int lv = page_hist ? INT_MAX : __shfl_sync(0xffffffffu, lim_l, r);
+          const float mv = __shfl_sync(0xffffffffu, m_l, r);
+          const bool vis = in && (hist || pos <= lv);
+          sc[r] = vis ? fmaf(kss, sc[r], kzs * qv) : -INFINITY;
+          dmax = fmaxf(dmax, sc[r] - mv);
         }
+        need = dmax > kSlack;
         if (i < 4) trace_dep(st == 0 ? 65 + 4 * i : kTraceSlots, sc[N - 1] + (need ? 1.f : 0.f));
+        const unsigned long long cl1 = clock_dep(sc[N - 1] + (need ? 1.f : 0.f));
+        if (st == 0 && i < 4) trace_val(80 + i, cl1 - cl0);
       }
       // P' buffer b (and alpha/upd slot b) are free once P.V(i-2) and the stats of page i-2 are done
       if (ok && i >= 2)
@@ -720,6 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           if (a != 1.f) *resc_flag = 1;
         }
         sm100::bar_sync(kBarSoft, 128);
+        m_l = msm[lane % N];
         if (*resc_flag && i > 0) {  // O^T holds pages < i: rescale its columns once P.V(i-1) is done
           bool ok2 = sm100::mbar_wait(&B.p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, p.status,
                                       kTimeoutAccFull, kBudgetNs);
@@ -732,14 +763,15 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         }
       }
       if (st == 0) upd[b] = upd_now ? 1 : 0;
+      ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         uint32_t pk[N / 2];
+        const float mref_l = m_l == -INFINITY ? 0.f : m_l;
 #pragma unroll
         for (int r = 0; r < N; r += 2) {
-          const float m0 = msm[r], m1 = msm[r + 1];
-          const float p0 = exp2f(sc[r] - (m0 == -INFINITY ? 0.f : m0));
-          const float p1 = exp2f(sc[r + 1] - (m1 == -INFINITY ? 0.f : m1));
-          pk[r / 2] = mma::h2_u32(p0 * vs, p1 * vs);
+          const float p0 = exp2f(sc[r] - __shfl_sync(0xffffffffu, mref_l, r)) * vs;
+          const float p1 = exp2f(sc[r + 1] - __shfl_sync(0xffffffffu, mref_l, r + 1)) * vs;
+          pk[r / 2] = mma::h2_u32(p0, p1);
         }
         // P' row of token st: N fp16 = N/8 chunks of 16 B, MN-major swizzled (64 B / 32 B rows)
         uint8_t* prow = ps + b * L::kPBytes + st * (N * 2);

@@ -308,8 +308,13 @@ extern "C" int oscar_act_quant(const __nv_bfloat16* x, long long ld, int T, int 
                                cudaStream_t s) {
   if (T <= 0) return 0;
   if (K % 8 || ld % 8) return -401;
-  constexpr int NT = 256;
-  OSCAR_PV_DISPATCH(K / 8, NT, (row_quant_kernel<NT, PV, 1><<<T, NT, 0, s>>>(x, ld, K, out, scale)));
+  if (K <= 256 * 8 * 8) {
+    constexpr int NT = 256;
+    OSCAR_PV_DISPATCH(K / 8, NT, (row_quant_kernel<NT, PV, 1><<<T, NT, 0, s>>>(x, ld, K, out, scale)));
+  } else {  // rows up to 32768 wide (e.g. the TP1 down projection's input)
+    constexpr int NT = 512;
+    OSCAR_PV_DISPATCH(K / 8, NT, (row_quant_kernel<NT, PV, 1><<<T, NT, 0, s>>>(x, ld, K, out, scale)));
+  }
   return (int)cudaGetLastError();
 }
 

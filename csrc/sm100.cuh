@@ -46,18 +46,23 @@ OSCAR_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait on an mbarrier phase.  Returns false (after recording `code` in
 // the status word and raising the CTA-local abort flag) when the budget expires
-// or another role of the same CTA has already aborted.
+// or another role of the same CTA has already aborted.  The timer is read only
+// every 32 polls.
 OSCAR_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
                             int code, uint64_t budget_ns) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  uint64_t t0 = 0;
+  for (uint32_t n = 0;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > budget_ns) {
-      *abort_flag = 1;
-      record_status(status, code);
-      return false;
+    if ((n & 31u) == 0u) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      if (now - t0 > budget_ns) {
+        *abort_flag = 1;
+        record_status(status, code);
+        return false;
+      }
     }
   }
 }
