@@ -67,105 +67,153 @@ OSCAR_DEVICE uint32_t bf2_u32(float lo, float hi) {
 OSCAR_DEVICE float softplusf(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 // ------------------------------------------------------------------ conv + gates
-// One CTA (256 threads) per token of a long request.  q/k heads: a half-warp per
-// head, 8 channels per lane (one 16-byte row segment), L2 norm by a 16-lane
-// butterfly.  v heads: 8 channels per thread-iteration.
+// One CTA (256 threads) per (block of kConvTok consecutive tokens of one long request,
+// slice of 256 16-byte channel chunks).  Each thread owns 8 channels and slides the
+// 4-tap window over the block's tokens, so every qkvz row is read about once (plus a
+// 3-row halo per block).  q / k chunks come first in channel order and a head's 16
+// chunks sit in one half-warp: its L2 norm is a 16-lane butterfly per token.
 constexpr int kConvThreads = 256;
+constexpr int kConvTok = 16;
+
+// Locates token block `bi` (kConvTok tokens) among the long requests.
+OSCAR_DEVICE bool find_tok_block(const GdnParams& p, int bi, int& req, int& b) {
+  for (int q = 0; q < p.R; ++q) {
+    if (!is_long(p, q)) continue;
+    const int n = (p.q_start[q + 1] - p.q_start[q] + kConvTok - 1) / kConvTok;
+    if (bi < n) {
+      req = q;
+      b = bi;
+      return true;
+    }
+    bi -= n;
+  }
+  return false;
+}
 
 __global__ void __launch_bounds__(kConvThreads) gdn_conv_kernel(GdnParams p) {
-  const int tok = blockIdx.x;
-  int req = 0;
-  while (req < p.R && p.q_start[req + 1] <= tok) ++req;
-  if (req >= p.R || !is_long(p, req)) return;
-  const int t0 = p.q_start[req], T = p.q_start[req + 1] - t0, t = tok - t0;
+  int req, blk;
+  if (!find_tok_block(p, blockIdx.x, req, blk)) return;
+  const int t0 = p.q_start[req], T = p.q_start[req + 1] - t0;
+  const int tb0 = blk * kConvTok, tb1 = min(T, tb0 + kConvTok);
   const int tid = threadIdx.x;
   const int r = p.Hv / p.Hk;
   const int Kd = p.Hk * kD;
   const int conv_dim = 2 * Kd + p.Hv * kD;
+  const int n_qk = 2 * p.Hk * (kD / 8);  // q / k chunks
+  const int n_chunks = conv_dim / 8;
+  const int ck = blockIdx.y * kConvThreads + tid;  // this thread's channel chunk
   const long long grp = 2 * kD + 2 * r * kD;  // qkvz elements per key-head group
   const int slot = p.req_slot[req], par = p.parity[req];
   const __nv_bfloat16* cs = p.conv_state + ((long long)par * p.slots + slot) * conv_dim * 3;
   __nv_bfloat16* cs_out = p.conv_state + ((long long)(1 - par) * p.slots + slot) * conv_dim * 3;
-  const bool last = t == T - 1;
 
-  // 8 channels starting at conv channel c0, whose raw inputs sit at element `off` of a
-  // qkvz row: returns conv + SiLU, writes the new conv window at the last token
-  auto conv8 = [&](int c0, long long off, float (&y)[8]) {
-    float x[4][8];  // x[i] = raw input of token t - 3 + i
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int tt = t - 3 + i;
-      if (tt >= 0) {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(p.qkvz + (long long)(t0 + tt) * p.ld_qkvz + off));
-        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&w);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = __bfloat162float(h[e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = __bfloat162float(cs[(long long)(c0 + e) * 3 + (3 + tt)]);
-      }
+  // gates of the block's tokens (first slice only)
+  if (blockIdx.y == 0) {
+    for (int idx = tid; idx < (tb1 - tb0) * p.Hv; idx += kConvThreads) {
+      const int tok = t0 + tb0 + idx / p.Hv, h = idx % p.Hv;
+      const int gk = h / r, hh = h % r;
+      const __nv_bfloat16* barow = p.ba + (long long)tok * p.ld_ba + (long long)gk * 2 * r;
+      const float bb = __bfloat162float(barow[hh]), aa = __bfloat162float(barow[r + hh]);
+      p.ws_beta[(long long)tok * p.Hv + h] = sigmoidf_(bb);
+      p.ws_lg[(long long)tok * p.Hv + h] = -__expf(p.A_log[h]) * softplusf(aa + p.dt_bias[h]);
     }
+  }
+  if (blockIdx.y * kConvThreads >= n_chunks) return;  // whole warps leave together (256 | slices)
+  const bool active = ck < n_chunks;
+  // channel chunk -> conv channel c0 and qkvz element offset
+  int c0 = 0, head = 0;
+  long long off = 0;
+  bool isqk = false, isk = false;
+  if (active) {
+    if (ck < n_qk) {
+      isqk = true;
+      head = ck / (kD / 8);  // 0 .. 2 Hk - 1
+      isk = head >= p.Hk;
+      const int gk = isk ? head - p.Hk : head, seg = ck % (kD / 8);
+      c0 = (isk ? Kd : 0) + gk * kD + 8 * seg;
+      off = gk * grp + (isk ? kD : 0) + 8 * seg;
+    } else {
+      const int vc = ck - n_qk, h = vc / (kD / 8), seg = vc % (kD / 8);
+      const int gk = h / r, hh = h % r;
+      head = h;
+      c0 = 2 * Kd + h * kD + 8 * seg;
+      off = gk * grp + 2 * kD + (long long)hh * kD + 8 * seg;
+    }
+  }
+  float w[8][4];
+  float x0[8], x1[8], x2[8];  // raw inputs of tokens t-3, t-2, t-1
+  if (active) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const float4 w4 = __ldg(reinterpret_cast<const float4*>(p.conv_w) + (c0 + e));
-      const float a = w4.x * x[0][e] + w4.y * x[1][e] + w4.z * x[2][e] + w4.w * x[3][e];
-      y[e] = silu(a);
+      w[e][0] = w4.x;
+      w[e][1] = w4.y;
+      w[e][2] = w4.z;
+      w[e][3] = w4.w;
     }
-    if (last) {
+    auto load_raw = [&](int tt, float (&x)[8]) {
+      if (tt >= 0) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.qkvz + (long long)(t0 + tt) * p.ld_qkvz + off));
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
+        for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(h[e]);
+      } else {
 #pragma unroll
-        for (int i = 0; i < 3; ++i) cs_out[(long long)(c0 + e) * 3 + i] = __float2bfloat16(x[i + 1][e]);
+        for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(cs[(long long)(c0 + e) * 3 + (3 + tt)]);
+      }
+    };
+    load_raw(tb0 - 3, x0);
+    load_raw(tb0 - 2, x1);
+    load_raw(tb0 - 1, x2);
+  }
+  const float qscale = rsqrtf((float)kD);
+  for (int t = tb0; t < tb1; ++t) {
+    float y[8];
+    float ss = 0.f;
+    if (active) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.qkvz + (long long)(t0 + t) * p.ld_qkvz + off));
+      const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xt = __bfloat162float(hb[e]);
+        const float a = w[e][0] * x0[e] + w[e][1] * x1[e] + w[e][2] * x2[e] + w[e][3] * xt;
+        y[e] = silu(a);
+        ss += y[e] * y[e];
+        x0[e] = x1[e];
+        x1[e] = x2[e];
+        x2[e] = xt;
+      }
     }
-  };
-
-  // q and k heads: half-warp per head
-  {
-    const int hw = tid >> 4, l16 = tid & 15;
-    for (int head = hw; head < 2 * p.Hk; head += kConvThreads / 16) {
-      const bool isk = head >= p.Hk;
-      const int gk = isk ? head - p.Hk : head;
-      const int c0 = (isk ? Kd : 0) + gk * kD + 8 * l16;
-      const long long off = gk * grp + (isk ? kD : 0) + 8 * l16;
-      float y[8];
-      conv8(c0, off, y);
-      float ss = 0.f;
+    // L2 norm over the head's 16 chunks (half-warp); every lane takes part
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss += y[e] * y[e];
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float sc = rsqrtf(ss + 1e-6f) * (isk ? 1.f : rsqrtf((float)kD));
-      uint4 o4;
+    for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (!active) continue;
+    const long long tok = t0 + t;
+    uint4 o4;
+    if (isqk) {
+      const float sc = rsqrtf(ss + 1e-6f) * (isk ? 1.f : qscale);
       o4.x = bf2_u32(y[0] * sc, y[1] * sc);
       o4.y = bf2_u32(y[2] * sc, y[3] * sc);
       o4.z = bf2_u32(y[4] * sc, y[5] * sc);
       o4.w = bf2_u32(y[6] * sc, y[7] * sc);
-      __nv_bfloat16* dst = (isk ? p.ws_k : p.ws_q) + ((long long)tok * p.Hk + gk) * kD + 8 * l16;
-      *reinterpret_cast<uint4*>(dst) = o4;
+      const int gk = isk ? head - p.Hk : head;
+      *reinterpret_cast<uint4*>((isk ? p.ws_k : p.ws_q) + (tok * p.Hk + gk) * kD + (c0 % kD)) = o4;
+    } else {
+      o4.x = bf2_u32(y[0], y[1]);
+      o4.y = bf2_u32(y[2], y[3]);
+      o4.z = bf2_u32(y[4], y[5]);
+      o4.w = bf2_u32(y[6], y[7]);
+      *reinterpret_cast<uint4*>(p.ws_v + (tok * p.Hv + head) * kD + (c0 % kD)) = o4;
     }
   }
-  // v heads
-  for (int it = tid; it < p.Hv * (kD / 8); it += kConvThreads) {
-    const int h = it / (kD / 8), seg = it % (kD / 8);
-    const int gk = h / r, hh = h % r;
-    const int c0 = 2 * Kd + h * kD + 8 * seg;
-    const long long off = gk * grp + 2 * kD + (long long)hh * kD + 8 * seg;
-    float y[8];
-    conv8(c0, off, y);
-    uint4 o4;
-    o4.x = bf2_u32(y[0], y[1]);
-    o4.y = bf2_u32(y[2], y[3]);
-    o4.z = bf2_u32(y[4], y[5]);
-    o4.w = bf2_u32(y[6], y[7]);
-    *reinterpret_cast<uint4*>(p.ws_v + ((long long)tok * p.Hv + h) * kD + 8 * seg) = o4;
-  }
-  // gates
-  for (int h = tid; h < p.Hv; h += kConvThreads) {
-    const int gk = h / r, hh = h % r;
-    const __nv_bfloat16* barow = p.ba + (long long)tok * p.ld_ba + (long long)gk * 2 * r;
-    const float b = __bfloat162float(barow[hh]), a = __bfloat162float(barow[r + hh]);
-    p.ws_beta[(long long)tok * p.Hv + h] = sigmoidf_(b);
-    p.ws_lg[(long long)tok * p.Hv + h] = -__expf(p.A_log[h]) * softplusf(a + p.dt_bias[h]);
+  // the conv window after the request's last token
+  if (active && tb1 == T) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      cs_out[(long long)(c0 + e) * 3 + 0] = __float2bfloat16(x0[e]);
+      cs_out[(long long)(c0 + e) * 3 + 1] = __float2bfloat16(x1[e]);
+      cs_out[(long long)(c0 + e) * 3 + 2] = __float2bfloat16(x2[e]);
+    }
   }
 }
 
@@ -645,7 +693,11 @@ extern "C" int oscar_gdn_chunked(oscar::GdnParams* params, int T, void* ws, cuda
         cudaFuncSetAttribute(gdn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ScanLayout::kTotal));
     attr = true;
   }
-  gdn_conv_kernel<<<T, kConvThreads, 0, stream>>>(p);
+  {
+    const int conv_dim = 2 * p.Hk * kD + p.Hv * kD;
+    const int slices = (conv_dim / 8 + kConvThreads - 1) / kConvThreads;
+    gdn_conv_kernel<<<dim3(T / kConvTok + p.R, slices), kConvThreads, 0, stream>>>(p);
+  }
   gdn_wy_kernel<<<dim3(p.max_chunks, p.Hv), kWyThreads, WyLayout::kTotal, stream>>>(p);
   gdn_scan_kernel<<<dim3(p.R, p.Hv), kScanThreads, ScanLayout::kTotal, stream>>>(p);
   return (int)cudaGetLastError();

@@ -197,13 +197,36 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const bool row_ok = m < M;
       const float sa = row_ok ? ep.scale_a[m] : 0.f;
       const bool empty_split = kb0 >= kb1;
+      const bool red_vec = (ep.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
         sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c, r);
         sm100::tmem_ld_wait();
-        if (!row_ok || empty_split) continue;
+        if (empty_split) continue;
         const int nb = n0 + c;
+        if (ep.mode == 1 && red_vec && !ep.trans) {
+          // fp32 accumulate with 16-byte reductions (a quarter of the L2 reduction ops); the
+          // swapped layout keeps scalar reductions (a lane-quad transpose measured slower)
+          if (row_ok) {
+            float* dst = reinterpret_cast<float*>(ep.out) + (long long)m * ep.ldo + nb;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              if (nb + j + 3 < N) {
+                const float4 sb = __ldg(reinterpret_cast<const float4*>(ep.scale_b + nb + j));
+                asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + j),
+                             "f"((float)(int)r[j] * sa * sb.x), "f"((float)(int)r[j + 1] * sa * sb.y),
+                             "f"((float)(int)r[j + 2] * sa * sb.z), "f"((float)(int)r[j + 3] * sa * sb.w)
+                             : "memory");
+              } else {
+                for (int e = 0; e < 4 && nb + j + e < N; ++e)
+                  atomicAdd(dst + j + e, (float)(int)r[j + e] * sa * ep.scale_b[nb + j + e]);
+              }
+            }
+          }
+          continue;
+        }
+        if (!row_ok) continue;
         if (ep.mode == 0 && !ep.trans && nb + 32 <= N && (ep.ldo % 8) == 0 &&
             (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0) {
           __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long long)m * ep.ldo + nb;

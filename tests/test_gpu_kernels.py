@@ -38,8 +38,11 @@ def test_gemm_i8_bf16(M, N, K):
     assert _rel(y, ref) < 5e-3
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 5120, 6144), (16, 1280, 4352), (512, 640, 1536)])
+@pytest.mark.parametrize("M,N,K", [(128, 5120, 6144), (16, 1280, 4352), (512, 640, 1536), (300, 1030, 1024),
+                                   (24, 2050, 1024)])
 def test_gemm_i8_accumulate_splitk(M, N, K):
+    """Swapped (decode) and plain (prefill, 16-byte reductions) accumulate layouts, and the
+    scalar fallback for rows that are not 16-byte aligned."""
     g = torch.Generator(device=DEV).manual_seed(N)
     x = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=DEV, generator=g)
     w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=DEV, generator=g)
