@@ -256,6 +256,12 @@ class GDNLayer:
         # logical rows: [qkvz grouped per key head | ba grouped per key head]
         self.inp = _rand_qlinear(nk * grp + 2 * nv, H, base + 1, device, rows=[
             _blocks(k0, k0 + self.Hk, grp), _blocks(k0, k0 + self.Hk, 2 * self.r, nk * grp)])
+        # zero output rows up to a multiple of 8: the projection's rows stay 16-byte
+        # aligned (bf16), which the chunked prefill kernels' vector loads need at every TP size
+        pad = -self.inp.q.shape[0] % 8
+        if pad:
+            self.inp = QLinear(torch.cat([self.inp.q, self.inp.q.new_zeros(pad, H)]).contiguous(),
+                               torch.cat([self.inp.s, self.inp.s.new_ones(pad)]).contiguous())
         self.out = _rand_qlinear(H, nv * self.dv, base + 2, device, cols=_blocks(v0, v0 + self.Hv, self.dv))
         g = _gen(base + 3, device)
         Kd = nk * self.dk
@@ -293,7 +299,7 @@ class GDNLayer:
         proj = F.linear_i8(xq, xs, self.inp.q, self.inp.s, status=status)
         T = proj.shape[0]
         o = torch.empty(T, self.Hv * self.dv, dtype=torch.bfloat16, device=proj.device)
-        gdn_step(proj[:, :self.n_qkvz], proj[:, self.n_qkvz:], Hk=self.Hk, Hv=self.Hv, dk=self.dk, dv=self.dv,
+        gdn_step(proj[:, :self.n_qkvz], proj[:, self.n_qkvz:self.n_qkvz + self.n_ba], Hk=self.Hk, Hv=self.Hv, dk=self.dk, dv=self.dv,
                  conv_w=self.conv_w, A_log=self.A_log, dt_bias=self.dt_bias, norm_w=self.norm_w, eps=self.eps,
                  state=self.state, conv_state=self.conv_state, pend_x=self.pend_x, pend_ba=self.pend_ba,
                  parity=b.parity, req_slot=b.req_slot, q_start=b.q_start, n_commit=b.n_commit,
