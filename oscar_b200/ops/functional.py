@@ -7,6 +7,8 @@ numerics oracle of the GPU tests.
 """
 from __future__ import annotations
 
+import os
+
 import math
 from dataclasses import dataclass
 
@@ -108,6 +110,10 @@ class GemmPlan:
     splits: int
 
 
+# split-K work units per SM for accumulate GEMMs with fewer output tiles than SMs
+SPLIT_WAVES = int(os.environ.get("OSCAR_GEMM_SPLIT_WAVES", "1"))
+
+
 def plan_gemm(M: int, N: int, K: int, sms: int, allow_split: bool) -> GemmPlan:
     """Tile plan for ``y[M,N] = x[M,K] W[N,K]^T`` on ``sms`` SMs."""
     kblocks = max(1, (K + 127) // 128)
@@ -121,7 +127,7 @@ def plan_gemm(M: int, N: int, K: int, sms: int, allow_split: bool) -> GemmPlan:
         swap = False
     splits = 1
     if allow_split and tiles < sms:
-        splits = max(1, min(sms // max(tiles, 1), kblocks // 4, 16))
+        splits = max(1, min((SPLIT_WAVES * sms) // max(tiles, 1), kblocks // 4, 16))
     return GemmPlan(swap, bn, splits)
 
 
