@@ -240,11 +240,26 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             *reinterpret_cast<uint4*>(o + j) = v;
           }
         } else {
+          // the chunk's 32 column scales with 16-byte loads, ahead of the element loop
+          float sbv[32];
+          if (nb + 32 <= N && (reinterpret_cast<uintptr_t>(ep.scale_b + nb) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 f = __ldg(reinterpret_cast<const float4*>(ep.scale_b + nb + j));
+              sbv[j] = f.x;
+              sbv[j + 1] = f.y;
+              sbv[j + 2] = f.z;
+              sbv[j + 3] = f.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sbv[j] = nb + j < N ? __ldg(ep.scale_b + nb + j) : 0.f;
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int n = nb + j;
             if (n >= N) break;
-            const float v = (float)(int)r[j] * sa * ep.scale_b[n];
+            const float v = (float)(int)r[j] * sa * sbv[j];
             const long long idx = ep.trans ? (long long)n * ep.ldo + m : (long long)m * ep.ldo + n;
             if (ep.mode == 0) {
               reinterpret_cast<__nv_bfloat16*>(ep.out)[idx] = __float2bfloat16(v);
