@@ -330,7 +330,10 @@ class LLMEngine:
                 "max_qlen": max((q_start[i + 1] - q_start[i] for i in range(len(order))), default=0)}
         if self.dev.type == "cuda":
             fixed = 0
-            if static:
+            decode_only = all((q_start[i + 1] - q_start[i]) * self.g <= A.LONG_ROWS for i in range(len(order)))
+            if static or decode_only:
+                # decode / verify steps use the fixed split layout whether or not they are
+                # replayed from a CUDA graph, so both paths compute the same partials
                 n_blocks = sum((q_start[i + 1] - q_start[i]) * self.g // A.ROWS + 1 for i in range(len(order)))
                 fixed = max(1, (3 * self.sms) // max(1, self.Hk * n_blocks))
             plan_np = A.plan_attention_host(q_start, seq_lens, self.g, self.Hk, self.sms, fixed_splits=fixed)
