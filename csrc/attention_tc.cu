@@ -65,14 +65,14 @@ constexpr int kBarSoft = 1, kBarStats = 3;
 // unless a buffer was installed with oscar_attn_tc_trace (slot layout: 96 u64 per CTA).
 __device__ unsigned long long* g_tc_trace = nullptr;
 constexpr int kTraceSlots = 96;
-OSCAR_DEVICE void trace(int ev) {
-  unsigned long long* t = g_tc_trace;
+// The trace buffer pointer is read once per CTA (kernel start) so that a trace point costs
+// a timer read and a store, not a global load.
+OSCAR_DEVICE void trace(unsigned long long* t, int ev) {
   if (t != nullptr && ev < kTraceSlots)
     t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * kTraceSlots + ev] = globaltimer_ns();
 }
 // Raw value into a trace slot (e.g. a clock64 difference).
-OSCAR_DEVICE void trace_val(int ev, unsigned long long v) {
-  unsigned long long* t = g_tc_trace;
+OSCAR_DEVICE void trace_val(unsigned long long* t, int ev, unsigned long long v) {
   if (t != nullptr && ev < kTraceSlots) t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * kTraceSlots + ev] = v;
 }
 OSCAR_DEVICE unsigned long long clock_dep(float dep) {
@@ -81,8 +81,7 @@ OSCAR_DEVICE unsigned long long clock_dep(float dep) {
   return v;
 }
 // Same, ordered after the computation of `dep` (the timer read consumes it).
-OSCAR_DEVICE void trace_dep(int ev, float dep) {
-  unsigned long long* t = g_tc_trace;
+OSCAR_DEVICE void trace_dep(unsigned long long* t, int ev, float dep) {
   if (t != nullptr && ev < kTraceSlots) {
     uint64_t v;
     asm volatile("{\n\t.reg .f32 d;\n\tmov.f32 d, %1;\n\tmov.u64 %0, %%globaltimer;\n\t}" : "=l"(v) : "f"(dep));
@@ -276,6 +275,7 @@ OSCAR_DEVICE float rows_reduce(float (&v)[N]) {
 
 template <int N>
 __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnParams p) {
+  unsigned long long* const tr = g_tc_trace;  // per-CTA copy of the trace buffer pointer
   using L = TcLayout<N>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // swizzled operand tiles need 1024-byte aligned shared addresses
@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   const int n_pages = kv_stop > kv_begin ? (kv_stop - 1) / kPage - p_first + 1 : 0;
 
   // ---------------------------------------------------------------- setup
-  if (tid == 0) trace(0);
+  if (tid == 0) trace(tr, 0);
   if (warp == 0) {
     sm100::tmem_alloc(tmem_slot, kTmemCols);
     sm100::tmem_relinquish();
@@ -367,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  if (tid == 0) trace(1);
+  if (tid == 0) trace(tr, 1);
 
   if (warp == 0) {
     // ------------------------------------------------------------ page producer
@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           sm100::bulk_load(dst + kPageBytes, p.owner + (long long)(blk % p.stage_rows) * kPage, kPage * 4,
                            &B.raw_full[s]);
         issued = i + 1;
-        if (i < 8) trace(8 + i);
+        if (i < 8) trace(tr, 8 + i);
       }
       if (*abort_flag) {  // copies in flight must land before the CTA exits
         const uint64_t t0 = globaltimer_ns();
@@ -443,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           sm100::umma_f16_tmem_a(tbase + kColS + (i & 1) * N, tbase + kColK + kk * 8, qd, idq, kk > 0 ? 1u : 0u);
         }
         sm100::umma_commit(&B.s_full[i & 1]);
-        if (i < 8) trace(16 + i);
+        if (i < 8) trace(tr, 16 + i);
         sm100::umma_commit(B.k_empty);
         if (i >= 1) ok = pv(i - 1);
       }
@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       }
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(B.k_full);
-      if (ct == 0 && i < 8) trace(24 + i);
+      if (ct == 0 && i < 8) trace(tr, 24 + i);
 
       // V^T of dims ct and ct + 128 -> 2 x 64 columns
       if (i >= 2 && !sm100::mbar_wait(&B.v_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
@@ -558,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       sm100::tmem_st_wait();
       sm100::tc_fence_before();
       __syncwarp();
-      if (ct == 0 && i < 8) trace(32 + i);
+      if (ct == 0 && i < 8) trace(tr, 32 + i);
       if (lane == 0) {
         sm100::mbar_arrive(&B.v_full[i & 1]);
         sm100::mbar_arrive(&B.raw_empty[s]);
@@ -657,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       const int s = i % kRing, b = i & 1;
       bool ok = !dead && sm100::mbar_wait(&B.s_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
                                           kBudgetNs);
-      if (st == 0 && i < 4) trace(48 + 4 * i);
+      if (st == 0 && i < 4) trace(tr, 48 + 4 * i);
       float sc[N];
       if (ok) {
         uint32_t raw[N];
@@ -675,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         ok = sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs);
       }
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform before the shuffles below
-      if (st == 0 && i < 4) trace(49 + 4 * i);
+      if (st == 0 && i < 4) trace(tr, 49 + 4 * i);
       float vs = 0.f;
       bool need = false;
       if (ok) {
@@ -697,7 +697,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           }
         }
         const bool hist = pos < prefix;
-        if (i < 4) trace_dep(st == 0 ? 64 + 4 * i : kTraceSlots, ks + kz + vs);
+        if (i < 4) trace_dep(tr, st == 0 ? 64 + 4 * i : kTraceSlots, ks + kz + vs);
         const unsigned long long cl0 = clock_dep(ks + kz + vs);
         // per-row constants with 16-byte shared loads; the causal limits only matter on
         // pages that reach the current chunk
@@ -714,20 +714,20 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           dmax = fmaxf(dmax, sc[r] - mv);
         }
         need = dmax > kSlack;
-        if (i < 4) trace_dep(st == 0 ? 65 + 4 * i : kTraceSlots, sc[N - 1] + (need ? 1.f : 0.f));
+        if (i < 4) trace_dep(tr, st == 0 ? 65 + 4 * i : kTraceSlots, sc[N - 1] + (need ? 1.f : 0.f));
         const unsigned long long cl1 = clock_dep(sc[N - 1] + (need ? 1.f : 0.f));
-        if (st == 0 && i < 4) trace_val(80 + i, cl1 - cl0);
+        if (st == 0 && i < 4) trace_val(tr, 80 + i, cl1 - cl0);
       }
       // P' buffer b (and alpha/upd slot b) are free once P.V(i-2) and the stats of page i-2 are done
       if (ok && i >= 2)
         ok = sm100::mbar_wait(&B.p_empty[b], ((i >> 1) - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
-      if (st == 0 && i < 4) trace(50 + 4 * i);
+      if (st == 0 && i < 4) trace(tr, 50 + 4 * i);
       if (sm100::bar_red_or(kBarSoft, 128, !ok)) {
         aborted = true;
         break;
       }
       const bool upd_now = sm100::bar_red_or(kBarSoft, 128, need);
-      if (st == 0 && i < 4) trace(51 + 4 * i);
+      if (st == 0 && i < 4) trace(tr, 51 + 4 * i);
       if (upd_now) {
         // agree on the new row maxima
         {
@@ -784,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         __syncwarp();
         if (lane == 0) {
           sm100::mbar_arrive(&B.p_full[b]);
-          if (st == 0 && i < 8) trace(40 + i);
+          if (st == 0 && i < 8) trace(tr, 40 + i);
           sm100::mbar_arrive(&B.raw_empty[s]);
         }
       }
@@ -844,10 +844,10 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   }
 
   // ---------------------------------------------------------------- teardown
-  if (tid == 256) trace(2);  // softmax role done (outputs written)
+  if (tid == 256) trace(tr, 2);  // softmax role done (outputs written)
   sm100::tc_fence_before();
   __syncthreads();
-  if (tid == 0) trace(3);
+  if (tid == 0) trace(tr, 3);
   if (warp == 0) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tbase, kTmemCols);
