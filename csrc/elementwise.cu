@@ -86,11 +86,12 @@ __global__ void __launch_bounds__(NT) rmsnorm_quant_kernel(float* __restrict__ x
   float4* xr = reinterpret_cast<float4*>(x + (long long)t * ldx);
   float4* dr = delta ? reinterpret_cast<float4*>(delta + (long long)t * ldd) : nullptr;
   const float4* wr = reinterpret_cast<const float4*>(w);
-  float4 v[PV];
+  float4 v[PV], wv[PV];
   float ss = 0.f;
 #pragma unroll
   for (int e = 0; e < PV; ++e) {
     const int i = threadIdx.x + e * NT;
+    wv[e] = i < nv ? __ldg(wr + i) : make_float4(0.f, 0.f, 0.f, 0.f);  // in flight with the row loads
     v[e] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     if (dr && i < nv) {
       const float4 d = dr[i];
@@ -107,7 +108,7 @@ __global__ void __launch_bounds__(NT) rmsnorm_quant_kernel(float* __restrict__ x
   for (int e = 0; e < PV; ++e) {
     const int i = threadIdx.x + e * NT;
     if (i < nv) {
-      const float4 ww = wr[i];
+      const float4 ww = wv[e];
       v[e].x = __bfloat162float(__float2bfloat16(v[e].x * inv * (off + ww.x)));
       v[e].y = __bfloat162float(__float2bfloat16(v[e].y * inv * (off + ww.y)));
       v[e].z = __bfloat162float(__float2bfloat16(v[e].z * inv * (off + ww.z)));
@@ -219,12 +220,37 @@ __global__ void __launch_bounds__(kT) argmax_kernel(const __nv_bfloat16* __restr
   const __nv_bfloat16* r = logits + (long long)t * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += kT) {
-    const float x = __bfloat162float(r[i]);
+  auto take = [&](float x, int i) {
     if (x > bv || (x == bv && i < bi)) {
       bv = x;
       bi = i;
     }
+  };
+  if ((reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+    // 16-byte loads (8 logits), four in flight per thread; scalar tail
+    const int nv = V / 8;
+    const uint4* r4 = reinterpret_cast<const uint4*>(r);
+    int c = threadIdx.x;
+    for (; c + 3 * kT < nv; c += 4 * kT) {
+      uint4 w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) w[u] = __ldg(r4 + c + u * kT);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&w[u]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) take(__bfloat162float(h[e]), 8 * (c + u * kT) + e);
+      }
+    }
+    for (; c < nv; c += kT) {
+      const uint4 w = __ldg(r4 + c);
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) take(__bfloat162float(h[e]), 8 * c + e);
+    }
+    for (int i = 8 * nv + threadIdx.x; i < V; i += kT) take(__bfloat162float(r[i]), i);
+  } else {
+    for (int i = threadIdx.x; i < V; i += kT) take(__bfloat162float(r[i]), i);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {

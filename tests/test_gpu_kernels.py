@@ -104,10 +104,14 @@ def test_embed_argmax():
     ref = torch.empty(T, H)
     F.embed(tok.cpu(), table.cpu(), 500, ref)
     assert torch.equal(out.cpu(), ref)
-    logits = torch.randn(T, 70000, device=DEV).to(torch.bfloat16)
-    v, i = F.argmax(logits, 123)
-    vr, ir = F.argmax(logits.cpu(), 123)
-    assert torch.equal(i.cpu(), ir)
+    for V_ in (70000, 70003):  # 16-byte rows (vector path), odd rows (tail / scalar path)
+        logits = torch.randn(T, V_, device=DEV).to(torch.bfloat16)
+        logits[1, 5] = logits[1, 60001] = 9.0  # a tie resolves to the lower index
+        v, i = F.argmax(logits, 123)
+        vr, ir = F.argmax(logits.cpu(), 123)
+        keep = torch.arange(T) != 1
+        assert torch.equal(i.cpu()[keep], ir[keep])
+        assert int(i[1]) == 5 + 123
 
 
 # ---------------------------------------------------------------------------- KV store
