@@ -102,3 +102,54 @@ def test_tensor_parallel_matches_single_rank():
     err = (res[0][1] - single_hid).norm() / single_hid.norm()
     assert err < 0.15, err
     assert [o[0] for o in res[0][0]] == [o[0] for o in single]
+
+
+# Four ranks with more query heads than KV heads per rank and fewer KV heads than ranks:
+# each rank holds 3 query heads and a replica of its group's KV head, and 1 GDN key head
+# with its 3 value heads - the head layout of the target model at TP8.
+_TP4_CFG = dict(num_layers=4, num_attention_heads=12, num_key_value_heads=2, linear_num_key_heads=4,
+                linear_num_value_heads=12)
+
+
+def _tp4_hidden(tp=None):
+    m = HybridModel(tiny(**_TP4_CFG), tp=tp, device="cpu", seed=2)
+    eng = LLMEngine(m, num_blocks=64, max_slots=4, max_batched_tokens=512)
+    for p in PROMPTS:
+        eng.add_request(p, 4)
+    eng.step()  # one prefill step
+    out = [eng.requests[r].output[:1] for r in sorted(eng.requests)]
+    return eng.last[0].float().clone(), out
+
+
+def _tp4_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from oscar_b200.parallel.groups import init_distributed, make_groups
+    import torch.distributed as dist
+    init_distributed("gloo", timeout_s=180)
+    try:
+        hid, out = _tp4_hidden(make_groups(world))
+        q.put((rank, hid.numpy(), out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp4_with_replicated_kv_heads_matches_single_rank():
+    """TP=4 over 2 KV heads (replicated, two ranks per KV head) and 4 GDN key heads:
+    the ranks agree exactly and match TP=1 up to the per-shard activation quantisation
+    (same bound as the TP=2 test above)."""
+    single_hid, single_out = _tp4_hidden()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp4_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = {r: (torch.from_numpy(h), o) for r, h, o in (q.get(timeout=600) for _ in procs)}
+    for p in procs:
+        p.join(60)
+    for r in (1, 2, 3):
+        assert torch.equal(res[0][0], res[r][0])
+        assert res[0][1] == res[r][1]
+    err = (res[0][0] - single_hid).norm() / single_hid.norm()
+    assert err < 0.15, err
