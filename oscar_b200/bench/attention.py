@@ -18,7 +18,7 @@ then the attention kernel alone is timed with CUDA events, L2 flushed before eve
 sample, median of warm samples.  Reported: microseconds, bytes of KV the kernel must
 read, achieved GB/s and its fraction of the measured HBM copy bandwidth.
 
-    python -m oscar_b200.bench.attention [--hist 1024,8192,32768] [--batch 1,8,32] [--qlen 1,4]
+    python -m oscar_b200.bench.attention [--hist 1024,8192,32768] [--batch 1,8,32] [--qlen 1,4] [--trace]
 """
 from __future__ import annotations
 
@@ -177,6 +177,52 @@ def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16
     return res
 
 
+# Event slots of the tcgen05 decode kernel's per-CTA timeline (globaltimer ns, 96 per CTA):
+# 0 start, 1 setup done, 2 softmax role done, 3 end; 8+i page i copy issued, 16+i S(i)
+# issued, 24+i K(i) converted, 32+i V(i) converted, 40+i P(i) written; for pages 0-3 the
+# softmax marks 48+4i S ready, 49+4i S loaded, 50+4i P buffer free, 51+4i maxima agreed,
+# 64+4i metadata loaded, 65+4i score loop done, and slot 80+i the score loop's clock64 cycles.
+TRACE_EVENTS = {"issue": (8, 16), "qk": (16, 24), "kdone": (24, 32), "vdone": (32, 40), "pdone": (40, 48)}
+
+
+def trace_case(hist: int, batch: int, qlen: int, show: int = 3) -> dict:
+    """Per-CTA timeline of the tcgen05 INT2 decode kernel (one traced launch after warm-up).
+
+    Returns the kernel span, the CTA duration quantiles and, for the ``show`` longest CTAs,
+    every recorded event relative to the CTA's start (µs)."""
+    c = build_case(hist, batch, qlen)
+    fn = _kernel_only(c, 0, True)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    n_cta = c["plan"].n_work * c["hk"]
+    buf = torch.zeros(n_cta * 96, dtype=torch.int64, device=c["q"].device)
+    ext().attn_tc_trace(buf.data_ptr())
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        ext().attn_tc_trace(0)
+    t = buf.view(n_cta, 96).cpu().numpy().astype(np.float64)
+    started = t[:, 0] > 0
+    t0 = t[started, 0].min()
+    rel = np.where(t[:, :80] > 0, (t[:, :80] - t0) / 1000.0, np.nan)
+    dur = rel[:, 3] - rel[:, 0]
+    out = {"hist": hist, "batch": batch, "qlen": qlen, "ctas": int(n_cta),
+           "span_us": round(float(np.nanmax(rel[:, 3])), 2),
+           "cta_us_min_med_max": [round(float(np.nanmin(dur)), 2), round(float(np.nanmedian(dur)), 2),
+                                  round(float(np.nanmax(dur)), 2)], "ctas_shown": []}
+    for idx in np.argsort(-np.nan_to_num(dur))[:show]:
+        r = rel[idx]
+        ev = {k: [round(float(x - r[0]), 2) for x in r[a:b] if not np.isnan(x)] for k, (a, b) in TRACE_EVENTS.items()}
+        ev["softmax_pages"] = [[round(float(x - r[0]), 2) for x in r[48 + 4 * q:52 + 4 * q] if not np.isnan(x)]
+                               for q in range(4)]
+        ev["score_loop_cycles"] = [int(t[idx, 80 + q]) for q in range(4)]
+        out["ctas_shown"].append({"cta": int(idx), "work": c["plan"].work[idx % c["plan"].n_work].tolist(),
+                                  "dur_us": round(float(dur[idx]), 2), "events": ev})
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--hist", default="1024,8192,32768")
@@ -184,8 +230,16 @@ def main(argv=None):
     ap.add_argument("--qlen", default="1,4")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--prefill", action="store_true", help="also run the 9256-over-15360 continuation")
+    ap.add_argument("--trace", action="store_true",
+                    help="print the per-CTA timeline of the tcgen05 decode kernel instead of timing")
     args = ap.parse_args(argv)
     torch.cuda.init()
+    if args.trace:
+        for hist in map(int, args.hist.split(",")):
+            for batch in map(int, args.batch.split(",")):
+                for qlen in map(int, args.qlen.split(",")):
+                    print(json.dumps(trace_case(hist, batch, qlen)), flush=True)
+        return
     for hist in map(int, args.hist.split(",")):
         for batch in map(int, args.batch.split(",")):
             for qlen in map(int, args.qlen.split(",")):
