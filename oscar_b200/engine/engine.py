@@ -27,9 +27,10 @@ import numpy as np
 import torch
 
 from ..kv.offload import HostKVStore
-from ..models.qwen35 import HybridModel, StepBatch
+from ..models.qwen35 import P_MAX, HybridModel, StepBatch
 from ..ops import attention as A
 from ..ops.functional import num_sms
+from . import checks
 from .block_manager import BlockManager, SlotManager
 from .staging import seat_plan
 from ..utils import launches as _launches
@@ -341,6 +342,9 @@ class LLMEngine:
             meta["max_rb"], meta["n_work"] = plan_np[3], plan_np[4]
             meta["n_short"], meta["rpi_short"] = plan_np[6], plan_np[7]
             meta["n_tiles"] = int((plan_np[5][:, 2] >= 0).sum()) if plan_np[4] > plan_np[6] else 0
+        if checks.enabled():  # OSCAR_CHECK_STEPS=1: validate what the kernels will index with
+            checks.check_step(arrays, meta, num_blocks=self.bm.num_blocks, max_slots=self.slots.n, g=self.g,
+                              stage_rows=self.stage_rows, max_pending=P_MAX)
         return arrays, meta
 
     def _batch(self, d: dict, meta: dict) -> StepBatch:
