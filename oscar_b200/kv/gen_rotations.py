@@ -11,6 +11,9 @@ Same procedure as the reference's ``tools/gen_rotations.py:73-245``:
 4. eigen-decompose in fp64 on the CPU and compose ``R = U · H · P_br``,
 5. check orthogonality (1e-6) and save the v2 ``oscar_rotations.pt``.
 
+Weights: ``--weights DIR`` loads a Hugging Face checkpoint (the calibration then sees
+the real model's activations), else seeded random weights (``--weights-seed``).
+
 Prompts: ``--prompts FILE`` (one prompt per line, whitespace-separated token ids), or
 seeded random tokens (``--num-prompts``, ``--prompt-len``) for the random-weight
 models.  ``OSCAR_ASCEND_GEN_MAXLEN`` caps the prompt length like the reference.
@@ -81,6 +84,8 @@ def main(argv=None) -> int:
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--weights-seed", type=int, default=0)
+    ap.add_argument("--weights", default=None,
+                    help="Hugging Face model directory (config.json + safetensors); default: seeded random weights")
     ap.add_argument("--device", default=None, help="cpu: torch reference path")
     args = ap.parse_args(argv)
 
@@ -93,9 +98,16 @@ def main(argv=None) -> int:
     dev = torch.device("cpu") if args.device == "cpu" else torch.device("cuda", local)
     if dev.type == "cuda":
         torch.cuda.set_device(dev)
-    cfg = CONFIGS[args.model](**({} if args.layers is None else {"num_layers": args.layers}))
-    model = HybridModel(cfg, make_groups(world), device=dev, seed=args.weights_seed,
-                        oscar=OscarConfig.from_env(head_dim=cfg.head_dim), rotation="identity", mtp=False)
+    if args.weights:
+        from ..models.loader import config_from_hf, from_pretrained
+        hd = config_from_hf(args.weights).head_dim
+        model = from_pretrained(args.weights, make_groups(world), device=dev, oscar=OscarConfig.from_env(head_dim=hd),
+                                rotation="identity", mtp=False, num_layers=args.layers)
+        cfg = model.cfg
+    else:
+        cfg = CONFIGS[args.model](**({} if args.layers is None else {"num_layers": args.layers}))
+        model = HybridModel(cfg, make_groups(world), device=dev, seed=args.weights_seed,
+                            oscar=OscarConfig.from_env(head_dim=cfg.head_dim), rotation="identity", mtp=False)
     stats = calibrate(model, _prompts(args, cfg.vocab_size))
     merged = merge_across_ranks(stats, cfg.head_dim)
     if rank == 0:

@@ -19,6 +19,7 @@ framework's model that the reference runs on (``delivery/serve_oscar.sh:76-99``)
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass, field
 
@@ -77,6 +78,22 @@ class StepBatch:
         return int(self.tokens.shape[0])
 
 
+_RANDOM_INIT = [True]
+
+
+@contextlib.contextmanager
+def no_random_init():
+    """Inside this context the constructors allocate zero weights (unit scales) of the
+    same shapes instead of drawing random ones: the model is about to be overwritten by
+    a checkpoint, and drawing the random logical matrices of a 27B model first would
+    cost more time than loading it."""
+    _RANDOM_INIT.append(False)
+    try:
+        yield
+    finally:
+        _RANDOM_INIT.pop()
+
+
 def _gen(seed: int, device) -> torch.Generator:
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -88,6 +105,11 @@ def _rand_qlinear(N: int, K: int, seed: int, device, rows=None, cols=None) -> QL
     part: ``rows`` = list of ``(begin, end)`` row ranges (column-parallel) or ``cols`` =
     one ``(begin, end)`` column range (row-parallel; the per-row scale stays whole).  Every
     tensor-parallel size therefore holds slices of the same model."""
+    if not _RANDOM_INIT[-1]:
+        n = N if rows is None else sum(b - a for a, b in rows)
+        k = K if cols is None else cols[1] - cols[0]
+        return QLinear(torch.zeros(n, k, dtype=torch.int8, device=device),
+                       torch.ones(n, dtype=torch.float32, device=device))
     g = _gen(seed, device)
     q = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g, device=device)
     s = ((torch.rand(N, generator=g, device=device) * 0.5 + 0.75) / (73.3 * math.sqrt(K))).float()
@@ -100,6 +122,8 @@ def _rand_qlinear(N: int, K: int, seed: int, device, rows=None, cols=None) -> QL
 
 
 def _rand_vec(n: int, seed: int, device, std: float = 0.02, mean: float = 0.0) -> torch.Tensor:
+    if not _RANDOM_INIT[-1]:
+        return torch.full((n,), float(mean), dtype=torch.float32, device=device)
     g = _gen(seed, device)
     return (torch.randn(n, generator=g, device=device) * std + mean).float()
 
@@ -134,6 +158,7 @@ class FullAttentionLayer:
         nq, nk = cfg.num_attention_heads, cfg.num_key_value_heads
         h0 = tp.rank * self.Hq
         k0 = (tp.rank * nk) // tp.world if nk < tp.world else tp.rank * self.Hk
+        self.h0, self.k0 = h0, k0  # first query / KV head of this rank (checkpoint loading)
         kv_base = nq * 2 * D
         self.qkv = _rand_qlinear(nq * 2 * D + 2 * nk * D, H, base + 1, device, rows=[
             _blocks(h0, h0 + self.Hq, 2 * D), _blocks(k0, k0 + self.Hk, D, kv_base),
@@ -252,6 +277,7 @@ class GDNLayer:
         base = seed * 1000 + layer_id * 17
         nk, nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
         k0, v0 = tp.rank * self.Hk, tp.rank * self.Hv
+        self.k0, self.v0 = k0, v0  # first key / value head of this rank (checkpoint loading)
         grp = 2 * self.dk + 2 * self.r * self.dv
         # logical rows: [qkvz grouped per key head | ba grouped per key head]
         self.inp = _rand_qlinear(nk * grp + 2 * nv, H, base + 1, device, rows=[
@@ -314,6 +340,7 @@ class MLP:
         base = seed * 1000 + layer_id * 17 + 50
         I_full = cfg.intermediate_size
         i0 = tp.rank * self.I
+        self.i0 = i0  # first intermediate column of this rank (checkpoint loading)
         self.gate_up = _rand_qlinear(2 * I_full, H, base + 1, device, rows=[
             (i0, i0 + self.I), (I_full + i0, I_full + i0 + self.I)])
         self.down = _rand_qlinear(H, I_full, base + 2, device, cols=(i0, i0 + self.I))
@@ -344,7 +371,8 @@ class HybridModel:
         g = _gen(base + 999, dev)
         v0, v1 = self.vocab_begin, min(V, self.vocab_begin + self.V_local)
         emb = torch.zeros(self.V_local, H, dtype=torch.bfloat16, device=dev)
-        emb[:v1 - v0] = (torch.randn(V, H, generator=g, device=dev) * 0.02)[v0:v1].to(torch.bfloat16)
+        if _RANDOM_INIT[-1]:
+            emb[:v1 - v0] = (torch.randn(V, H, generator=g, device=dev) * 0.02)[v0:v1].to(torch.bfloat16)
         self.embed = emb
         self.lm_head = _rand_qlinear(V, H, base + 998, dev, rows=[(v0, v1)])  # only real vocab rows
         self.final_norm = _rand_vec(H, base + 997, dev)

@@ -9,8 +9,10 @@ concurrent sequences, MTP with 3 draft tokens, OSCAR INT2 KV for the FULL layers
 (rotations from ``OSCAR_ASCEND_K_ROTATION_PATH`` / ``V_ROTATION_PATH`` when set, else
 seeded random orthogonal), the cache sized from free memory by the budget seam.
 Every rank prints its READY manifest; rank 0 serves HTTP, the others follow it in
-lockstep.  Weights are random (seeded) - this framework ships no checkpoint loader
-for the target model's real weights.
+lockstep.  ``--weights DIR`` serves a Hugging Face Qwen3.5 checkpoint (``config.json``
+and safetensors, quantised to W8A8 at load, each rank reading its own slices; the
+tokenizer is taken from the same directory when it has one), else the weights are
+random (seeded) of the ``--model`` shape.
 """
 from __future__ import annotations
 
@@ -37,6 +39,8 @@ def parse(argv=None):
     ap.add_argument("--gpu-memory-utilization", type=float, default=0.9)
     ap.add_argument("--num-blocks", type=int, default=None, help="fixed block count (testing)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--weights", default=None,
+                    help="Hugging Face model directory (config.json + safetensors); default: random weights")
     ap.add_argument("--tokenizer", default=None, help="local HF tokenizer directory (optional)")
     ap.add_argument("--device", default=None, help="cpu runs the torch reference path (testing)")
     return ap.parse_args(argv)
@@ -55,12 +59,22 @@ def build(args):
     if dev.type == "cuda":
         torch.cuda.set_device(dev)
     tp = make_groups(tp=world)
-    cfg = CONFIGS[args.model](**({} if args.layers is None else {"num_layers": args.layers}))
+    if args.weights:
+        from ..models.loader import config_from_hf
+        cfg = config_from_hf(args.weights)
+    else:
+        cfg = CONFIGS[args.model](**({} if args.layers is None else {"num_layers": args.layers}))
     oscar = OscarConfig.from_env(head_dim=cfg.head_dim)
     rot = "random"
     if oscar.k_rotation_path:
         rot = oscar.k_rotation_path
-    model = HybridModel(cfg, tp, device=dev, seed=args.seed, oscar=oscar, kv_mode=args.kv, rotation=rot)
+    if args.weights:
+        from ..models.loader import from_pretrained
+        model = from_pretrained(args.weights, tp, device=dev, oscar=oscar, kv_mode=args.kv, rotation=rot,
+                                num_layers=args.layers, seed=args.seed)
+        cfg = model.cfg
+    else:
+        model = HybridModel(cfg, tp, device=dev, seed=args.seed, oscar=oscar, kv_mode=args.kv, rotation=rot)
     if args.num_blocks is not None:
         blocks, budget = args.num_blocks, None
     else:
@@ -102,9 +116,12 @@ def main(argv=None) -> int:
     from .server import create_app
 
     tok = None
-    if args.tokenizer:
+    tok_dir = args.tokenizer
+    if tok_dir is None and args.weights and os.path.exists(os.path.join(args.weights, "tokenizer_config.json")):
+        tok_dir = args.weights
+    if tok_dir:
         from transformers import AutoTokenizer
-        tok = AutoTokenizer.from_pretrained(args.tokenizer, local_files_only=True)
+        tok = AutoTokenizer.from_pretrained(tok_dir, local_files_only=True)
     worker = EngineWorker(eng, control).start()
     app = create_app(worker, tok, mans, model_name=model.cfg.name, vocab_size=model.cfg.vocab_size)
     try:
