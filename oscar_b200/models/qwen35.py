@@ -32,6 +32,7 @@ from ..kv.rotation import get_layer_rotation, random_orthogonal
 from ..ops import attention as A
 from ..ops import functional as F
 from ..ops.gdn import gdn_step
+from ..ops import sampling as samp
 from ..parallel.fused import NcclRowReduce, make_row_reduce
 from ..parallel.groups import TPGroup
 from .config import HybridConfig
@@ -429,6 +430,17 @@ class HybridModel:
         if self.mtp is not None:
             self.mtp.layer.allocate_cache(num_blocks, self.device)
 
+    def reset_state_slots(self, slots: list) -> None:
+        """Zero the recurrent state and conv window of GDN state slots taken by new
+        requests: the kernels start a request from ``state[slot]`` and the conv window of
+        the slot, which still hold the previous occupant's."""
+        if not slots:
+            return
+        idx = torch.as_tensor(list(slots), dtype=torch.long).to(self.device)
+        for m in self.gdn_layers:
+            m.state.index_fill_(0, idx, 0)
+            m.conv_state.index_fill_(1, idx, 0)
+
     def cache_bytes(self) -> dict:
         full = sum(m.cache_bytes() for m in self.full_layers)
         gdn = sum(m.cache_bytes() for m in self.gdn_layers)
@@ -486,12 +498,15 @@ class HybridModel:
         xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, self.cfg.rms_norm_eps, want_bf16=True,
                                       status=self.status, **pending)
         rows = b.logit_rows
-        tok = self.sample(xq[rows], xs[rows])
+        tok = self.sample(xq[rows], xs[rows], b.extra.get("sampling"))
         return hid, tok
 
-    def sample(self, xq, xs) -> torch.Tensor:
-        """Greedy sampling over the vocab-parallel lm_head (global argmax across ranks)."""
+    def sample(self, xq, xs, rows: "samp.SampleRows | None" = None) -> torch.Tensor:
+        """Tokens over the vocab-parallel lm_head: greedy (global argmax across ranks), or,
+        with ``rows``, per-row temperature / top-k / top-p sampling and draft verification."""
         logits = F.linear_i8(xq, xs, self.lm_head.q, self.lm_head.s, status=self.status)
+        if rows is not None:
+            return samp.sample(logits, self.vocab_begin, rows, self.tp)
         v, i = F.argmax(logits, self.vocab_begin)
         if self.tp.world > 1:
             vs = self.tp.all_gather(v.unsqueeze(0))      # [world, n]

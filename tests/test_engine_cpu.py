@@ -153,3 +153,14 @@ def test_tp4_with_replicated_kv_heads_matches_single_rank():
         assert res[0][1] == res[r][1]
     err = (res[0][0] - single_hid).norm() / single_hid.norm()
     assert err < 0.15, err
+
+
+def test_reused_state_slot_starts_from_zero_state():
+    """A request that takes over a freed GDN state slot starts from a zero recurrent
+    state and conv window, not from the previous occupant's: with one slot, requests
+    run one after another give what each gives on a fresh engine."""
+    m = HybridModel(tiny(num_layers=4), device="cpu", seed=1)
+    eng = LLMEngine(m, num_blocks=64, max_slots=1, max_batched_tokens=512)
+    seq = [eng.generate([p], 5)[0] for p in (PROMPTS[0], PROMPTS[1], PROMPTS[0])]
+    fresh = [_gen(prompts=[p], n=5)[0][0] for p in (PROMPTS[0], PROMPTS[1])]
+    assert seq == [fresh[0], fresh[1], fresh[0]]
