@@ -9,9 +9,10 @@ A step:
    reference's packed serve setting ``delivery/serve_oscar.sh:64-74``);
 2. builds all step metadata on the host (block tables, slots, staging seat plan,
    attention work list, GDN commit counts) and uploads it once;
-3. runs the main model, verifies drafts (greedy or a seeded acceptance pattern),
-   then runs the MTP head over the step's rows and chains ``num_spec - 1`` more
-   single-token draft passes.
+3. runs the main model, verifies drafts (greedy, a seeded acceptance pattern, or, for
+   requests with sampling parameters, exact speculative sampling: see
+   :mod:`oscar_b200.ops.sampling`), then runs the MTP head over the step's rows and
+   chains ``num_spec - 1`` more single-token draft passes.
 
 The GDN layers use deferred commit (see :mod:`oscar_b200.ops.gdn`), so a rejected
 draft costs no state rollback; FULL-layer KV of rejected positions is simply
@@ -30,6 +31,7 @@ from ..kv.offload import HostKVStore
 from ..models.qwen35 import P_MAX, HybridModel, StepBatch
 from ..ops import attention as A
 from ..ops.functional import num_sms
+from ..ops import sampling as samp
 from . import checks
 from .block_manager import BlockManager, SlotManager
 from .staging import seat_plan
@@ -51,6 +53,8 @@ class Request:
     first_token_time: float | None = None
     finish_time: float | None = None
     accepted: list = field(default_factory=list)
+    sampling: samp.SamplingParams | None = None  # None or temperature 0: greedy
+    seed: int = 0
 
     @property
     def prefill_done(self) -> bool:
@@ -77,8 +81,9 @@ class SeededAcceptance:
 class LLMEngine:
     def __init__(self, model: HybridModel, num_blocks: int, max_slots: int, max_batched_tokens: int = 15360,
                  num_spec: int = 3, acceptance: SeededAcceptance | None = None, prefill_policy: str = "fcfs",
-                 timer=time.perf_counter, offload: bool = False):
+                 timer=time.perf_counter, offload: bool = False, seed: int = 0):
         self.model = model
+        self.seed = int(seed)  # seeds the sampled requests that bring no seed of their own
         self.dev = model.device
         self.num_spec = num_spec if model.mtp is not None else 0
         self.bm = BlockManager(num_blocks)
@@ -133,9 +138,14 @@ class LLMEngine:
         if rid in self.finished:
             self.finished.remove(rid)
 
-    def add_request(self, prompt, max_new_tokens: int) -> int:
+    def add_request(self, prompt, max_new_tokens: int, sampling: samp.SamplingParams | None = None) -> int:
         rid = next(self._ids)
-        self.requests[rid] = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer())
+        r = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer())
+        if sampling is not None and not sampling.validate().greedy:
+            r.sampling = sampling
+            r.seed = int(sampling.seed) if sampling.seed is not None else int(
+                samp.hash32(torch.tensor([(self.seed * 0x9E3779B1 + rid) & 0xFFFFFFFF])).item())
+        self.requests[rid] = r
         self.waiting.append(rid)
         return rid
 
@@ -183,8 +193,11 @@ class LLMEngine:
             self._swap_out(victims[0])
         return True
 
-    def generate(self, prompts, max_new_tokens: int) -> list[list[int]]:
-        ids = [self.add_request(p, max_new_tokens) for p in prompts]
+    def generate(self, prompts, max_new_tokens: int, sampling=None) -> list[list[int]]:
+        """Runs ``prompts`` to completion; ``sampling`` is one :class:`SamplingParams` for
+        all of them, a list with one per prompt, or None (greedy)."""
+        sps = sampling if isinstance(sampling, (list, tuple)) else [sampling] * len(prompts)
+        ids = [self.add_request(p, max_new_tokens, sp) for p, sp in zip(prompts, sps)]
         while self.has_work():
             self.step()
         return [self.requests[i].output[:max_new_tokens] for i in ids]
@@ -213,6 +226,7 @@ class LLMEngine:
             sched.append((rid, "verify", n))
             scheduled.add(rid)
             budget -= n
+        fresh: list = []  # state slots of requests starting this step
         candidates = [rid for rid in self.running if not self.requests[rid].prefill_done] + list(self.waiting)
         if self.prefill_policy == "wide" and candidates:
             share = max(1, budget // len(candidates))
@@ -230,11 +244,13 @@ class LLMEngine:
             self.bm.ensure(rid, r.num_computed + n + extra)
             if r.slot < 0:
                 r.slot = self.slots.acquire(rid)
+                fresh.append(r.slot)
             if rid in self.waiting:
                 self.waiting.remove(rid)
                 self.running.append(rid)
             sched.append((rid, "prefill", n))
             budget -= n
+        self.model.reset_state_slots(fresh)
         return sched
 
     # ------------------------------------------------------------------ metadata
@@ -275,7 +291,7 @@ class LLMEngine:
             out[k] = dbuf[o:o + sz].view(np.asarray(v).shape)
         return out
 
-    def _arrays(self, rows, logit_rows, commit_info, keep, static: bool = False):
+    def _arrays(self, rows, logit_rows, commit_info, keep, static: bool = False, extra: dict | None = None):
         """Host metadata of one batch: ``(arrays, meta)``.
 
         ``static=True`` makes every array shape depend only on the batch shape (bucketed
@@ -327,6 +343,8 @@ class LLMEngine:
         arrays = dict(tokens=toks, positions=poss, slots=slots, q_start=q_start, seq_lens=seq_lens, bt=bt,
                       tok_req=tok_req, stage_seat=stage_seat, owner_seat=owner_seat, owner_val=owner_val,
                       req_slot=req_slot, n_commit=n_commit, keep=keep_p, parity=parity, logit_rows=logit_rows)
+        if extra:
+            arrays.update(extra)
         meta = {"q_start": q_start, "seq_lens": seq_lens, "order": order,
                 "max_qlen": max((q_start[i + 1] - q_start[i] for i in range(len(order))), default=0)}
         if self.dev.type == "cuda":
@@ -363,11 +381,13 @@ class LLMEngine:
             logit_rows=d["logit_rows"].long())
         b.extra["order"] = meta["order"]
         b.extra["max_qlen"] = meta["max_qlen"]
+        if "samp_t" in d:
+            b.extra["sampling"] = samp.rows_from_arrays(d)
         return b
 
-    def _build(self, rows, logit_rows, commit_info, keep):
+    def _build(self, rows, logit_rows, commit_info, keep, extra: dict | None = None):
         """Eager batch: host metadata uploaded with one copy."""
-        arrays, meta = self._arrays(rows, logit_rows, commit_info, keep)
+        arrays, meta = self._arrays(rows, logit_rows, commit_info, keep, extra=extra)
         return self._batch(self._upload(arrays), meta)
 
     # ------------------------------------------------------------------ CUDA graphs
@@ -440,6 +460,7 @@ class LLMEngine:
             return {}
         rows, logit_rows, commit, keep = [], [], {}, {}
         info = []
+        sp_rows = []  # per logit row: (request, position sampled, draft verified there or -1)
         for rid, kind, n in sched:
             r = self.requests[rid]
             base = len(rows)
@@ -447,23 +468,29 @@ class LLMEngine:
                 toks = [r.last_token] + r.drafts
                 keep[rid] = True
                 logit_rows.extend(range(base, base + n))
+                sp_rows += [(r, r.num_computed + i + 1, r.drafts[i] if i < len(r.drafts) else -1) for i in range(n)]
             else:
                 toks = r.prompt[r.num_computed:r.num_computed + n]
                 keep[rid] = False
                 if r.num_computed + n == len(r.prompt):
                     logit_rows.append(base + n - 1)
+                    sp_rows.append((r, len(r.prompt), -1))
             commit[rid] = r.pending_commit
             for i, t in enumerate(toks):
                 rows.append((rid, t, r.num_computed + i))
             info.append((rid, kind, n, base))
+        sampled = None
+        if any(r.sampling is not None for r, _, _ in sp_rows):
+            sampled = samp.host_rows([r.sampling for r, _, _ in sp_rows], [r.seed for r, _, _ in sp_rows],
+                                     [p for _, p, _ in sp_rows], [d for _, _, d in sp_rows])
         static = self.use_graphs and all(kind == "verify" for _, kind, _, _ in info)
         if static:
-            arrays, meta = self._arrays(rows, logit_rows, commit, keep, static=True)
+            arrays, meta = self._arrays(rows, logit_rows, commit, keep, static=True, extra=sampled)
             b = (arrays, meta)
             with self._segment():
                 hid, tok = self._run_phase("main", [(arrays, meta)], lambda bs: self._main_fn(bs[0]))
         else:
-            b = self._build(rows, logit_rows, commit, keep)
+            b = self._build(rows, logit_rows, commit, keep, extra=sampled)
             with self._segment():
                 hid, tok = self._main_fn(b)
         tok_h = tok.tolist()

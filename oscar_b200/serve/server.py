@@ -3,8 +3,12 @@
 The reference serves through vLLM's OpenAI server (``delivery/serve_oscar.sh:64-99``);
 this is the same surface for this framework's engine, kept minimal:
 
-* ``POST /v1/completions`` - ``{"prompt": str | [int], "max_tokens": int}``; returns the
-  generated token ids and, when a tokenizer is configured, the text;
+* ``POST /v1/completions`` - ``{"prompt": str | [int], "max_tokens": int, "temperature",
+  "top_k", "top_p", "seed"}``; returns the generated token ids and, when a tokenizer is
+  configured, the text.  Decoding is greedy unless ``temperature > 0`` (this server's
+  default is greedy, the benchmarks' setting, where OpenAI's is 1.0); ``top_k`` 0 or -1
+  and ``top_p`` 1 switch truncation off; a request without ``seed`` gets one derived from
+  the engine seed and its id;
 * ``GET /health``, ``GET /ready`` (the READY manifests), ``GET /metrics`` (Prometheus:
   requests, output tokens, TTFT / TPOT histograms, draft acceptance, free KV blocks).
 
@@ -21,6 +25,7 @@ from fastapi import FastAPI, HTTPException
 from fastapi.responses import PlainTextResponse
 from pydantic import BaseModel
 
+from ..ops.sampling import SamplingParams
 from .worker import EngineWorker
 
 
@@ -40,6 +45,10 @@ class CompletionRequest(BaseModel):
     prompt: str | list[int]
     max_tokens: int = 16
     model: str | None = None
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    seed: int | None = None
 
 
 def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = None, model_name: str = "oscar-b200",
@@ -73,8 +82,17 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             raise HTTPException(400, f"token ids must be in [0, {vocab_size})")
         if req.max_tokens < 1:
             raise HTTPException(400, "max_tokens must be >= 1")
+        sp = None
+        if req.temperature > 0:
+            sp = SamplingParams(req.temperature, max(0, req.top_k), req.top_p, req.seed)
+            try:
+                sp.validate()
+            except ValueError as e:
+                raise HTTPException(400, str(e)) from e
+        elif req.temperature < 0:
+            raise HTTPException(400, "temperature must be >= 0")
         t0 = time.time()
-        fut = worker.submit(prompt, req.max_tokens)
+        fut = worker.submit(prompt, req.max_tokens, sp)
         try:
             out = await asyncio.wrap_future(fut)
         except Exception as e:  # noqa: BLE001

@@ -3,10 +3,11 @@
 Rank 0 owns the request queue.  Every iteration it drains newly submitted requests,
 broadcasts them (with a stop flag) to the other ranks over a CPU (gloo) control
 group, adds them to its engine and runs one engine step; the other ranks receive the
-same message, add the same requests in the same order and run the same step.  The
-scheduler is deterministic and the sampled tokens are identical on every rank (the
-vocab-parallel argmax is all-gathered), so the engines stay in lockstep without any
-other coordination.  While idle, rank 0 sends an empty message every
+same message, add the same requests (with their sampling parameters) in the same order
+and run the same step.  The scheduler is deterministic and the sampled tokens are
+identical on every rank (the vocab-parallel argmax, or the sampler's per-rank
+statistics, are all-gathered and every rank draws the same seeded noise), so the
+engines stay in lockstep without any other coordination.  While idle, rank 0 sends an empty message every
 ``heartbeat_s`` so that the followers' blocking receive never hits the process-group
 timeout.
 """
@@ -19,6 +20,8 @@ from concurrent.futures import Future
 from dataclasses import dataclass, field
 
 import torch.distributed as dist
+
+from ..ops.sampling import SamplingParams
 
 
 @dataclass
@@ -75,11 +78,14 @@ class EngineWorker:
         self._last_msg = 0.0
         self.error: BaseException | None = None
 
-    def submit(self, prompt: list[int], max_tokens: int) -> Future:
+    def submit(self, prompt: list[int], max_tokens: int, sampling=None) -> Future:
+        """Queues a request; ``sampling`` is a :class:`SamplingParams` (None: greedy)."""
         if self.error is not None:
             raise RuntimeError(f"engine worker failed: {self.error!r}")
+        if sampling is not None:
+            sampling.validate()
         fut: Future = Future()
-        self.q.put((list(map(int, prompt)), int(max_tokens), fut))
+        self.q.put((list(map(int, prompt)), int(max_tokens), sampling, fut))
         if self.error is not None:  # the loop died while this was being queued
             self._fail_queued(self.error)
         return fut
@@ -87,7 +93,7 @@ class EngineWorker:
     def _fail_queued(self, err: BaseException) -> None:
         while True:
             try:
-                _, _, fut = self.q.get_nowait()
+                *_, fut = self.q.get_nowait()
             except queue.Empty:
                 return
             if not fut.done():
@@ -123,12 +129,13 @@ class EngineWorker:
                 new = self._drain(block=not eng.has_work() and not stop)
                 now = time.perf_counter()
                 if self.control is not None and (new or eng.has_work() or stop or now - self._last_msg > self.heartbeat_s):
-                    self.control.exchange(([(p, m) for p, m, _ in new], stop))
+                    self.control.exchange(([(p, m, None if sp is None else sp.to_dict()) for p, m, sp, _ in new],
+                                           stop))
                     self._last_msg = now
                 if stop:
                     break
-                for p, m, fut in new:
-                    rid = eng.add_request(p, m)
+                for p, m, sp, fut in new:
+                    rid = eng.add_request(p, m, sp)
                     self.futures[rid] = fut
                     self.metrics.requests += 1
                 new = []
@@ -138,7 +145,7 @@ class EngineWorker:
                     self._resolve()
         except BaseException as e:  # noqa: BLE001 - surfaced to every pending request
             self.error = e
-            for fut in list(self.futures.values()) + [f for _, _, f in new]:
+            for fut in list(self.futures.values()) + [item[-1] for item in new]:
                 if not fut.done():
                     fut.set_exception(e)
             self._fail_queued(e)
@@ -165,8 +172,8 @@ def follower_loop(engine, control: ControlChannel) -> None:
         new, stop = control.exchange(None)
         if stop:
             return
-        for p, m in new:
-            engine.add_request(p, m)
+        for p, m, sp in new:
+            engine.add_request(p, m, None if sp is None else SamplingParams(**sp))
         if engine.has_work():
             engine.step()
             for rid in [rid for rid, r in engine.requests.items() if r.finished]:
