@@ -55,6 +55,9 @@ class Request:
     accepted: list = field(default_factory=list)
     sampling: samp.SamplingParams | None = None  # None or temperature 0: greedy
     seed: int = 0
+    stop_ids: frozenset = frozenset()  # generating one of these ends the request (it is kept)
+    stopped: bool = False
+    aborted: bool = False
 
     @property
     def prefill_done(self) -> bool:
@@ -62,7 +65,29 @@ class Request:
 
     @property
     def finished(self) -> bool:
-        return len(self.output) >= self.max_new_tokens
+        return self.stopped or self.aborted or len(self.output) >= self.max_new_tokens
+
+    @property
+    def finish_reason(self) -> str | None:
+        """``"stop"`` (a stop token), ``"length"`` (max_new_tokens), ``"abort"``, or None."""
+        if self.aborted:
+            return "abort"
+        if self.stopped:
+            return "stop"
+        return "length" if len(self.output) >= self.max_new_tokens else None
+
+    def emit(self, tokens: list) -> int:
+        """Appends generated tokens up to the first stop token or max_new_tokens; returns
+        how many were kept."""
+        n = 0
+        for t in tokens:
+            if len(self.output) >= self.max_new_tokens or self.stopped:
+                break
+            self.output.append(t)
+            n += 1
+            if t in self.stop_ids:
+                self.stopped = True
+        return n
 
 
 class SeededAcceptance:
@@ -138,9 +163,12 @@ class LLMEngine:
         if rid in self.finished:
             self.finished.remove(rid)
 
-    def add_request(self, prompt, max_new_tokens: int, sampling: samp.SamplingParams | None = None) -> int:
+    def add_request(self, prompt, max_new_tokens: int, sampling: samp.SamplingParams | None = None,
+                    stop_ids=None) -> int:
+        """Queues a request; ``stop_ids``: token ids that end it (an EOS id, say)."""
         rid = next(self._ids)
-        r = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer())
+        r = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer(),
+                    stop_ids=frozenset(int(t) for t in (stop_ids or ())))
         if sampling is not None and not sampling.validate().greedy:
             r.sampling = sampling
             r.seed = int(sampling.seed) if sampling.seed is not None else int(
@@ -151,6 +179,28 @@ class LLMEngine:
 
     def has_work(self) -> bool:
         return bool(self.waiting or self.running or self.swapped_q)
+
+    def abort(self, rid: int) -> None:
+        """Ends a request between steps (a client went away, a stop string was seen): its
+        blocks and state slot are freed; the tokens generated so far stay in ``output``."""
+        r = self.requests.get(rid)
+        if r is None or r.finished:
+            return
+        r.aborted = True
+        r.finish_time = self.timer()
+        if rid in self.waiting:
+            self.waiting.remove(rid)
+        if rid in self.running:
+            self.running.remove(rid)
+        if rid in self.swapped_q:
+            self.swapped_q.remove(rid)
+            self.offload.discard(rid)
+        else:
+            self.bm.free(rid)
+            self.slots.release(rid)
+        r.slot = -1
+        self.finished.append(rid)
+        self.stats["aborted"] = self.stats.get("aborted", 0) + 1
 
     # ------------------------------------------------------------------ preemption
     def _swap_out(self, rid: int) -> None:
@@ -193,11 +243,11 @@ class LLMEngine:
             self._swap_out(victims[0])
         return True
 
-    def generate(self, prompts, max_new_tokens: int, sampling=None) -> list[list[int]]:
+    def generate(self, prompts, max_new_tokens: int, sampling=None, stop_ids=None) -> list[list[int]]:
         """Runs ``prompts`` to completion; ``sampling`` is one :class:`SamplingParams` for
         all of them, a list with one per prompt, or None (greedy)."""
         sps = sampling if isinstance(sampling, (list, tuple)) else [sampling] * len(prompts)
-        ids = [self.add_request(p, max_new_tokens, sp) for p, sp in zip(prompts, sps)]
+        ids = [self.add_request(p, max_new_tokens, sp, stop_ids) for p, sp in zip(prompts, sps)]
         while self.has_work():
             self.step()
         return [self.requests[i].output[:max_new_tokens] for i in ids]
@@ -526,8 +576,7 @@ class LLMEngine:
                 r.num_computed += n_acc + 1
                 r.pending_commit = n_acc + 1
                 self.slots.parity[r.slot] ^= 1
-                r.output.extend(emitted)
-                self.stats["tokens_out"] += len(emitted)
+                self.stats["tokens_out"] += r.emit(emitted)
                 r.last_token = emitted[-1]
                 draft_rows.append((rid, base + n_acc))
             else:
@@ -538,8 +587,7 @@ class LLMEngine:
                     y = tok_h[li]
                     li += 1
                     next_row_tok[base + n - 1] = y
-                    r.output.append(y)
-                    self.stats["tokens_out"] += 1
+                    self.stats["tokens_out"] += r.emit([y])
                     r.last_token = y
                     r.first_token_time = now
                     draft_rows.append((rid, base + n - 1))

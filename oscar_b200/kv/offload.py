@@ -183,6 +183,12 @@ class HostKVStore:
         return sw
 
     # ------------------------------------------------------------ swap in
+    def discard(self, rid: int) -> None:
+        """Drop the host copy of a swapped-out request that will not come back (aborted)."""
+        sw = self.swapped.pop(rid, None)
+        if sw is not None and sw.event is not None:
+            sw.event.synchronize()  # no copy into the host buffers is still in flight
+
     def swap_in(self, rid: int, blocks: list[int], slot: int):
         """Restore ``rid`` into new ``blocks`` / ``slot``.  Returns ``(parity, seats, tags)``:
         the saved slot parity and the staging owner-tag updates (numpy, or None)."""

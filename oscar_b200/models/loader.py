@@ -91,6 +91,20 @@ def config_from_hf(source, name: str | None = None) -> HybridConfig:
     return cfg
 
 
+def eos_token_ids(path: str) -> list[int]:
+    """End-of-sequence token ids of a Hugging Face model directory: ``generation_config.json``
+    first, else ``config.json`` (its ``text_config`` too); an int or a list there."""
+    for fname in ("generation_config.json", "config.json"):
+        f = os.path.join(path, fname)
+        if not os.path.exists(f):
+            continue
+        raw = _read_json(f)
+        e = raw.get("eos_token_id", (raw.get("text_config") or {}).get("eos_token_id"))
+        if e is not None:
+            return [int(e)] if isinstance(e, int) else [int(x) for x in e]
+    return []
+
+
 def check_supported(cfg: HybridConfig) -> None:
     """Raises :class:`CheckpointError` when the geometry is not one the kernels implement."""
     bad = []

@@ -123,7 +123,12 @@ def main(argv=None) -> int:
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(tok_dir, local_files_only=True)
     worker = EngineWorker(eng, control).start()
-    app = create_app(worker, tok, mans, model_name=model.cfg.name, vocab_size=model.cfg.vocab_size)
+    eos = None
+    if args.weights:
+        from ..models.loader import eos_token_ids
+        eos = eos_token_ids(args.weights) or None  # None: the tokenizer's, if any
+    app = create_app(worker, tok, mans, model_name=model.cfg.name, vocab_size=model.cfg.vocab_size,
+                     eos_token_ids=eos, max_model_len=model.cfg.max_position)
     try:
         uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     finally:

@@ -4,11 +4,17 @@ The reference serves through vLLM's OpenAI server (``delivery/serve_oscar.sh:64-
 this is the same surface for this framework's engine, kept minimal:
 
 * ``POST /v1/completions`` - ``{"prompt": str | [int], "max_tokens": int, "temperature",
-  "top_k", "top_p", "seed"}``; returns the generated token ids and, when a tokenizer is
-  configured, the text.  Decoding is greedy unless ``temperature > 0`` (this server's
-  default is greedy, the benchmarks' setting, where OpenAI's is 1.0); ``top_k`` 0 or -1
-  and ``top_p`` 1 switch truncation off; a request without ``seed`` gets one derived from
-  the engine seed and its id;
+  "top_k", "top_p", "seed", "stream", "stop", "stop_token_ids", "ignore_eos"}``; returns
+  the generated token ids, the text and the finish reason (``"stop"`` or ``"length"``).
+  Decoding is greedy unless ``temperature > 0`` (this server's default is greedy, the
+  benchmarks' setting, where OpenAI's is 1.0); ``top_k`` 0 or -1 and ``top_p`` 1 switch
+  truncation off; a request without ``seed`` gets one derived from the engine seed and
+  its id.  ``stream: true`` answers with server-sent events, one per engine step that
+  produced tokens, then ``data: [DONE]``.  A stop string ends the request when it appears
+  in the text (it is cut from the text, and the request is aborted in the engine); stop
+  token ids and the model's EOS ids (unless ``ignore_eos``) end it in the engine.  A
+  streaming client that disconnects aborts its request;
+* ``GET /v1/models``;
 * ``GET /health``, ``GET /ready`` (the READY manifests), ``GET /metrics`` (Prometheus:
   requests, output tokens, TTFT / TPOT histograms, draft acceptance, free KV blocks).
 
@@ -19,10 +25,11 @@ from __future__ import annotations
 
 import asyncio
 import itertools
+import json
 import time
 
 from fastapi import FastAPI, HTTPException
-from fastapi.responses import PlainTextResponse
+from fastapi.responses import PlainTextResponse, StreamingResponse
 from pydantic import BaseModel
 
 from ..ops.sampling import SamplingParams
@@ -49,13 +56,63 @@ class CompletionRequest(BaseModel):
     top_k: int = 0
     top_p: float = 1.0
     seed: int | None = None
+    stream: bool = False
+    stop: str | list[str] | None = None
+    stop_token_ids: list[int] | None = None
+    ignore_eos: bool = False
+
+
+def _decoder(tok):
+    def decode(ids):
+        try:
+            return tok.decode(ids, skip_special_tokens=True)
+        except TypeError:
+            return tok.decode(ids)
+    return decode
+
+
+async def _events(aq: asyncio.Queue, decode, stops: list[str], on_stop):
+    """Text deltas of one request from its ``(new_ids, finish_reason)`` updates.  A stop
+    string ends the request (``on_stop`` aborts it) and is cut from the text; text that
+    could still become a stop string, or ends in an incomplete character, is held back
+    until the next update."""
+    ids: list[int] = []
+    sent = ""
+    hold = max((len(x) for x in stops), default=1) - 1
+    while True:
+        new, reason = await aq.get()
+        ids += new
+        text = decode(ids)
+        cuts = [text.find(x) for x in stops if x and x in text]
+        if cuts:
+            text = text[:min(cuts)]
+            if reason is None:
+                on_stop()
+            reason = "stop"
+        elif reason is None:
+            end = len(text) - hold
+            while end > len(sent) and text[end - 1:end] == "\ufffd":
+                end -= 1
+            text = text[:max(end, len(sent))]
+        delta = text[len(sent):] if text.startswith(sent) else ""
+        sent = text if text.startswith(sent) else sent
+        yield delta, new, reason
+        if reason is not None:
+            return
 
 
 def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = None, model_name: str = "oscar-b200",
-               vocab_size: int | None = None) -> FastAPI:
+               vocab_size: int | None = None, eos_token_ids=None, max_model_len: int | None = None) -> FastAPI:
+    """``eos_token_ids`` end every request that does not set ``ignore_eos`` (default: the
+    tokenizer's ``eos_token_id``, if it has one)."""
     app = FastAPI(title="oscar-b200")
     tok = tokenizer or ByteTokenizer()
+    decode = _decoder(tok)
     ids = itertools.count()
+    if eos_token_ids is None:
+        e = getattr(tokenizer, "eos_token_id", None)
+        eos_token_ids = [] if e is None else ([e] if isinstance(e, int) else list(e))
+    eos = [int(x) for x in eos_token_ids]
 
     @app.get("/health")
     def health():
@@ -66,6 +123,11 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
     @app.get("/ready")
     def ready():
         return {"manifests": manifests or []}
+
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "oscar-b200",
+                                            "max_model_len": max_model_len}]}
 
     @app.get("/metrics", response_class=PlainTextResponse)
     def metrics():
@@ -91,14 +153,78 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                 raise HTTPException(400, str(e)) from e
         elif req.temperature < 0:
             raise HTTPException(400, "temperature must be >= 0")
+        stops = [req.stop] if isinstance(req.stop, str) else list(req.stop or [])
+        stop_ids = list(req.stop_token_ids or []) + ([] if req.ignore_eos else eos)
+        loop = asyncio.get_running_loop()
+        aq: asyncio.Queue = asyncio.Queue()
         t0 = time.time()
-        fut = worker.submit(prompt, req.max_tokens, sp)
-        try:
-            out = await asyncio.wrap_future(fut)
-        except Exception as e:  # noqa: BLE001
-            raise HTTPException(500, f"generation failed: {e!r}") from e
-        return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(t0), "model": model_name,
-                "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": "length"}],
+
+        def on_tokens(new, reason):
+            if not loop.is_closed():  # the handler may have returned (stop string) before the engine ended
+                loop.call_soon_threadsafe(aq.put_nowait, (new, reason))
+
+        fut = worker.submit(prompt, req.max_tokens, sp, stop_ids, on_tokens=on_tokens)
+        cid = f"cmpl-{next(ids)}"
+
+        def chunk(text, token_ids, reason):
+            return {"id": cid, "object": "text_completion", "created": int(t0), "model": model_name,
+                    "choices": [{"index": 0, "text": text, "token_ids": token_ids, "logprobs": None,
+                                 "finish_reason": reason}]}
+
+        ended = asyncio.Event()
+        fut.add_done_callback(lambda _: None if loop.is_closed() else loop.call_soon_threadsafe(ended.set))
+
+        async def failed():
+            """The engine's error once the request's future resolved (None: no error).  The
+            future is watched, never awaited: cancelling an awaiting task would cancel it."""
+            await ended.wait()
+            return None if fut.cancelled() else fut.exception()
+
+        watch = asyncio.ensure_future(failed())
+        events = _events(aq, decode, stops, lambda: worker.abort(fut))
+
+        async def next_event():
+            """The next text delta, or the engine's error if it failed first."""
+            nxt = asyncio.ensure_future(events.__anext__())
+            await asyncio.wait({nxt, watch}, return_when=asyncio.FIRST_COMPLETED)
+            if not nxt.done():
+                err = watch.result()
+                if err is not None:
+                    nxt.cancel()
+                    raise RuntimeError(f"generation failed: {err!r}")
+                await nxt  # the future resolved; its last update is already queued
+            return nxt.result()
+
+        if req.stream:
+            async def sse():
+                done = False
+                try:
+                    reason = None
+                    while reason is None:
+                        try:
+                            text, new, reason = await next_event()
+                        except RuntimeError as e:
+                            yield f"data: {json.dumps({'error': str(e)})}\n\n"
+                            break
+                        yield f"data: {json.dumps(chunk(text, new, reason))}\n\n"
+                    done = True
+                    yield "data: [DONE]\n\n"
+                finally:
+                    if not done:
+                        worker.abort(fut)  # the client went away
+
+            return StreamingResponse(sse(), media_type="text/event-stream")
+
+        text, out, reason = "", [], None
+        while reason is None:
+            try:
+                delta, new, reason = await next_event()
+            except RuntimeError as e:
+                raise HTTPException(500, str(e)) from e
+            text += delta
+            out += new
+        return {"id": cid, "object": "text_completion", "created": int(t0), "model": model_name,
+                "choices": [{"index": 0, "text": text, "token_ids": out, "finish_reason": reason}],
                 "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(out),
                           "total_tokens": len(prompt) + len(out)}}
 

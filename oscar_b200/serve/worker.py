@@ -13,6 +13,7 @@ timeout.
 """
 from __future__ import annotations
 
+import itertools
 import queue
 import threading
 import time
@@ -46,7 +47,7 @@ class Metrics:
 
 
 class ControlChannel:
-    """Broadcast of (new requests, stop) from rank 0 over a gloo group."""
+    """Broadcast of (new requests, aborted request ids, stop) from rank 0 over a gloo group."""
 
     def __init__(self, group=None, src: int = 0):
         self.group = group
@@ -63,32 +64,64 @@ class ControlChannel:
         return obj[0]
 
 
+def _settle(fut: Future, result=None, error: BaseException | None = None) -> None:
+    """Resolves ``fut`` unless its consumer already cancelled it."""
+    if fut.done():
+        return
+    try:
+        if error is not None:
+            fut.set_exception(error)
+        else:
+            fut.set_result(result)
+    except Exception:  # noqa: BLE001 - cancelled concurrently
+        pass
+
+
 class EngineWorker:
-    """Rank-0 side: thread-safe submission, background stepping, futures per request."""
+    """Rank-0 side: thread-safe submission, background stepping, futures per request.
+
+    A request's future resolves to its generated token ids (``fut.finish_reason`` is set
+    first: ``"stop"``, ``"length"`` or ``"abort"``).  ``on_tokens(new_ids, finish_reason)``
+    is called from the engine thread after every step that produced tokens for the
+    request (``finish_reason`` None until the last call); :meth:`abort` ends a request
+    between steps, on every rank."""
 
     def __init__(self, engine, control: ControlChannel | None = None, heartbeat_s: float = 1.0):
         self.engine = engine
         self.control = control
         self.heartbeat_s = heartbeat_s
         self.q: queue.Queue = queue.Queue()
+        self.aborts: queue.Queue = queue.Queue()
         self.futures: dict[int, Future] = {}
         self.metrics = Metrics()
         self._stop = threading.Event()
         self._thread: threading.Thread | None = None
         self._last_msg = 0.0
+        self._handles = itertools.count()
+        self._rid_of: dict[int, int] = {}   # handle -> request id
+        self._sent: dict[int, int] = {}     # request id -> tokens passed to on_tokens
         self.error: BaseException | None = None
 
-    def submit(self, prompt: list[int], max_tokens: int, sampling=None) -> Future:
-        """Queues a request; ``sampling`` is a :class:`SamplingParams` (None: greedy)."""
+    def submit(self, prompt: list[int], max_tokens: int, sampling=None, stop_ids=None, on_tokens=None) -> Future:
+        """Queues a request; ``sampling`` is a :class:`SamplingParams` (None: greedy),
+        ``stop_ids`` token ids that end it.  The future has a ``handle`` for :meth:`abort`."""
         if self.error is not None:
             raise RuntimeError(f"engine worker failed: {self.error!r}")
         if sampling is not None:
             sampling.validate()
         fut: Future = Future()
-        self.q.put((list(map(int, prompt)), int(max_tokens), sampling, fut))
+        fut.handle = next(self._handles)
+        fut.finish_reason = None
+        fut.on_tokens = on_tokens
+        self.q.put((list(map(int, prompt)), int(max_tokens), sampling,
+                    tuple(int(t) for t in (stop_ids or ())), fut))
         if self.error is not None:  # the loop died while this was being queued
             self._fail_queued(self.error)
         return fut
+
+    def abort(self, fut: Future) -> None:
+        """Ends the request of ``fut`` at the next step boundary (no effect once finished)."""
+        self.aborts.put(fut.handle)
 
     def _fail_queued(self, err: BaseException) -> None:
         while True:
@@ -96,8 +129,7 @@ class EngineWorker:
                 *_, fut = self.q.get_nowait()
             except queue.Empty:
                 return
-            if not fut.done():
-                fut.set_exception(err)
+            _settle(fut, error=err)
 
     def start(self) -> "EngineWorker":
         self._thread = threading.Thread(target=self._run, name="oscar-engine", daemon=True)
@@ -120,41 +152,81 @@ class EngineWorker:
             pass
         return items
 
+    def _take_aborts(self, new: list) -> tuple[list, list]:
+        """Aborted handles -> (requests of this iteration still to add, request ids to abort)."""
+        handles = set()
+        while True:
+            try:
+                handles.add(self.aborts.get_nowait())
+            except queue.Empty:
+                break
+        if not handles:
+            return new, []
+        keep = []
+        for item in new:  # aborted before it was ever added: resolve it empty
+            fut = item[-1]
+            if fut.handle in handles:
+                fut.finish_reason = "abort"
+                if fut.on_tokens is not None:
+                    try:
+                        fut.on_tokens([], "abort")
+                    except Exception:  # noqa: BLE001
+                        pass
+                _settle(fut, [])
+            else:
+                keep.append(item)
+        rids = [self._rid_of[h] for h in handles if h in self._rid_of]
+        return keep, rids
+
     def _run(self) -> None:
         eng = self.engine
         new: list = []
         try:
             while True:
                 stop = self._stop.is_set()
-                new = self._drain(block=not eng.has_work() and not stop)
+                new = self._drain(block=not eng.has_work() and not stop and self.aborts.empty())
+                new, aborts = self._take_aborts(new)
                 now = time.perf_counter()
-                if self.control is not None and (new or eng.has_work() or stop or now - self._last_msg > self.heartbeat_s):
-                    self.control.exchange(([(p, m, None if sp is None else sp.to_dict()) for p, m, sp, _ in new],
-                                           stop))
+                if self.control is not None and (new or aborts or eng.has_work() or stop
+                                                 or now - self._last_msg > self.heartbeat_s):
+                    self.control.exchange(([(p, m, None if sp is None else sp.to_dict(), st) for p, m, sp, st, _ in new],
+                                           aborts, stop))
                     self._last_msg = now
                 if stop:
                     break
-                for p, m, sp, fut in new:
-                    rid = eng.add_request(p, m, sp)
+                for p, m, sp, st, fut in new:
+                    rid = eng.add_request(p, m, sp, st)
                     self.futures[rid] = fut
+                    self._rid_of[fut.handle] = rid
                     self.metrics.requests += 1
                 new = []
+                for rid in aborts:
+                    eng.abort(rid)
                 if eng.has_work():
                     eng.step()
                     self.metrics.steps += 1
-                    self._resolve()
+                self._resolve()
         except BaseException as e:  # noqa: BLE001 - surfaced to every pending request
             self.error = e
             for fut in list(self.futures.values()) + [item[-1] for item in new]:
-                if not fut.done():
-                    fut.set_exception(e)
+                _settle(fut, error=e)
             self._fail_queued(e)
 
     def _resolve(self) -> None:
         eng = self.engine
-        done = [rid for rid, f in self.futures.items() if eng.requests[rid].finished]
-        for rid in done:
+        for rid, fut in list(self.futures.items()):
             r = eng.requests[rid]
+            cb = fut.on_tokens
+            if cb is not None:
+                sent = self._sent.get(rid, 0)
+                if len(r.output) > sent or r.finished:
+                    self._sent[rid] = len(r.output)
+                    try:
+                        cb(list(r.output[sent:]), r.finish_reason if r.finished else None)
+                    except Exception:  # noqa: BLE001 - a consumer that went away must not stop the engine
+                        fut.on_tokens = None
+            if not r.finished:
+                continue
             out = r.output[:r.max_new_tokens]
             self.metrics.finished += 1
             self.metrics.tokens_out += len(out)
@@ -162,18 +234,24 @@ class EngineWorker:
                 self.metrics.ttft_s.append(r.first_token_time - r.arrival)
                 if len(out) > 1 and r.finish_time is not None:
                     self.metrics.tpot_s.append((r.finish_time - r.first_token_time) / (len(out) - 1))
-            self.futures.pop(rid).set_result(out)
+            self.futures.pop(rid)
+            self._sent.pop(rid, None)
+            self._rid_of.pop(fut.handle, None)
+            fut.finish_reason = r.finish_reason
+            _settle(fut, out)
             eng.release(rid)
 
 
 def follower_loop(engine, control: ControlChannel) -> None:
     """Ranks != 0: mirror rank 0's requests and steps until it says stop."""
     while True:
-        new, stop = control.exchange(None)
+        new, aborts, stop = control.exchange(None)
         if stop:
             return
-        for p, m, sp in new:
-            engine.add_request(p, m, None if sp is None else SamplingParams(**sp))
+        for p, m, sp, st in new:
+            engine.add_request(p, m, None if sp is None else SamplingParams(**sp), st)
+        for rid in aborts:
+            engine.abort(rid)
         if engine.has_work():
             engine.step()
             for rid in [rid for rid, r in engine.requests.items() if r.finished]:

@@ -252,3 +252,10 @@ def test_serve_and_rotation_calibration_take_a_checkpoint(exported, tmp_path, mo
     assert gen_main(["--out", str(out), "--weights", path, "--num-prompts", "2", "--prompt-len", "64",
                      "--device", "cpu"]) == 0
     assert sorted(Rt.load_checkpoint(str(out))) == [3]
+
+
+def test_eos_token_ids(tmp_path):
+    (tmp_path / "config.json").write_text(json.dumps({"text_config": {"eos_token_id": 7}}))
+    assert L.eos_token_ids(str(tmp_path)) == [7]
+    (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [3, 9]}))
+    assert L.eos_token_ids(str(tmp_path)) == [3, 9]

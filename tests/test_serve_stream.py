@@ -1,0 +1,215 @@
+"""Stop conditions, aborts and streaming (CPU): stop token ids end a request (also in
+the middle of an accepted MTP draft run), an abort frees a request's blocks between
+steps on every rank, the worker reports tokens step by step, and the HTTP server
+streams server-sent events, cuts stop strings and honours EOS / ``ignore_eos``."""
+from __future__ import annotations
+
+import json
+import os
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+from oscar_b200.engine.engine import LLMEngine
+from oscar_b200.models.config import tiny
+from oscar_b200.models.qwen35 import HybridModel
+from oscar_b200.serve.worker import EngineWorker
+
+PROMPTS = [[1, 2, 3, 4, 5] * 12, [7, 8, 9] * 10, list(range(11, 60))]
+
+
+def _engine(num_spec=3, tp=None):
+    m = HybridModel(tiny(num_layers=4), tp=tp, device="cpu", seed=1)
+    return LLMEngine(m, num_blocks=64, max_slots=4, max_batched_tokens=512, num_spec=num_spec)
+
+
+@pytest.mark.parametrize("num_spec", [0, 3])
+def test_stop_token_ends_the_request(num_spec):
+    full = _engine(num_spec).generate(PROMPTS, 12)
+    eng = _engine(num_spec)
+    stop = {full[0][4], full[1][2]}
+    rids = [eng.add_request(p, 12, stop_ids=stop) for p in PROMPTS]
+    while eng.has_work():
+        eng.step()
+    for rid, want in zip(rids, full):
+        r = eng.requests[rid]
+        cut = next((i for i, t in enumerate(want) if t in stop), None)
+        if cut is None:
+            assert r.output == want and r.finish_reason == "length"
+        else:
+            assert r.output == want[:cut + 1] and r.finish_reason == "stop"
+    assert eng.bm.free_blocks == 64
+
+
+def test_abort_frees_blocks_and_leaves_the_others_unchanged():
+    want = _engine().generate(PROMPTS, 10)
+    eng = _engine()
+    rids = [eng.add_request(p, 10) for p in PROMPTS]
+    for _ in range(3):
+        eng.step()
+    eng.abort(rids[1])
+    r = eng.requests[rids[1]]
+    assert r.finished and r.finish_reason == "abort" and r.output == want[1][:len(r.output)]
+    while eng.has_work():
+        eng.step()
+    assert [eng.requests[i].output for i in (rids[0], rids[2])] == [want[0], want[2]]
+    assert eng.bm.free_blocks == 64 and eng.slots.free_slots == 4
+    eng.abort(rids[0])  # finished: no effect
+    assert eng.requests[rids[0]].finish_reason == "length"
+
+
+def test_worker_streams_tokens_and_aborts():
+    want = _engine().generate(PROMPTS[:1], 8)[0]
+    w = EngineWorker(_engine()).start()
+    try:
+        seen = []
+        fut = w.submit(PROMPTS[0], 8, on_tokens=lambda new, reason: seen.append((list(new), reason)))
+        assert fut.result(timeout=120) == want
+        assert fut.finish_reason == "length"
+        assert sum((n for n, _ in seen), []) == want
+        assert [r for _, r in seen][-1] == "length" and all(r is None for _, r in seen[:-1])
+        hits = []
+
+        def stop_early(new, reason):
+            hits.append(len(new))
+            if len(hits) == 1:
+                w.abort(f2)
+
+        f2 = w.submit(PROMPTS[1], 400, on_tokens=stop_early)
+        out = f2.result(timeout=120)
+        assert f2.finish_reason == "abort" and 0 < len(out) < 400
+    finally:
+        w.stop()
+
+
+class _SpaceTokenizer:
+    """Token ids as space-separated numbers: stop strings are easy to place."""
+
+    eos_token_id = None
+
+    def encode(self, text):
+        return [int(x) for x in text.split()]
+
+    def decode(self, ids, skip_special_tokens=True):
+        return "".join(f" {i}" for i in ids)
+
+
+def _client(eos=None, tokenizer=None):
+    from fastapi.testclient import TestClient
+
+    from oscar_b200.serve.server import create_app
+
+    eng = _engine()
+    w = EngineWorker(eng).start()
+    app = create_app(w, tokenizer, vocab_size=eng.model.cfg.vocab_size, eos_token_ids=eos, max_model_len=8192)
+    return TestClient(app), w
+
+
+def _sse(resp):
+    events = [ln[len("data: "):] for ln in resp.iter_lines() if ln.startswith("data: ")]
+    assert events[-1] == "[DONE]"
+    return [json.loads(e) for e in events[:-1]]
+
+
+def test_http_streaming_matches_the_plain_response():
+    c, w = _client()
+    try:
+        body = {"prompt": PROMPTS[2], "max_tokens": 9}
+        plain = c.post("/v1/completions", json=body).json()["choices"][0]
+        with c.stream("POST", "/v1/completions", json={**body, "stream": True}) as resp:
+            chunks = _sse(resp)
+        ids = sum((ch["choices"][0]["token_ids"] for ch in chunks), [])
+        assert ids == plain["token_ids"]
+        assert "".join(ch["choices"][0]["text"] for ch in chunks) == plain["text"]
+        assert chunks[-1]["choices"][0]["finish_reason"] == "length" == plain["finish_reason"]
+        assert all(ch["choices"][0]["finish_reason"] is None for ch in chunks[:-1])
+        assert c.get("/v1/models").json()["data"][0]["max_model_len"] == 8192
+    finally:
+        w.stop()
+
+
+def test_http_stop_strings_stop_ids_and_eos():
+    c, w = _client(tokenizer=_SpaceTokenizer())
+    try:
+        prompt = " ".join(map(str, PROMPTS[2]))
+        full = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 10}).json()["choices"][0]
+        ids = full["token_ids"]
+        stop = f" {ids[3]}"
+        for stream in (False, True):
+            body = {"prompt": prompt, "max_tokens": 10, "stop": [stop, " never"], "stream": stream}
+            if stream:
+                with c.stream("POST", "/v1/completions", json=body) as resp:
+                    chunks = _sse(resp)
+                text = "".join(ch["choices"][0]["text"] for ch in chunks)
+                reason = chunks[-1]["choices"][0]["finish_reason"]
+            else:
+                got = c.post("/v1/completions", json=body).json()["choices"][0]
+                text, reason = got["text"], got["finish_reason"]
+            assert text == full["text"][:full["text"].find(stop)] and reason == "stop"
+        got = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 10,
+                                              "stop_token_ids": [ids[5]]}).json()["choices"][0]
+        assert got["token_ids"] == ids[:ids.index(ids[5]) + 1] and got["finish_reason"] == "stop"
+    finally:
+        w.stop()
+    c, w = _client(eos=[ids[2]], tokenizer=_SpaceTokenizer())
+    try:
+        got = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 10}).json()["choices"][0]
+        assert got["token_ids"] == ids[:ids.index(ids[2]) + 1] and got["finish_reason"] == "stop"
+        got = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 10,
+                                              "ignore_eos": True}).json()["choices"][0]
+        assert got["token_ids"] == ids and got["finish_reason"] == "length"
+    finally:
+        w.stop()
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _lockstep_abort(rank, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    from oscar_b200.parallel.groups import init_distributed, make_groups
+    from oscar_b200.serve.worker import ControlChannel, follower_loop
+    init_distributed("gloo", timeout_s=120)
+    try:
+        eng = _engine(tp=make_groups(2))
+        ctl = ControlChannel.create([0, 1])
+        if rank == 0:
+            w = EngineWorker(eng, ctl, heartbeat_s=0.2).start()
+            hits = []
+
+            def stop_early(new, reason):
+                hits.append(len(new))
+                if len(hits) == 2:
+                    w.abort(f2)
+
+            f1 = w.submit(PROMPTS[0], 6)
+            f2 = w.submit(PROMPTS[1], 300, on_tokens=stop_early)
+            outs = [f1.result(timeout=240), f2.result(timeout=240)]
+            w.stop()
+            q.put((0, [len(o) for o in outs], f2.finish_reason, eng.stats["steps"], eng.bm.free_blocks))
+        else:
+            follower_loop(eng, ctl)
+            q.put((1, None, None, eng.stats["steps"], eng.bm.free_blocks))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_abort_reaches_every_rank():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_lockstep_abort, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {r[0]: r[1:] for r in (q.get(timeout=300) for _ in ps)}
+    for p in ps:
+        p.join(60)
+    lens, reason, steps0, free0 = res[0]
+    assert lens[0] == 6 and 0 < lens[1] < 300 and reason == "abort"
+    assert res[1][2] == steps0 and res[1][3] == free0 == 64
