@@ -3,7 +3,8 @@
 BASELINE config 5 runs DP2 x TP4 on 8 GPUs; the reference rejects DP != 1
 (``oscar_ascend/integration.py:75-76``).  Here every DP replica is an independent
 TP serve group (``python -m oscar_b200.serve`` on its own port) and this router
-forwards each completion to the replica with the least outstanding work: prompt +
+forwards each completion or chat completion (streamed ones as a pass-through of the
+replica's server-sent events) to the replica with the least outstanding work: prompt +
 requested tokens of the requests it has sent there and not yet seen answered, ties
 broken by replica index (deterministic, so a replayed trace lands identically).
 
@@ -16,6 +17,7 @@ import threading
 
 import httpx
 from fastapi import FastAPI, HTTPException, Request
+from fastapi.responses import StreamingResponse
 
 
 class DPRouter:
@@ -41,8 +43,11 @@ class DPRouter:
 
 
 def request_cost(body: dict) -> int:
-    p = body.get("prompt", [])
-    n = len(p) if isinstance(p, list) else len(str(p).encode())
+    if "messages" in body:
+        n = sum(len(str(m.get("content", "")).encode()) for m in body["messages"])
+    else:
+        p = body.get("prompt", [])
+        n = len(p) if isinstance(p, list) else len(str(p).encode())
     return n + int(body.get("max_tokens", 16))
 
 
@@ -56,13 +61,36 @@ def create_router_app(backends: list[str], transport: httpx.AsyncBaseTransport |
     async def health():
         return {"ok": True, "replicas": len(backends), "load": router.load, "sent": router.sent}
 
-    @app.post("/v1/completions")
-    async def completions(req: Request):
+    async def forward(path: str, req: Request):
         body = await req.json()
         cost = request_cost(body)
         i = router.acquire(cost)
+        url = backends[i].rstrip("/") + path
+        if body.get("stream"):
+            # server-sent events pass through as they come; the replica's load is
+            # released when the stream ends (or the client goes away)
+            try:
+                r = await client.send(client.build_request("POST", url, json=body), stream=True)
+            except httpx.HTTPError as e:
+                router.release(i, cost)
+                raise HTTPException(502, f"replica {i} unreachable: {e!r}") from e
+            if r.status_code != 200:
+                text = (await r.aread()).decode(errors="replace")
+                await r.aclose()
+                router.release(i, cost)
+                raise HTTPException(r.status_code, text)
+
+            async def relay():
+                try:
+                    async for part in r.aiter_bytes():
+                        yield part
+                finally:
+                    await r.aclose()
+                    router.release(i, cost)
+
+            return StreamingResponse(relay(), media_type="text/event-stream", headers={"x-replica": str(i)})
         try:
-            r = await client.post(backends[i].rstrip("/") + "/v1/completions", json=body)
+            r = await client.post(url, json=body)
         except httpx.HTTPError as e:
             raise HTTPException(502, f"replica {i} unreachable: {e!r}") from e
         finally:
@@ -72,6 +100,14 @@ def create_router_app(backends: list[str], transport: httpx.AsyncBaseTransport |
         out = r.json()
         out["replica"] = i
         return out
+
+    @app.post("/v1/completions")
+    async def completions(req: Request):
+        return await forward("/v1/completions", req)
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: Request):
+        return await forward("/v1/chat/completions", req)
 
     app.state.router = router
     return app

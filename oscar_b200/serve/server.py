@@ -14,6 +14,10 @@ this is the same surface for this framework's engine, kept minimal:
   in the text (it is cut from the text, and the request is aborted in the engine); stop
   token ids and the model's EOS ids (unless ``ignore_eos``) end it in the engine.  A
   streaming client that disconnects aborts its request;
+* ``POST /v1/chat/completions`` - ``{"messages": [{"role", "content"}], ...}`` with the same
+  generation fields; the prompt is the tokenizer's chat template (``<|role|>`` headers
+  with the byte tokenizer), the answer a ``chat.completion`` (``chat.completion.chunk``
+  events when streaming);
 * ``GET /v1/models``;
 * ``GET /health``, ``GET /ready`` (the READY manifests), ``GET /metrics`` (Prometheus:
   requests, output tokens, TTFT / TPOT histograms, draft acceptance, free KV blocks).
@@ -60,6 +64,37 @@ class CompletionRequest(BaseModel):
     stop: str | list[str] | None = None
     stop_token_ids: list[int] | None = None
     ignore_eos: bool = False
+
+
+class ChatMessage(BaseModel):
+    role: str
+    content: str
+
+
+class ChatRequest(BaseModel):
+    messages: list[ChatMessage]
+    max_tokens: int = 16
+    model: str | None = None
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    seed: int | None = None
+    stream: bool = False
+    stop: str | list[str] | None = None
+    stop_token_ids: list[int] | None = None
+    ignore_eos: bool = False
+
+
+def chat_prompt(tok, messages: list[dict]) -> list[int]:
+    """Token ids of a chat: the tokenizer's chat template with the assistant turn opened,
+    or, for a tokenizer without one, ``<|role|>`` headers over the plain text."""
+    if hasattr(tok, "apply_chat_template"):
+        out = tok.apply_chat_template(messages, add_generation_prompt=True, tokenize=True)
+        if hasattr(out, "keys"):  # a BatchEncoding
+            out = out["input_ids"]
+        return [int(t) for t in out]
+    text = "".join(f"<|{m['role']}|>\n{m['content']}\n" for m in messages) + "<|assistant|>\n"
+    return tok.encode(text)
 
 
 def _decoder(tok):
@@ -135,9 +170,9 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
         lines = [f"oscar_{k} {float(v)}" for k, v in m.items() if v is not None]
         return "\n".join(lines) + "\n"
 
-    @app.post("/v1/completions")
-    async def completions(req: CompletionRequest):
-        prompt = tok.encode(req.prompt) if isinstance(req.prompt, str) else list(req.prompt)
+    async def generate(prompt: list[int], req, cid: str, chunk, final):
+        """Runs one request: ``chunk(text, ids, reason, first)`` builds a streamed event,
+        ``final(text, ids, reason)`` the plain response."""
         if not prompt:
             raise HTTPException(400, "empty prompt")
         if vocab_size is not None and (min(prompt) < 0 or max(prompt) >= vocab_size):
@@ -157,20 +192,12 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
         stop_ids = list(req.stop_token_ids or []) + ([] if req.ignore_eos else eos)
         loop = asyncio.get_running_loop()
         aq: asyncio.Queue = asyncio.Queue()
-        t0 = time.time()
 
         def on_tokens(new, reason):
             if not loop.is_closed():  # the handler may have returned (stop string) before the engine ended
                 loop.call_soon_threadsafe(aq.put_nowait, (new, reason))
 
         fut = worker.submit(prompt, req.max_tokens, sp, stop_ids, on_tokens=on_tokens)
-        cid = f"cmpl-{next(ids)}"
-
-        def chunk(text, token_ids, reason):
-            return {"id": cid, "object": "text_completion", "created": int(t0), "model": model_name,
-                    "choices": [{"index": 0, "text": text, "token_ids": token_ids, "logprobs": None,
-                                 "finish_reason": reason}]}
-
         ended = asyncio.Event()
         fut.add_done_callback(lambda _: None if loop.is_closed() else loop.call_soon_threadsafe(ended.set))
 
@@ -199,14 +226,15 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             async def sse():
                 done = False
                 try:
-                    reason = None
+                    reason, first = None, True
                     while reason is None:
                         try:
                             text, new, reason = await next_event()
                         except RuntimeError as e:
                             yield f"data: {json.dumps({'error': str(e)})}\n\n"
                             break
-                        yield f"data: {json.dumps(chunk(text, new, reason))}\n\n"
+                        yield f"data: {json.dumps(chunk(text, new, reason, first))}\n\n"
+                        first = False
                     done = True
                     yield "data: [DONE]\n\n"
                 finally:
@@ -223,9 +251,43 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                 raise HTTPException(500, str(e)) from e
             text += delta
             out += new
-        return {"id": cid, "object": "text_completion", "created": int(t0), "model": model_name,
-                "choices": [{"index": 0, "text": text, "token_ids": out, "finish_reason": reason}],
-                "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(out),
-                          "total_tokens": len(prompt) + len(out)}}
+        res = final(text, out, reason)
+        res["usage"] = {"prompt_tokens": len(prompt), "completion_tokens": len(out),
+                        "total_tokens": len(prompt) + len(out)}
+        return res
+
+    @app.post("/v1/completions")
+    async def completions(req: CompletionRequest):
+        prompt = tok.encode(req.prompt) if isinstance(req.prompt, str) else list(req.prompt)
+        cid, t0 = f"cmpl-{next(ids)}", int(time.time())
+        head = {"id": cid, "object": "text_completion", "created": t0, "model": model_name}
+
+        def chunk(text, token_ids, reason, first):
+            return {**head, "choices": [{"index": 0, "text": text, "token_ids": token_ids, "logprobs": None,
+                                         "finish_reason": reason}]}
+
+        def final(text, token_ids, reason):
+            return {**head, "choices": [{"index": 0, "text": text, "token_ids": token_ids,
+                                         "finish_reason": reason}]}
+
+        return await generate(prompt, req, cid, chunk, final)
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: ChatRequest):
+        prompt = chat_prompt(tok, [m.model_dump() for m in req.messages])
+        cid, t0 = f"chatcmpl-{next(ids)}", int(time.time())
+        head = {"id": cid, "created": t0, "model": model_name}
+
+        def chunk(text, token_ids, reason, first):
+            delta = {"role": "assistant", "content": text} if first else {"content": text}
+            return {**head, "object": "chat.completion.chunk",
+                    "choices": [{"index": 0, "delta": delta, "finish_reason": reason}]}
+
+        def final(text, token_ids, reason):
+            return {**head, "object": "chat.completion",
+                    "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
+                                 "finish_reason": reason}]}
+
+        return await generate(prompt, req, cid, chunk, final)
 
     return app

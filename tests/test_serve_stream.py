@@ -213,3 +213,60 @@ def test_abort_reaches_every_rank():
     lens, reason, steps0, free0 = res[0]
     assert lens[0] == 6 and 0 < lens[1] < 300 and reason == "abort"
     assert res[1][2] == steps0 and res[1][3] == free0 == 64
+
+
+class _TemplateTokenizer(_SpaceTokenizer):
+    """A tokenizer with a chat template that returns a BatchEncoding-like dict."""
+
+    def apply_chat_template(self, messages, add_generation_prompt=True, tokenize=True):
+        ids = [len(m["content"]) + 3 for m in messages] + ([9] if add_generation_prompt else [])
+        return {"input_ids": ids}
+
+
+def test_chat_completions():
+    from oscar_b200.serve.server import chat_prompt
+
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}]
+    assert chat_prompt(_TemplateTokenizer(), msgs) == [11, 5, 9]
+    c, w = _client()
+    try:
+        body = {"messages": msgs, "max_tokens": 6}
+        got = c.post("/v1/chat/completions", json=body).json()
+        assert got["object"] == "chat.completion" and got["choices"][0]["message"]["role"] == "assistant"
+        assert got["usage"]["completion_tokens"] == 6 and got["choices"][0]["finish_reason"] == "length"
+        # the fallback template, tokenised as text, is the prompt of a plain completion
+        from oscar_b200.serve.server import ByteTokenizer
+        plain = c.post("/v1/completions", json={"prompt": chat_prompt(ByteTokenizer(), msgs),
+                                                "max_tokens": 6}).json()["choices"][0]
+        assert got["choices"][0]["message"]["content"] == plain["text"]
+        with c.stream("POST", "/v1/chat/completions", json={**body, "stream": True}) as resp:
+            chunks = _sse(resp)
+        assert all(ch["object"] == "chat.completion.chunk" for ch in chunks)
+        assert chunks[0]["choices"][0]["delta"]["role"] == "assistant"
+        assert "".join(ch["choices"][0]["delta"]["content"] for ch in chunks) == plain["text"]
+    finally:
+        w.stop()
+
+
+def test_router_streams_through():
+    import httpx
+    from fastapi.testclient import TestClient
+
+    from oscar_b200.serve.router import create_router_app
+
+    sse = b'data: {"choices": [{"text": "a"}]}\n\ndata: {"choices": [{"text": "b"}]}\n\ndata: [DONE]\n\n'
+    seen = []
+
+    def handler(request: httpx.Request):
+        seen.append((str(request.url), json.loads(request.content)))
+        return httpx.Response(200, content=sse, headers={"content-type": "text/event-stream"})
+
+    app = create_router_app(["http://r0", "http://r1"], transport=httpx.MockTransport(handler))
+    with TestClient(app) as cl:
+        with cl.stream("POST", "/v1/chat/completions",
+                       json={"messages": [{"role": "user", "content": "x"}], "stream": True}) as resp:
+            body = b"".join(resp.iter_bytes())
+            assert resp.headers["x-replica"] == "0"
+        assert body == sse
+        assert cl.get("/health").json()["load"] == [0, 0]  # released when the stream ended
+    assert seen[0][0] == "http://r0/v1/chat/completions" and seen[0][1]["stream"] is True
