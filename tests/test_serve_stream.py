@@ -270,3 +270,36 @@ def test_router_streams_through():
         assert body == sse
         assert cl.get("/health").json()["load"] == [0, 0]  # released when the stream ended
     assert seen[0][0] == "http://r0/v1/chat/completions" and seen[0][1]["stream"] is True
+
+
+def test_serving_benchmark_client_against_a_live_server():
+    """The serving benchmark client drives a real uvicorn server on localhost."""
+    import asyncio
+    import threading
+    import time
+
+    import uvicorn
+
+    from oscar_b200.bench import serve_client as SC
+    from oscar_b200.serve.server import create_app
+
+    eng = _engine()
+    w = EngineWorker(eng).start()
+    port = _port()
+    server = uvicorn.Server(uvicorn.Config(create_app(w, vocab_size=eng.model.cfg.vocab_size), host="127.0.0.1",
+                                           port=port, log_level="warning"))
+    th = threading.Thread(target=server.run, daemon=True)
+    th.start()
+    try:
+        t0 = time.time()
+        while not server.started and time.time() - t0 < 30:
+            time.sleep(0.05)
+        prompts = SC.make_prompts(5, 40, 1024, seed=1)
+        out = asyncio.run(SC.run(f"http://127.0.0.1:{port}", prompts, output_len=7, concurrency=3))
+        assert out["completed"] == 5 and out["failed"] == 0 and out["output_tokens"] == 35
+        assert out["ttft_ms"]["mean"] > 0 and out["tpot_ms"]["mean"] > 0 and out["output_tok_per_s"] > 0
+        assert out["itl_ms"]["p99"] is not None
+    finally:
+        server.should_exit = True
+        th.join(30)
+        w.stop()
