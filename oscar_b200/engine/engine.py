@@ -163,9 +163,33 @@ class LLMEngine:
         if rid in self.finished:
             self.finished.remove(rid)
 
+    def max_request_tokens(self) -> int:
+        """Longest prompt + output a request may have: the RoPE tables end at the model's
+        ``max_position`` (a position past it would index outside them on the device), and a
+        request must fit in the KV pool with room for its speculative positions."""
+        spare = 2 * self.num_spec + 2
+        return min(self.model.cfg.max_position, self.bm.num_blocks * self.bm.page) - spare
+
+    def validate_request(self, prompt, max_new_tokens: int) -> None:
+        """Raises ValueError for a request the engine could never run (safe to call from
+        any thread: it reads only constants)."""
+        if len(prompt) == 0:
+            raise ValueError("empty prompt")
+        if int(max_new_tokens) < 1:
+            raise ValueError("max_new_tokens must be >= 1")
+        V = self.model.cfg.vocab_size
+        lo, hi = min(prompt), max(prompt)
+        if lo < 0 or hi >= V:
+            raise ValueError(f"prompt token ids must be in [0, {V})")
+        n, cap = len(prompt) + int(max_new_tokens), self.max_request_tokens()
+        if n > cap:
+            raise ValueError(f"prompt ({len(prompt)}) + max_new_tokens ({max_new_tokens}) = {n} tokens exceeds "
+                             f"the {cap} this engine serves")
+
     def add_request(self, prompt, max_new_tokens: int, sampling: samp.SamplingParams | None = None,
                     stop_ids=None) -> int:
         """Queues a request; ``stop_ids``: token ids that end it (an EOS id, say)."""
+        self.validate_request(prompt, max_new_tokens)
         rid = next(self._ids)
         r = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer(),
                     stop_ids=frozenset(int(t) for t in (stop_ids or ())))

@@ -197,7 +197,10 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             if not loop.is_closed():  # the handler may have returned (stop string) before the engine ended
                 loop.call_soon_threadsafe(aq.put_nowait, (new, reason))
 
-        fut = worker.submit(prompt, req.max_tokens, sp, stop_ids, on_tokens=on_tokens)
+        try:
+            fut = worker.submit(prompt, req.max_tokens, sp, stop_ids, on_tokens=on_tokens)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
         ended = asyncio.Event()
         fut.add_done_callback(lambda _: None if loop.is_closed() else loop.call_soon_threadsafe(ended.set))
 

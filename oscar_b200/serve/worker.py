@@ -109,6 +109,7 @@ class EngineWorker:
             raise RuntimeError(f"engine worker failed: {self.error!r}")
         if sampling is not None:
             sampling.validate()
+        self.engine.validate_request(prompt, max_tokens)  # raises here, not in the engine thread
         fut: Future = Future()
         fut.handle = next(self._handles)
         fut.finish_reason = None

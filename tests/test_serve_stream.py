@@ -303,3 +303,24 @@ def test_serving_benchmark_client_against_a_live_server():
         server.should_exit = True
         th.join(30)
         w.stop()
+
+
+def test_requests_the_engine_cannot_run_are_rejected_up_front():
+    """Too long for the RoPE tables or the KV pool, out-of-vocabulary ids, empty prompts:
+    rejected when submitted (HTTP 400), and the engine thread keeps serving."""
+    eng = _engine()
+    cap = eng.max_request_tokens()
+    assert cap == min(eng.model.cfg.max_position, 64 * 128) - 8
+    for prompt, n in (([1] * (cap - 3), 4), ([], 3), ([1, 2, 5000], 3), ([1, 2], 0), ([-1, 2], 3)):
+        with pytest.raises(ValueError):
+            eng.add_request(prompt, n)
+    eng.add_request([1] * (cap - 4), 4)  # exactly at the limit
+    c, w = _client()
+    try:
+        r = c.post("/v1/completions", json={"prompt": [1] * cap, "max_tokens": 4})
+        assert r.status_code == 400 and "exceeds" in r.json()["detail"]
+        ok = c.post("/v1/completions", json={"prompt": PROMPTS[0], "max_tokens": 3})
+        assert ok.status_code == 200 and len(ok.json()["choices"][0]["token_ids"]) == 3
+        assert w.error is None
+    finally:
+        w.stop()
