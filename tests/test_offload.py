@@ -33,3 +33,24 @@ def test_swap_preemption_matches_cpu():
 @pytest.mark.gpu
 def test_swap_preemption_matches_gpu():
     _check("cuda")
+
+
+def test_abort_of_a_swapped_out_request():
+    """Aborting a request while it sits in host memory drops its host copy; the others
+    finish as without preemption and every block comes back."""
+    ref, _ = _run(64, False)
+    m = HybridModel(tiny(num_layers=4), device="cpu", seed=6)
+    eng = LLMEngine(m, num_blocks=6, max_slots=4, max_batched_tokens=512, offload=True)
+    rids = [eng.add_request(p, 60) for p in PROMPTS]
+    victim = None
+    while eng.has_work():
+        eng.step()
+        if victim is None and eng.swapped_q:
+            victim = eng.swapped_q[0]
+            eng.abort(victim)
+            assert victim not in eng.offload.swapped and eng.requests[victim].finish_reason == "abort"
+    assert victim is not None
+    for rid, want in zip(rids, ref):
+        if rid != victim:
+            assert eng.requests[rid].output == want
+    assert eng.bm.free_blocks == 6 and not eng.offload.swapped
