@@ -30,6 +30,7 @@ class HybridConfig:
     rms_norm_eps: float = 1e-6
     num_mtp_layers: int = 1
     max_position: int = 262144
+    rope_scaling: dict | None = None  # e.g. {"rope_type": "yarn", "factor": 4.0, "original_max_position_embeddings": ...}
     name: str = "qwen35-27b"
     layer_types: list = field(default_factory=list)
 

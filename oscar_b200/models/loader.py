@@ -45,6 +45,10 @@ import torch
 from .config import HybridConfig
 from .qwen35 import GDNLayer, FullAttentionLayer, HybridModel, MLP, QLinear, no_random_init
 
+# RoPE scaling fields carried over from a checkpoint's rope_parameters
+YARN_KEYS = ("factor", "original_max_position_embeddings", "beta_fast", "beta_slow", "mscale", "mscale_all_dim",
+             "attention_factor", "truncate")
+
 # geometry the kernels are built for
 KERNEL_HEAD_DIM = 256
 KERNEL_LINEAR_HEAD_DIM = 128
@@ -73,6 +77,14 @@ def config_from_hf(source, name: str | None = None) -> HybridConfig:
     rope = dict(c.get("rope_parameters") or c.get("rope_scaling") or {})
     theta = rope.get("rope_theta", c.get("rope_theta", 1.0e7))
     partial = rope.get("partial_rotary_factor", c.get("partial_rotary_factor", 0.25))
+    kind = rope.get("rope_type", rope.get("type", "default"))
+    if kind == "yarn":
+        scaling = {k: rope[k] for k in YARN_KEYS if k in rope}
+        scaling["rope_type"] = "yarn"
+    elif kind in ("default", "mrope", None):
+        scaling = None
+    else:
+        raise CheckpointError(f"unsupported rope scaling {kind!r} (supported: default, yarn)")
     layers = int(c["num_hidden_layers"])
     interval = int(c.get("full_attention_interval", 4))
     types = list(c.get("layer_types") or [])
@@ -86,7 +98,8 @@ def config_from_hf(source, name: str | None = None) -> HybridConfig:
         linear_key_head_dim=int(c["linear_key_head_dim"]), linear_value_head_dim=int(c["linear_value_head_dim"]),
         linear_conv_kernel_dim=int(c.get("linear_conv_kernel_dim", 4)), rms_norm_eps=float(c.get("rms_norm_eps", 1e-6)),
         num_mtp_layers=int(c.get("mtp_num_hidden_layers", raw.get("mtp_num_hidden_layers", 0)) or 0),
-        max_position=int(c.get("max_position_embeddings", 262144)), name=name or "qwen35-hf", layer_types=types)
+        max_position=int(c.get("max_position_embeddings", 262144)), name=name or "qwen35-hf", layer_types=types,
+        rope_scaling=scaling)
     check_supported(cfg)
     return cfg
 
@@ -384,13 +397,14 @@ def load_checkpoint(model: HybridModel, source, strict: bool = True) -> LoadRepo
 
 def from_pretrained(path: str, tp=None, device="cpu", oscar=None, kv_mode: str = "int2", rotation: str = "random",
                     mtp: bool = True, num_layers: int | None = None, strict: bool = True,
-                    seed: int = 0) -> HybridModel:
+                    seed: int = 0, config: HybridConfig | None = None) -> HybridModel:
     """A :class:`HybridModel` of this rank holding the checkpoint in ``path`` (a Hugging Face
     model directory: ``config.json`` and ``*.safetensors``).  ``num_layers`` keeps only the
     first layers (testing); the MTP head is built when the config has one and ``mtp``;
     ``seed`` seeds what a checkpoint does not hold (the random KV rotations of
-    ``rotation="random"``)."""
-    cfg = config_from_hf(path)
+    ``rotation="random"``); ``config`` replaces the checkpoint's ``config.json`` (an
+    override such as a RoPE scaling applied to it)."""
+    cfg = config if config is not None else config_from_hf(path)
     if num_layers is not None and num_layers < cfg.num_layers:
         cfg = HybridConfig(**{**cfg.to_dict(), "num_layers": num_layers, "layer_types": cfg.layer_types[:num_layers]})
     with no_random_init():
@@ -486,7 +500,7 @@ def hf_config(cfg: HybridConfig) -> dict:
         "hidden_act": "silu", "tie_word_embeddings": False,
         "rope_parameters": {"rope_type": "default", "rope_theta": cfg.rope_theta,
                             "partial_rotary_factor": cfg.partial_rotary_factor, "mrope_section": [11, 11, 10],
-                            "mrope_interleaved": True},
+                            "mrope_interleaved": True, **(cfg.rope_scaling or {})},
     }
 
 

@@ -386,7 +386,7 @@ class HybridModel:
                 mixer = GDNLayer(cfg, self.tp, i, seed, dev)
             self.layers.append((mixer, MLP(cfg, self.tp, i, seed, dev)))
         self.mtp = MTPHead(self, seed) if (mtp and cfg.num_mtp_layers > 0) else None
-        self.rope = F.rope_tables(cfg.max_position, cfg.rot_dim, cfg.rope_theta, dev)
+        self.rope = F.rope_tables(cfg.max_position, cfg.rot_dim, cfg.rope_theta, dev, cfg.rope_scaling)
         self.stage_rows = 0
         self.owner = None
         self.status = torch.zeros(1, dtype=torch.int32, device=dev) if dev.type == "cuda" else None

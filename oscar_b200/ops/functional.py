@@ -7,9 +7,8 @@ numerics oracle of the GPU tests.
 """
 from __future__ import annotations
 
-import os
-
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -207,11 +206,60 @@ def argmax(logits: torch.Tensor, index_offset: int = 0) -> tuple[torch.Tensor, t
 # ---------------------------------------------------------------------------
 # RoPE tables
 # ---------------------------------------------------------------------------
-def rope_tables(max_pos: int, rot_dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
-    """fp32 ``cos/sin [max_pos, rot_dim/2]`` for rotate-half RoPE."""
-    inv = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.float64) / rot_dim))
+def rope_inv_freq(rot_dim: int, theta: float, scaling: dict | None = None,
+                  max_position: int | None = None) -> tuple[torch.Tensor, float]:
+    """float64 inverse frequencies ``[rot_dim / 2]`` and the cos/sin scale of RoPE.
+
+    ``scaling`` None (or ``rope_type`` "default"): ``theta^(-2j / rot_dim)``, scale 1.
+    ``rope_type`` "yarn" (Peng et al. 2023, "YaRN: Efficient Context Window Extension of
+    Large Language Models"), with ``factor`` s (default ``max_position /
+    original_max_position_embeddings``), ``original_max_position_embeddings`` L,
+    ``beta_fast`` (32) and ``beta_slow`` (1): the dimension whose wavelength completes r
+    rotations over L is ``d(r) = rot_dim ln(L / (2 pi r)) / (2 ln theta)``; frequencies of
+    index ``j <= d(beta_fast)`` are kept, those of index ``j >= d(beta_slow)`` divided by s
+    (bounds floored / ceiled unless ``truncate`` is false, clamped to the dimensions), with
+    a linear ramp in ``j`` between.  The scale is ``0.1 ln s + 1`` (s > 1), or the ratio of
+    that form with ``mscale`` / ``mscale_all_dim`` when both are given, or an explicit
+    ``attention_factor``."""
+    j = torch.arange(0, rot_dim // 2, dtype=torch.float64)
+    base = 1.0 / (theta ** (2.0 * j / rot_dim))
+    kind = (scaling or {}).get("rope_type", (scaling or {}).get("type", "default"))
+    if kind in ("default", None, "mrope"):
+        return base, 1.0
+    if kind != "yarn":
+        raise ValueError(f"unsupported rope scaling {kind!r} (supported: default, yarn)")
+    L = float(scaling["original_max_position_embeddings"])
+    s = scaling.get("factor")
+    s = float(s) if s is not None else float(max_position) / L
+
+    def ms(x: float, m: float = 1.0) -> float:
+        return 1.0 if x <= 1 else 0.1 * m * math.log(x) + 1.0
+
+    scale = scaling.get("attention_factor")
+    if scale is None:
+        m1, m2 = scaling.get("mscale"), scaling.get("mscale_all_dim")
+        scale = ms(s, m1) / ms(s, m2) if (m1 and m2) else ms(s)
+
+    def dim_of(rot: float) -> float:
+        return rot_dim * math.log(L / (2 * math.pi * rot)) / (2 * math.log(theta))
+
+    lo, hi = dim_of(float(scaling.get("beta_fast") or 32)), dim_of(float(scaling.get("beta_slow") or 1))
+    if scaling.get("truncate", True):
+        lo, hi = math.floor(lo), math.ceil(hi)
+    lo, hi = max(lo, 0), min(hi, rot_dim - 1)
+    if hi == lo:
+        hi += 0.001
+    ramp = ((j - lo) / (hi - lo)).clamp(0.0, 1.0)  # 0: keep the frequency, 1: divide it by s
+    return base * (1.0 - ramp) + (base / s) * ramp, float(scale)
+
+
+def rope_tables(max_pos: int, rot_dim: int, theta: float, device,
+                scaling: dict | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 ``cos/sin [max_pos, rot_dim/2]`` for rotate-half RoPE (scaled by the RoPE
+    scaling's cos/sin factor; see :func:`rope_inv_freq`)."""
+    inv, scale = rope_inv_freq(rot_dim, theta, scaling, max_pos)
     ang = torch.arange(max_pos, dtype=torch.float64).unsqueeze(1) * inv.unsqueeze(0)
-    return ang.cos().float().to(device), ang.sin().float().to(device)
+    return (ang.cos() * scale).float().to(device), (ang.sin() * scale).float().to(device)
 
 
 def apply_rope_ref(x: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, rot_dim: int):

@@ -42,6 +42,9 @@ def parse(argv=None):
     ap.add_argument("--weights", default=None,
                     help="Hugging Face model directory (config.json + safetensors); default: random weights")
     ap.add_argument("--tokenizer", default=None, help="local HF tokenizer directory (optional)")
+    ap.add_argument("--rope-scaling", default=None,
+                    help='RoPE scaling override as JSON, e.g. \'{"rope_type": "yarn", "factor": 4.0, '
+                         '"original_max_position_embeddings": 262144}\' (the reference serve script\'s override)')
     ap.add_argument("--device", default=None, help="cpu runs the torch reference path (testing)")
     return ap.parse_args(argv)
 
@@ -64,6 +67,8 @@ def build(args):
         cfg = config_from_hf(args.weights)
     else:
         cfg = CONFIGS[args.model](**({} if args.layers is None else {"num_layers": args.layers}))
+    if args.rope_scaling:
+        cfg.rope_scaling = json.loads(args.rope_scaling)
     oscar = OscarConfig.from_env(head_dim=cfg.head_dim)
     rot = "random"
     if oscar.k_rotation_path:
@@ -71,7 +76,7 @@ def build(args):
     if args.weights:
         from ..models.loader import from_pretrained
         model = from_pretrained(args.weights, tp, device=dev, oscar=oscar, kv_mode=args.kv, rotation=rot,
-                                num_layers=args.layers, seed=args.seed)
+                                num_layers=args.layers, seed=args.seed, config=cfg)
         cfg = model.cfg
     else:
         model = HybridModel(cfg, tp, device=dev, seed=args.seed, oscar=oscar, kv_mode=args.kv, rotation=rot)
