@@ -245,3 +245,14 @@ def test_http_sampling_parameters():
         assert g == _engine().generate([PROMPTS[0]], 5)[0]
     finally:
         w.stop()
+
+
+def test_static_metadata_form_samples_the_same_tokens():
+    """The graph form of a decode step's metadata (bucketed block tables, padded owner
+    updates, the sampler's rows) gives the same sampled tokens; on CPU it runs eagerly."""
+    sp = [S.SamplingParams(temperature=0.8, top_k=40, seed=1), S.SamplingParams(temperature=1.0, top_p=0.9, seed=2),
+          None]
+    plain = _engine().generate(PROMPTS, 10, sp)
+    eng = _engine()
+    eng.use_graphs = True  # static metadata; _run_phase runs it eagerly off the GPU
+    assert eng.generate(PROMPTS, 10, sp) == plain
