@@ -49,14 +49,21 @@ _M32 = 0xFFFFFFFF
 
 @dataclass
 class SamplingParams:
-    """Per-request sampling (the OpenAI completions fields of the same names)."""
+    """Per-request sampling (the OpenAI completions fields of the same names).  The
+    offline API (:class:`oscar_b200.LLM`) also reads ``max_tokens``, ``stop_token_ids`` and
+    ``ignore_eos``; the engine takes those as arguments of ``add_request``."""
 
     temperature: float = 0.0   # <= 0: greedy
     top_k: int = 0             # 0: off
     top_p: float = 1.0         # 1: off
     seed: int | None = None    # None: derived from the engine seed and the request id
+    max_tokens: int = 16
+    stop_token_ids: list | None = None
+    ignore_eos: bool = False
 
     def validate(self) -> "SamplingParams":
+        if int(self.max_tokens) < 1:
+            raise ValueError(f"max_tokens {self.max_tokens} must be >= 1")
         if not np.isfinite(self.temperature) or self.temperature < 0:
             raise ValueError(f"temperature {self.temperature} must be >= 0")
         if not 0 <= int(self.top_k) <= MAX_TOP_K:
@@ -70,7 +77,8 @@ class SamplingParams:
         return self.temperature <= 0
 
     def to_dict(self) -> dict:
-        return {"temperature": self.temperature, "top_k": self.top_k, "top_p": self.top_p, "seed": self.seed}
+        return {"temperature": self.temperature, "top_k": self.top_k, "top_p": self.top_p, "seed": self.seed,
+                "max_tokens": self.max_tokens, "stop_token_ids": self.stop_token_ids, "ignore_eos": self.ignore_eos}
 
 
 @dataclass

@@ -50,50 +50,14 @@ def parse(argv=None):
 
 
 def build(args):
-    from ..config import OscarConfig
     from ..engine import budget as B
-    from ..engine.engine import LLMEngine
-    from ..models.config import CONFIGS
-    from ..models.qwen35 import HybridModel
-    from ..parallel.groups import init_distributed, make_groups
+    from ..llm import create_engine
 
-    rank, world, local = init_distributed(backend="gloo" if args.device == "cpu" else None)
-    dev = torch.device(args.device) if args.device == "cpu" else torch.device("cuda", local)
-    if dev.type == "cuda":
-        torch.cuda.set_device(dev)
-    tp = make_groups(tp=world)
-    if args.weights:
-        from ..models.loader import config_from_hf
-        cfg = config_from_hf(args.weights)
-    else:
-        cfg = CONFIGS[args.model](**({} if args.layers is None else {"num_layers": args.layers}))
-    if args.rope_scaling:
-        cfg.rope_scaling = json.loads(args.rope_scaling)
-    oscar = OscarConfig.from_env(head_dim=cfg.head_dim)
-    rot = "random"
-    if oscar.k_rotation_path:
-        rot = oscar.k_rotation_path
-    if args.weights:
-        from ..models.loader import from_pretrained
-        model = from_pretrained(args.weights, tp, device=dev, oscar=oscar, kv_mode=args.kv, rotation=rot,
-                                num_layers=args.layers, seed=args.seed, config=cfg)
-        cfg = model.cfg
-    else:
-        model = HybridModel(cfg, tp, device=dev, seed=args.seed, oscar=oscar, kv_mode=args.kv, rotation=rot)
-    if args.num_blocks is not None:
-        blocks, budget = args.num_blocks, None
-    else:
-        geo = B.geometry_of(model, max_slots=args.max_num_seqs)
-        avail = B.available_memory(dev, args.gpu_memory_utilization)
-        budget = B.memory_budget(avail, geo)
-        blocks = budget.blocks
-        if world > 1:  # every rank uses the smallest budget
-            t = torch.tensor([blocks], device=dev if dev.type == "cuda" else "cpu")
-            dist.all_reduce(t, op=dist.ReduceOp.MIN)
-            blocks = int(t.item())
-    eng = LLMEngine(model, num_blocks=blocks, max_slots=args.max_num_seqs,
-                    max_batched_tokens=args.max_batched_tokens, num_spec=args.num_spec)
-    B.verify_layers(cfg.full_layer_ids, [m.layer_id for m in model.full_layers])
+    rank, world, model, eng, budget = create_engine(
+        args.model, weights=args.weights, layers=args.layers, kv=args.kv, num_spec=args.num_spec,
+        max_num_seqs=args.max_num_seqs, max_batched_tokens=args.max_batched_tokens,
+        gpu_memory_utilization=args.gpu_memory_utilization, num_blocks=args.num_blocks, seed=args.seed,
+        device=args.device, rope_scaling=args.rope_scaling)
     man = B.ready_manifest(model, rank, world, budget)
     print(man.line(), flush=True)
     mans = [None] * world

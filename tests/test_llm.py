@@ -1,0 +1,49 @@
+"""Offline generation API (CPU): ``LLM.generate`` over a config name or a Hugging Face
+checkpoint directory gives the engine's tokens, with max_tokens, stop ids, EOS and
+seeded sampling taken from ``SamplingParams``."""
+from __future__ import annotations
+
+import json
+
+import torch
+
+import oscar_b200
+from oscar_b200.engine.engine import LLMEngine
+from oscar_b200.models import loader as L
+from oscar_b200.models.config import tiny
+from oscar_b200.models.qwen35 import HybridModel
+
+KW = dict(device="cpu", num_blocks=64, max_num_seqs=4, max_batched_tokens=512)
+
+
+def test_generate_matches_the_engine():
+    llm = oscar_b200.LLM("qwen35-tiny", **KW)
+    SP = oscar_b200.SamplingParams
+    outs = llm.generate(["hello there", list(range(5, 40))], SP(max_tokens=6))
+    eng = LLMEngine(HybridModel(tiny(), device="cpu", seed=0), num_blocks=64, max_slots=4, max_batched_tokens=512)
+    want = eng.generate([[b + 3 for b in b"hello there"], list(range(5, 40))], 6)
+    assert [o.outputs[0].token_ids for o in outs] == want
+    assert outs[0].prompt == "hello there" and outs[1].prompt is None
+    assert all(o.outputs[0].finish_reason == "length" for o in outs)
+    # stop ids, EOS (none for the byte tokenizer) and seeded sampling
+    stop = want[1][2]
+    o = llm.generate(list(range(5, 40)), SP(max_tokens=6, stop_token_ids=[stop]))[0].outputs[0]
+    assert o.token_ids == want[1][:want[1].index(stop) + 1] and o.finish_reason == "stop"
+    a = llm.generate(list(range(5, 40)), SP(temperature=0.9, seed=3, max_tokens=6))[0].outputs[0].token_ids
+    b = llm.generate(list(range(5, 40)), SP(temperature=0.9, seed=3, max_tokens=6))[0].outputs[0].token_ids
+    assert a == b and len(a) == 6
+    assert not llm.engine.requests  # released
+
+
+def test_checkpoint_directory(tmp_path):
+    m = HybridModel(tiny(), device="cpu", seed=4)
+    L.save_hf_checkpoint(m, str(tmp_path), dtype=torch.float32)
+    want = LLMEngine(L.from_pretrained(str(tmp_path), device="cpu"), num_blocks=64, max_slots=4,
+                     max_batched_tokens=512).generate([list(range(9, 50))], 5)[0]
+    (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": want[3]}))
+    llm = oscar_b200.LLM(str(tmp_path), **KW)
+    assert llm.eos_token_ids == [want[3]]
+    o = llm.generate([list(range(9, 50))], oscar_b200.SamplingParams(max_tokens=5))[0].outputs[0]
+    assert o.token_ids == want[:want.index(want[3]) + 1] and o.finish_reason == "stop"
+    o = llm.generate([list(range(9, 50))], oscar_b200.SamplingParams(max_tokens=5, ignore_eos=True))[0].outputs[0]
+    assert o.token_ids == want and o.finish_reason == "length"
