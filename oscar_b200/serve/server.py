@@ -20,7 +20,8 @@ this is the same surface for this framework's engine, kept minimal:
   events when streaming);
 * ``GET /v1/models``;
 * ``GET /health``, ``GET /ready`` (the READY manifests), ``GET /metrics`` (Prometheus:
-  requests, output tokens, TTFT / TPOT histograms, draft acceptance, free KV blocks).
+  requests, output tokens, running / waiting / preempted, draft acceptance, free KV blocks
+  as gauges; TTFT / TPOT histograms; finished requests per finish reason).
 
 Prompts given as text are tokenised with the configured tokenizer, or byte-level
 (UTF-8 bytes + 3) for the random-weight models the benchmarks use.
@@ -166,9 +167,7 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
 
     @app.get("/metrics", response_class=PlainTextResponse)
     def metrics():
-        m = worker.metrics.snapshot(worker.engine)
-        lines = [f"oscar_{k} {float(v)}" for k, v in m.items() if v is not None]
-        return "\n".join(lines) + "\n"
+        return worker.metrics.exposition(worker.engine)
 
     async def generate(prompt: list[int], req, cid: str, chunk, final):
         """Runs one request: ``chunk(text, ids, reason, first)`` builds a streamed event,

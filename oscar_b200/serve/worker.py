@@ -25,13 +25,46 @@ import torch.distributed as dist
 from ..ops.sampling import SamplingParams
 
 
+class Histogram:
+    """Fixed-bucket histogram in the Prometheus form (cumulative bucket counts, sum, count):
+    constant memory however long the server runs."""
+
+    def __init__(self, bounds):
+        self.bounds = list(bounds)
+        self.counts = [0] * (len(self.bounds) + 1)  # last: +Inf
+        self.sum = 0.0
+        self.count = 0
+
+    def observe(self, v: float) -> None:
+        i = next((j for j, b in enumerate(self.bounds) if v <= b), len(self.bounds))
+        self.counts[i] += 1
+        self.sum += v
+        self.count += 1
+
+    @property
+    def mean(self) -> float:
+        return self.sum / max(1, self.count)
+
+    def lines(self, name: str) -> list[str]:
+        out, acc = [f"# TYPE {name} histogram"], 0
+        for b, c in zip(self.bounds + ["+Inf"], self.counts):
+            acc += c
+            out.append(f'{name}_bucket{{le="{b}"}} {acc}')
+        return out + [f"{name}_sum {self.sum}", f"{name}_count {self.count}"]
+
+
+TTFT_BUCKETS = (0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1, 2.5, 5, 10, 25, 50, 100)
+TPOT_BUCKETS = (0.001, 0.0025, 0.005, 0.0075, 0.01, 0.015, 0.02, 0.03, 0.05, 0.1, 0.25, 0.5)
+
+
 @dataclass
 class Metrics:
     requests: int = 0
     finished: int = 0
     tokens_out: int = 0
-    ttft_s: list = field(default_factory=list)
-    tpot_s: list = field(default_factory=list)
+    ttft: Histogram = field(default_factory=lambda: Histogram(TTFT_BUCKETS))
+    tpot: Histogram = field(default_factory=lambda: Histogram(TPOT_BUCKETS))
+    finish_reasons: dict = field(default_factory=dict)
     steps: int = 0
     started: float = field(default_factory=time.perf_counter)
 
@@ -41,9 +74,17 @@ class Metrics:
         acc = st.get("drafts_accepted", 0) / max(1, st.get("drafts_proposed", 0))
         return {"requests": self.requests, "finished": self.finished, "tokens_out": self.tokens_out,
                 "tok_per_s": self.tokens_out / el, "steps": self.steps, "draft_acceptance": acc,
-                "ttft_ms_mean": 1e3 * sum(self.ttft_s) / max(1, len(self.ttft_s)),
-                "tpot_ms_mean": 1e3 * sum(self.tpot_s) / max(1, len(self.tpot_s)),
-                "kv_blocks_free": engine.bm.free_blocks}
+                "ttft_ms_mean": 1e3 * self.ttft.mean, "tpot_ms_mean": 1e3 * self.tpot.mean,
+                "kv_blocks_free": engine.bm.free_blocks, "running": len(engine.running),
+                "waiting": len(engine.waiting), "preempted": st.get("preempted", 0)}
+
+    def exposition(self, engine) -> str:
+        """Prometheus text: the snapshot as gauges, the latency histograms, finish reasons."""
+        lines = [f"oscar_{k} {float(v)}" for k, v in self.snapshot(engine).items() if v is not None]
+        lines += self.ttft.lines("oscar_ttft_seconds") + self.tpot.lines("oscar_tpot_seconds")
+        lines.append("# TYPE oscar_finish_reason_total counter")
+        lines += [f'oscar_finish_reason_total{{reason="{r}"}} {n}' for r, n in sorted(self.finish_reasons.items())]
+        return "\n".join(lines) + "\n"
 
 
 class ControlChannel:
@@ -232,9 +273,11 @@ class EngineWorker:
             self.metrics.finished += 1
             self.metrics.tokens_out += len(out)
             if r.first_token_time is not None:
-                self.metrics.ttft_s.append(r.first_token_time - r.arrival)
+                self.metrics.ttft.observe(r.first_token_time - r.arrival)
                 if len(out) > 1 and r.finish_time is not None:
-                    self.metrics.tpot_s.append((r.finish_time - r.first_token_time) / (len(out) - 1))
+                    self.metrics.tpot.observe((r.finish_time - r.first_token_time) / (len(out) - 1))
+            fr = r.finish_reason or "unknown"
+            self.metrics.finish_reasons[fr] = self.metrics.finish_reasons.get(fr, 0) + 1
             self.futures.pop(rid)
             self._sent.pop(rid, None)
             self._rid_of.pop(fut.handle, None)

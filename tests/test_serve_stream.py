@@ -324,3 +324,24 @@ def test_requests_the_engine_cannot_run_are_rejected_up_front():
         assert w.error is None
     finally:
         w.stop()
+
+
+def test_metrics_histograms_and_finish_reasons():
+    from oscar_b200.serve.worker import Histogram
+
+    h = Histogram((0.1, 1.0))
+    for v in (0.05, 0.5, 0.7, 3.0):
+        h.observe(v)
+    assert h.lines("x")[1:4] == ['x_bucket{le="0.1"} 1', 'x_bucket{le="1.0"} 3', 'x_bucket{le="+Inf"} 4']
+    assert h.count == 4 and abs(h.sum - 4.25) < 1e-12
+    c, w = _client()
+    try:
+        c.post("/v1/completions", json={"prompt": PROMPTS[0], "max_tokens": 4})
+        c.post("/v1/completions", json={"prompt": PROMPTS[1], "max_tokens": 4, "stop_token_ids": list(range(1024))})
+        text = c.get("/metrics").text
+        assert 'oscar_finish_reason_total{reason="length"} 1' in text
+        assert 'oscar_finish_reason_total{reason="stop"} 1' in text
+        assert 'oscar_ttft_seconds_bucket{le="+Inf"} 2' in text and "oscar_tpot_seconds_count 1" in text
+        assert "oscar_finished 2.0" in text
+    finally:
+        w.stop()
