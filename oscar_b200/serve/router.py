@@ -101,6 +101,14 @@ def create_router_app(backends: list[str], transport: httpx.AsyncBaseTransport |
         out["replica"] = i
         return out
 
+    @app.get("/v1/models")
+    async def models():
+        try:
+            r = await client.get(backends[0].rstrip("/") + "/v1/models")
+        except httpx.HTTPError as e:
+            raise HTTPException(502, f"replica 0 unreachable: {e!r}") from e
+        return r.json()
+
     @app.post("/v1/completions")
     async def completions(req: Request):
         return await forward("/v1/completions", req)

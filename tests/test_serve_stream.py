@@ -258,6 +258,8 @@ def test_router_streams_through():
     seen = []
 
     def handler(request: httpx.Request):
+        if request.url.path == "/v1/models":
+            return httpx.Response(200, json={"object": "list", "data": [{"id": "m"}]})
         seen.append((str(request.url), json.loads(request.content)))
         return httpx.Response(200, content=sse, headers={"content-type": "text/event-stream"})
 
@@ -269,6 +271,7 @@ def test_router_streams_through():
             assert resp.headers["x-replica"] == "0"
         assert body == sse
         assert cl.get("/health").json()["load"] == [0, 0]  # released when the stream ended
+        assert cl.get("/v1/models").json()["data"][0]["id"] == "m"
     assert seen[0][0] == "http://r0/v1/chat/completions" and seen[0][1]["stream"] is True
 
 
