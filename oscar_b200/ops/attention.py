@@ -101,30 +101,37 @@ def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int
     target_items = max(1, (waves * sms) // max(Hk, 1))
     # page-aligned (128-token) split ranges: every split streams whole pages
     chunk = max(min_chunk, int(math.ceil(total / target_items / 128.0)) * 128) if total else min_chunk
-    work = []
     first = np.zeros(R * max_rb, dtype=np.int32)
     count = np.zeros(R * max_rb, dtype=np.int32)
     rpi_short = 0
-    for r, row0, need, _ in short:
-        rb = row0 // ROWS
-        rows = (q_start[r + 1] - q_start[r]) * g
-        rpi_short = max(rpi_short, min(ROWS, rows - row0))
-        first[r * max_rb + rb] = len(work)
+    if short:
+        sb = np.asarray([(r, row0, need) for r, row0, need, _ in short], dtype=np.int64)
+        r_, row0_, need_ = sb[:, 0], sb[:, 1], sb[:, 2]
+        qs = np.asarray(q_start, dtype=np.int64)
+        rows_ = (qs[r_ + 1] - qs[r_]) * g
+        rpi_short = int(np.minimum(ROWS, rows_ - row0_).max())
         if fixed_splits > 0:
-            splits = fixed_splits
-            per = max(128, int(math.ceil(need / splits / 128.0)) * 128)
-            for s in range(splits):
-                b0 = min(need, s * per)
-                work.append((r, row0, b0, min(need, b0 + per)))
+            splits = np.full(len(short), fixed_splits, dtype=np.int64)
+            step = np.maximum(128, np.ceil(need_ / splits / 128.0).astype(np.int64) * 128)
         else:
-            splits = max(1, (need + chunk - 1) // chunk)
-            for s in range(splits):
-                work.append((r, row0, s * chunk, min(need, (s + 1) * chunk)))
-        count[r * max_rb + rb] = splits
-    n_short = len(work)
+            splits = np.maximum(1, (need_ + chunk - 1) // chunk)
+            step = np.full(len(short), chunk, dtype=np.int64)
+        off = np.concatenate([[0], np.cumsum(splits)[:-1]])
+        slot = r_ * max_rb + row0_ // ROWS
+        first[slot] = off
+        count[slot] = splits
+        blk = np.repeat(np.arange(len(short)), splits)
+        sidx = np.arange(int(splits.sum())) - off[blk]
+        b0 = np.minimum(need_[blk], sidx * step[blk])
+        b1 = np.minimum(need_[blk], b0 + step[blk])
+        work_short = np.stack([r_[blk], row0_[blk], b0, b1], axis=1)
+    else:
+        work_short = np.zeros((0, 4), dtype=np.int64)
+    work = []
+    n_short = int(work_short.shape[0])
     for r, row0, need, _ in longb:
         rb = row0 // ROWS
-        first[r * max_rb + rb] = len(work)
+        first[r * max_rb + rb] = n_short + len(work)
         count[r * max_rb + rb] = 1
         work.append((r, row0, 0, need))
     tiles = []
@@ -137,8 +144,10 @@ def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int
         tiles.append((r, row0, int(first[r * max_rb + rb]), item_b))
     # longest tiles (most keys) first
     tiles.sort(key=lambda t: -(seq_lens[t[0]] - (q_start[t[0] + 1] - q_start[t[0]]) + t[1] // g))
-    n_work = len(work)
-    wt = np.asarray(work if work else [(0, 0, 0, 0)], dtype=np.int32).reshape(-1, 4)
+    n_work = n_short + len(work)
+    wt = np.concatenate([work_short, np.asarray(work, dtype=np.int64).reshape(-1, 4)]).astype(np.int32)
+    if not n_work:
+        wt = np.zeros((1, 4), dtype=np.int32)
     tt = np.asarray(tiles if tiles else [(0, 0, -1, -1)], dtype=np.int32).reshape(-1, 4)
     return wt, first, count, max_rb, n_work, tt, n_short, rpi_short
 
