@@ -348,3 +348,52 @@ def test_metrics_histograms_and_finish_reasons():
         assert "oscar_finished 2.0" in text
     finally:
         w.stop()
+
+
+def test_longbench_style_eval_client(tmp_path):
+    """Prompt template, middle truncation, answer extraction and scoring against a mock
+    server; then the whole path against the real app (random weights: only completion is
+    checked)."""
+    import asyncio
+
+    import httpx
+
+    from oscar_b200.bench import longbench as LB
+
+    assert LB.extract("The correct answer is (C).") == "C"
+    assert LB.extract("Hmm... B or maybe D") == "D" and LB.extract("no idea") is None
+    assert LB.middle_truncate("abcdefghij", 4) == "abij"
+    recs = [{"_id": str(i), "context": "x" * 50, "question": f"q{i}", "choice_A": "a", "choice_B": "b",
+             "choice_C": "c", "choice_D": "d", "answer": "ABCD"[i % 4], "difficulty": ["easy", "hard"][i % 2]}
+            for i in range(8)]
+    data = tmp_path / "lb.jsonl"
+    data.write_text("\n".join(json.dumps(r) for r in recs))
+    assert LB.load(str(data), limit=5) == recs[:5]
+    prompt = LB.prompt_of(recs[1], max_chars=10)
+    assert "x" * 10 in prompt and "x" * 11 not in prompt and "(B) b" in prompt
+
+    def handler(request: httpx.Request):
+        body = json.loads(request.content)
+        q = body["messages"][0]["content"].split("question: ")[1].split("\n")[0]
+        i = int(q[1:])
+        if i == 7:
+            return httpx.Response(500, text="boom")
+        guess = "ABCD"[i % 4] if i < 4 else "A"  # right on 0-3 and on 4; wrong on 5, 6; 7 fails
+        return httpx.Response(200, json={"choices": [{"message": {"content": f"The correct answer is ({guess})"}}],
+                                         "usage": {"completion_tokens": 6}})
+
+    out = asyncio.run(LB.run("http://mock", recs, concurrency=3, transport=httpx.MockTransport(handler)))
+    assert out["cases"] == 8 and out["failed"] == 1 and out["accuracy"] == 5 / 8
+    assert out["accuracy_by"] == {"difficulty=easy": 3 / 4, "difficulty=hard": 2 / 4}
+    # the real server end to end
+    from oscar_b200.serve.server import create_app
+
+    eng = _engine()
+    w = EngineWorker(eng).start()
+    try:
+        app = create_app(w, vocab_size=eng.model.cfg.vocab_size)
+        out = asyncio.run(LB.run("http://app", recs[:3], concurrency=2, max_tokens=4,
+                                 transport=httpx.ASGITransport(app=app)))
+        assert out["completed"] == 3 and out["completion_tokens"] == 12
+    finally:
+        w.stop()
