@@ -397,3 +397,33 @@ def test_longbench_style_eval_client(tmp_path):
         assert out["completed"] == 3 and out["completion_tokens"] == 12
     finally:
         w.stop()
+
+
+def test_launcher_gates_and_ready_check(tmp_path, monkeypatch):
+    """The one-shot launcher on CPU: self-check, fingerprint, a v2 rotation checkpoint
+    reused, the serve process up, every READY manifest validated, /health answered."""
+    import subprocess
+    import sys
+
+    from oscar_b200.kv.gen_rotations import main as gen_main
+
+    rot = tmp_path / "rot.pt"
+    monkeypatch.setenv("OSCAR_ASCEND_CALIB_TOKEN_CAP", "64")
+    assert gen_main(["--out", str(rot), "--model", "qwen35-tiny", "--layers", "4", "--num-prompts", "1",
+                     "--prompt-len", "64", "--device", "cpu"]) == 0
+    logf = tmp_path / "serve.log"
+    cmd = [sys.executable, "-m", "oscar_b200.serve.launch", "--device", "cpu", "--model", "qwen35-tiny",
+           "--rotations", str(rot), "--skip-probes", "--port", str(_port()), "--log", str(logf),
+           "--ready-timeout", "240", "--exit-after-ready", "--num-blocks", "16", "--max-num-seqs", "2",
+           "--max-batched-tokens", "256"]
+    p = subprocess.run(cmd, capture_output=True, text=True, timeout=400)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
+    assert "reusing v2 checkpoint" in p.stdout and "LAUNCH OK: 1 rank(s)" in p.stdout
+    assert "READY" in logf.read_text()
+    # a checkpoint that is not v2, without calibration: random rotations, still ready
+    bad = tmp_path / "old.pt"
+    import torch
+    torch.save({"3": torch.eye(256)}, bad)
+    cmd[cmd.index(str(rot))] = str(bad)
+    p = subprocess.run(cmd + ["--no-calibrate"], capture_output=True, text=True, timeout=400)
+    assert p.returncode == 0 and "not a v2 checkpoint" in p.stdout and "seeded random rotations" in p.stdout
