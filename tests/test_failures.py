@@ -1,12 +1,15 @@
 """Failure detection, injected on the host (no GPU fault): a missing extension fails
 loudly, a dead tensor-parallel peer ends the survivor's collective with an error
-within the process-group timeout instead of hanging it, and the serving worker turns
-that error into failed requests."""
+within the process-group timeout instead of hanging it, the serving worker turns
+that error into failed requests, an allocator out-of-memory error inside a step fails
+the pending requests and the health check, and a kernel status code ends the step with
+an error naming it."""
 import os
 import socket
 import time
 
 import pytest
+import torch
 import torch.multiprocessing as mp
 
 from oscar_b200.ops import _ext
@@ -81,3 +84,65 @@ def test_dead_peer_is_detected(mode):
             p.kill()
     assert kind != "no error", "the survivor did not notice the dead peer"
     assert dt < 60
+
+
+def _engine_cpu():
+    from oscar_b200.engine.engine import LLMEngine
+    from oscar_b200.models.config import tiny
+    from oscar_b200.models.qwen35 import HybridModel
+    return LLMEngine(HybridModel(tiny(num_layers=4), device="cpu"), num_blocks=16, max_slots=2,
+                     max_batched_tokens=128)
+
+
+def test_allocator_oom_in_a_step_fails_requests_and_health(monkeypatch):
+    """An out-of-memory error raised inside a step (host-side injection at the GEMM wrapper)
+    reaches every pending request, /health turns 503, and new submissions are refused."""
+    from fastapi.testclient import TestClient
+
+    from oscar_b200.ops import functional as F
+    from oscar_b200.serve.server import create_app
+    from oscar_b200.serve.worker import EngineWorker
+
+    real = F.linear_i8
+    calls = {"n": 0}
+
+    def flaky(*a, **k):
+        calls["n"] += 1
+        if calls["n"] == 40:
+            raise torch.OutOfMemoryError("simulated: allocator out of memory")
+        return real(*a, **k)
+
+    monkeypatch.setattr(F, "linear_i8", flaky)
+    w = EngineWorker(_engine_cpu()).start()
+    try:
+        futs = [w.submit(list(range(3, 30)), 20), w.submit(list(range(5, 50)), 20)]
+        for f in futs:
+            with pytest.raises(torch.OutOfMemoryError, match="simulated"):
+                f.result(timeout=120)
+        c = TestClient(create_app(w))
+        assert c.get("/health").status_code == 503
+        with pytest.raises(RuntimeError, match="engine worker failed"):
+            w.submit([1, 2, 3], 2)
+    finally:
+        w.stop()
+
+
+def test_kernel_status_word_ends_the_step_with_a_clear_error(monkeypatch):
+    """A kernel that gives up a bounded wait (or finds a bad index) records a code in the
+    model's status word; the engine reads it after the step and raises, naming the code."""
+    from oscar_b200.ops import functional as F
+
+    eng = _engine_cpu()
+    eng.model.status = torch.zeros(1, dtype=torch.int32)
+    real = F.rmsnorm_quant
+
+    def reports(*a, **k):
+        st = k.get("status")
+        if st is not None:
+            st.fill_(5)  # kTimeoutPeerFlag: what a timed-out peer-flag wait records
+        return real(*a, **{kk: v for kk, v in k.items()})
+
+    monkeypatch.setattr(F, "rmsnorm_quant", reports)
+    eng.add_request(list(range(3, 30)), 4)
+    with pytest.raises(RuntimeError, match="status 5"):
+        eng.step()
