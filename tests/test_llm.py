@@ -47,3 +47,40 @@ def test_checkpoint_directory(tmp_path):
     assert o.token_ids == want[:want.index(want[3]) + 1] and o.finish_reason == "stop"
     o = llm.generate([list(range(9, 50))], oscar_b200.SamplingParams(max_tokens=5, ignore_eos=True))[0].outputs[0]
     assert o.token_ids == want and o.finish_reason == "length"
+
+
+def _rank(rank, port, q):
+    import os
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    try:
+        llm = oscar_b200.LLM("qwen35-tiny", **KW)
+        outs = llm.generate([list(range(5, 40)), "hi"], oscar_b200.SamplingParams(max_tokens=5, temperature=0.8,
+                                                                                  seed=2))
+        q.put((rank, llm.world, [o.outputs[0].token_ids for o in outs]))
+        llm.close()
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_every_rank_of_a_tp_launch_returns_the_same_outputs():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {r: (w, o) for r, w, o in (q.get(timeout=300) for _ in ps)}
+    for p in ps:
+        p.join(60)
+    assert res[0][0] == res[1][0] == 2
+    assert res[0][1] == res[1][1] and all(len(o) == 5 for o in res[0][1])
