@@ -336,6 +336,13 @@ def load_checkpoint(model: HybridModel, source, strict: bool = True) -> LoadRepo
     layer that the mapping does not use (a bias, say), is an error; otherwise the MTP
     head keeps its weights and such tensors are only reported."""
     reader = source if isinstance(source, CheckpointReader) else CheckpointReader(source)
+    try:
+        return _load(model, reader, strict)
+    finally:
+        reader.close()
+
+
+def _load(model: HybridModel, reader: CheckpointReader, strict: bool) -> LoadReport:
     cfg = model.cfg
     check_supported(cfg)
     names = reader.names()
@@ -391,7 +398,6 @@ def load_checkpoint(model: HybridModel, source, strict: bool = True) -> LoadRepo
         odd = [n for n in rep.unused if any(n.startswith(p) for p in pfxs) and not n.endswith("inv_freq")]
         if odd:
             raise CheckpointError(f"tensors of loaded layers that the mapping does not use: {odd[:6]}")
-    reader.close()
     return rep
 
 

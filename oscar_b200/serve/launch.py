@@ -23,7 +23,6 @@ in the foreground until the server exits (``--exit-after-ready``: stop it once r
 from __future__ import annotations
 
 import argparse
-import json
 import os
 import signal
 import socket
@@ -111,7 +110,9 @@ def serve(args, extra: list[str], env: dict, sha: str) -> int:
     logf = open(args.log, "w")
     proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, env=env, text=True,
                             start_new_session=True)
-    lines: list[str] = []
+    lines: list[str] = []  # kept only until the READY check passed
+    watching = threading.Event()
+    watching.set()
     done = threading.Event()
 
     def pump():
@@ -119,7 +120,8 @@ def serve(args, extra: list[str], env: dict, sha: str) -> int:
             logf.write(ln)
             logf.flush()
             sys.stdout.write(ln)
-            lines.append(ln)
+            if watching.is_set():
+                lines.append(ln)
         done.set()
 
     threading.Thread(target=pump, daemon=True).start()
@@ -155,6 +157,8 @@ def serve(args, extra: list[str], env: dict, sha: str) -> int:
                 stop()
                 return 1
             time.sleep(0.2)
+        watching.clear()
+        lines.clear()
         log(f"LAUNCH OK: {len(mans)} rank(s), FULL layers {mans[0]['layer_ids']}, source {sha[:12]}, "
             f"http://{args.host}:{args.port}")
         if args.exit_after_ready:
