@@ -46,6 +46,11 @@ def parse():
     ap.add_argument("--kv", choices=["int2", "bf16"], default="int2")
     ap.add_argument("--prefill-policy", choices=["fcfs", "wide"], default="wide")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--dp", type=int, default=1,
+                    help="data-parallel replicas, each TP over gpus/dp ranks (BASELINE config 5: DP2 x TP4)")
+    ap.add_argument("--offload", action="store_true", help="swap-based host KV offload when the block pool runs out")
+    ap.add_argument("--num-blocks", type=int, default=None,
+                    help="KV blocks per rank (default: every request of the replica fits)")
     return ap.parse_args()
 
 
@@ -88,7 +93,9 @@ def main():
     rank, world, local = init_distributed(timeout_s=600)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    tp = make_groups(tp=world, dp=1)
+    if args.dp < 1 or world % args.dp or args.requests % args.dp:
+        raise SystemExit(f"--dp {args.dp} must divide the GPU count ({world}) and --requests ({args.requests})")
+    tp = make_groups(tp=world // args.dp, dp=args.dp)
     overrides = {} if args.layers is None else {"num_layers": args.layers}
     cfg = CONFIGS[args.model](**overrides)
     oscar = OscarConfig.from_env(head_dim=cfg.head_dim)
@@ -96,13 +103,13 @@ def main():
     model = HybridModel(cfg, tp, device=dev, seed=args.seed, oscar=oscar, kv_mode=args.kv, rotation="random")
     torch.cuda.synchronize()
     t_init = time.perf_counter() - t0
-    R = args.requests
+    R = args.requests // args.dp  # requests of this rank's replica
     per_req = args.prompt_len + args.output_len + 16 * (args.num_spec + 2)
-    num_blocks = R * ((per_req + 127) // 128) + 64
+    num_blocks = args.num_blocks or R * ((per_req + 127) // 128) + 64
     acc = SeededAcceptance(args.num_spec, args.accept_mean, seed=args.seed + 1)
     eng = LLMEngine(model, num_blocks=num_blocks, max_slots=R, num_spec=args.num_spec, acceptance=acc,
-                    prefill_policy=args.prefill_policy)
-    rng = np.random.default_rng(args.seed)
+                    prefill_policy=args.prefill_policy, offload=args.offload)
+    rng = np.random.default_rng(args.seed + tp.dp_rank)
     prompts = rng.integers(0, cfg.vocab_size, size=(R, args.prompt_len)).tolist()
     ids = [eng.add_request(p, args.output_len) for p in prompts]
 
@@ -172,11 +179,17 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     busy_ms, span_ms, wall = t.tolist()
+    mem = torch.cuda.max_memory_allocated(dev) / 2**30
+    if world > 1 and (args.dp > 1 or args.offload):
+        # every replica's tokens (each TP rank holds its replica's count), peak HBM of any GPU
+        tt = torch.tensor([tokens / tp.world, mem], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt[:1])
+        dist.all_reduce(tt[1:], op=dist.ReduceOp.MAX)
+        tokens, mem = int(round(tt[0].item())), float(tt[1].item())
     value = tokens / (busy_ms / 1e3)
     e2e = tokens / wall
-    steps_tok = tokens / args.steps / R  # output tokens per request per step
+    steps_tok = tokens / args.steps / (R * args.dp)  # output tokens per request per step
     tpot = (busy_ms / args.steps) / steps_tok
-    mem = torch.cuda.max_memory_allocated(dev) / 2**30
     if rank == 0:
         clocks = sampler.summary() if local == 0 else {}
         line = {
@@ -184,8 +197,10 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(busy_ms / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": round(value / BASELINE_TOK_S, 2), "dtype": "bf16",
             "data": "synthetic (uniform-random prompt tokens, random-init weights, seeded acceptance pattern)",
-            "config": {"model": cfg.name, "layers": cfg.num_layers, "global_batch": R, "seq_len": args.prompt_len,
-                       "output_len": args.output_len, "parallelism": f"tp{world}", "kv": args.kv,
+            "config": {"model": cfg.name, "layers": cfg.num_layers, "global_batch": R * args.dp,
+                       "seq_len": args.prompt_len, "output_len": args.output_len,
+                       "parallelism": f"tp{world}" if args.dp == 1 else f"dp{args.dp}xtp{world // args.dp}",
+                       "kv": args.kv,
                        "quantization": "W8A8 int8 linear layers, INT2 KV (FULL layers), BF16 MTP shadow KV",
                        "mtp_drafts": args.num_spec, "accept_mean": args.accept_mean,
                        "l2": "inputs larger than L2 (all weights streamed every step)",
@@ -201,6 +216,12 @@ def main():
             "gpu_launches": n_launch, "clocks": clocks, "peak_hbm_gib": round(mem, 2),
             "init_s": round(t_init, 1),
         }
+        if args.offload or args.num_blocks:
+            off = eng.offload.stats if eng.offload is not None else None
+            line["config"]["kv_blocks_per_rank"] = num_blocks
+            line["offload"] = {"enabled": bool(args.offload), "preempted": eng.stats.get("preempted", 0),
+                               "swapped_out_gib": round(off.bytes_out / 2**30, 3) if off else 0.0,
+                               "swapped_in_gib": round(off.bytes_in / 2**30, 3) if off else 0.0}
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:
