@@ -138,20 +138,33 @@ class LLM:
             raise ValueError(f"{len(params)} sampling params for {len(prompts)} prompts")
         eng = self.engine
         reqs = []
+        strings: dict = {}  # request id -> stop strings
         for p, sp in zip(prompts, params):
             sp = (sp or SamplingParams()).validate()
             ids = self.tokenizer.encode(p) if isinstance(p, str) else [int(t) for t in p]
             stop = list(sp.stop_token_ids or []) + ([] if sp.ignore_eos else self.eos_token_ids)
             rid = eng.add_request(ids, sp.max_tokens, None if sp.greedy else sp, stop)
             reqs.append((rid, p if isinstance(p, str) else None, ids))
+            if sp.stop:
+                strings[rid] = [x for x in ([sp.stop] if isinstance(sp.stop, str) else sp.stop) if x]
+        cut: dict = {}  # request id -> text up to its first stop string
         while eng.has_work():
             eng.step()
+            for rid, stops in strings.items():
+                r = eng.requests[rid]
+                if rid in cut or not r.output:
+                    continue
+                text = self._decode(list(r.output))
+                hits = [text.find(x) for x in stops if x in text]
+                if hits:
+                    cut[rid] = text[:min(hits)]
+                    eng.abort(rid)  # nothing past the stop string is generated
         out = []
         for rid, text, ids in reqs:
             r = eng.requests[rid]
             toks = list(r.output)
-            out.append(RequestOutput(rid, text, ids, [CompletionOutput(0, self._decode(toks), toks,
-                                                                       r.finish_reason)]))
+            body, reason = (cut[rid], "stop") if rid in cut else (self._decode(toks), r.finish_reason)
+            out.append(RequestOutput(rid, text, ids, [CompletionOutput(0, body, toks, reason)]))
             eng.release(rid)
         return out
 

@@ -50,8 +50,9 @@ _M32 = 0xFFFFFFFF
 @dataclass
 class SamplingParams:
     """Per-request sampling (the OpenAI completions fields of the same names).  The
-    offline API (:class:`oscar_b200.LLM`) also reads ``max_tokens``, ``stop_token_ids`` and
-    ``ignore_eos``; the engine takes those as arguments of ``add_request``."""
+    offline API (:class:`oscar_b200.LLM`) also reads ``max_tokens``, ``stop_token_ids``,
+    ``ignore_eos`` and ``stop``; the engine takes the token-level ones as arguments of
+    ``add_request``."""
 
     temperature: float = 0.0   # <= 0: greedy
     top_k: int = 0             # 0: off
@@ -60,6 +61,7 @@ class SamplingParams:
     max_tokens: int = 16
     stop_token_ids: list | None = None
     ignore_eos: bool = False
+    stop: list | None = None   # stop strings (the offline API and the server cut the text there)
 
     def validate(self) -> "SamplingParams":
         if int(self.max_tokens) < 1:
@@ -78,7 +80,8 @@ class SamplingParams:
 
     def to_dict(self) -> dict:
         return {"temperature": self.temperature, "top_k": self.top_k, "top_p": self.top_p, "seed": self.seed,
-                "max_tokens": self.max_tokens, "stop_token_ids": self.stop_token_ids, "ignore_eos": self.ignore_eos}
+                "max_tokens": self.max_tokens, "stop_token_ids": self.stop_token_ids, "ignore_eos": self.ignore_eos,
+                "stop": self.stop}
 
 
 @dataclass

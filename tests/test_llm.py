@@ -84,3 +84,14 @@ def test_every_rank_of_a_tp_launch_returns_the_same_outputs():
         p.join(60)
     assert res[0][0] == res[1][0] == 2
     assert res[0][1] == res[1][1] and all(len(o) == 5 for o in res[0][1])
+
+
+def test_stop_strings_cut_the_text_and_end_the_request():
+    llm = oscar_b200.LLM("qwen35-tiny", **KW)
+    full = llm.generate([list(range(5, 40))], oscar_b200.SamplingParams(max_tokens=12))[0].outputs[0]
+    stop = full.text[3:5]
+    assert stop and stop in full.text
+    got = llm.generate([list(range(5, 40))], oscar_b200.SamplingParams(max_tokens=12, stop=[stop]))[0].outputs[0]
+    assert got.text == full.text[:full.text.find(stop)] and got.finish_reason == "stop"
+    assert len(got.token_ids) < len(full.token_ids)  # the engine stopped generating
+    assert full.token_ids[:len(got.token_ids)] == got.token_ids
