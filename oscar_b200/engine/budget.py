@@ -99,6 +99,23 @@ def memory_budget(avail_bytes: int, geo: CacheGeometry, pp: int = 1,
     return Budget(int(blocks), int(blocks * native), int(blocks * shadow), int(fixed))
 
 
+def memory_line(rank: int, budget: Budget, geo: CacheGeometry, avail_bytes: int, allocated: dict,
+                device=None) -> str:
+    """``[oscar-b200] MEMORY {json}``: the budget derived from free memory and what the
+    allocation took (the reference prints the same line from its budget seam)."""
+    rec = {"rank": rank, "avail_bytes": int(avail_bytes), "fixed_bytes": geo.fixed_bytes,
+           "native_per_block": geo.native_per_block, "shadow_per_block": geo.shadow_per_block,
+           "blocks": budget.blocks, "native_bytes": budget.native_bytes, "shadow_bytes": budget.shadow_bytes,
+           "budget_bytes": budget.total, "allocated": {k: int(v) for k, v in allocated.items()},
+           "allocated_bytes": int(sum(allocated.values()))}
+    if device is not None and getattr(device, "type", "cpu") == "cuda":
+        import torch
+        free, total = torch.cuda.mem_get_info(device)
+        rec.update(gpu_free_bytes=int(free), gpu_total_bytes=int(total),
+                   allocator_peak_bytes=int(torch.cuda.max_memory_allocated(device)))
+    return "[oscar-b200] MEMORY " + json.dumps(rec, sort_keys=True)
+
+
 def check_allocation(actual_bytes: int, budget: Budget, slack: float = 0.0) -> None:
     """The allocated cache must not exceed the budget it was sized from."""
     if actual_bytes > budget.total * (1.0 + slack):

@@ -61,7 +61,8 @@ def create_engine(model: str = "qwen35-27b", *, weights: str | None = None, laye
                             seed=seed, config=cfg)
     else:
         m = HybridModel(cfg, tp, device=dev, seed=seed, oscar=oscar, kv_mode=kv, rotation=rot)
-    budget = None
+    budget = geo = None
+    avail = 0
     if num_blocks is None:
         geo = B.geometry_of(m, max_slots=max_num_seqs)
         avail = B.available_memory(dev, gpu_memory_utilization)
@@ -74,6 +75,10 @@ def create_engine(model: str = "qwen35-27b", *, weights: str | None = None, laye
     eng = LLMEngine(m, num_blocks=num_blocks, max_slots=max_num_seqs, max_batched_tokens=max_batched_tokens,
                     num_spec=num_spec, offload=offload, seed=seed)
     B.verify_layers(m.cfg.full_layer_ids, [x.layer_id for x in m.full_layers])
+    if budget is not None:  # the allocation may not exceed the budget it was sized from
+        alloc = m.cache_bytes()
+        print(B.memory_line(rank, budget, geo, avail, alloc, dev), flush=True)
+        B.check_allocation(sum(alloc.values()), budget)
     return rank, world, m, eng, budget
 
 

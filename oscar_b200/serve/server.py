@@ -21,7 +21,8 @@ this is the same surface for this framework's engine, kept minimal:
 * ``GET /v1/models``;
 * ``GET /health``, ``GET /ready`` (the READY manifests), ``GET /metrics`` (Prometheus:
   requests, output tokens, running / waiting / preempted, draft acceptance, free KV blocks
-  as gauges; TTFT / TPOT histograms; finished requests per finish reason).
+  as gauges; TTFT / TPOT histograms; finished requests per finish reason; verify steps per
+  number of accepted drafts).
 
 Prompts given as text are tokenised with the configured tokenizer, or byte-level
 (UTF-8 bytes + 3) for the random-weight models the benchmarks use.

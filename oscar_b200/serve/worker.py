@@ -65,6 +65,7 @@ class Metrics:
     ttft: Histogram = field(default_factory=lambda: Histogram(TTFT_BUCKETS))
     tpot: Histogram = field(default_factory=lambda: Histogram(TPOT_BUCKETS))
     finish_reasons: dict = field(default_factory=dict)
+    accepted: dict = field(default_factory=dict)  # drafts accepted in a verify step -> count
     steps: int = 0
     started: float = field(default_factory=time.perf_counter)
 
@@ -84,6 +85,8 @@ class Metrics:
         lines += self.ttft.lines("oscar_ttft_seconds") + self.tpot.lines("oscar_tpot_seconds")
         lines.append("# TYPE oscar_finish_reason_total counter")
         lines += [f'oscar_finish_reason_total{{reason="{r}"}} {n}' for r, n in sorted(self.finish_reasons.items())]
+        lines.append("# TYPE oscar_verify_steps_total counter")
+        lines += [f'oscar_verify_steps_total{{accepted="{k}"}} {n}' for k, n in sorted(self.accepted.items())]
         return "\n".join(lines) + "\n"
 
 
@@ -278,6 +281,8 @@ class EngineWorker:
                     self.metrics.tpot.observe((r.finish_time - r.first_token_time) / (len(out) - 1))
             fr = r.finish_reason or "unknown"
             self.metrics.finish_reasons[fr] = self.metrics.finish_reasons.get(fr, 0) + 1
+            for k in r.accepted:  # the accepted-length histogram of MTP verification
+                self.metrics.accepted[k] = self.metrics.accepted.get(k, 0) + 1
             self.futures.pop(rid)
             self._sent.pop(rid, None)
             self._rid_of.pop(fut.handle, None)

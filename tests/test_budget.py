@@ -96,3 +96,32 @@ def test_ready_line_roundtrip():
     assert parsed[0]["shadow_layers"] == [4]
     B.validate(parsed, world_size=1)
     json.dumps(parsed)
+
+
+def test_budget_terms_equal_the_allocation():
+    """The budget's per-block and fixed terms are the bytes the engine allocates: the INT2
+    pool, the BF16 shadow pool, and the staging arena, owner tags and GDN state slots (the
+    fixed term also counts the rotation matrices, which live with the weights)."""
+    import json
+
+    from oscar_b200.engine import budget as B
+    from oscar_b200.engine.engine import LLMEngine
+    from oscar_b200.models.config import tiny
+    from oscar_b200.models.qwen35 import HybridModel
+
+    m = HybridModel(tiny(num_layers=8), device="cpu")
+    geo = B.geometry_of(m, max_slots=3)
+    budget = B.memory_budget(64 * 2**20, geo)
+    LLMEngine(m, num_blocks=budget.blocks, max_slots=3, max_batched_tokens=256)
+    full = m.full_layers
+    pools = sum(x.pool.numel() for x in full)
+    staging = sum(x.stage_k.numel() * 4 + x.stage_v.numel() * 4 for x in full)
+    alloc = m.cache_bytes()
+    assert pools == budget.native_bytes
+    assert alloc["mtp_shadow"] == budget.shadow_bytes
+    rot = len(full) * 4 * 256 * 256 * 4
+    assert staging + alloc["owner"] + alloc["gdn_state"] == geo.fixed_bytes - rot
+    B.check_allocation(sum(alloc.values()), budget)
+    line = B.memory_line(0, budget, geo, 64 * 2**20, alloc)
+    rec = json.loads(line.split("MEMORY ", 1)[1])
+    assert rec["blocks"] == budget.blocks and rec["allocated_bytes"] == sum(alloc.values())

@@ -346,6 +346,8 @@ def test_metrics_histograms_and_finish_reasons():
         assert 'oscar_finish_reason_total{reason="stop"} 1' in text
         assert 'oscar_ttft_seconds_bucket{le="+Inf"} 2' in text and "oscar_tpot_seconds_count 1" in text
         assert "oscar_finished 2.0" in text
+        verify = [ln for ln in text.splitlines() if ln.startswith("oscar_verify_steps_total")]
+        assert verify and all(0 <= int(ln.split('"')[1]) <= 3 for ln in verify)
     finally:
         w.stop()
 
