@@ -58,6 +58,8 @@ class Request:
     stop_ids: frozenset = frozenset()  # generating one of these ends the request (it is kept)
     stopped: bool = False
     aborted: bool = False
+    logprobs: int | None = None  # report the k most likely tokens per output token (0: the token's only)
+    lp: list = field(default_factory=list)  # per output token: (logprob, [(id, logprob), ...])
 
     @property
     def prefill_done(self) -> bool:
@@ -187,12 +189,17 @@ class LLMEngine:
                              f"the {cap} this engine serves")
 
     def add_request(self, prompt, max_new_tokens: int, sampling: samp.SamplingParams | None = None,
-                    stop_ids=None) -> int:
-        """Queues a request; ``stop_ids``: token ids that end it (an EOS id, say)."""
+                    stop_ids=None, logprobs: int | None = None) -> int:
+        """Queues a request; ``stop_ids``: token ids that end it (an EOS id, say);
+        ``logprobs``: record every output token's log-probability and the ``logprobs`` most
+        likely tokens (steps with such requests run without CUDA graphs)."""
         self.validate_request(prompt, max_new_tokens)
+        if logprobs is not None and not 0 <= int(logprobs) <= 20:
+            raise ValueError(f"logprobs {logprobs} must be in [0, 20]")
         rid = next(self._ids)
         r = Request(rid, list(map(int, prompt)), int(max_new_tokens), arrival=self.timer(),
-                    stop_ids=frozenset(int(t) for t in (stop_ids or ())))
+                    stop_ids=frozenset(int(t) for t in (stop_ids or ())),
+                    logprobs=None if logprobs is None else int(logprobs))
         if sampling is not None and not sampling.validate().greedy:
             r.sampling = sampling
             r.seed = int(sampling.seed) if sampling.seed is not None else int(
@@ -557,7 +564,9 @@ class LLMEngine:
         if any(r.sampling is not None for r, _, _ in sp_rows):
             sampled = samp.host_rows([r.sampling for r, _, _ in sp_rows], [r.seed for r, _, _ in sp_rows],
                                      [p for _, p, _ in sp_rows], [d for _, _, d in sp_rows])
-        static = self.use_graphs and all(kind == "verify" for _, kind, _, _ in info)
+        lp_k = max((self.requests[rid].logprobs for rid, _, _, _ in info
+                    if self.requests[rid].logprobs is not None), default=None)
+        static = self.use_graphs and lp_k is None and all(kind == "verify" for _, kind, _, _ in info)
         if static:
             arrays, meta = self._arrays(rows, logit_rows, commit, keep, static=True, extra=sampled)
             b = (arrays, meta)
@@ -565,9 +574,15 @@ class LLMEngine:
                 hid, tok = self._run_phase("main", [(arrays, meta)], lambda bs: self._main_fn(bs[0]))
         else:
             b = self._build(rows, logit_rows, commit, keep, extra=sampled)
+            if lp_k is not None:
+                b.extra["logprobs_k"] = lp_k
             with self._segment():
                 hid, tok = self._main_fn(b)
         tok_h = tok.tolist()
+        lp_h = None
+        if lp_k is not None:
+            tl, ti, tv = self.model.last_logprobs
+            lp_h = (tl.tolist(), ti.tolist(), tv.tolist())
         self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * len(tok_h)
         self.last = (hid, tok)
         self._check_status()
@@ -583,6 +598,7 @@ class LLMEngine:
                 next_row_tok[base + i] = r.prompt[p + 1] if p + 1 < len(r.prompt) else 0
             if kind == "verify":
                 targets = tok_h[li:li + n]
+                li0 = li
                 li += n
                 d = r.drafts
                 if self.acceptance is not None:
@@ -600,7 +616,10 @@ class LLMEngine:
                 r.num_computed += n_acc + 1
                 r.pending_commit = n_acc + 1
                 self.slots.parity[r.slot] ^= 1
-                self.stats["tokens_out"] += r.emit(emitted)
+                kept = r.emit(emitted)
+                self.stats["tokens_out"] += kept
+                if r.logprobs is not None:  # an accepted draft is its row's token
+                    self._record_lp(r, lp_h, li0, kept)
                 r.last_token = emitted[-1]
                 draft_rows.append((rid, base + n_acc))
             else:
@@ -609,9 +628,12 @@ class LLMEngine:
                 self.slots.parity[r.slot] ^= 1
                 if r.prefill_done:
                     y = tok_h[li]
+                    kept = r.emit([y])
+                    if r.logprobs is not None:
+                        self._record_lp(r, lp_h, li, kept)
                     li += 1
                     next_row_tok[base + n - 1] = y
-                    self.stats["tokens_out"] += r.emit([y])
+                    self.stats["tokens_out"] += kept
                     r.last_token = y
                     r.first_token_time = now
                     draft_rows.append((rid, base + n - 1))
@@ -631,6 +653,12 @@ class LLMEngine:
                 self.slots.release(rid)
         self.stats["steps"] += 1
         return {"scheduled": sched}
+
+    @staticmethod
+    def _record_lp(r: Request, lp_h, row0: int, n: int) -> None:
+        tl, ti, tv = lp_h
+        for j in range(row0, row0 + n):
+            r.lp.append((tl[j], list(zip(ti[j][:r.logprobs], tv[j][:r.logprobs]))))
 
     def _main_fn(self, b: StepBatch):
         """Main model; the hidden states land in a persistent buffer so that a captured

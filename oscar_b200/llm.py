@@ -88,6 +88,7 @@ class CompletionOutput:
     text: str
     token_ids: list
     finish_reason: str | None
+    logprobs: list | None = None  # per token: {token id: logprob} of the token and the k most likely
 
 
 @dataclass
@@ -148,7 +149,7 @@ class LLM:
             sp = (sp or SamplingParams()).validate()
             ids = self.tokenizer.encode(p) if isinstance(p, str) else [int(t) for t in p]
             stop = list(sp.stop_token_ids or []) + ([] if sp.ignore_eos else self.eos_token_ids)
-            rid = eng.add_request(ids, sp.max_tokens, None if sp.greedy else sp, stop)
+            rid = eng.add_request(ids, sp.max_tokens, None if sp.greedy else sp, stop, sp.logprobs)
             reqs.append((rid, p if isinstance(p, str) else None, ids))
             if sp.stop:
                 strings[rid] = [x for x in ([sp.stop] if isinstance(sp.stop, str) else sp.stop) if x]
@@ -169,7 +170,10 @@ class LLM:
             r = eng.requests[rid]
             toks = list(r.output)
             body, reason = (cut[rid], "stop") if rid in cut else (self._decode(toks), r.finish_reason)
-            out.append(RequestOutput(rid, text, ids, [CompletionOutput(0, body, toks, reason)]))
+            lps = None
+            if r.logprobs is not None:
+                lps = [{t: lp, **dict(top)} for t, (lp, top) in zip(toks, r.lp)]
+            out.append(RequestOutput(rid, text, ids, [CompletionOutput(0, body, toks, reason, lps)]))
             eng.release(rid)
         return out
 

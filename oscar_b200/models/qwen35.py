@@ -498,15 +498,24 @@ class HybridModel:
         xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, self.cfg.rms_norm_eps, want_bf16=True,
                                       status=self.status, **pending)
         rows = b.logit_rows
-        tok = self.sample(xq[rows], xs[rows], b.extra.get("sampling"))
+        tok = self.sample(xq[rows], xs[rows], b.extra.get("sampling"), b.extra.get("logprobs_k"))
         return hid, tok
 
-    def sample(self, xq, xs, rows: "samp.SampleRows | None" = None) -> torch.Tensor:
+    def sample(self, xq, xs, rows: "samp.SampleRows | None" = None, logprobs_k: int | None = None) -> torch.Tensor:
         """Tokens over the vocab-parallel lm_head: greedy (global argmax across ranks), or,
-        with ``rows``, per-row temperature / top-k / top-p sampling and draft verification."""
+        with ``rows``, per-row temperature / top-k / top-p sampling and draft verification.
+        With ``logprobs_k`` the chosen tokens' log-probabilities and the ``logprobs_k`` most
+        likely tokens of every row are left in ``self.last_logprobs``."""
         logits = F.linear_i8(xq, xs, self.lm_head.q, self.lm_head.s, status=self.status)
         if rows is not None:
-            return samp.sample(logits, self.vocab_begin, rows, self.tp)
+            tok = samp.sample(logits, self.vocab_begin, rows, self.tp)
+        else:
+            tok = self._greedy(logits)
+        if logprobs_k is not None:
+            self.last_logprobs = samp.logprobs(logits, self.vocab_begin, tok, logprobs_k, self.tp)
+        return tok
+
+    def _greedy(self, logits) -> torch.Tensor:
         v, i = F.argmax(logits, self.vocab_begin)
         if self.tp.world > 1:
             vs = self.tp.all_gather(v.unsqueeze(0))      # [world, n]

@@ -62,6 +62,7 @@ class SamplingParams:
     stop_token_ids: list | None = None
     ignore_eos: bool = False
     stop: list | None = None   # stop strings (the offline API and the server cut the text there)
+    logprobs: int | None = None  # the offline API reports the k most likely tokens per output token
 
     def validate(self) -> "SamplingParams":
         if int(self.max_tokens) < 1:
@@ -81,7 +82,7 @@ class SamplingParams:
     def to_dict(self) -> dict:
         return {"temperature": self.temperature, "top_k": self.top_k, "top_p": self.top_p, "seed": self.seed,
                 "max_tokens": self.max_tokens, "stop_token_ids": self.stop_token_ids, "ignore_eos": self.ignore_eos,
-                "stop": self.stop}
+                "stop": self.stop, "logprobs": self.logprobs}
 
 
 @dataclass
@@ -254,3 +255,32 @@ def probabilities(logits: torch.Tensor, params: SamplingParams) -> torch.Tensor:
     p = torch.zeros_like(z)
     p[order] = w / w.sum()
     return p
+
+
+def logprobs(logits: torch.Tensor, vocab_begin: int, tokens: torch.Tensor, k: int, tp=None):
+    """Log-probabilities under the model's distribution (the raw logits, before temperature
+    or truncation) of ``tokens [n]`` and the ``k`` most likely tokens of every row, over
+    vocab-parallel logits (one all-gather of ``[n, 3 + 2k]``).  Returns ``(token_lp [n],
+    top_ids [n, k], top_lp [n, k])``."""
+    z = logits.float()
+    n, v = z.shape
+    kk = max(1, min(int(k), v))
+    mx = z.max(dim=1).values
+    s = torch.exp(z - mx.unsqueeze(1)).sum(dim=1)
+    tv, ti = torch.topk(z, kk, dim=1)
+    t = tokens.long()
+    local = (t >= vocab_begin) & (t < vocab_begin + v)
+    tl = torch.where(local, z.gather(1, (t - vocab_begin).clamp(0, v - 1).unsqueeze(1)).squeeze(1),
+                     torch.full_like(mx, float("-inf")))
+    pack = torch.cat([mx.unsqueeze(1), s.unsqueeze(1), tl.unsqueeze(1), tv, (ti + vocab_begin).float()], dim=1)
+    pack = pack.unsqueeze(0)
+    if tp is not None and tp.world > 1:
+        pack = tp.all_gather(pack)
+    mr, sr, tlr = pack[:, :, 0], pack[:, :, 1], pack[:, :, 2]
+    m = mr.max(dim=0).values
+    lse = m + torch.log((sr * torch.exp(mr - m)).sum(dim=0))
+    tok_lp = tlr.max(dim=0).values - lse
+    vals = pack[:, :, 3:3 + kk].permute(1, 0, 2).reshape(n, -1)
+    ids = pack[:, :, 3 + kk:].permute(1, 0, 2).reshape(n, -1)
+    best, where = torch.topk(vals, kk, dim=1)
+    return tok_lp, ids.gather(1, where).long(), best - lse.unsqueeze(1)

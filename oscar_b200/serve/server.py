@@ -13,7 +13,9 @@ this is the same surface for this framework's engine, kept minimal:
   produced tokens, then ``data: [DONE]``.  A stop string ends the request when it appears
   in the text (it is cut from the text, and the request is aborted in the engine); stop
   token ids and the model's EOS ids (unless ``ignore_eos``) end it in the engine.  A
-  streaming client that disconnects aborts its request;
+  streaming client that disconnects aborts its request.  ``logprobs: k`` (0-20) returns the
+  OpenAI ``logprobs`` object (token, its log-probability, the k most likely tokens) in the
+  plain response;
 * ``POST /v1/chat/completions`` - ``{"messages": [{"role", "content"}], ...}`` with the same
   generation fields; the prompt is the tokenizer's chat template (``<|role|>`` headers
   with the byte tokenizer), the answer a ``chat.completion`` (``chat.completion.chunk``
@@ -66,6 +68,7 @@ class CompletionRequest(BaseModel):
     stop: str | list[str] | None = None
     stop_token_ids: list[int] | None = None
     ignore_eos: bool = False
+    logprobs: int | None = None
 
 
 class ChatMessage(BaseModel):
@@ -197,8 +200,11 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             if not loop.is_closed():  # the handler may have returned (stop string) before the engine ended
                 loop.call_soon_threadsafe(aq.put_nowait, (new, reason))
 
+        lp = getattr(req, "logprobs", None)
+        if lp is not None and not 0 <= lp <= 20:
+            raise HTTPException(400, "logprobs must be in [0, 20]")
         try:
-            fut = worker.submit(prompt, req.max_tokens, sp, stop_ids, on_tokens=on_tokens)
+            fut = worker.submit(prompt, req.max_tokens, sp, stop_ids, on_tokens=on_tokens, logprobs=lp)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         ended = asyncio.Event()
@@ -255,6 +261,13 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             text += delta
             out += new
         res = final(text, out, reason)
+        if lp is not None and "text" in res["choices"][0]:  # the completions logprobs object
+            await watch  # the worker attaches the logprobs when it resolves the future
+            entries = (fut.logprobs or [])[:len(out)] if not fut.cancelled() else []
+            res["choices"][0]["logprobs"] = {
+                "tokens": [decode([t]) for t in out[:len(entries)]],
+                "token_logprobs": [e[0] for e in entries],
+                "top_logprobs": [{decode([i]): v for i, v in e[1]} for e in entries]}
         res["usage"] = {"prompt_tokens": len(prompt), "completion_tokens": len(out),
                         "total_tokens": len(prompt) + len(out)}
         return res

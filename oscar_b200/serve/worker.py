@@ -146,7 +146,8 @@ class EngineWorker:
         self._sent: dict[int, int] = {}     # request id -> tokens passed to on_tokens
         self.error: BaseException | None = None
 
-    def submit(self, prompt: list[int], max_tokens: int, sampling=None, stop_ids=None, on_tokens=None) -> Future:
+    def submit(self, prompt: list[int], max_tokens: int, sampling=None, stop_ids=None, on_tokens=None,
+               logprobs: int | None = None) -> Future:
         """Queues a request; ``sampling`` is a :class:`SamplingParams` (None: greedy),
         ``stop_ids`` token ids that end it.  The future has a ``handle`` for :meth:`abort`."""
         if self.error is not None:
@@ -158,8 +159,9 @@ class EngineWorker:
         fut.handle = next(self._handles)
         fut.finish_reason = None
         fut.on_tokens = on_tokens
+        fut.logprobs = None
         self.q.put((list(map(int, prompt)), int(max_tokens), sampling,
-                    tuple(int(t) for t in (stop_ids or ())), fut))
+                    tuple(int(t) for t in (stop_ids or ())), logprobs, fut))
         if self.error is not None:  # the loop died while this was being queued
             self._fail_queued(self.error)
         return fut
@@ -234,13 +236,13 @@ class EngineWorker:
                 now = time.perf_counter()
                 if self.control is not None and (new or aborts or eng.has_work() or stop
                                                  or now - self._last_msg > self.heartbeat_s):
-                    self.control.exchange(([(p, m, None if sp is None else sp.to_dict(), st) for p, m, sp, st, _ in new],
-                                           aborts, stop))
+                    self.control.exchange(([(p, m, None if sp is None else sp.to_dict(), st, lp)
+                                            for p, m, sp, st, lp, _ in new], aborts, stop))
                     self._last_msg = now
                 if stop:
                     break
-                for p, m, sp, st, fut in new:
-                    rid = eng.add_request(p, m, sp, st)
+                for p, m, sp, st, lp, fut in new:
+                    rid = eng.add_request(p, m, sp, st, lp)
                     self.futures[rid] = fut
                     self._rid_of[fut.handle] = rid
                     self.metrics.requests += 1
@@ -287,6 +289,7 @@ class EngineWorker:
             self._sent.pop(rid, None)
             self._rid_of.pop(fut.handle, None)
             fut.finish_reason = r.finish_reason
+            fut.logprobs = list(r.lp) if r.logprobs is not None else None
             _settle(fut, out)
             eng.release(rid)
 
@@ -297,8 +300,8 @@ def follower_loop(engine, control: ControlChannel) -> None:
         new, aborts, stop = control.exchange(None)
         if stop:
             return
-        for p, m, sp, st in new:
-            engine.add_request(p, m, None if sp is None else SamplingParams(**sp), st)
+        for p, m, sp, st, lp in new:
+            engine.add_request(p, m, None if sp is None else SamplingParams(**sp), st, lp)
         for rid in aborts:
             engine.abort(rid)
         if engine.has_work():

@@ -256,3 +256,73 @@ def test_static_metadata_form_samples_the_same_tokens():
     eng = _engine()
     eng.use_graphs = True  # static metadata; _run_phase runs it eagerly off the GPU
     assert eng.generate(PROMPTS, 10, sp) == plain
+
+
+def test_logprobs_over_vocab_shards_and_through_the_engine():
+    """Token and top-k log-probabilities: equal to log_softmax on one shard, the same when
+    the vocabulary is split over ranks (emulated), and attached to every output token by
+    the engine, the offline API and the server."""
+    g = torch.Generator().manual_seed(1)
+    logits = torch.randn(5, 300, generator=g) * 2
+    tok = torch.tensor([3, 299, 150, 0, 77])
+    tl, ti, tv = S.logprobs(logits, 0, tok, 4)
+    ref = torch.log_softmax(logits.double(), 1)
+    assert torch.allclose(tl.double(), ref.gather(1, tok[:, None]).squeeze(1), atol=1e-5)
+    rv, ri = ref.topk(4, dim=1)
+    assert torch.equal(ti, ri) and torch.allclose(tv.double(), rv, atol=1e-5)
+
+    class Recorder:  # rank 1: remembers the pack it would contribute to the all-gather
+        world = 2
+
+        def all_gather(self, x):
+            self.pack = x
+            return x
+
+    rec = Recorder()
+    S.logprobs(logits[:, 120:], 120, tok, 4, rec)
+
+    class WithPeer:  # rank 0: its own pack, then rank 1's
+        world = 2
+
+        def all_gather(self, x):
+            return torch.cat([x, rec.pack])
+
+    sl, si, sv = S.logprobs(logits[:, :120], 0, tok, 4, WithPeer())
+    assert torch.allclose(sl, tl, atol=1e-5) and torch.equal(si, ti) and torch.allclose(sv, tv, atol=1e-5)
+    # engine: greedy and sampled requests, with and without MTP
+    for num_spec in (0, 3):
+        eng = _engine(num_spec=num_spec)
+        rid = eng.add_request(PROMPTS[0], 6, logprobs=2)
+        rid2 = eng.add_request(PROMPTS[1], 6, S.SamplingParams(temperature=0.8, seed=5), logprobs=0)
+        while eng.has_work():
+            eng.step()
+        r, r2 = eng.requests[rid], eng.requests[rid2]
+        assert len(r.lp) == len(r.output) == 6 and len(r2.lp) == 6
+        for t, (lp, top) in zip(r.output, r.lp):
+            assert len(top) == 2 and top[0][0] == t and abs(top[0][1] - lp) < 1e-5  # greedy: the argmax
+            assert lp <= 0 and top[0][1] >= top[1][1]
+        assert all(top == [] and lp <= 0 for lp, top in r2.lp)
+    # the outputs do not change when logprobs are requested
+    assert _engine().generate([PROMPTS[0]], 6)[0] == r.output
+
+
+def test_logprobs_in_the_api_and_server():
+    import oscar_b200
+    from fastapi.testclient import TestClient
+
+    from oscar_b200.serve.server import create_app
+    from oscar_b200.serve.worker import EngineWorker
+
+    llm = oscar_b200.LLM("qwen35-tiny", device="cpu", num_blocks=64, max_num_seqs=4, max_batched_tokens=512)
+    o = llm.generate([PROMPTS[2]], S.SamplingParams(max_tokens=4, logprobs=3))[0].outputs[0]
+    assert len(o.logprobs) == 4 and all(t in d and len(d) >= 3 for t, d in zip(o.token_ids, o.logprobs))
+    eng = _engine()
+    w = EngineWorker(eng).start()
+    try:
+        c = TestClient(create_app(w, vocab_size=eng.model.cfg.vocab_size))
+        got = c.post("/v1/completions", json={"prompt": PROMPTS[0], "max_tokens": 5, "logprobs": 2}).json()
+        lp = got["choices"][0]["logprobs"]
+        assert len(lp["token_logprobs"]) == 5 and all(len(d) >= 1 for d in lp["top_logprobs"])
+        assert c.post("/v1/completions", json={"prompt": PROMPTS[0], "max_tokens": 5, "logprobs": 50}).status_code == 400
+    finally:
+        w.stop()
