@@ -88,6 +88,8 @@ class ChatRequest(BaseModel):
     stop: str | list[str] | None = None
     stop_token_ids: list[int] | None = None
     ignore_eos: bool = False
+    logprobs: bool = False
+    top_logprobs: int | None = None
 
 
 def chat_prompt(tok, messages: list[dict]) -> list[int]:
@@ -173,9 +175,10 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
     def metrics():
         return worker.metrics.exposition(worker.engine)
 
-    async def generate(prompt: list[int], req, cid: str, chunk, final):
+    async def generate(prompt: list[int], req, cid: str, chunk, final, lp: int | None = None):
         """Runs one request: ``chunk(text, ids, reason, first)`` builds a streamed event,
-        ``final(text, ids, reason)`` the plain response."""
+        ``final(text, ids, reason, logprobs)`` the plain response (``logprobs``: per output
+        token ``(logprob, [(id, logprob), ...])`` when ``lp`` asked for them)."""
         if not prompt:
             raise HTTPException(400, "empty prompt")
         if vocab_size is not None and (min(prompt) < 0 or max(prompt) >= vocab_size):
@@ -200,7 +203,6 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             if not loop.is_closed():  # the handler may have returned (stop string) before the engine ended
                 loop.call_soon_threadsafe(aq.put_nowait, (new, reason))
 
-        lp = getattr(req, "logprobs", None)
         if lp is not None and not 0 <= lp <= 20:
             raise HTTPException(400, "logprobs must be in [0, 20]")
         try:
@@ -260,14 +262,11 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                 raise HTTPException(500, str(e)) from e
             text += delta
             out += new
-        res = final(text, out, reason)
-        if lp is not None and "text" in res["choices"][0]:  # the completions logprobs object
+        entries = None
+        if lp is not None:
             await watch  # the worker attaches the logprobs when it resolves the future
             entries = (fut.logprobs or [])[:len(out)] if not fut.cancelled() else []
-            res["choices"][0]["logprobs"] = {
-                "tokens": [decode([t]) for t in out[:len(entries)]],
-                "token_logprobs": [e[0] for e in entries],
-                "top_logprobs": [{decode([i]): v for i, v in e[1]} for e in entries]}
+        res = final(text, out, reason, entries)
         res["usage"] = {"prompt_tokens": len(prompt), "completion_tokens": len(out),
                         "total_tokens": len(prompt) + len(out)}
         return res
@@ -282,11 +281,15 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             return {**head, "choices": [{"index": 0, "text": text, "token_ids": token_ids, "logprobs": None,
                                          "finish_reason": reason}]}
 
-        def final(text, token_ids, reason):
-            return {**head, "choices": [{"index": 0, "text": text, "token_ids": token_ids,
-                                         "finish_reason": reason}]}
+        def final(text, token_ids, reason, entries):
+            ch = {"index": 0, "text": text, "token_ids": token_ids, "finish_reason": reason}
+            if entries is not None:  # the completions logprobs object
+                ch["logprobs"] = {"tokens": [decode([t]) for t in token_ids[:len(entries)]],
+                                  "token_logprobs": [e[0] for e in entries],
+                                  "top_logprobs": [{decode([i]): v for i, v in e[1]} for e in entries]}
+            return {**head, "choices": [ch]}
 
-        return await generate(prompt, req, cid, chunk, final)
+        return await generate(prompt, req, cid, chunk, final, req.logprobs)
 
     @app.post("/v1/chat/completions")
     async def chat(req: ChatRequest):
@@ -299,11 +302,16 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             return {**head, "object": "chat.completion.chunk",
                     "choices": [{"index": 0, "delta": delta, "finish_reason": reason}]}
 
-        def final(text, token_ids, reason):
-            return {**head, "object": "chat.completion",
-                    "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
-                                 "finish_reason": reason}]}
+        def final(text, token_ids, reason, entries):
+            ch = {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
+            if entries is not None:  # the chat logprobs object
+                ch["logprobs"] = {"content": [
+                    {"token": decode([t]), "logprob": e[0],
+                     "top_logprobs": [{"token": decode([i]), "logprob": v} for i, v in e[1]]}
+                    for t, e in zip(token_ids, entries)]}
+            return {**head, "object": "chat.completion", "choices": [ch]}
 
-        return await generate(prompt, req, cid, chunk, final)
+        lp = (req.top_logprobs or 0) if req.logprobs else None
+        return await generate(prompt, req, cid, chunk, final, lp)
 
     return app

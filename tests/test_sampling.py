@@ -326,3 +326,23 @@ def test_logprobs_in_the_api_and_server():
         assert c.post("/v1/completions", json={"prompt": PROMPTS[0], "max_tokens": 5, "logprobs": 50}).status_code == 400
     finally:
         w.stop()
+
+
+def test_chat_logprobs():
+    from fastapi.testclient import TestClient
+
+    from oscar_b200.serve.server import create_app
+    from oscar_b200.serve.worker import EngineWorker
+
+    eng = _engine()
+    w = EngineWorker(eng).start()
+    try:
+        c = TestClient(create_app(w, vocab_size=eng.model.cfg.vocab_size))
+        body = {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4, "logprobs": True, "top_logprobs": 2}
+        got = c.post("/v1/chat/completions", json=body).json()["choices"][0]
+        content = got["logprobs"]["content"]
+        assert len(content) == 4 and all(len(x["top_logprobs"]) == 2 and x["logprob"] <= 0 for x in content)
+        plain = c.post("/v1/chat/completions", json={**body, "logprobs": False}).json()["choices"][0]
+        assert "logprobs" not in plain and plain["message"] == got["message"]
+    finally:
+        w.stop()
