@@ -74,6 +74,8 @@ def config_from_hf(source, name: str | None = None) -> HybridConfig:
         raw = _read_json(path)
         name = name or os.path.basename(os.path.dirname(os.path.abspath(path)))
     c = raw.get("text_config") or raw
+    if int(c.get("num_experts") or 0) > 0:
+        raise CheckpointError("mixture-of-experts checkpoints are not supported (dense SwiGLU MLP only)")
     rope = dict(c.get("rope_parameters") or c.get("rope_scaling") or {})
     theta = rope.get("rope_theta", c.get("rope_theta", 1.0e7))
     partial = rope.get("partial_rotary_factor", c.get("partial_rotary_factor", 0.25))

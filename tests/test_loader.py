@@ -80,6 +80,8 @@ def test_config_round_trip_and_nested_form():
     assert nested.layer_types == cfg.layer_types
     with pytest.raises(L.CheckpointError, match="head_dim"):
         L.config_from_hf({**raw, "head_dim": 128})
+    with pytest.raises(L.CheckpointError, match="mixture-of-experts"):
+        L.config_from_hf({**raw, "num_experts": 8})
 
 
 @pytest.fixture(scope="module")
