@@ -120,6 +120,18 @@ def eos_token_ids(path: str) -> list[int]:
     return []
 
 
+def generation_defaults(path: str) -> dict:
+    """The sampling defaults a checkpoint recommends (``generation_config.json``:
+    ``temperature``, ``top_k``, ``top_p``); empty when it recommends none."""
+    f = os.path.join(path, "generation_config.json")
+    if not os.path.exists(f):
+        return {}
+    raw = _read_json(f)
+    if raw.get("do_sample") is False:
+        return {"temperature": 0.0}
+    return {k: raw[k] for k in ("temperature", "top_k", "top_p") if raw.get(k) is not None}
+
+
 def check_supported(cfg: HybridConfig) -> None:
     """Raises :class:`CheckpointError` when the geometry is not one the kernels implement."""
     bad = []

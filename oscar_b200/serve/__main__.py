@@ -45,6 +45,9 @@ def parse(argv=None):
     ap.add_argument("--rope-scaling", default=None,
                     help='RoPE scaling override as JSON, e.g. \'{"rope_type": "yarn", "factor": 4.0, '
                          '"original_max_position_embeddings": 262144}\' (the reference serve script\'s override)')
+    ap.add_argument("--generation-config", choices=["auto", "none"], default="auto",
+                    help="auto: requests without temperature / top_k / top_p take the checkpoint's "
+                         "generation_config.json values; none: greedy")
     ap.add_argument("--device", default=None, help="cpu runs the torch reference path (testing)")
     return ap.parse_args(argv)
 
@@ -96,8 +99,12 @@ def main(argv=None) -> int:
     if args.weights:
         from ..models.loader import eos_token_ids
         eos = eos_token_ids(args.weights) or None  # None: the tokenizer's, if any
+    gen = None
+    if args.weights and args.generation_config == "auto":
+        from ..models.loader import generation_defaults
+        gen = generation_defaults(args.weights) or None
     app = create_app(worker, tok, mans, model_name=model.cfg.name, vocab_size=model.cfg.vocab_size,
-                     eos_token_ids=eos, max_model_len=model.cfg.max_position)
+                     eos_token_ids=eos, max_model_len=model.cfg.max_position, sampling_defaults=gen)
     try:
         uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     finally:

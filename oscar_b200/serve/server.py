@@ -6,9 +6,10 @@ this is the same surface for this framework's engine, kept minimal:
 * ``POST /v1/completions`` - ``{"prompt": str | [int], "max_tokens": int, "temperature",
   "top_k", "top_p", "seed", "stream", "stop", "stop_token_ids", "ignore_eos"}``; returns
   the generated token ids, the text and the finish reason (``"stop"`` or ``"length"``).
-  Decoding is greedy unless ``temperature > 0`` (this server's default is greedy, the
-  benchmarks' setting, where OpenAI's is 1.0); ``top_k`` 0 or -1 and ``top_p`` 1 switch
-  truncation off; a request without ``seed`` gets one derived from the engine seed and
+  Decoding is greedy unless ``temperature > 0``; fields a request leaves out take the
+  server's defaults: greedy (the benchmarks' setting, where OpenAI's is 1.0), or, when it
+  serves a checkpoint, that checkpoint's ``generation_config.json`` recommendation (as
+  vLLM does by default); ``top_k`` 0 or -1 and ``top_p`` 1 switch truncation off; a request without ``seed`` gets one derived from the engine seed and
   its id.  ``stream: true`` answers with server-sent events, one per engine step that
   produced tokens, then ``data: [DONE]``.  A stop string ends the request when it appears
   in the text (it is cut from the text, and the request is aborted in the engine); stop
@@ -60,9 +61,9 @@ class CompletionRequest(BaseModel):
     prompt: str | list[int]
     max_tokens: int = 16
     model: str | None = None
-    temperature: float = 0.0
-    top_k: int = 0
-    top_p: float = 1.0
+    temperature: float | None = None  # None: the server's default (greedy, or the checkpoint's)
+    top_k: int | None = None
+    top_p: float | None = None
     seed: int | None = None
     stream: bool = False
     stop: str | list[str] | None = None
@@ -80,9 +81,9 @@ class ChatRequest(BaseModel):
     messages: list[ChatMessage]
     max_tokens: int = 16
     model: str | None = None
-    temperature: float = 0.0
-    top_k: int = 0
-    top_p: float = 1.0
+    temperature: float | None = None  # None: the server's default (greedy, or the checkpoint's)
+    top_k: int | None = None
+    top_p: float | None = None
     seed: int | None = None
     stream: bool = False
     stop: str | list[str] | None = None
@@ -144,9 +145,12 @@ async def _events(aq: asyncio.Queue, decode, stops: list[str], on_stop):
 
 
 def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = None, model_name: str = "oscar-b200",
-               vocab_size: int | None = None, eos_token_ids=None, max_model_len: int | None = None) -> FastAPI:
+               vocab_size: int | None = None, eos_token_ids=None, max_model_len: int | None = None,
+               sampling_defaults: dict | None = None) -> FastAPI:
     """``eos_token_ids`` end every request that does not set ``ignore_eos`` (default: the
-    tokenizer's ``eos_token_id``, if it has one)."""
+    tokenizer's ``eos_token_id``, if it has one); ``sampling_defaults`` (``temperature``,
+    ``top_k``, ``top_p``) fill the fields a request leaves out (default: greedy)."""
+    defaults = {"temperature": 0.0, "top_k": 0, "top_p": 1.0, **(sampling_defaults or {})}
     app = FastAPI(title="oscar-b200")
     tok = tokenizer or ByteTokenizer()
     decode = _decoder(tok)
@@ -185,14 +189,17 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             raise HTTPException(400, f"token ids must be in [0, {vocab_size})")
         if req.max_tokens < 1:
             raise HTTPException(400, "max_tokens must be >= 1")
+        temp = defaults["temperature"] if req.temperature is None else req.temperature
+        top_k = defaults["top_k"] if req.top_k is None else req.top_k
+        top_p = defaults["top_p"] if req.top_p is None else req.top_p
         sp = None
-        if req.temperature > 0:
-            sp = SamplingParams(req.temperature, max(0, req.top_k), req.top_p, req.seed)
+        if temp > 0:
+            sp = SamplingParams(float(temp), max(0, int(top_k)), float(top_p), req.seed)
             try:
                 sp.validate()
             except ValueError as e:
                 raise HTTPException(400, str(e)) from e
-        elif req.temperature < 0:
+        elif temp < 0:
             raise HTTPException(400, "temperature must be >= 0")
         stops = [req.stop] if isinstance(req.stop, str) else list(req.stop or [])
         stop_ids = list(req.stop_token_ids or []) + ([] if req.ignore_eos else eos)

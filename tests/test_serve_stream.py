@@ -429,3 +429,31 @@ def test_launcher_gates_and_ready_check(tmp_path, monkeypatch):
     cmd[cmd.index(str(rot))] = str(bad)
     p = subprocess.run(cmd + ["--no-calibrate"], capture_output=True, text=True, timeout=400)
     assert p.returncode == 0 and "not a v2 checkpoint" in p.stdout and "seeded random rotations" in p.stdout
+
+
+def test_sampling_defaults_fill_omitted_fields(tmp_path):
+    """A checkpoint's generation_config.json recommendation applies to requests that leave
+    the sampling fields out; explicit fields win."""
+    from fastapi.testclient import TestClient
+
+    from oscar_b200.models.loader import generation_defaults
+    from oscar_b200.serve.server import create_app
+
+    (tmp_path / "generation_config.json").write_text(json.dumps({"temperature": 0.9, "top_k": 20, "top_p": 0.95}))
+    d = generation_defaults(str(tmp_path))
+    assert d == {"temperature": 0.9, "top_k": 20, "top_p": 0.95}
+    (tmp_path / "generation_config.json").write_text(json.dumps({"do_sample": False, "temperature": 0.9}))
+    assert generation_defaults(str(tmp_path)) == {"temperature": 0.0}
+    greedy = _engine().generate([PROMPTS[2]], 6)[0]
+    eng = _engine()
+    w = EngineWorker(eng).start()
+    try:
+        c = TestClient(create_app(w, vocab_size=eng.model.cfg.vocab_size, sampling_defaults=d))
+        body = {"prompt": PROMPTS[2], "max_tokens": 6, "seed": 3}
+        a = c.post("/v1/completions", json=body).json()["choices"][0]["token_ids"]
+        assert a == c.post("/v1/completions", json=body).json()["choices"][0]["token_ids"]  # seeded
+        assert a != greedy  # sampled with the defaults
+        g = c.post("/v1/completions", json={**body, "temperature": 0}).json()["choices"][0]["token_ids"]
+        assert g == greedy
+    finally:
+        w.stop()
