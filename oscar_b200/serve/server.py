@@ -15,8 +15,8 @@ this is the same surface for this framework's engine, kept minimal:
   in the text (it is cut from the text, and the request is aborted in the engine); stop
   token ids and the model's EOS ids (unless ``ignore_eos``) end it in the engine.  A
   streaming client that disconnects aborts its request.  ``logprobs: k`` (0-20) returns the
-  OpenAI ``logprobs`` object (token, its log-probability, the k most likely tokens) in the
-  plain response;
+  OpenAI ``logprobs`` object (token, its log-probability, the k most likely tokens), in the
+  plain response or in every streamed chunk for that chunk's tokens;
 * ``POST /v1/chat/completions`` - ``{"messages": [{"role", "content"}], ...}`` with the same
   generation fields; the prompt is the tokenizer's chat template (``<|role|>`` headers
   with the byte tokenizer), the answer a ``chat.completion`` (``chat.completion.chunk``
@@ -244,14 +244,18 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             async def sse():
                 done = False
                 try:
-                    reason, first = None, True
+                    reason, first, n_sent = None, True, 0
                     while reason is None:
                         try:
                             text, new, reason = await next_event()
                         except RuntimeError as e:
                             yield f"data: {json.dumps({'error': str(e)})}\n\n"
                             break
-                        yield f"data: {json.dumps(chunk(text, new, reason, first))}\n\n"
+                        entries = None
+                        if lp is not None:  # this chunk's tokens' logprobs, recorded before the update
+                            entries = list(getattr(fut, "lp_live", None) or [])[n_sent:n_sent + len(new)]
+                        n_sent += len(new)
+                        yield f"data: {json.dumps(chunk(text, new, reason, first, entries))}\n\n"
                         first = False
                     done = True
                     yield "data: [DONE]\n\n"
@@ -284,16 +288,20 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
         cid, t0 = f"cmpl-{next(ids)}", int(time.time())
         head = {"id": cid, "object": "text_completion", "created": t0, "model": model_name}
 
-        def chunk(text, token_ids, reason, first):
-            return {**head, "choices": [{"index": 0, "text": text, "token_ids": token_ids, "logprobs": None,
+        def lp_object(token_ids, entries):  # the completions logprobs object
+            return {"tokens": [decode([t]) for t in token_ids[:len(entries)]],
+                    "token_logprobs": [e[0] for e in entries],
+                    "top_logprobs": [{decode([i]): v for i, v in e[1]} for e in entries]}
+
+        def chunk(text, token_ids, reason, first, entries=None):
+            return {**head, "choices": [{"index": 0, "text": text, "token_ids": token_ids,
+                                         "logprobs": None if entries is None else lp_object(token_ids, entries),
                                          "finish_reason": reason}]}
 
         def final(text, token_ids, reason, entries):
             ch = {"index": 0, "text": text, "token_ids": token_ids, "finish_reason": reason}
-            if entries is not None:  # the completions logprobs object
-                ch["logprobs"] = {"tokens": [decode([t]) for t in token_ids[:len(entries)]],
-                                  "token_logprobs": [e[0] for e in entries],
-                                  "top_logprobs": [{decode([i]): v for i, v in e[1]} for e in entries]}
+            if entries is not None:
+                ch["logprobs"] = lp_object(token_ids, entries)
             return {**head, "choices": [ch]}
 
         return await generate(prompt, req, cid, chunk, final, req.logprobs)
@@ -304,18 +312,22 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
         cid, t0 = f"chatcmpl-{next(ids)}", int(time.time())
         head = {"id": cid, "created": t0, "model": model_name}
 
-        def chunk(text, token_ids, reason, first):
+        def lp_object(token_ids, entries):  # the chat logprobs object
+            return {"content": [{"token": decode([t]), "logprob": e[0],
+                                 "top_logprobs": [{"token": decode([i]), "logprob": v} for i, v in e[1]]}
+                                for t, e in zip(token_ids, entries)]}
+
+        def chunk(text, token_ids, reason, first, entries=None):
             delta = {"role": "assistant", "content": text} if first else {"content": text}
-            return {**head, "object": "chat.completion.chunk",
-                    "choices": [{"index": 0, "delta": delta, "finish_reason": reason}]}
+            ch = {"index": 0, "delta": delta, "finish_reason": reason}
+            if entries is not None:
+                ch["logprobs"] = lp_object(token_ids, entries)
+            return {**head, "object": "chat.completion.chunk", "choices": [ch]}
 
         def final(text, token_ids, reason, entries):
             ch = {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
-            if entries is not None:  # the chat logprobs object
-                ch["logprobs"] = {"content": [
-                    {"token": decode([t]), "logprob": e[0],
-                     "top_logprobs": [{"token": decode([i]), "logprob": v} for i, v in e[1]]}
-                    for t, e in zip(token_ids, entries)]}
+            if entries is not None:
+                ch["logprobs"] = lp_object(token_ids, entries)
             return {**head, "object": "chat.completion", "choices": [ch]}
 
         lp = (req.top_logprobs or 0) if req.logprobs else None

@@ -268,6 +268,8 @@ class EngineWorker:
                 sent = self._sent.get(rid, 0)
                 if len(r.output) > sent or r.finished:
                     self._sent[rid] = len(r.output)
+                    if r.logprobs is not None:  # what a streaming consumer reads for these tokens
+                        fut.lp_live = list(r.lp)
                     try:
                         cb(list(r.output[sent:]), r.finish_reason if r.finished else None)
                     except Exception:  # noqa: BLE001 - a consumer that went away must not stop the engine

@@ -346,3 +346,36 @@ def test_chat_logprobs():
         assert "logprobs" not in plain and plain["message"] == got["message"]
     finally:
         w.stop()
+
+
+def test_streamed_logprobs_match_the_plain_response():
+    import json as _json
+
+    from fastapi.testclient import TestClient
+
+    from oscar_b200.serve.server import create_app
+    from oscar_b200.serve.worker import EngineWorker
+
+    def sse(resp):
+        ev = [ln[6:] for ln in resp.iter_lines() if ln.startswith("data: ")]
+        assert ev[-1] == "[DONE]"
+        return [_json.loads(e) for e in ev[:-1]]
+
+    eng = _engine()
+    w = EngineWorker(eng).start()
+    try:
+        c = TestClient(create_app(w, vocab_size=eng.model.cfg.vocab_size))
+        body = {"prompt": PROMPTS[1], "max_tokens": 7, "logprobs": 2}
+        plain = c.post("/v1/completions", json=body).json()["choices"][0]["logprobs"]
+        with c.stream("POST", "/v1/completions", json={**body, "stream": True}) as r:
+            chunks = sse(r)
+        got = sum((ch["choices"][0]["logprobs"]["token_logprobs"] for ch in chunks), [])
+        assert got == plain["token_logprobs"] and len(got) == 7
+        cb = {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 5, "logprobs": True,
+              "top_logprobs": 1, "stream": True}
+        with c.stream("POST", "/v1/chat/completions", json=cb) as r:
+            chunks = sse(r)
+        content = sum((ch["choices"][0]["logprobs"]["content"] for ch in chunks), [])
+        assert len(content) == 5 and all(len(x["top_logprobs"]) == 1 for x in content)
+    finally:
+        w.stop()
