@@ -48,7 +48,7 @@ def request_cost(body: dict) -> int:
     else:
         p = body.get("prompt", [])
         n = len(p) if isinstance(p, list) else len(str(p).encode())
-    return n + int(body.get("max_tokens", 16))
+    return n + int(body.get("max_tokens", 16)) * max(1, int(body.get("n", 1) or 1))
 
 
 def create_router_app(backends: list[str], transport: httpx.AsyncBaseTransport | None = None,

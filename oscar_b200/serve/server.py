@@ -17,6 +17,7 @@ this is the same surface for this framework's engine, kept minimal:
   streaming client that disconnects aborts its request.  ``logprobs: k`` (0-20) returns the
   OpenAI ``logprobs`` object (token, its log-probability, the k most likely tokens), in the
   plain response or in every streamed chunk for that chunk's tokens;
+  ``n`` (1-16, not with ``stream``) returns that many choices, sampled with seeds ``seed + i``;
 * ``POST /v1/chat/completions`` - ``{"messages": [{"role", "content"}], ...}`` with the same
   generation fields; the prompt is the tokenizer's chat template (``<|role|>`` headers
   with the byte tokenizer), the answer a ``chat.completion`` (``chat.completion.chunk``
@@ -70,6 +71,7 @@ class CompletionRequest(BaseModel):
     stop_token_ids: list[int] | None = None
     ignore_eos: bool = False
     logprobs: int | None = None
+    n: int = 1
 
 
 class ChatMessage(BaseModel):
@@ -91,6 +93,7 @@ class ChatRequest(BaseModel):
     ignore_eos: bool = False
     logprobs: bool = False
     top_logprobs: int | None = None
+    n: int = 1
 
 
 def chat_prompt(tok, messages: list[dict]) -> list[int]:
@@ -282,6 +285,23 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                         "total_tokens": len(prompt) + len(out)}
         return res
 
+    async def generate_n(prompt: list[int], req, cid: str, chunk, final, lp: int | None = None):
+        """``n`` choices of one prompt: ``n`` requests whose seeds differ (``seed + i``, or the
+        per-request default), answered as one response (not with ``stream``)."""
+        n = int(req.n or 1)
+        if n == 1:
+            return await generate(prompt, req, cid, chunk, final, lp)
+        if not 1 <= n <= 16:
+            raise HTTPException(400, "n must be in [1, 16]")
+        if req.stream:
+            raise HTTPException(400, "n > 1 is not supported with stream")
+        reqs = [req.model_copy(update={"seed": None if req.seed is None else req.seed + i, "n": 1}) for i in range(n)]
+        res = await asyncio.gather(*(generate(prompt, r, cid, chunk, final, lp) for r in reqs))
+        choices = [{**x["choices"][0], "index": i} for i, x in enumerate(res)]
+        done = sum(x["usage"]["completion_tokens"] for x in res)
+        return {**res[0], "choices": choices,
+                "usage": {"prompt_tokens": len(prompt), "completion_tokens": done, "total_tokens": len(prompt) + done}}
+
     @app.post("/v1/completions")
     async def completions(req: CompletionRequest):
         prompt = tok.encode(req.prompt) if isinstance(req.prompt, str) else list(req.prompt)
@@ -304,7 +324,7 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                 ch["logprobs"] = lp_object(token_ids, entries)
             return {**head, "choices": [ch]}
 
-        return await generate(prompt, req, cid, chunk, final, req.logprobs)
+        return await generate_n(prompt, req, cid, chunk, final, req.logprobs)
 
     @app.post("/v1/chat/completions")
     async def chat(req: ChatRequest):
@@ -331,6 +351,6 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             return {**head, "object": "chat.completion", "choices": [ch]}
 
         lp = (req.top_logprobs or 0) if req.logprobs else None
-        return await generate(prompt, req, cid, chunk, final, lp)
+        return await generate_n(prompt, req, cid, chunk, final, lp)
 
     return app

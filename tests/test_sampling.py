@@ -379,3 +379,27 @@ def test_streamed_logprobs_match_the_plain_response():
         assert len(content) == 5 and all(len(x["top_logprobs"]) == 1 for x in content)
     finally:
         w.stop()
+
+
+def test_n_choices():
+    from fastapi.testclient import TestClient
+
+    from oscar_b200.serve.server import create_app
+    from oscar_b200.serve.worker import EngineWorker
+
+    eng = _engine()
+    w = EngineWorker(eng).start()
+    try:
+        c = TestClient(create_app(w, vocab_size=eng.model.cfg.vocab_size))
+        body = {"prompt": PROMPTS[2], "max_tokens": 5, "temperature": 1.0, "seed": 40, "n": 3}
+        got = c.post("/v1/completions", json=body).json()
+        toks = [ch["token_ids"] for ch in got["choices"]]
+        assert [ch["index"] for ch in got["choices"]] == [0, 1, 2] and got["usage"]["completion_tokens"] == 15
+        one = c.post("/v1/completions", json={**body, "n": 1, "seed": 41}).json()["choices"][0]["token_ids"]
+        assert toks[1] == one and len({tuple(t) for t in toks}) > 1  # choice i is seed + i
+        chat = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}], "max_tokens": 3,
+                                                    "n": 2}).json()
+        assert len(chat["choices"]) == 2
+        assert c.post("/v1/completions", json={**body, "stream": True}).status_code == 400
+    finally:
+        w.stop()
