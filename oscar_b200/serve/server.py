@@ -18,6 +18,7 @@ this is the same surface for this framework's engine, kept minimal:
   OpenAI ``logprobs`` object (token, its log-probability, the k most likely tokens), in the
   plain response or in every streamed chunk for that chunk's tokens;
   ``n`` (1-16, not with ``stream``) returns that many choices, sampled with seeds ``seed + i``;
+  ``stream_options: {"include_usage": true}`` adds a last streamed chunk with the token counts;
 * ``POST /v1/chat/completions`` - ``{"messages": [{"role", "content"}], ...}`` with the same
   generation fields; the prompt is the tokenizer's chat template (``<|role|>`` headers
   with the byte tokenizer), the answer a ``chat.completion`` (``chat.completion.chunk``
@@ -72,6 +73,7 @@ class CompletionRequest(BaseModel):
     ignore_eos: bool = False
     logprobs: int | None = None
     n: int = 1
+    stream_options: dict | None = None
 
 
 class ChatMessage(BaseModel):
@@ -94,6 +96,7 @@ class ChatRequest(BaseModel):
     logprobs: bool = False
     top_logprobs: int | None = None
     n: int = 1
+    stream_options: dict | None = None
 
 
 def chat_prompt(tok, messages: list[dict]) -> list[int]:
@@ -248,6 +251,7 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                 done = False
                 try:
                     reason, first, n_sent = None, True, 0
+                    usage = bool((req.stream_options or {}).get("include_usage"))
                     while reason is None:
                         try:
                             text, new, reason = await next_event()
@@ -260,6 +264,11 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                         n_sent += len(new)
                         yield f"data: {json.dumps(chunk(text, new, reason, first, entries))}\n\n"
                         first = False
+                    if usage:  # a last chunk with no choices and the token counts
+                        last = {**chunk("", [], None, False), "choices": []}
+                        last["usage"] = {"prompt_tokens": len(prompt), "completion_tokens": n_sent,
+                                         "total_tokens": len(prompt) + n_sent}
+                        yield f"data: {json.dumps(last)}\n\n"
                     done = True
                     yield "data: [DONE]\n\n"
                 finally:

@@ -457,3 +457,18 @@ def test_sampling_defaults_fill_omitted_fields(tmp_path):
         assert g == greedy
     finally:
         w.stop()
+
+
+def test_stream_usage_chunk():
+    c, w = _client()
+    try:
+        body = {"prompt": PROMPTS[0], "max_tokens": 6, "stream": True, "stream_options": {"include_usage": True}}
+        with c.stream("POST", "/v1/completions", json=body) as resp:
+            chunks = _sse(resp)
+        assert chunks[-1]["choices"] == [] and chunks[-1]["usage"] == {
+            "prompt_tokens": len(PROMPTS[0]), "completion_tokens": 6, "total_tokens": len(PROMPTS[0]) + 6}
+        assert sum(len(ch["choices"][0]["token_ids"]) for ch in chunks[:-1]) == 6
+        with c.stream("POST", "/v1/completions", json={**body, "stream_options": None}) as resp:
+            assert all(ch["choices"] for ch in _sse(resp))
+    finally:
+        w.stop()
