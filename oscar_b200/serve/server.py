@@ -96,6 +96,7 @@ class ChatRequest(BaseModel):
     logprobs: bool = False
     top_logprobs: int | None = None
     n: int = 1
+    max_completion_tokens: int | None = None  # the newer name of max_tokens
     stream_options: dict | None = None
 
 
@@ -337,6 +338,8 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
 
     @app.post("/v1/chat/completions")
     async def chat(req: ChatRequest):
+        if req.max_completion_tokens is not None:
+            req = req.model_copy(update={"max_tokens": req.max_completion_tokens})
         prompt = chat_prompt(tok, [m.model_dump() for m in req.messages])
         cid, t0 = f"chatcmpl-{next(ids)}", int(time.time())
         head = {"id": cid, "created": t0, "model": model_name}

@@ -472,3 +472,13 @@ def test_stream_usage_chunk():
             assert all(ch["choices"] for ch in _sse(resp))
     finally:
         w.stop()
+
+
+def test_chat_max_completion_tokens():
+    c, w = _client()
+    try:
+        got = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}], "max_tokens": 9,
+                                                   "max_completion_tokens": 3}).json()
+        assert got["usage"]["completion_tokens"] == 3
+    finally:
+        w.stop()
