@@ -12,6 +12,9 @@ at most ``--concurrency`` in flight, and measures per request:
 * ITL - the gaps between token-carrying events (one event per engine step, so with MTP
   a gap covers up to 1 + drafts tokens).
 
+Output tokens are counted from each event's ``token_ids`` (one per text event when a
+server sends none), and from the final usage chunk when the server sends one.
+
 Prints one JSON line: output tok/s over the run's wall time, request rate, and mean /
 median / p99 of TTFT, TPOT and ITL in milliseconds.  The same measurement the reference's
 delivery runs with vLLM's serving benchmark against its OpenAI server (the north star
@@ -64,6 +67,10 @@ async def _one(client, url: str, body: dict) -> Result:
                 if "error" in ev:
                     res.error = str(ev["error"])
                     return res
+                if not ev.get("choices"):  # the usage chunk: the server's own token count
+                    if ev.get("usage"):
+                        res.tokens = int(ev["usage"]["completion_tokens"])
+                    continue
                 ch = ev["choices"][0]
                 n = len(ch.get("token_ids") or []) if "token_ids" in ch else (1 if ch.get("text") else 0)
                 if n:
@@ -92,7 +99,7 @@ async def run(url: str, prompts: list, output_len: int, concurrency: int, temper
         async def bounded(p):
             async with sem:
                 body = {"prompt": p, "max_tokens": output_len, "stream": True, "ignore_eos": True,
-                        "temperature": temperature}
+                        "temperature": temperature, "stream_options": {"include_usage": True}}
                 return await _one(client, endpoint, body)
 
         t0 = time.perf_counter()
