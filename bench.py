@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--offload", action="store_true", help="swap-based host KV offload when the block pool runs out")
     ap.add_argument("--num-blocks", type=int, default=None,
                     help="KV blocks per rank (default: every request of the replica fits)")
+    ap.add_argument("--kernel-profile", default=None, metavar="PREFIX",
+                    help="after the timed region (untimed), run 2 more steps under torch.profiler and write "
+                         "each rank's per-kernel device time to PREFIX.rank<r>.json")
     return ap.parse_args()
 
 
@@ -223,6 +226,11 @@ def main():
                                "swapped_out_gib": round(off.bytes_out / 2**30, 3) if off else 0.0,
                                "swapped_in_gib": round(off.bytes_in / 2**30, 3) if off else 0.0}
         print(json.dumps(line), flush=True)
+    if args.kernel_profile:
+        from oscar_b200.utils.kernel_profile import profile_steps
+        eng.use_graphs = False  # same kernels, launched eagerly (see profile_steps)
+        profile_steps(eng.step, 2, args.kernel_profile, rank)
+        barrier_sync()
     eng.close()
     if world > 1:
         dist.barrier()
