@@ -253,11 +253,13 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                 try:
                     reason, first, n_sent = None, True, 0
                     usage = bool((req.stream_options or {}).get("include_usage"))
+                    failed = False
                     while reason is None:
                         try:
                             text, new, reason = await next_event()
                         except RuntimeError as e:
                             yield f"data: {json.dumps({'error': str(e)})}\n\n"
+                            failed = True
                             break
                         entries = None
                         if lp is not None:  # this chunk's tokens' logprobs, recorded before the update
@@ -265,7 +267,7 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
                         n_sent += len(new)
                         yield f"data: {json.dumps(chunk(text, new, reason, first, entries))}\n\n"
                         first = False
-                    if usage:  # a last chunk with no choices and the token counts
+                    if usage and not failed:  # a last chunk with no choices and the token counts
                         last = {**chunk("", [], None, False), "choices": []}
                         last["usage"] = {"prompt_tokens": len(prompt), "completion_tokens": n_sent,
                                          "total_tokens": len(prompt) + n_sent}
@@ -279,13 +281,17 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
             return StreamingResponse(sse(), media_type="text/event-stream")
 
         text, out, reason = "", [], None
-        while reason is None:
-            try:
-                delta, new, reason = await next_event()
-            except RuntimeError as e:
-                raise HTTPException(500, str(e)) from e
-            text += delta
-            out += new
+        try:
+            while reason is None:
+                try:
+                    delta, new, reason = await next_event()
+                except RuntimeError as e:
+                    raise HTTPException(500, str(e)) from e
+                text += delta
+                out += new
+        except asyncio.CancelledError:
+            worker.abort(fut)  # the client went away, or a sibling choice failed
+            raise
         entries = None
         if lp is not None:
             await watch  # the worker attaches the logprobs when it resolves the future
@@ -306,7 +312,15 @@ def create_app(worker: EngineWorker, tokenizer=None, manifests: list | None = No
         if req.stream:
             raise HTTPException(400, "n > 1 is not supported with stream")
         reqs = [req.model_copy(update={"seed": None if req.seed is None else req.seed + i, "n": 1}) for i in range(n)]
-        res = await asyncio.gather(*(generate(prompt, r, cid, chunk, final, lp) for r in reqs))
+        tasks = [asyncio.ensure_future(generate(prompt, r, cid, chunk, final, lp)) for r in reqs]
+        try:
+            res = await asyncio.gather(*tasks)
+        except BaseException:
+            # one choice failed or the client went away: the others stop too (their
+            # cancellation aborts their engine requests)
+            for t in tasks:
+                t.cancel()
+            raise
         choices = [{**x["choices"][0], "index": i} for i, x in enumerate(res)]
         done = sum(x["usage"]["completion_tokens"] for x in res)
         return {**res[0], "choices": choices,

@@ -482,3 +482,38 @@ def test_chat_max_completion_tokens():
         assert got["usage"]["completion_tokens"] == 3
     finally:
         w.stop()
+
+
+def test_failed_choice_aborts_its_siblings():
+    """With ``n`` choices, a choice whose engine request fails ends the response with an
+    error and aborts the other choices' requests (they would otherwise run to max_tokens)."""
+    from concurrent.futures import Future
+
+    c, w = _client()
+    real_submit, real_abort = w.submit, w.abort
+    subs, aborted = [], []
+
+    def submit(*a, **k):
+        if len(subs) == 1:  # the second choice fails at once
+            f = Future()
+            f.set_exception(RuntimeError("injected engine failure"))
+            subs.append(f)
+            return f
+        f = real_submit(*a, **k)
+        subs.append(f)
+        return f
+
+    def abort(f):
+        aborted.append(f)
+        return real_abort(f)
+
+    w.submit, w.abort = submit, abort
+    try:
+        r = c.post("/v1/completions", json={"prompt": PROMPTS[0], "max_tokens": 400, "n": 3, "seed": 1,
+                                            "temperature": 0.8})
+        assert r.status_code == 500
+        others = [f for i, f in enumerate(subs) if i != 1]
+        assert len(others) == 2 and all(f in aborted for f in others)
+    finally:
+        w.submit, w.abort = real_submit, real_abort
+        w.stop()
