@@ -44,7 +44,10 @@ def parse():
     ap.add_argument("--num-spec", type=int, default=3)
     ap.add_argument("--accept-mean", type=float, default=2.0)
     ap.add_argument("--kv", choices=["int2", "bf16"], default="int2")
-    ap.add_argument("--prefill-policy", choices=["fcfs", "wide"], default="wide")
+    ap.add_argument("--prefill-policy", choices=["fcfs", "wide"], default="fcfs",
+                    help="fcfs: prompts are prefilled in arrival order (15,360 tokens per step) and each request "
+                         "starts decoding when its prompt is done, so TTFT is per request; wide: every prompt "
+                         "advances together (every first token waits for the whole prefill)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--dp", type=int, default=1,
                     help="data-parallel replicas, each TP over gpus/dp ranks (BASELINE config 5: DP2 x TP4)")
@@ -210,7 +213,9 @@ def main():
                        "baseline_value_tok_s": BASELINE_TOK_S,
                        "baseline_source": "plan/audits/PERFORMANCE-20260908.md:76 (910B4 x4)"},
             "tpot_ms": round(tpot, 3), "ttft_ms_mean": round(1e3 * float(np.mean(ttft)), 1),
+            "ttft_ms_p50": round(1e3 * float(np.median(ttft)), 1),
             "ttft_ms_max": round(1e3 * float(np.max(ttft)), 1), "prefill_s": round(t_prefill, 2),
+            "prefill_policy": args.prefill_policy,
             "span_ms_per_step": round(span_ms / args.steps, 3), "tokens_timed": tokens,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": int(h2d_step),
                     "d2h_bytes_per_step": int(d2h_step),

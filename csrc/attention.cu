@@ -14,6 +14,8 @@
 // online softmax; each CTA writes a normalised partial output and its LSE.
 #include "common.cuh"
 #include "params.h"
+#include "oscar_attention.h"
+#include <cstddef>
 
 #include <mutex>
 
@@ -388,6 +390,28 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(MergeParams p) {
 
 extern "C" int oscar_int2_attention(const oscar::AttnParams* params, cudaStream_t stream);
 
+extern "C" int oscar_params_layout(long long* out, int cap) {
+  using oscar::AttnParams;
+  using oscar::MergeParams;
+#define OSCAR_A(f) (long long)offsetof(AttnParams, f)
+#define OSCAR_M(f) (long long)offsetof(MergeParams, f)
+  const long long v[] = {
+      (long long)sizeof(AttnParams), OSCAR_A(q), OSCAR_A(k_fresh), OSCAR_A(v_fresh), OSCAR_A(Hq), OSCAR_A(Hk),
+      OSCAR_A(D), OSCAR_A(scale), OSCAR_A(kv_mode), OSCAR_A(pool), OSCAR_A(page_bytes), OSCAR_A(kc), OSCAR_A(vc),
+      OSCAR_A(stage_k), OSCAR_A(stage_v), OSCAR_A(owner), OSCAR_A(stage_rows), OSCAR_A(block_tables),
+      OSCAR_A(bt_stride), OSCAR_A(q_start), OSCAR_A(seq_lens), OSCAR_A(work), OSCAR_A(n_work), OSCAR_A(part_o),
+      OSCAR_A(part_lse), OSCAR_A(status),
+      (long long)sizeof(MergeParams), OSCAR_M(part_o), OSCAR_M(part_lse), OSCAR_M(item_first), OSCAR_M(item_count),
+      OSCAR_M(max_rb), OSCAR_M(tok_req), OSCAR_M(q_start), OSCAR_M(Hq), OSCAR_M(Hk), OSCAR_M(D), OSCAR_M(RvT),
+      OSCAR_M(gate), OSCAR_M(gate_ld), OSCAR_M(gate_hstride), OSCAR_M(out_bf16), OSCAR_M(out_i8),
+      OSCAR_M(out_scale), OSCAR_M(T)};
+#undef OSCAR_A
+#undef OSCAR_M
+  const int n = (int)(sizeof(v) / sizeof(v[0]));
+  for (int i = 0; i < n && i < cap; ++i) out[i] = v[i];
+  return n;
+}
+
 extern "C" int oscar_paged_attention(const oscar::AttnParams* params, cudaStream_t stream) {
   using namespace oscar;
   const AttnParams& p = *params;
@@ -395,11 +419,7 @@ extern "C" int oscar_paged_attention(const oscar::AttnParams* params, cudaStream
   if (p.kv_mode == 0) return oscar_int2_attention(params, stream);  // pipelined code-domain kernel
   if (p.D != kD) return -300;
   const size_t smem = (kRows + 2 * kTile) * kRowBytes;
-  static bool attr = false;
-  if (!attr) {
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr = true;
-  }
+  OSCAR_RC(ensure_smem(paged_attention_kernel, (int)smem));
   dim3 grid(p.n_work, p.Hk);
   paged_attention_kernel<<<grid, kThreads, smem, stream>>>(p);
   return (int)cudaGetLastError();
@@ -411,11 +431,7 @@ extern "C" int oscar_attn_merge(const oscar::MergeParams* params, cudaStream_t s
   if (p.T <= 0) return 0;
   if (p.D != kD) return -301;
   const size_t smem = (size_t)p.Hq * p.D * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(attn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    attr = true;
-  }
+  OSCAR_RC(ensure_smem(attn_merge_kernel, 200 * 1024));
   attn_merge_kernel<<<p.T, 256, smem, stream>>>(p);
   return (int)cudaGetLastError();
 }
@@ -452,7 +468,7 @@ extern "C" int oscar_attn_merge(const oscar::MergeParams* params, cudaStream_t s
 // ============================================================================
 namespace oscar {
 namespace {
-constexpr int kNoAllocItems = 256;
+constexpr int kNoAllocItems = OSCAR_NOALLOC_MAX_ITEMS;
 constexpr size_t kNoAllocPartO = (size_t)kNoAllocItems * kRows * kD;  // floats
 constexpr size_t kNoAllocPartL = (size_t)kNoAllocItems * kRows;       // floats
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocPartO + kNoAllocPartL];

@@ -522,12 +522,7 @@ int cache_map(CUtensorMap* map, const void* base, long long rows, long long cols
 template <int N>
 int launch_bf16(const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p, cudaStream_t stream) {
   using L = BfLayout<N>;
-  static int attr = 0;
-  if (!attr) {
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(bf16_attention_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          L::kTotal));
-    attr = 1;
-  }
+  OSCAR_RC(ensure_smem(bf16_attention_tc_kernel<N>, L::kTotal));
   dim3 grid(p.n_work, p.Hk);
   bf16_attention_tc_kernel<N><<<grid, kThreads, L::kTotal, stream>>>(tk, tv, p);
   return (int)cudaGetLastError();

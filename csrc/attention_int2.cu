@@ -451,11 +451,7 @@ extern "C" int oscar_int2_attention(const oscar::AttnParams* params, cudaStream_
   if (p.page_bytes % 16) return -321;
   const Smem L = smem_layout(p.page_bytes);
   if (L.total > 227 * 1024) return -322;
-  static int attr = 0;
-  if (attr < L.total) {
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(int2_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total));
-    attr = L.total;
-  }
+  OSCAR_RC(ensure_smem(int2_attention_kernel, L.total));
   dim3 grid(p.n_work, p.Hk);
   int2_attention_kernel<<<grid, kThreads, L.total, stream>>>(p);
   return (int)cudaGetLastError();

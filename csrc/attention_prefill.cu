@@ -617,12 +617,7 @@ extern "C" int oscar_int2_prefill_tc(const oscar::AttnParams* params, const void
   if (rc) return rc;
   rc = fresh_map(&tv, p.v_fresh, fresh_rows, (long long)p.Hk * kD);
   if (rc) return rc;
-  static int attr = 0;
-  if (!attr) {
-    OSCAR_CUDA_CHECK(
-        cudaFuncSetAttribute(int2_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PfLayout::kAlloc));
-    attr = 1;
-  }
+  OSCAR_RC(ensure_smem(int2_prefill_tc_kernel, PfLayout::kAlloc));
   dim3 grid(n_tiles, p.Hk);
   int2_prefill_tc_kernel<<<grid, kThreads, PfLayout::kAlloc, stream>>>(tk, tv, p,
                                                                          reinterpret_cast<const int4*>(tiles));

@@ -857,12 +857,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
 template <int N>
 int launch_tc(const AttnParams& p, cudaStream_t stream) {
   using L = TcLayout<N>;
-  static int attr = 0;
-  if (!attr) {
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(int2_attention_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          L::kAlloc));
-    attr = 1;
-  }
+  OSCAR_RC(ensure_smem(int2_attention_tc_kernel<N>, L::kAlloc));
   dim3 grid(p.n_work, p.Hk);
   int2_attention_tc_kernel<N><<<grid, kThreads, L::kAlloc, stream>>>(p);
   return (int)cudaGetLastError();

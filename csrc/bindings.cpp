@@ -4,6 +4,7 @@
 // pure-torch oracle only for CPU tensors.
 #include <torch/extension.h>
 #include <cstdlib>
+#include <vector>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -34,7 +35,7 @@ int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long long ldd, co
 int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                      const float* scale_a, const float* scale_b, void* out, long long ldo, int mode, int trans, int bn,
                      int splits, int* status, int* done_counter, int* epoch, unsigned** peer_signals, int rank,
-                     int world, float* ws, int* tile_cnt, cudaStream_t stream);
+                     int world, float* ws, int* tile_cnt, cudaStream_t stream, int static_ops);
 int oscar_swiglu_quant(const __nv_bfloat16* gu, long long ld, int T, int I, int8_t* out, float* scale,
                        cudaStream_t s);
 int oscar_act_quant(const __nv_bfloat16* x, long long ld, int T, int K, int8_t* out, float* scale, cudaStream_t s);
@@ -43,6 +44,18 @@ int oscar_embed(const int* tok, const __nv_bfloat16* table, int T, int H, int vo
 int oscar_argmax(const __nv_bfloat16* logits, long long ld, int T, int V, int index_offset, float* best_val,
                  int* best_idx, cudaStream_t s);
 int oscar_f32_to_bf16(const float* x, long long n, __nv_bfloat16* y, cudaStream_t s);
+int oscar_gemm_i8_rs(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                     const float* scale_a, const float* scale_b, int trans, int bn, int splits, float* const* peer_out,
+                     int rows_per_rank, long long ldo, long long slot_stride, int* done_counter, int* epoch,
+                     unsigned** peer_signals, int rank, int world, float* ws, int* tile_cnt, int* status,
+                     cudaStream_t stream);
+int oscar_rmsnorm_ag(float* x, long long ldx, const float* delta, long long ldd, int n_slots, long long slot_stride,
+                     const float* w, float off, float eps, int H,
+                     int rows, int row0, int8_t* const* xq, float* const* xs, __nv_bfloat16* const* hid,
+                     unsigned* const* slots, int world, int* done, int* epoch, const unsigned* rs_signals,
+                     const int* rs_epoch, int* status, long long budget_ns, cudaStream_t s);
+int oscar_wait_flags(const unsigned* signals, const int* epoch, int world, int* status, long long budget_ns,
+                     cudaStream_t s);
 }
 
 namespace {
@@ -125,8 +138,121 @@ void gemm_i8_allreduce(const Tensor& A, const Tensor& B, const Tensor& scale_a, 
                             ptr<float>(scale_b), reinterpret_cast<void*>(mc_ptr), ldo, 3, (int)trans, (int)bn,
                             (int)splits, optr<int>(status), ptr<int>(done_counter), ptr<int>(epoch),
                             reinterpret_cast<unsigned**>(peer_signals_dev), (int)rank, (int)world, ptr<float>(ws),
-                            ptr<int>(tile_cnt), stream()),
+                            ptr<int>(tile_cnt), stream(), trans ? 1 : 2),
            "gemm_i8_allreduce");
+}
+
+// Split-K GEMM with a bf16 result: every split adds its fp32 partial into `ws` (zero
+// between calls, same indexing as `out`); the last split of each (tile, row quarter),
+// counted in `tile_cnt`, converts those rows to bf16 and zeroes them again.
+void gemm_i8_split(const Tensor& A, const Tensor& B, const Tensor& scale_a, const Tensor& scale_b, Tensor& out,
+                   int64_t trans, int64_t bn, int64_t splits, Tensor& ws, Tensor& tile_cnt,
+                   const optional<Tensor>& status) {
+  CHECK_CUDA(A);
+  CHECK_CUDA(B);
+  CHECK_DTYPE(A, at::kChar);
+  CHECK_DTYPE(B, at::kChar);
+  CHECK_DTYPE(scale_a, at::kFloat);
+  CHECK_DTYPE(scale_b, at::kFloat);
+  CHECK_DTYPE(out, at::kBFloat16);
+  CHECK_DTYPE(ws, at::kFloat);
+  CHECK_DTYPE(tile_cnt, at::kInt);
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_i8_split: A [M,K], B [N,K]");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_i8_split: K must be contiguous");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "gemm_i8_split: out must be row-major 2-D");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  TORCH_CHECK(scale_a.numel() >= M && scale_b.numel() >= N, "gemm_i8_split: scale sizes");
+  if (trans) {
+    TORCH_CHECK(out.size(0) >= N && out.size(1) >= M, "gemm_i8_split: out shape (transposed)");
+  } else {
+    TORCH_CHECK(out.size(0) >= M && out.size(1) >= N, "gemm_i8_split: out shape");
+  }
+  const long long need = trans ? (long long)(N - 1) * out.stride(0) + M : (long long)(M - 1) * out.stride(0) + N;
+  TORCH_CHECK(ws.numel() >= need, "gemm_i8_split: workspace too small");
+  const long long tiles = (long long)((M + 127) / 128) * ((N + bn - 1) / bn);
+  TORCH_CHECK(tile_cnt.numel() >= tiles * 4, "gemm_i8_split: tile counters too small");
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_rc(oscar_gemm_i8_ex(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), M, N, K, ptr<float>(scale_a),
+                            ptr<float>(scale_b), out.data_ptr(), out.stride(0), 4, (int)trans, (int)bn, (int)splits,
+                            optr<int>(status), nullptr, nullptr, nullptr, 0, 1, ptr<float>(ws), ptr<int>(tile_cnt),
+                            stream(), trans ? 1 : 2),
+           "gemm_i8_split");
+}
+
+// Row-parallel GEMM with the reduce-scatter epilogue (sequence-parallel TP): token row t
+// of the fp32 result is added into rank t / rows_per_rank's buffer; peer_out_dev is a
+// device array of `world` float pointers, peer_signals_dev one of `world` signal slots.
+void gemm_i8_rs(const Tensor& A, const Tensor& B, const Tensor& scale_a, const Tensor& scale_b, int64_t trans,
+                int64_t bn, int64_t splits, int64_t peer_out_dev, int64_t rows_per_rank, int64_t ldo,
+                int64_t slot_stride, Tensor& done_counter, Tensor& epoch, int64_t peer_signals_dev, int64_t rank, int64_t world, Tensor& ws,
+                Tensor& tile_cnt, const optional<Tensor>& status) {
+  CHECK_CUDA(A);
+  CHECK_DTYPE(A, at::kChar);
+  CHECK_DTYPE(B, at::kChar);
+  CHECK_DTYPE(ws, at::kFloat);
+  CHECK_DTYPE(tile_cnt, at::kInt);
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_i8_rs: K must be contiguous");
+  TORCH_CHECK(peer_out_dev != 0 && peer_signals_dev != 0, "gemm_i8_rs: peer pointer tables required");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  const long long tokens = trans ? N : M, cols = trans ? M : N;
+  TORCH_CHECK(cols <= ldo && ws.numel() >= tokens * ldo, "gemm_i8_rs: workspace too small");
+  TORCH_CHECK(tokens <= rows_per_rank * world, "gemm_i8_rs: more token rows than the ranks own");
+  const long long tiles = (long long)((M + 127) / 128) * ((N + bn - 1) / bn);
+  TORCH_CHECK(tile_cnt.numel() >= tiles * 4, "gemm_i8_rs: tile counters too small");
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_rc(oscar_gemm_i8_rs(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), M, N, K, ptr<float>(scale_a),
+                            ptr<float>(scale_b), (int)trans, (int)bn, (int)splits,
+                            reinterpret_cast<float* const*>(peer_out_dev), (int)rows_per_rank, ldo, slot_stride,
+                            ptr<int>(done_counter), ptr<int>(epoch), reinterpret_cast<unsigned**>(peer_signals_dev),
+                            (int)rank, (int)world, ptr<float>(ws), ptr<int>(tile_cnt), optr<int>(status), stream()),
+           "gemm_i8_rs");
+}
+
+// Sequence-parallel RMSNorm of this rank's `rows` residual rows with the all-gather
+// pushed to every rank (pointer lists hold one raw device address per rank).
+void rmsnorm_ag(Tensor& x, const optional<Tensor>& delta, int64_t n_slots, int64_t slot_stride, const Tensor& w,
+                double off, double eps, int64_t rows,
+                int64_t row0, const std::vector<int64_t>& xq, const std::vector<int64_t>& xs,
+                const std::vector<int64_t>& hid, const std::vector<int64_t>& slots, Tensor& done, Tensor& epoch,
+                int64_t rs_signals, const optional<Tensor>& rs_epoch, const optional<Tensor>& status,
+                int64_t budget_ns) {
+  CHECK_CUDA(x);
+  CHECK_DTYPE(x, at::kFloat);
+  CHECK_DTYPE(w, at::kFloat);
+  const int world = (int)xq.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && (int)xs.size() == world && (int)slots.size() == world &&
+                  (hid.empty() || (int)hid.size() == world),
+              "rmsnorm_ag: one pointer per rank");
+  TORCH_CHECK(x.stride(1) == 1 && x.size(0) >= rows, "rmsnorm_ag: residual rows");
+  const int H = x.size(1);
+  std::vector<int8_t*> pq(world);
+  std::vector<float*> ps(world);
+  std::vector<__nv_bfloat16*> ph(world);
+  std::vector<unsigned*> psl(world);
+  for (int q = 0; q < world; ++q) {
+    pq[q] = reinterpret_cast<int8_t*>(xq[q]);
+    ps[q] = reinterpret_cast<float*>(xs[q]);
+    ph[q] = hid.empty() ? nullptr : reinterpret_cast<__nv_bfloat16*>(hid[q]);
+    psl[q] = reinterpret_cast<unsigned*>(slots[q]);
+  }
+  float* d = optr_view<float>(delta);
+  const long long ldd = d ? delta->stride(0) : 0;
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(oscar_rmsnorm_ag(ptr<float>(x), x.stride(0), d, ldd, (int)n_slots, slot_stride, ptr<float>(w), (float)off,
+                            (float)eps, H, (int)rows,
+                            (int)row0, pq.data(), ps.data(), hid.empty() ? nullptr : ph.data(), psl.data(), world,
+                            ptr<int>(done), ptr<int>(epoch), reinterpret_cast<const unsigned*>(rs_signals),
+                            optr<int>(rs_epoch), optr<int>(status), budget_ns, stream()),
+           "rmsnorm_ag");
+}
+
+// Bounded wait until every rank has published this rank's current epoch into its
+// signal pad slots [signals, signals + world).
+void wait_flags(int64_t signals, const Tensor& epoch, int64_t world, const optional<Tensor>& status, int64_t budget_ns) {
+  const c10::cuda::CUDAGuard guard(epoch.device());
+  check_rc(oscar_wait_flags(reinterpret_cast<const unsigned*>(signals), ptr<int>(epoch), (int)world,
+                            optr<int>(status), budget_ns, stream()),
+           "wait_flags");
 }
 
 // Install a per-CTA timeline buffer for the tcgen05 attention kernel (0 removes it).
@@ -263,7 +389,12 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
   p.part_o = ptr<float>(part_o);
   p.part_lse = ptr<float>(part_lse);
   p.status = optr<int>(status);
+  CHECK_DTYPE(part_o, at::kFloat);
+  CHECK_DTYPE(part_lse, at::kFloat);
+  CHECK_CONTIG(part_o);
+  CHECK_CONTIG(part_lse);
   TORCH_CHECK(part_o.numel() >= (int64_t)p.n_work * Hk * 64 * D, "part_o too small");
+  TORCH_CHECK(part_lse.numel() >= (int64_t)p.n_work * Hk * 64, "part_lse too small");
   const c10::cuda::CUDAGuard guard(q.device());
   // Steps with prefill ("long") requests: the planner puts the short requests' items
   // first (decode / verify, split over the KV range) and gives every 64-row block of a
@@ -497,6 +628,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_i8", &gemm_i8);
   m.def("attn_tc_trace", &attn_tc_trace);
   m.def("gemm_i8_allreduce", &gemm_i8_allreduce);
+  m.def("gemm_i8_split", &gemm_i8_split);
+  m.def("gemm_i8_rs", &gemm_i8_rs);
+  m.def("rmsnorm_ag", &rmsnorm_ag);
+  m.def("wait_flags", &wait_flags);
   m.def("num_sms", &num_sms);
   m.def("kv_store", &kv_store);
   m.def("paged_attention", &paged_attention);

@@ -72,6 +72,11 @@ OSCAR_DEVICE uint64_t globaltimer_ns() {
   return t;
 }
 
+// Lets the next kernel of the stream start its CTAs now if it was launched as a
+// programmatic dependent (the W8A8 GEMM is): it waits for this kernel's completion
+// before it reads what this kernel writes, so issuing this early is always safe.
+OSCAR_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 OSCAR_DEVICE void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
@@ -98,6 +103,40 @@ OSCAR_DEVICE int8_t quant_i8(float x, float inv_scale) {
 }
 
 }  // namespace oscar
+
+#include <map>
+#include <mutex>
+#include <utility>
+namespace oscar {
+// cudaFuncSetAttribute acts on the current device only, so a process that drives
+// several GPUs must raise a kernel's dynamic shared-memory limit on each of them.
+// The (kernel, device) pairs already raised are remembered under a lock.
+inline int ensure_smem_attr(const void* fn, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  std::lock_guard<std::mutex> g(mu);
+  const auto key = std::make_pair(fn, dev);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return 0;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return (int)e;
+  done[key] = bytes;
+  return 0;
+}
+template <class F>
+inline int ensure_smem(F* fn, int bytes) {
+  return ensure_smem_attr(reinterpret_cast<const void*>(fn), bytes);
+}
+}  // namespace oscar
+
+#define OSCAR_RC(expr)          \
+  do {                          \
+    const int _rc = (expr);     \
+    if (_rc) return _rc;        \
+  } while (0)
 
 #define OSCAR_CUDA_CHECK(expr)                                                   \
   do {                                                                           \

@@ -80,6 +80,7 @@ __global__ void __launch_bounds__(NT) rmsnorm_quant_kernel(float* __restrict__ x
                                                          int zero_delta) {
   __shared__ float red[NT / 32];
   const int t = blockIdx.x;
+  pdl_trigger();
   wait_ranks(rw);
   __syncthreads();
   const int nv = H / 4;
@@ -151,6 +152,7 @@ __global__ void __launch_bounds__(NT) row_quant_kernel(const __nv_bfloat16* __re
                                                      int8_t* __restrict__ out, float* __restrict__ scale) {
   __shared__ float red[NT / 32];
   const int t = blockIdx.x;
+  pdl_trigger();
   const int nv = I / 8;
   const uint4* g = reinterpret_cast<const uint4*>(in + (long long)t * ld);
   const uint4* u = reinterpret_cast<const uint4*>(in + (long long)t * ld + I);
@@ -286,6 +288,139 @@ __global__ void __launch_bounds__(kT) argmax_kernel(const __nv_bfloat16* __restr
   }
 }
 
+// ---------------------------------------------------------------------------
+// Sequence-parallel tensor parallelism: every rank owns `rows` consecutive token
+// rows (from `row0`) of the fp32 residual stream.  The row-parallel GEMMs
+// reduce-scatter their partial sums into the owners' receive buffers, one slot per
+// source rank (GEMM epilogue mode 5); this kernel then, per owned row, waits for all
+// ranks' reduce-scatter epochs, adds the slots in rank order (deterministic) into the
+// residual, normalises, quantises, and writes the int8 row + scale (and the bf16 row
+// when asked) into the same rows of every rank's full-height buffers - the
+// all-gather, pushed over NVLink as the rows are produced.  The last CTA publishes
+// this rank's all-gather epoch into slot `rank` of every rank's signal pad; the
+// consumer waits for all slots (wait_flags_kernel) before the next GEMM reads.
+constexpr int kMaxRanks = 8;
+struct AgTargets {
+  int8_t* xq[kMaxRanks];          // [rows_full, H] per rank
+  float* xs[kMaxRanks];           // [rows_full] per rank
+  __nv_bfloat16* hid[kMaxRanks];  // [rows_full, H] per rank, or nullptr
+  unsigned* slot[kMaxRanks];      // slot `rank` of each rank's all-gather signal pad
+  int world;
+  int row0;   // first global row of this rank
+  int rows;   // rows owned by this rank (0 allowed: the kernel still publishes)
+  int* done;  // CTA completion counter, zero between launches
+  int* epoch; // this rank's all-gather epoch
+};
+
+template <int NT, int PV>
+__global__ void __launch_bounds__(NT) rmsnorm_ag_kernel(float* __restrict__ x, long long ldx,
+                                                      const float* __restrict__ delta, long long ldd,
+                                                      int n_slots, long long slot_stride,
+                                                      const float* __restrict__ w, float off, float eps, int H,
+                                                      RankWait rw, AgTargets ag) {
+  __shared__ float red[NT / 32];
+  wait_ranks(rw);
+  __syncthreads();
+  const int tl = blockIdx.x;
+  if (tl < ag.rows) {
+    const int t = ag.row0 + tl;
+    const int nv = H / 4;
+    float4* xr = reinterpret_cast<float4*>(x + (long long)tl * ldx);
+    const float4* dr = delta ? reinterpret_cast<const float4*>(delta + (long long)tl * ldd) : nullptr;
+    const float4* wr = reinterpret_cast<const float4*>(w);
+    float4 v[PV], wv[PV];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < PV; ++e) {
+      const int i = threadIdx.x + e * NT;
+      wv[e] = i < nv ? __ldg(wr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[e] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (dr) {
+      // slots written by other GPUs: read past L1, all slots' loads in flight together
+      float4 d[PV];
+#pragma unroll
+      for (int e = 0; e < PV; ++e) d[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < n_slots; ++q) {
+        const float4* dq = dr + q * (slot_stride / 4);
+#pragma unroll
+        for (int e = 0; e < PV; ++e) {
+          const int i = threadIdx.x + e * NT;
+          if (i < nv) {
+            const float4 a = __ldcg(dq + i);
+            d[e].x += a.x; d[e].y += a.y; d[e].z += a.z; d[e].w += a.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < PV; ++e) {
+        const int i = threadIdx.x + e * NT;
+        if (i < nv) {
+          v[e].x += d[e].x; v[e].y += d[e].y; v[e].z += d[e].z; v[e].w += d[e].w;
+          xr[i] = v[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < PV; ++e) ss += v[e].x * v[e].x + v[e].y * v[e].y + v[e].z * v[e].z + v[e].w * v[e].w;
+    ss = row_sum<NT>(ss, red);
+    const float inv = rsqrtf(ss / (float)H + eps);
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < PV; ++e) {
+      const int i = threadIdx.x + e * NT;
+      if (i < nv) {
+        const float4 ww = wv[e];
+        v[e].x = __bfloat162float(__float2bfloat16(v[e].x * inv * (off + ww.x)));
+        v[e].y = __bfloat162float(__float2bfloat16(v[e].y * inv * (off + ww.y)));
+        v[e].z = __bfloat162float(__float2bfloat16(v[e].z * inv * (off + ww.z)));
+        v[e].w = __bfloat162float(__float2bfloat16(v[e].w * inv * (off + ww.w)));
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[e].x), fabsf(v[e].y)), fmaxf(fabsf(v[e].z), fabsf(v[e].w))));
+        if (ag.hid[0]) {
+          const uint2 b = make_uint2(pack_bf16x2(v[e].x, v[e].y), pack_bf16x2(v[e].z, v[e].w));
+          for (int q = 0; q < ag.world; ++q) reinterpret_cast<uint2*>(ag.hid[q] + (long long)t * H)[i] = b;
+        }
+      }
+    }
+    amax = row_absmax<NT>(amax, red);
+    const float qi = amax > 0.f ? 127.f / amax : 0.f;
+#pragma unroll
+    for (int e = 0; e < PV; ++e) {
+      const int i = threadIdx.x + e * NT;
+      if (i < nv) {
+        const uint32_t packed = pack_i8x4(v[e].x, v[e].y, v[e].z, v[e].w, qi);
+        for (int q = 0; q < ag.world; ++q) reinterpret_cast<uint32_t*>(ag.xq[q] + (long long)t * H)[i] = packed;
+      }
+    }
+    if (threadIdx.x == 0) {
+      const float sc = amax > 0.f ? amax / 127.f : 1.f;
+      for (int q = 0; q < ag.world; ++q) ag.xs[q][t] = sc;
+    }
+  }
+  // every thread's pushes are visible system-wide before the CTA counts as done
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int done = atomicAdd(ag.done, 1) + 1;
+    if (done == (int)gridDim.x) {
+      __threadfence_system();
+      *ag.done = 0;
+      const int e = *ag.epoch + 1;
+      *ag.epoch = e;
+      for (int q = 0; q < ag.world; ++q)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ag.slot[q]), "r"((unsigned)e) : "memory");
+    }
+  }
+}
+
+// Waits (bounded) until every rank has published this rank's current epoch; the
+// next kernel, launched as a programmatic dependent, may start meanwhile and fetch
+// whatever does not depend on the wait (the GEMM's weights).
+__global__ void wait_flags_kernel(RankWait rw) {
+  pdl_trigger();
+  wait_ranks(rw);
+}
+
 // fp32 residual rows -> bf16 (final hidden state for the lm_head / MTP head).
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, long long n, __nv_bfloat16* __restrict__ y) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
@@ -318,6 +453,42 @@ extern "C" int oscar_rmsnorm_quant(float* x, long long ldx, float* delta, long l
   constexpr int NT = 256;
   RankWait rw{signals, epoch, world, status, (uint64_t)(wait_budget_ns > 0 ? wait_budget_ns : 5000000000ll)};
   OSCAR_PV_DISPATCH(H / 4, NT, (rmsnorm_quant_kernel<NT, PV><<<T, NT, 0, s>>>(x, ldx, delta, ldd, w, off, eps, H, out, scale, out_bf16, rw, zero_delta)));
+  return (int)cudaGetLastError();
+}
+
+// Sequence-parallel RMSNorm + all-gather (see rmsnorm_ag_kernel).  Pointer tables
+// hold `world` entries; hid may be all null.
+extern "C" int oscar_rmsnorm_ag(float* x, long long ldx, const float* delta, long long ldd, int n_slots,
+                                long long slot_stride, const float* w, float off,
+                                float eps, int H, int rows, int row0, int8_t* const* xq, float* const* xs,
+                                __nv_bfloat16* const* hid, unsigned* const* slots, int world, int* done, int* epoch,
+                                const unsigned* rs_signals, const int* rs_epoch, int* status, long long budget_ns,
+                                cudaStream_t s) {
+  if (world < 1 || world > kMaxRanks || rows < 0) return -410;
+  if (H % 4 || ldx % 4 || (delta && (ldd % 4 || slot_stride % 4))) return -401;
+  AgTargets ag{};
+  for (int q = 0; q < world; ++q) {
+    ag.xq[q] = xq[q];
+    ag.xs[q] = xs[q];
+    ag.hid[q] = hid ? hid[q] : nullptr;
+    ag.slot[q] = slots[q];
+  }
+  ag.world = world;
+  ag.row0 = row0;
+  ag.rows = rows;
+  ag.done = done;
+  ag.epoch = epoch;
+  constexpr int NT = 256;
+  RankWait rw{rs_signals, rs_epoch, world, status, (uint64_t)(budget_ns > 0 ? budget_ns : 5000000000ll)};
+  const int grid = rows > 0 ? rows : 1;
+  OSCAR_PV_DISPATCH(H / 4, NT, (rmsnorm_ag_kernel<NT, PV><<<grid, NT, 0, s>>>(x, ldx, delta, ldd, n_slots, slot_stride, w, off, eps, H, rw, ag)));
+  return (int)cudaGetLastError();
+}
+
+extern "C" int oscar_wait_flags(const unsigned* signals, const int* epoch, int world, int* status, long long budget_ns,
+                                cudaStream_t s) {
+  RankWait rw{signals, epoch, world, status, (uint64_t)(budget_ns > 0 ? budget_ns : 5000000000ll)};
+  wait_flags_kernel<<<1, 32, 0, s>>>(rw);
   return (int)cudaGetLastError();
 }
 

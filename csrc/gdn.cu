@@ -732,12 +732,8 @@ extern "C" int oscar_gdn_step(const oscar::GdnParams* params, int smem_state, cu
   dim3 grid(p.R, p.Hv);
   if (smem_state) {
     // long prefill chunks: fp32 state in shared memory across 16-token chunks
-    static bool attr = false;
     const int smem = kD * kD * sizeof(float);
-    if (!attr) {
-      OSCAR_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_kernel<16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr = true;
-    }
+    OSCAR_RC(ensure_smem(gdn_chunk_kernel<16, true>, smem));
     gdn_chunk_kernel<16, true><<<grid, kThreads, smem, stream>>>(p);
   } else if (smem_state == 0 && p.P <= kDecC) {
     // decode / verify: <= 8 tokens per request (commits + new) on the tensor cores

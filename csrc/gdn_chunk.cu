@@ -686,13 +686,8 @@ extern "C" int oscar_gdn_chunked(oscar::GdnParams* params, int T, void* ws, cuda
   p.ws_ut = p.ws_w + cH * kCk * kD;
   p.ws_p = p.ws_ut + cH * kCk * kD;
   p.ws_g = reinterpret_cast<float*>(p.ws_p + cH * kCk * kCk);
-  static bool attr = false;
-  if (!attr) {
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(gdn_wy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, WyLayout::kTotal));
-    OSCAR_CUDA_CHECK(
-        cudaFuncSetAttribute(gdn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ScanLayout::kTotal));
-    attr = true;
-  }
+  OSCAR_RC(ensure_smem(gdn_wy_kernel, WyLayout::kTotal));
+  OSCAR_RC(ensure_smem(gdn_scan_kernel, ScanLayout::kTotal));
   {
     const int conv_dim = 2 * p.Hk * kD + p.Hv * kD;
     const int slices = (conv_dim / 8 + kConvThreads - 1) / kConvThreads;

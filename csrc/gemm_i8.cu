@@ -18,6 +18,7 @@
 // atomic mode is also how row-parallel projections add straight into the fp32
 // residual stream.
 #include <cuda.h>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 #include "sm100.cuh"
@@ -43,6 +44,125 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
+
+// Reduce-scatter epilogue (mode 5): the fp32 value(s) of token `tok`, output
+// column(s) `col..` go to the rank owning that token, stored over NVLink into this
+// rank's slot of the owner's receive buffer (every value is written once; the owner
+// adds the slots of all ranks in a fixed order).
+OSCAR_DEVICE float* owner_dst(const GemmEpi& ep, int tok, int col) {
+  const int owner = tok / ep.rows_per_rank;
+  return ep.peer_out[owner] + ep.rank * ep.slot_stride + (long long)(tok - owner * ep.rows_per_rank) * ep.ldo + col;
+}
+OSCAR_DEVICE void red_to_owner(const GemmEpi& ep, int tok, int col, float4 v) {
+  *reinterpret_cast<float4*>(owner_dst(ep, tok, col)) = v;
+}
+OSCAR_DEVICE void red_to_owner1(const GemmEpi& ep, int tok, int col, float v) { *owner_dst(ep, tok, col) = v; }
+
+// One output value of a finished (fully reduced) element; used by the cluster
+// reduction for tails that do not fill a 4-wide vector.
+OSCAR_DEVICE void store_one(const GemmEpi& ep, int m, int n, float v) {
+  const long long idx = ep.trans ? (long long)n * ep.ldo + m : (long long)m * ep.ldo + n;
+  switch (ep.mode) {
+    case 0:
+    case 4: reinterpret_cast<__nv_bfloat16*>(ep.out)[idx] = __float2bfloat16(v); break;
+    case 1: atomicAdd(reinterpret_cast<float*>(ep.out) + idx, v); break;
+    case 2: reinterpret_cast<float*>(ep.out)[idx] = v; break;
+    case 3:
+      asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(reinterpret_cast<float*>(ep.out) + idx),
+                   "f"(v)
+                   : "memory");
+      break;
+    case 5: red_to_owner1(ep, ep.trans ? n : m, ep.trans ? m : n, v); break;
+  }
+}
+// Four consecutive output values at out index `idx` (16-byte aligned in fp32 terms).
+OSCAR_DEVICE void store_four(const GemmEpi& ep, long long idx, int tok, int col, float4 v) {
+  switch (ep.mode) {
+    case 0:
+    case 4:
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(ep.out) + idx) =
+          make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+      break;
+    case 1:
+      asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                       reinterpret_cast<float*>(ep.out) + idx),
+                   "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                   : "memory");
+      break;
+    case 2: *reinterpret_cast<float4*>(reinterpret_cast<float*>(ep.out) + idx) = v; break;
+    case 3:
+      asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                       reinterpret_cast<float*>(ep.out) + idx),
+                   "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                   : "memory");
+      break;
+    case 5: red_to_owner(ep, tok, col, v); break;
+  }
+}
+
+// Split-K through the cluster: CTA `me` of `S` (any S <= 8) sums its share of the
+// tile's rows - whole groups of 4 rows, [4*floor(32*me/S), 4*floor(32*(me+1)/S)) - of
+// the S partial int32 tiles that the CTAs staged in their shared memory (`red`,
+// [BN][BM+4] for the swapped layout, [BM][BN+4] otherwise), scales them and writes the
+// result.
+template <int BN>
+OSCAR_DEVICE void cluster_reduce_tile(const GemmEpi& ep, const int32_t* red, int m0, int n0, int M, int N, int e) {
+  constexpr int RS = BM + 4, CS = BN + 4;
+  const int S = ep.cluster_k;
+  const uint32_t me = sm100::cluster_ctarank();
+  const int r0 = 4 * ((BM / 4) * (int)me / S), R = 4 * ((BM / 4) * ((int)me + 1) / S) - r0;
+  const uint32_t base = smem_u32(red);
+  const bool vec_ok = (ep.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0;
+  if (ep.trans) {
+    // output (m, n) at out[n * ldo + m]: vectors of 4 consecutive m of one column n
+    const int per_col = R / 4;
+    for (int v = e; v < per_col * BN; v += 128) {
+      const int col = v / per_col, m4 = r0 + 4 * (v % per_col);
+      const int n = n0 + col, m = m0 + m4;
+      if (n >= N || m >= M) continue;
+      const uint32_t a = base + (uint32_t)(col * RS + m4) * 4u;
+      int4 acc = sm100::ld_dsmem_v4(sm100::mapa(a, 0));
+      for (int q = 1; q < S; ++q) {
+        const int4 x = sm100::ld_dsmem_v4(sm100::mapa(a, q));
+        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+      }
+      const float sb = __ldg(ep.scale_b + n);
+      if (m + 3 < M && (vec_ok || ep.mode == 5) && (reinterpret_cast<uintptr_t>(ep.scale_a + m) & 15) == 0) {
+        const float4 sa = __ldg(reinterpret_cast<const float4*>(ep.scale_a + m));
+        const float4 o = make_float4((float)acc.x * sa.x * sb, (float)acc.y * sa.y * sb, (float)acc.z * sa.z * sb,
+                                     (float)acc.w * sa.w * sb);
+        store_four(ep, (long long)n * ep.ldo + m, n, m, o);
+      } else {
+        const int a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        for (int j = 0; j < 4 && m + j < M; ++j) store_one(ep, m + j, n, (float)a4[j] * __ldg(ep.scale_a + m + j) * sb);
+      }
+    }
+  } else {
+    // output (m, n) at out[m * ldo + n]: vectors of 4 consecutive n of one row m
+    const int per_row = BN / 4;
+    for (int v = e; v < R * per_row; v += 128) {
+      const int row = r0 + v / per_row, c4 = 4 * (v % per_row);
+      const int m = m0 + row, n = n0 + c4;
+      if (m >= M || n >= N) continue;
+      const uint32_t a = base + (uint32_t)(row * CS + c4) * 4u;
+      int4 acc = sm100::ld_dsmem_v4(sm100::mapa(a, 0));
+      for (int q = 1; q < S; ++q) {
+        const int4 x = sm100::ld_dsmem_v4(sm100::mapa(a, q));
+        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+      }
+      const float sa = __ldg(ep.scale_a + m);
+      if (n + 3 < N && (vec_ok || ep.mode == 5) && (reinterpret_cast<uintptr_t>(ep.scale_b + n) & 15) == 0) {
+        const float4 sb = __ldg(reinterpret_cast<const float4*>(ep.scale_b + n));
+        const float4 o = make_float4((float)acc.x * sa * sb.x, (float)acc.y * sa * sb.y, (float)acc.z * sa * sb.z,
+                                     (float)acc.w * sa * sb.w);
+        store_four(ep, (long long)m * ep.ldo + n, m, n, o);
+      } else {
+        const int a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        for (int j = 0; j < 4 && n + j < N; ++j) store_one(ep, m, n + j, (float)a4[j] * sa * __ldg(ep.scale_b + n + j));
+      }
+    }
+  }
+}
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -88,6 +208,13 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Under programmatic dependent launch the set-up above overlapped the previous
+  // kernel; everything below that reads or writes memory it may touch waits for it.
+  // The TMA warp first fetches the static operand's first stages (below).
+  if (warp != 0) sm100::griddep_wait();
+  // the next kernel, if it is a programmatic dependent (another GEMM), may place its
+  // CTAs on SMs this grid leaves free and prefetch its weights there
+  sm100::griddep_launch_dependents();
 
   auto tile_coords = [&](int t, int& m0, int& n0, int& kb0, int& kb1) {
     const int split = t % splits;
@@ -108,16 +235,43 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t phase = 0;
       bool ok = true;
       uint32_t issued_mask = 0, issued_parity = 0;  // per stage: a copy was issued, with this phase
+      // The weights (the static operand) of the first tile's first stages are fetched
+      // before waiting for the previous kernel: they do not depend on it, and the
+      // fetch overlaps its tail.  Those stages are fresh, so no `empty` wait is needed.
+      const bool pre_a = ep.a_static != 0, pre_b = !pre_a && ep.b_static != 0;
+      int pre = 0;
+      if ((pre_a || pre_b) && (int)blockIdx.x < total) {
+        int m0, n0, kb0, kb1;
+        tile_coords(blockIdx.x, m0, n0, kb0, kb1);
+        pre = kb1 - kb0 < C::STAGES ? kb1 - kb0 : C::STAGES;
+        for (int i = 0; i < pre; ++i) {
+          uint8_t* sa = smem + i * C::STAGE_BYTES;
+          sm100::mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+          if (pre_a)
+            sm100::tma_load_2d(sa, &tmA, &full[i], (kb0 + i) * BK, m0);
+          else
+            sm100::tma_load_2d(sa + C::A_BYTES, &tmB, &full[i], (kb0 + i) * BK, n0);
+          issued_mask |= 1u << i;
+        }
+      }
+      sm100::griddep_wait();
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int m0, n0, kb0, kb1;
         tile_coords(t, m0, n0, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          if (pre > 0) {  // static half already in flight: add the dependent half
+            --pre;
+            if (!pre_a) sm100::tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+            if (pre_a) sm100::tma_load_2d(sb, &tmB, &full[stage], kb * BK, n0);
+            if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+            continue;
+          }
           if (!sm100::mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kTimeoutSlotEmpty, kWaitBudgetNs)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + stage * C::STAGE_BYTES;
-          uint8_t* sb = sa + C::A_BYTES;
           sm100::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           sm100::tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
           sm100::tma_load_2d(sb, &tmB, &full[stage], kb * BK, n0);
@@ -193,6 +347,32 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!sm100::mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kTimeoutAccFull, kWaitBudgetNs)) break;
       sm100::tc_fence_after();
+      if (ep.cluster_k > 1) {
+        // Stage this CTA's int32 partial tile in shared memory for the cluster reduction.
+        // The operand ring is free: this was the CTA's only tile and its MMAs are done.
+        int32_t* red = reinterpret_cast<int32_t*>(smem);
+        const bool zero = kb0 >= kb1;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c, r);
+          sm100::tmem_ld_wait();
+          if (ep.trans) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) red[(c + j) * (BM + 4) + row_in_tile] = zero ? 0 : (int32_t)r[j];
+          } else {
+            int4* dst = reinterpret_cast<int4*>(red + row_in_tile * (BN + 4) + c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = zero ? make_int4(0, 0, 0, 0)
+                            : make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2], (int)r[4 * j + 3]);
+          }
+        }
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&acc_empty[acc]);
+        continue;
+      }
       const int m = m0 + row_in_tile;
       const bool row_ok = m < M;
       const float sa = row_ok ? ep.scale_a[m] : 0.f;
@@ -265,9 +445,10 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               reinterpret_cast<__nv_bfloat16*>(ep.out)[idx] = __float2bfloat16(v);
             } else if (ep.mode == 1) {
               atomicAdd(reinterpret_cast<float*>(ep.out) + idx, v);
-            } else if (ep.mode == 3) {
-              // stage in the local workspace; the reduction through the switch is issued
-              // below with 16-byte transactions
+            } else if (ep.mode >= 3) {
+              // stage in the local workspace; the reduction through the switch (mode 3),
+              // the bf16 store (mode 4) or the reduce-scatter into the owning rank (mode 5)
+              // is issued below with 16-byte reads
               if (splits > 1)
                 atomicAdd(ep.ws + idx, v);
               else
@@ -281,7 +462,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&acc_empty[acc]);
-      if (ep.mode == 3) {
+      if (ep.mode >= 3) {
         // The rows of this (tile, row quarter) are complete in the workspace once every
         // split has added its part (split-K: counted in tile_cnt; else this warp alone).
         // The last contributor reads them back from L2 and reduces them into every rank
@@ -298,48 +479,81 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (last) __threadfence();
         }
         if (last) {
+          // Read back the summed rows in batches of eight independent 16-byte loads
+          // (one dependent load per iteration would serialise on the L2 latency).
           float* out = reinterpret_cast<float*>(ep.out);
+          auto emit4 = [&](long long base, int tok, int col, const float4& v) {
+            if (ep.mode == 5) {
+              red_to_owner(ep, tok, col, v);
+            } else if (ep.mode == 4) {
+              *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(ep.out) + base) =
+                  make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+            } else {
+              asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(out + base),
+                           "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                           : "memory");
+            }
+            *reinterpret_cast<float4*>(ep.ws + base) = make_float4(0.f, 0.f, 0.f, 0.f);
+          };
+          auto emit1 = [&](long long base, int tok, int col) {
+            const float v = __ldcg(ep.ws + base);
+            if (ep.mode == 5)
+              red_to_owner1(ep, tok, col, v);
+            else if (ep.mode == 4)
+              reinterpret_cast<__nv_bfloat16*>(ep.out)[base] = __float2bfloat16(v);
+            else
+              asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(out + base), "f"(v) : "memory");
+            ep.ws[base] = 0.f;
+          };
           const int mq = m0 + quarter * 32;  // first row of this warp
+          const int ncols = N - n0 < BN ? N - n0 : BN;
           if (ep.trans) {
             // element (m, n) at n * ldo + m: lanes cover 8 x 4 consecutive rows of 4 columns
             const int m4 = mq + 4 * (lane & 7);
-            for (int jj = lane >> 3; jj < BN; jj += 4) {
-              const int n = n0 + jj;
-              if (n >= N) break;
-              const long long base = (long long)n * ep.ldo + m4;
-              if (m4 + 3 < M) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(ep.ws + base));
-                asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(out + base),
-                             "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-                             : "memory");
-                *reinterpret_cast<float4*>(ep.ws + base) = make_float4(0.f, 0.f, 0.f, 0.f);
-              } else {
-                for (int e = 0; e < 4 && m4 + e < M; ++e) {
-                  const float v = __ldcg(ep.ws + base + e);
-                  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(out + base + e), "f"(v)
-                               : "memory");
-                  ep.ws[base + e] = 0.f;
+            const bool full4 = m4 + 3 < M;
+#pragma unroll 1
+            for (int jb = 0; jb < ncols; jb += 32) {
+              float4 v[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int jj = jb + 4 * u + (lane >> 3);
+                v[u] = (jj < ncols && full4)
+                           ? __ldcg(reinterpret_cast<const float4*>(ep.ws + (long long)(n0 + jj) * ep.ldo + m4))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int jj = jb + 4 * u + (lane >> 3);
+                if (jj >= ncols) continue;
+                const int n = n0 + jj;
+                const long long base = (long long)n * ep.ldo + m4;
+                if (full4) {
+                  emit4(base, n, m4, v[u]);
+                } else {
+                  for (int e = 0; m4 + e < M && e < 4; ++e) emit1(base + e, n, m4 + e);
                 }
               }
             }
           } else if (row_ok) {
             // element (m, n) at m * ldo + n: each thread owns a row
-            for (int j = 0; j < BN; j += 4) {
-              const int n = n0 + j;
-              if (n >= N) break;
-              const long long base = (long long)m * ep.ldo + n;
-              if (n + 3 < N) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(ep.ws + base));
-                asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(out + base),
-                             "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-                             : "memory");
-                *reinterpret_cast<float4*>(ep.ws + base) = make_float4(0.f, 0.f, 0.f, 0.f);
-              } else {
-                for (int e = 0; n + e < N; ++e) {
-                  const float v = __ldcg(ep.ws + base + e);
-                  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(out + base + e), "f"(v)
-                               : "memory");
-                  ep.ws[base + e] = 0.f;
+#pragma unroll 1
+            for (int jb = 0; jb < ncols; jb += 32) {
+              float4 v[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int j = jb + 4 * u;
+                v[u] = j + 3 < ncols ? __ldcg(reinterpret_cast<const float4*>(ep.ws + (long long)m * ep.ldo + n0 + j))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int j = jb + 4 * u;
+                if (j >= ncols) break;
+                const long long base = (long long)m * ep.ldo + n0 + j;
+                if (j + 3 < ncols) {
+                  emit4(base, m, n0 + j, v[u]);
+                } else {
+                  for (int e = 0; j + e < ncols; ++e) emit1(base + e, m, n0 + j + e);
                 }
               }
             }
@@ -351,14 +565,28 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   }
 
-  if (ep.mode == 3) __threadfence_system();  // this thread's reductions before the CTA's done count
+  if (ep.cluster_k > 1) {
+    // every CTA of the cluster has staged its partial tile (or aborted): reduce this
+    // CTA's rows across the cluster, then keep the shared memory alive until all peers
+    // have read it
+    __syncwarp();
+    sm100::cluster_sync();
+    if (warp >= 2 && !*abort_flag) {
+      int m0 = 0, n0 = 0, kb0 = 0, kb1 = 0;
+      tile_coords(blockIdx.x, m0, n0, kb0, kb1);
+      cluster_reduce_tile<BN>(ep, reinterpret_cast<const int32_t*>(smem), m0, n0, M, N, threadIdx.x - 64);
+    }
+    __syncwarp();
+    sm100::cluster_sync();
+  }
+  if (ep.mode == 3 || ep.mode == 5) __threadfence_system();  // this thread's reductions before the done count
   sm100::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
-  if (ep.mode == 3 && threadIdx.x == 0) {
+  if ((ep.mode == 3 || ep.mode == 5) && threadIdx.x == 0) {
     // every CTA's reductions are issued; the last CTA publishes the epoch to all ranks
     __threadfence_system();
     const int done = atomicAdd(ep.done_counter, 1) + 1;
@@ -448,23 +676,107 @@ int num_sms() {
   return n;
 }
 
+// Programmatic dependent launch of the GEMM (on unless OSCAR_PDL=0): its CTAs may
+// start while the previous kernel drains, set up TMEM and barriers and fetch their
+// first weight tiles, then wait for that kernel before touching its outputs.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("OSCAR_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// How many CTAs of gemm_i8_kernel<BN> can be resident at once when launched in
+// clusters of `S` (clusters must fit in one GPC, so this is below the SM count).
+template <int BN>
+int cluster_capacity(int S) {
+  using C = Cfg<BN>;
+  static std::mutex mu;
+  static std::unordered_map<long long, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long long key = (long long)dev * 64 + S;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  if (ensure_smem(gemm_i8_kernel<BN>, C::SMEM)) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_i8_kernel<BN>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = n * S;
+  return n * S;
+}
+
+bool cluster_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("OSCAR_GEMM_CLUSTER");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <int BN>
+int pick_cluster(int tiles, int splits) {
+  int S = splits < 8 ? splits : 8;
+  while (S >= 2 && tiles * S > cluster_capacity<BN>(S)) --S;
+  return S;
+}
+
 template <int BN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmEpi& ep, int M, int N, int K, int splits,
            int* status, cudaStream_t stream) {
   using C = Cfg<BN>;
-  static bool attr = false;
-  if (!attr) {
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(gemm_i8_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    attr = true;
-  }
+  OSCAR_RC(ensure_smem(gemm_i8_kernel<BN>, C::SMEM));
   const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
   const int total = m_tiles * n_tiles * splits;
-  const int grid = total < num_sms() ? total : num_sms();
-  gemm_i8_kernel<BN><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ep, M, N, K, splits, status);
-  return (int)cudaGetLastError();
+  // cluster split-K: one CTA per (tile, K slice), the slices of a tile in one cluster
+  const int grid = ep.cluster_k > 1 ? total : (total < num_sms() ? total : num_sms());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (ep.cluster_k > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = ep.cluster_k;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  OSCAR_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN>, ta, tb, ep, M, N, K, splits, status));
+  return 0;
 }
 
 }  // namespace
+
+int run_gemm(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K, const GemmEpi& ep,
+             int bn, int splits, int* status, cudaStream_t stream);
 }  // namespace oscar
 
 // A: [M, K] int8 (row stride lda bytes), B: [N, K] int8 (row stride ldb bytes).
@@ -473,43 +785,96 @@ extern "C" int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, lon
                                 const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
                                 int trans, int bn, int splits, int* status, int* done_counter, int* epoch,
                                 unsigned** peer_signals, int rank, int world, float* ws, int* tile_cnt,
-                                cudaStream_t stream);
+                                cudaStream_t stream, int static_ops);
 
 extern "C" int oscar_gemm_i8(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                              const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
                              int trans, int bn, int splits, int* status, cudaStream_t stream) {
   if (mode == 3) return -105;  // the multimem mode needs the completion state: use oscar_gemm_i8_ex
   return oscar_gemm_i8_ex(A, lda, B, ldb, M, N, K, scale_a, scale_b, out, ldo, mode, trans, bn, splits, status,
-                          nullptr, nullptr, nullptr, 0, 1, nullptr, nullptr, stream);
+                          nullptr, nullptr, nullptr, 0, 1, nullptr, nullptr, stream, trans ? 1 : 2);
 }
 
 extern "C" int oscar_gemm_i8_ex(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                                 const float* scale_a, const float* scale_b, void* out, long long ldo, int mode,
                                 int trans, int bn, int splits, int* status, int* done_counter, int* epoch,
                                 unsigned** peer_signals, int rank, int world, float* ws, int* tile_cnt,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, int static_ops) {
   using namespace oscar;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 16) || (lda % 16) || (ldb % 16)) return -102;
   if (splits < 1) splits = 1;
-  if (splits > 1 && mode != 1 && mode != 3) return -104;  // split-K partial sums must be accumulated
+  if (splits > 1 && mode != 1 && mode != 3 && mode != 4) return -104;  // split-K partial sums must be accumulated
+  if (mode == 4 && (splits < 2 || !ws || !tile_cnt)) return -109;
+  if (mode == 4 && (ldo % 4 || (reinterpret_cast<uintptr_t>(out) & 7) || (reinterpret_cast<uintptr_t>(ws) & 15)))
+    return -108;
   if (mode == 3 && (!done_counter || !epoch || !peer_signals || world < 1)) return -106;
   if (mode == 3 && (!ws || !tile_cnt)) return -107;
   if (mode == 3 && (ldo % 4 || (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(ws) & 15)))
     return -108;  // 16-byte reductions need 16-byte aligned rows
+  // static_ops: bit 0 = A, bit 1 = B does not depend on the previous kernel (weights)
+  GemmEpi ep{scale_a, scale_b, out, ldo, mode, trans, done_counter, epoch, peer_signals, rank, world, ws, tile_cnt,
+             static_ops & 1, (static_ops >> 1) & 1, nullptr, 0, 0, 0};
+  return oscar::run_gemm(A, lda, B, ldb, M, N, K, ep, bn, splits, status, stream);
+}
+
+// Row-parallel GEMM whose epilogue reduce-scatters over the tensor-parallel ranks:
+// the fp32 result row of token t is stored into slot `rank` (slot_stride floats apart)
+// of rank (t / rows_per_rank)'s receive buffer peer_out[owner] (device array of `world`
+// pointers) at row t % rows_per_rank.  Split-K slices are summed first, through the
+// thread-block cluster (or this rank's zeroed workspace `ws` when the slices do not
+// fit in clusters), so each value crosses NVLink once; the last CTA then bumps *epoch
+// and stores it with release semantics into slot `rank` of every rank's signal pad
+// (peer_signals[q] + rank).
+extern "C" int oscar_gemm_i8_rs(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                                const float* scale_a, const float* scale_b, int trans, int bn, int splits,
+                                float* const* peer_out, int rows_per_rank, long long ldo, long long slot_stride,
+                                int* done_counter, int* epoch, unsigned** peer_signals, int rank, int world, float* ws,
+                                int* tile_cnt, int* status, cudaStream_t stream) {
+  using namespace oscar;
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if ((K % 16) || (lda % 16) || (ldb % 16)) return -102;
+  if (splits < 1) splits = 1;
+  if (!peer_out || rows_per_rank < 1 || !done_counter || !epoch || !peer_signals || world < 1) return -110;
+  if (!ws || !tile_cnt || (ldo % 4) || (reinterpret_cast<uintptr_t>(ws) & 15)) return -111;
+  GemmEpi ep{scale_a, scale_b, ws, ldo, 5, trans, done_counter, epoch, peer_signals, rank, world, ws, tile_cnt,
+             trans ? 1 : 0, trans ? 0 : 1, peer_out, rows_per_rank, slot_stride, 0};
+  return run_gemm(A, lda, B, ldb, M, N, K, ep, bn, splits, status, stream);
+}
+
+namespace oscar {
+template <int BN>
+int run_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmEpi ep, int M, int N, int K, int splits, int* status,
+           cudaStream_t stream) {
+  // Split-K GEMMs reduce through a thread-block cluster when the tiles x slices fit
+  // on the GPU at once (modes that accumulate the slices: 1, 3, 4, 5).
+  ep.cluster_k = 0;
+  if (splits > 1 && ep.mode != 0 && ep.mode != 2 && cluster_enabled()) {
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int S = pick_cluster<BN>(tiles, splits);
+    if (S >= 2) {
+      ep.cluster_k = S;
+      splits = S;
+    }
+  }
+  return launch<BN>(ta, tb, ep, M, N, K, splits, status, stream);
+}
+
+int run_gemm(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K, const GemmEpi& ep,
+             int bn, int splits, int* status, cudaStream_t stream) {
   CUtensorMap ta, tb;
   int rc = make_map(&ta, A, M, K, lda, BM);
   if (rc) return rc;
   rc = make_map(&tb, B, N, K, ldb, bn);
   if (rc) return rc;
-  GemmEpi ep{scale_a, scale_b, out, ldo, mode, trans, done_counter, epoch, peer_signals, rank, world, ws, tile_cnt};
   switch (bn) {
-    case 32: return launch<32>(ta, tb, ep, M, N, K, splits, status, stream);
-    case 64: return launch<64>(ta, tb, ep, M, N, K, splits, status, stream);
-    case 128: return launch<128>(ta, tb, ep, M, N, K, splits, status, stream);
-    case 256: return launch<256>(ta, tb, ep, M, N, K, splits, status, stream);
+    case 32: return run_bn<32>(ta, tb, ep, M, N, K, splits, status, stream);
+    case 64: return run_bn<64>(ta, tb, ep, M, N, K, splits, status, stream);
+    case 128: return run_bn<128>(ta, tb, ep, M, N, K, splits, status, stream);
+    case 256: return run_bn<256>(ta, tb, ep, M, N, K, splits, status, stream);
     default: return -103;
   }
 }
+}  // namespace oscar
 
 extern "C" int oscar_num_sms() { return oscar::num_sms(); }

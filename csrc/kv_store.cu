@@ -174,13 +174,15 @@ __global__ void __launch_bounds__(kThreads) kv_prep_kernel(StoreParams p) {
 }
 
 // ---------------------------------------------------------------------------- rotate
-constexpr int kRT = 64;          // rows per rotation tile
+// rows per rotation tile: 16 rows (one m16 MMA slice) per CTA, so that a decode step's
+// few hundred rows spread over the SMs instead of queueing behind a handful of CTAs
+constexpr int kRT = 16;
 constexpr int kYStride = 264;    // fp32 row stride of the output tile (bank padding)
 
 struct RotSmem {
-  static constexpr int X = 0;                       // [64][256] bf16, swizzled (32 KB)
+  static constexpr int X = 0;                       // [kRT][256] bf16, swizzled
   static constexpr int R = kRT * 512;               // R^T chunk hi + lo: 2 x [256][64] bf16 (64 KB)
-  static constexpr int Y = R;                       // output [64][264] fp32, aliases R after the MMAs
+  static constexpr int Y = R;                       // output [kRT][264] fp32, aliases R after the MMAs
   static constexpr int Y_BYTES = kRT * kYStride * 4;
   static constexpr int TOTAL = R + (Y_BYTES > 65536 ? Y_BYTES : 65536);
 };
@@ -224,10 +226,10 @@ __global__ void __launch_bounds__(kThreads, 2) kv_rotate_kernel(StoreParams p, i
   __syncthreads();
 
   if (RT_hi) {
-    const int wm = warp & 3, wn = warp >> 2;  // 16-row slice, 128-column half
-    float acc[16][4];
+    const int wn = warp;  // the tile's 16 rows x a 32-column slice of the 256 outputs
+    float acc[4][4];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
     const uint32_t xa = smem_u32(xs), ha = smem_u32(rhi), la = smem_u32(rlo);
     for (int kc = 0; kc < 4; ++kc) {
       __syncthreads();
@@ -241,11 +243,11 @@ __global__ void __launch_bounds__(kThreads, 2) kv_rotate_kernel(StoreParams p, i
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
         uint32_t a0, a1, a2, a3;
-        mma::ldsm_x4(xa + mma::swz(wm * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, kc * 8 + 2 * ks + (lane >> 4)), a0,
-                     a1, a2, a3);
+        mma::ldsm_x4(xa + mma::swz((lane & 7) + ((lane >> 3) & 1) * 8, kc * 8 + 2 * ks + (lane >> 4)), a0, a1, a2,
+                     a3);
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
-          const int n = wn * 128 + np * 16 + (lane & 7) + (lane >> 4) * 8;
+        for (int np = 0; np < 2; ++np) {
+          const int n = wn * 32 + np * 16 + (lane & 7) + (lane >> 4) * 8;
           const int ch = 2 * ks + ((lane >> 3) & 1);
           uint32_t b0, b1, b2, b3;
           mma::ldsm_x4(ha + rswz(n, ch), b0, b1, b2, b3);
@@ -259,9 +261,9 @@ __global__ void __launch_bounds__(kThreads, 2) kv_rotate_kernel(StoreParams p, i
     }
     __syncthreads();  // R chunk dead: the output tile aliases it
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = wn * 128 + j * 8 + 2 * (lane & 3);
-      const int ra = wm * 16 + (lane >> 2);
+    for (int j = 0; j < 4; ++j) {
+      const int col = wn * 32 + j * 8 + 2 * (lane & 3);
+      const int ra = lane >> 2;
       *reinterpret_cast<float2*>(ys + ra * kYStride + col) = make_float2(acc[j][0], acc[j][1]);
       *reinterpret_cast<float2*>(ys + (ra + 8) * kYStride + col) = make_float2(acc[j][2], acc[j][3]);
     }
@@ -353,12 +355,8 @@ extern "C" int oscar_kv_store(const oscar::StoreParams* params, cudaStream_t str
   const int nh = p.Hq + 2 * p.Hk;
   const size_t smem_prep = (size_t)nh * p.D * sizeof(float);
   if (smem_prep > 200 * 1024) return -201;
-  static bool attr = false;
-  if (!attr) {
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(kv_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    OSCAR_CUDA_CHECK(cudaFuncSetAttribute(kv_rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RotSmem::TOTAL));
-    attr = true;
-  }
+  OSCAR_RC(ensure_smem(kv_prep_kernel, 200 * 1024));
+  OSCAR_RC(ensure_smem(kv_rotate_kernel, RotSmem::TOTAL));
   const int grid_prep = p.T > 0 ? p.T : 1;
   kv_prep_kernel<<<grid_prep, kThreads, smem_prep, stream>>>(p);
   if (p.T <= 0) return (int)cudaGetLastError();

@@ -11,7 +11,12 @@ struct GemmEpi {
   const float* scale_b;  // [N]
   void* out;             // mode 3: NVLS multicast address of the fp32 reduction buffer
   long long ldo;         // elements between consecutive output rows
-  int mode;              // 0: bf16 store, 1: fp32 atomic add, 2: fp32 store, 3: fp32 multimem add
+  int mode;              // 0: bf16 store, 1: fp32 atomic add, 2: fp32 store, 3: fp32 multimem add,
+                         // 4: bf16 store of split-K partials summed in the fp32 workspace ws
+                         //    (the last split of a (tile, row quarter) converts and re-zeroes),
+                         // 5: reduce-scatter: fp32 row of token t stored into slot `rank` of rank
+                         //    t / rows_per_rank's receive buffer peer_out[owner], at row
+                         //    t % rows_per_rank (ldo floats per row, slot_stride per slot)
   int trans;             // 0: out[m * ldo + n], 1: out[n * ldo + m]
   // mode 3 completion: the last CTA bumps *epoch and stores it into slot `rank` of
   // every peer's signal pad (peer_signals[q] + rank) with release semantics.
@@ -25,6 +30,18 @@ struct GemmEpi {
   // re-zeroes them.
   float* ws;
   int* tile_cnt;
+  // Operands that no earlier kernel writes (the weights): under programmatic dependent
+  // launch their first tiles are fetched before the kernel waits for its predecessor.
+  int a_static, b_static;
+  // mode 5 (reduce-scatter): per-rank fp32 destination buffers (device array of world
+  // pointers, this rank's included) and the token rows each rank owns
+  float* const* peer_out;
+  int rows_per_rank;
+  long long slot_stride;  // mode 5: elements between the per-source-rank slots of a receive buffer
+  // split-K over a thread-block cluster of cluster_k CTAs (one per K slice of a tile):
+  // partial int32 tiles are summed through distributed shared memory, each CTA writes
+  // BM / cluster_k rows of the result.  0 or 1: no cluster.
+  int cluster_k;
 };
 
 struct StoreParams {

@@ -257,6 +257,39 @@ OSCAR_DEVICE void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// Programmatic dependent launch.  griddep_wait: block until the preceding kernel in
+// the stream has completed and its memory is visible (a no-op when this kernel was
+// not launched as a programmatic dependent).  griddep_launch_dependents: allow the
+// next kernel, if it was launched as a programmatic dependent, to start its CTAs now.
+OSCAR_DEVICE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+OSCAR_DEVICE void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Thread-block clusters: rank of this CTA in its cluster, a full cluster barrier
+// (every thread of every CTA of the cluster; release / acquire orders shared-memory
+// writes before it with reads after it), and distributed shared memory: the address
+// of the same shared variable in CTA `rank` of the cluster, and a 16-byte load there.
+OSCAR_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+OSCAR_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+OSCAR_DEVICE uint32_t mapa(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+OSCAR_DEVICE int4 ld_dsmem_v4(uint32_t addr) {
+  int4 v;
+  asm volatile("ld.shared::cluster.v4.s32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 OSCAR_DEVICE bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

@@ -30,7 +30,7 @@ import torch
 from ..kv.offload import HostKVStore
 from ..models.qwen35 import P_MAX, HybridModel, StepBatch
 from ..ops import attention as A
-from ..ops.functional import num_sms
+from ..ops.functional import num_sms, reserve_split_workspace
 from ..ops import sampling as samp
 from . import checks
 from .block_manager import BlockManager, SlotManager
@@ -136,6 +136,8 @@ class LLMEngine:
         self._hid_static = None
         model.allocate_cache(num_blocks, max_slots)
         model.setup_row_reduce(max_batched_tokens + max_slots * (1 + self.num_spec))
+        if self.dev.type == "cuda":
+            reserve_split_workspace(self.dev)
         cfg = model.oscar
         self.stage_rows = model.stage_rows
         self._owner_host = np.full(max(1, self.stage_rows) * 128, -1, dtype=np.int32)

@@ -460,17 +460,16 @@ class HybridModel:
         return self.row_reduce
 
     def decoder(self, b: StepBatch, residual: torch.Tensor) -> dict:
-        """All decoder layers; returns the pending (all-reduced) MLP delta of the last
-        layer as the keyword arguments of the RMSNorm that consumes it."""
+        """All decoder layers over the residual rows this rank keeps (all rows, or its own
+        rows under sequence parallelism); returns the pending reduction of the last MLP,
+        which the final norm consumes."""
         red = self._reducer()
-        T, H = residual.shape
-        red.begin(T, H, residual.device)
         eps = self.cfg.rms_norm_eps
-        pending: dict = {}
+        pending: dict | None = None
         first_full = True
         k = 0
         for mixer, mlp in self.layers:
-            xq, xs, _ = F.rmsnorm_quant(residual, mixer.input_norm, eps, status=self.status, **pending)
+            xq, xs, _ = red.norm(residual, mixer.input_norm, eps, pending, status=self.status)
             if isinstance(mixer, FullAttentionLayer):
                 oq, os_ = mixer.attention(xq, xs, b, self.rope, self.owner, self.stage_rows,
                                           write_owner=first_full, status=self.status)
@@ -480,7 +479,7 @@ class HybridModel:
                 oq, os_ = mixer.mixer(xq, xs, b, status=self.status)
                 w_o = mixer.out
             pending = red.gemm(oq, os_, w_o, k, status=self.status)
-            xq, xs, _ = F.rmsnorm_quant(residual, mixer.post_norm, eps, status=self.status, **pending)
+            xq, xs, _ = red.norm(residual, mixer.post_norm, eps, pending, status=self.status)
             gu = F.linear_i8(xq, xs, mlp.gate_up.q, mlp.gate_up.s, status=self.status)
             hq, hs = F.swiglu_quant(gu, mlp.I)
             pending = red.gemm(hq, hs, mlp.down, k + 1, status=self.status)
@@ -491,12 +490,12 @@ class HybridModel:
         """Main model on a step.  Returns ``(hidden_bf16 [T, H], next_tokens [n_sel])``."""
         T = b.T
         H = self.cfg.hidden_size
-        residual = torch.empty(T, H, dtype=torch.float32, device=self.device)
-        F.embed(b.tokens, self.embed, self.vocab_begin, residual)
-        self.tp.all_reduce_(residual)
+        red = self._reducer()
+        red.begin(T, H, self.device)
+        residual = red.embed_in(b.tokens, self.embed, self.vocab_begin)
         pending = self.decoder(b, residual)
-        xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, self.cfg.rms_norm_eps, want_bf16=True,
-                                      status=self.status, **pending)
+        xq, xs, hid = red.norm(residual, self.final_norm, self.cfg.rms_norm_eps, pending, want_bf16=True,
+                               status=self.status)
         rows = b.logit_rows
         tok = self.sample(xq[rows], xs[rows], b.extra.get("sampling"), b.extra.get("logprobs_k"))
         return hid, tok
@@ -569,18 +568,18 @@ class MTPHead:
         _, _, h_n = F.rmsnorm_quant(hf, self.norm_hid, eps, want_q=False, want_bf16=True)
         cat = torch.cat([e_n, h_n], dim=1)
         cq, cs = F.act_quant(cat)
-        residual = torch.zeros(T, H, dtype=torch.float32, device=m.device)
-        F.linear_i8(cq, cs, self.fc.q, self.fc.s, out=residual, accumulate=True, status=m.status)
-        xq, xs, _ = F.rmsnorm_quant(residual, self.layer.input_norm, eps)
-        oq, os_ = self.layer.attention(xq, xs, b, m.rope, None, 0, write_owner=False, status=m.status)
         red = m._reducer()
-        red.begin(T, H, residual.device)
+        red.begin(T, H, m.device)
+        # the fc projection is replicated: each rank computes the residual rows it keeps
+        residual = red.fc_rows(cq, cs, self.fc, m.status)
+        xq, xs, _ = red.norm(residual, self.layer.input_norm, eps, None, status=m.status)
+        oq, os_ = self.layer.attention(xq, xs, b, m.rope, None, 0, write_owner=False, status=m.status)
         pending = red.gemm(oq, os_, self.layer.o, 0, status=m.status)
-        xq, xs, _ = F.rmsnorm_quant(residual, self.layer.post_norm, eps, status=m.status, **pending)
+        xq, xs, _ = red.norm(residual, self.layer.post_norm, eps, pending, status=m.status)
         gu = F.linear_i8(xq, xs, self.mlp.gate_up.q, self.mlp.gate_up.s, status=m.status)
         hq, hs = F.swiglu_quant(gu, self.mlp.I)
         pending = red.gemm(hq, hs, self.mlp.down, 1, status=m.status)
-        xq, xs, hid = F.rmsnorm_quant(residual, self.final_norm, eps, want_bf16=True, status=m.status, **pending)
+        xq, xs, hid = red.norm(residual, self.final_norm, eps, pending, want_bf16=True, status=m.status)
         rows = b.logit_rows
         tok = m.sample(xq[rows], xs[rows])
         return hid, tok

@@ -130,13 +130,48 @@ def plan_gemm(M: int, N: int, K: int, sms: int, allow_split: bool) -> GemmPlan:
     return GemmPlan(swap, bn, splits)
 
 
+# Split-K GEMMs with a bf16 result sum their fp32 partials in a per-device workspace
+# that is all zero between calls (the kernel's last split of a tile re-zeroes its
+# rows).  Buffers only grow, outside CUDA-graph capture, and replaced ones are kept
+# alive: a captured graph may still address them.
+_SPLIT_WS: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+_SPLIT_WS_OLD: list = []
+SPLIT_BF16 = os.environ.get("OSCAR_GEMM_SPLIT_BF16", "1") != "0"
+
+
+def _split_ws(device: torch.device, elems: int, counters: int):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    cur = _SPLIT_WS.get(idx)
+    if cur is not None and cur[0].numel() >= elems and cur[1].numel() >= counters:
+        return cur
+    if torch.cuda.is_current_stream_capturing():
+        return None
+    n_ws = max(elems, cur[0].numel() if cur else 0, 1 << 20)
+    n_cnt = max(counters, cur[1].numel() if cur else 0, 1 << 12)
+    if cur is not None:
+        _SPLIT_WS_OLD.append(cur)
+    cur = (torch.zeros(n_ws, dtype=torch.float32, device=device), torch.zeros(n_cnt, dtype=torch.int32, device=device))
+    _SPLIT_WS[idx] = cur
+    return cur
+
+
+def reserve_split_workspace(device: torch.device, sms: int | None = None) -> None:
+    """Size the split-K workspace up front (before any CUDA-graph capture).  A GEMM is
+    split only when it has fewer output tiles than SMs, so its result has at most
+    ``sms x 128 x 256`` elements (the largest tile) and ``sms x 8`` tiles of the swapped
+    layout's 32-token minimum, four counters each."""
+    sms = sms or num_sms(device)
+    _split_ws(device, sms * 128 * 256, sms * 8 * 4)
+
+
 def linear_i8(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
               out: torch.Tensor | None = None, accumulate: bool = False,
               status: torch.Tensor | None = None) -> torch.Tensor:
     """``out = (xq @ wq^T) * xs[:, None] * ws[None, :]``.
 
     bf16 output by default.  With ``accumulate=True`` the result is *added* in fp32 to
-    ``out`` (the fp32 residual-delta buffer), which also enables split-K.
+    ``out`` (the fp32 residual-delta buffer).  Either way a GEMM with fewer output tiles
+    than SMs is split along K (bf16 results through the zeroed fp32 workspace).
     """
     M, K = xq.shape
     N = wq.shape[0]
@@ -152,7 +187,7 @@ def linear_i8(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Te
             return out
         return y
     e = ext()
-    plan = plan_gemm(M, N, K, num_sms(xq.device), allow_split=accumulate)
+    plan = plan_gemm(M, N, K, num_sms(xq.device), allow_split=accumulate or SPLIT_BF16)
     if accumulate:
         assert out is not None and out.dtype == torch.float32
         mode = 1
@@ -160,6 +195,19 @@ def linear_i8(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Te
         if out is None:
             out = torch.empty(M, N, dtype=torch.bfloat16, device=xq.device)
         mode = 0
+        if plan.splits > 1:
+            ld = out.stride(0)
+            elems = (N - 1) * ld + M if plan.swap else (M - 1) * ld + N
+            rows, cols = (N, M) if plan.swap else (M, N)
+            tiles = ((rows + 127) // 128) * ((cols + plan.bn - 1) // plan.bn)
+            wsb = _split_ws(xq.device, elems, tiles * 4) if ld % 4 == 0 else None
+            if wsb is not None:
+                if plan.swap:
+                    e.gemm_i8_split(wq, xq, ws, xs, out, 1, plan.bn, plan.splits, wsb[0], wsb[1], status)
+                else:
+                    e.gemm_i8_split(xq, wq, xs, ws, out, 0, plan.bn, plan.splits, wsb[0], wsb[1], status)
+                return out
+            plan = GemmPlan(plan.swap, plan.bn, 1)
     if plan.swap:
         e.gemm_i8(wq, xq, ws, xs, out, mode, 1, plan.bn, plan.splits if accumulate else 1, status)
     else:

@@ -40,7 +40,30 @@ from ..ops._ext import ext
 from .groups import TPGroup
 
 
-class NcclRowReduce:
+class FullRows:
+    """Every rank keeps all ``T`` rows of the residual stream (the all-reduce designs):
+    the embedding is all-reduced, a replicated projection fills every row, and each
+    norm runs over all rows, consuming the pending reduction's keyword arguments."""
+
+    seq_parallel = False
+
+    def embed_in(self, tokens: torch.Tensor, table: torch.Tensor, vocab_begin: int) -> torch.Tensor:
+        T = tokens.shape[0]
+        residual = torch.empty(T, table.shape[1], dtype=torch.float32, device=table.device)
+        F.embed(tokens, table, vocab_begin, residual)
+        self.tp.all_reduce_(residual)
+        return residual
+
+    def fc_rows(self, xq, xs, w, status=None) -> torch.Tensor:
+        residual = torch.zeros(xq.shape[0], w.q.shape[0], dtype=torch.float32, device=xq.device)
+        F.linear_i8(xq, xs, w.q, w.s, out=residual, accumulate=True, status=status)
+        return residual
+
+    def norm(self, residual, w, eps: float, pending: dict | None = None, want_bf16: bool = False, status=None):
+        return F.rmsnorm_quant(residual, w, eps, want_bf16=want_bf16, status=status, **(pending or {}))
+
+
+class NcclRowReduce(FullRows):
     """Baseline: local fp32 delta, GEMM accumulate, NCCL all-reduce."""
 
     fused = False
@@ -63,7 +86,7 @@ class NcclRowReduce:
         return {"delta": d}
 
 
-class FusedRowReduce:
+class FusedRowReduce(FullRows):
     """GEMM epilogue reduces through NVLS multicast; the RMSNorm waits on peer flags."""
 
     fused = True
@@ -119,24 +142,38 @@ class FusedRowReduce:
                 "zero_delta": True}
 
 
-def make_row_reduce(tp: TPGroup, max_rows: int, H: int, device):
-    """Row-parallel reduction of a TP group.
+def tp_comm_mode() -> str:
+    """``OSCAR_TP_COMM``: ``sp`` (default: sequence-parallel residual with the
+    reduce-scatter in the row-parallel GEMM epilogue and the all-gather pushed by the
+    RMSNorm, :mod:`oscar_b200.parallel.seqpar`), ``nvls`` (GEMM epilogue all-reduce
+    through NVLS multicast, :class:`FusedRowReduce`; also ``OSCAR_FUSED_AR=1``) or
+    ``nccl`` (GEMM + NCCL all-reduce, the baseline)."""
+    mode = os.environ.get("OSCAR_TP_COMM", "").strip().lower()
+    if not mode:
+        mode = "nvls" if os.environ.get("OSCAR_FUSED_AR", "0") in ("1", "auto") else "sp"
+    if mode not in ("sp", "nvls", "nccl"):
+        raise ValueError(f"OSCAR_TP_COMM={mode!r}: expected sp, nvls or nccl")
+    return mode
 
-    ``OSCAR_FUSED_AR=1`` (fused path, error if NVLS is missing) or ``auto`` (fused path
-    when NVLS multicast is available) select :class:`FusedRowReduce`; unset or ``0``
-    selects :class:`NcclRowReduce`.  The NCCL path is the default because it measured
-    faster on the target step at TP2 (decode 14.1 vs 15.8 ms per step, prefill of
-    8 x 8192 tokens 2.4 vs 4.1 s): the fused epilogue stages its partials through a
-    local workspace and orders every CTA's switch reductions with a system-scope fence
-    before it publishes the epoch.
-    """
-    want = os.environ.get("OSCAR_FUSED_AR", "0") in ("1", "auto")
+
+def make_row_reduce(tp: TPGroup, max_rows: int, H: int, device):
+    """Row-parallel reduction of a TP group (:func:`tp_comm_mode`).  CPU groups (gloo)
+    and single ranks use :class:`NcclRowReduce`; a fused mode that cannot be set up
+    (no symmetric memory / NVLS on the system) falls back to it with a message, unless
+    it was asked for explicitly."""
     dev = torch.device(device)
-    if tp.world > 1 and want and dev.type == "cuda":
-        try:
+    if tp.world == 1 or dev.type != "cuda":
+        return NcclRowReduce(tp)
+    mode = tp_comm_mode()
+    explicit = bool(os.environ.get("OSCAR_TP_COMM")) or os.environ.get("OSCAR_FUSED_AR") == "1"
+    try:
+        if mode == "sp":
+            from .seqpar import SeqParallelTP
+            return SeqParallelTP(tp, max_rows, H, dev)
+        if mode == "nvls":
             return FusedRowReduce(tp, max_rows, H, dev)
-        except (RuntimeError, ImportError) as exc:  # no NVLS on this system
-            if os.environ.get("OSCAR_FUSED_AR") == "1":
-                raise
-            print(f"[oscar_b200] fused all-reduce unavailable ({exc}); using NCCL all-reduce")
+    except (RuntimeError, ImportError, ValueError) as exc:
+        if explicit:
+            raise
+        print(f"[oscar_b200] {mode} tensor-parallel path unavailable ({exc}); using NCCL all-reduce")
     return NcclRowReduce(tp)

@@ -56,6 +56,29 @@ def test_gemm_i8_accumulate_splitk(M, N, K):
     assert _rel(out, ref) < 1e-5
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 1024, 5120), (32, 3584, 5120), (100, 1030, 2048), (300, 1792, 5120)])
+def test_gemm_i8_bf16_splitk(M, N, K):
+    """bf16 GEMMs with fewer output tiles than SMs are split along K: the partials meet in
+    the zeroed fp32 workspace and the last split of a tile writes bf16.  A second call is as
+    accurate (the workspace and tile counters are left at zero; the fp32 order in which
+    splits add up may differ between calls)."""
+    plan = F.plan_gemm(M, N, K, F.num_sms(torch.device(DEV)), allow_split=True)
+    assert plan.splits > 1
+    g = torch.Generator(device=DEV).manual_seed(M + N)
+    x = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=DEV, generator=g)
+    w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=DEV, generator=g)
+    xs = torch.rand(M, device=DEV, generator=g) * 0.01 + 0.001
+    ws = torch.rand(N, device=DEV, generator=g) * 0.01 + 0.001
+    y1 = F.linear_i8(x, xs, w, ws)
+    y2 = F.linear_i8(x, xs, w, ws)
+    torch.cuda.synchronize()
+    ref = (x.double() @ w.double().t()) * xs.double()[:, None] * ws.double()[None, :]
+    assert _rel(y1, ref) < 5e-3 and _rel(y2, ref) < 5e-3
+    assert _rel(y1, y2) < 1e-3
+    wsb = F._SPLIT_WS[torch.device(DEV).index or 0]
+    assert wsb[0].abs().max().item() == 0.0 and wsb[1].abs().max().item() == 0
+
+
 def test_gemm_status_clean():
     st = torch.zeros(1, dtype=torch.int32, device=DEV)
     x = torch.randint(-127, 128, (64, 256), dtype=torch.int8, device=DEV)

@@ -39,11 +39,31 @@ class MergeParams(ctypes.Structure):
                 ("out_scale", P), ("T", I)]
 
 
-def _lib():
+def _so():
     import oscar_b200._C as C
 
-    lib = ctypes.CDLL(C.__file__)
-    fn = lib.oscar_paged_attention_noalloc
+    return ctypes.CDLL(C.__file__)
+
+
+def _layout(cls):
+    return [ctypes.sizeof(cls)] + [getattr(cls, name).offset for name, _ in cls._fields_]
+
+
+def test_ctypes_mirror_matches_library_layout():
+    """The structs above mirror csrc/params.h; the library reports its own compiled
+    sizes and field offsets (``oscar_params_layout``), so a field added or moved in the
+    header fails here instead of passing misaligned pointers."""
+    fn = _so().oscar_params_layout
+    fn.argtypes = [ctypes.POINTER(ctypes.c_longlong), I]
+    fn.restype = I
+    n = fn(None, 0)
+    buf = (ctypes.c_longlong * n)()
+    assert fn(buf, n) == n
+    assert list(buf) == _layout(AttnParams) + _layout(MergeParams)
+
+
+def _lib():
+    fn = _so().oscar_paged_attention_noalloc
     fn.argtypes = [ctypes.POINTER(AttnParams), ctypes.POINTER(MergeParams), P]
     fn.restype = ctypes.c_int
     return fn
