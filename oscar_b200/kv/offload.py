@@ -8,6 +8,16 @@ the MTP layer's BF16 shadow pages, the request's staged sink/recent values and i
 recurrent state - frees its blocks and slot, and swaps it back in (new physical blocks,
 new slot) when room returns.  Outputs are identical to an uninterrupted run.
 
+Why whole requests and not cold pages: a FULL-attention decode step reads every
+history page of every running request (the INT2 page *is* the cold storage - 136 B per
+token and head), so a page kept on the host would cross PCIe on every step; the
+capacity that offload buys is for requests that are not running.
+
+Host memory comes from one pinned pool (:class:`PinnedPool`), sized when the engine
+starts (``OSCAR_OFFLOAD_HOST_GIB``, default 4 GiB) and grown only in whole chunks when a
+swap does not fit; a swap takes byte ranges from it and returns them when the request
+comes back, so the serving path does not pin memory per swap.
+
 The request's pages are gathered (``index_select``) on the compute stream, and the
 copies to pinned host memory run on a side stream; the blocks return to the free list
 once the copies' event has completed (:meth:`HostKVStore.poll` / ``drain``).  Swap-in
@@ -18,11 +28,72 @@ the CPU reference path the same code runs without streams.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 
 import torch
 
 PAGE = 128
+_ALIGN = 256
+
+
+class PinnedPool:
+    """Byte ranges of a few large pinned host buffers (first fit, coalescing frees).
+
+    Buffers are allocated at construction (``initial_bytes``) and then only when a
+    request does not fit, ``chunk_bytes`` or more at a time; they are never returned to
+    the system while the pool lives."""
+
+    def __init__(self, initial_bytes: int = 0, chunk_bytes: int = 1 << 30, pin: bool = True):
+        self.chunk_bytes = chunk_bytes
+        self.pin = pin
+        self.chunks: list[torch.Tensor] = []
+        self.free: list[list[int]] = []  # [chunk, offset, size], sorted by (chunk, offset)
+        self.allocations = 0             # buffers allocated from the system (not per request)
+        if initial_bytes > 0:
+            self._grow(initial_bytes)
+
+    @property
+    def capacity(self) -> int:
+        return sum(c.numel() - _ALIGN for c in self.chunks)
+
+    def _grow(self, need: int) -> None:
+        size = max(self.chunk_bytes, (need + (1 << 20) - 1) // (1 << 20) * (1 << 20))
+        buf = torch.empty(size + _ALIGN, dtype=torch.uint8, pin_memory=self.pin)
+        pad = (-buf.data_ptr()) % _ALIGN  # ranges start on 256-byte boundaries
+        self.chunks.append(buf)
+        self.free.append([len(self.chunks) - 1, pad, size])
+        self.allocations += 1
+
+    def alloc(self, nbytes: int):
+        """Returns ``(uint8 view, handle)``."""
+        n = max(_ALIGN, (nbytes + _ALIGN - 1) // _ALIGN * _ALIGN)
+        for attempt in range(2):
+            for i, (c, off, size) in enumerate(self.free):
+                if size >= n:
+                    if size == n:
+                        self.free.pop(i)
+                    else:
+                        self.free[i] = [c, off + n, size - n]
+                    return self.chunks[c][off:off + nbytes], (c, off, n)
+            if attempt == 0:
+                self._grow(n)
+        raise MemoryError(f"pinned pool cannot hold {nbytes} bytes")
+
+    def release(self, handle) -> None:
+        c, off, n = handle
+        self.free.append([c, off, n])
+        self.free.sort()
+        merged: list[list[int]] = []
+        for e in self.free:
+            if merged and merged[-1][0] == e[0] and merged[-1][1] + merged[-1][2] == e[1]:
+                merged[-1][2] += e[2]
+            else:
+                merged.append(list(e))
+        self.free = merged
+
+    def used(self) -> int:
+        return self.capacity - sum(e[2] for e in self.free)
 
 
 @dataclass
@@ -40,6 +111,7 @@ class Swapped:
     event: object = None   # completion of the device->host copies
     nbytes: int = 0
     owner_cleared: object = None  # staging seats whose tags were reset (numpy)
+    handles: list = field(default_factory=list)  # pinned-pool ranges of the host tensors
 
 
 @dataclass
@@ -53,7 +125,7 @@ class OffloadStats:
 
 
 class HostKVStore:
-    def __init__(self, model, pin: bool | None = None):
+    def __init__(self, model, pin: bool | None = None, host_bytes: int | None = None):
         self.model = model
         dev = model.device
         self.cuda = dev.type == "cuda"
@@ -62,6 +134,10 @@ class HostKVStore:
         self.swapped: dict[int, Swapped] = {}
         self.stats = OffloadStats()
         self._pending_free: list = []  # (event, callback)
+        if host_bytes is None:
+            host_bytes = int(float(os.environ.get("OSCAR_OFFLOAD_HOST_GIB", "4")) * (1 << 30)) if self.cuda else 0
+        self.pool = PinnedPool(host_bytes, pin=self.pin)
+        self._handles: list = []  # ranges taken by the current _to_host call
 
     # ------------------------------------------------------------ helpers
     def _to_host(self, dev_tensors: list) -> list:
@@ -71,9 +147,12 @@ class HostKVStore:
         main = torch.cuda.current_stream(self.model.device)
         self.stream.wait_stream(main)
         out = []
+        self._handles = []
         with torch.cuda.stream(self.stream):
             for t in dev_tensors:
-                h = torch.empty(t.shape, dtype=t.dtype, pin_memory=self.pin)
+                raw, hd = self.pool.alloc(t.numel() * t.element_size())
+                self._handles.append(hd)
+                h = raw.view(t.dtype).view(t.shape)
                 h.copy_(t, non_blocking=True)
                 t.record_stream(self.stream)
                 out.append(h)
@@ -172,6 +251,7 @@ class HostKVStore:
         gdn = [tuple(next(it) for _ in range(4)) for _ in m.gdn_layers]
         nbytes = sum(t.numel() * t.element_size() for t in host)
         sw = Swapped(rid, len(blocks), pages, shadow, mask, staged, gdn, parity, ev, nbytes)
+        sw.handles, self._handles = self._handles, []
         sw.owner_cleared = owner_cleared.cpu().numpy() if owner_cleared is not None else None
         self.swapped[rid] = sw
         self._pending_free.append((ev, on_freed))
@@ -186,8 +266,12 @@ class HostKVStore:
     def discard(self, rid: int) -> None:
         """Drop the host copy of a swapped-out request that will not come back (aborted)."""
         sw = self.swapped.pop(rid, None)
-        if sw is not None and sw.event is not None:
-            sw.event.synchronize()  # no copy into the host buffers is still in flight
+        if sw is not None:
+            if sw.event is not None:
+                sw.event.synchronize()  # no copy into the host buffers is still in flight
+            for hd in sw.handles:
+                self.pool.release(hd)
+            self.stats._host_now -= sw.nbytes
 
     def swap_in(self, rid: int, blocks: list[int], slot: int):
         """Restore ``rid`` into new ``blocks`` / ``slot``.  Returns ``(parity, seats, tags)``:
@@ -236,6 +320,8 @@ class HostKVStore:
         for g in m.gdn_layers:
             for t, dim in self._gdn_views(g):
                 t.index_copy_(dim, s, next(d))
+        for hd in sw.handles:  # _to_device waited for the copies out of these ranges
+            self.pool.release(hd)
         st = self.stats
         st.swapped_in += 1
         st.bytes_in += sw.nbytes

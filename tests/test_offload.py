@@ -54,3 +54,26 @@ def test_abort_of_a_swapped_out_request():
         if rid != victim:
             assert eng.requests[rid].output == want
     assert eng.bm.free_blocks == 6 and not eng.offload.swapped
+
+
+def test_pinned_pool_reuses_its_buffers():
+    """Swaps take byte ranges of the pool and give them back; memory is allocated from the
+    system only when the pool is created or when a request does not fit."""
+    from oscar_b200.kv.offload import PinnedPool
+
+    pool = PinnedPool(initial_bytes=1 << 20, chunk_bytes=1 << 20, pin=False)
+    assert pool.allocations == 1 and pool.capacity == 1 << 20
+    a, ha = pool.alloc(1000)
+    b, hb = pool.alloc(300_000)
+    assert a.numel() == 1000 and b.numel() == 300_000 and a.data_ptr() % 256 == 0 and b.data_ptr() % 256 == 0
+    pool.release(ha)
+    pool.release(hb)
+    assert pool.used() == 0 and len(pool.free) == 1  # coalesced back into one range
+    for _ in range(10):  # repeated swaps of the same size reuse the same range
+        x, hx = pool.alloc(500_000)
+        pool.release(hx)
+    assert pool.allocations == 1
+    big, hbig = pool.alloc(3 << 20)  # does not fit: one new chunk of at least that size
+    assert pool.allocations == 2 and big.numel() == 3 << 20
+    pool.release(hbig)
+    assert pool.used() == 0
