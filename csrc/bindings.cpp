@@ -56,6 +56,9 @@ int oscar_rmsnorm_ag(float* x, long long ldx, const float* delta, long long ldd,
                      const int* rs_epoch, int* status, long long budget_ns, cudaStream_t s);
 int oscar_wait_flags(const unsigned* signals, const int* epoch, int world, int* status, long long budget_ns,
                      cudaStream_t s);
+int oscar_sample_pass(const __nv_bfloat16* logits, long long ld, int n, int V, int vocab_begin, const float* temp,
+                      const float* tau, const int* draft, const int* seed, const int* pos, float* out,
+                      cudaStream_t s);
 }
 
 namespace {
@@ -253,6 +256,29 @@ void wait_flags(int64_t signals, const Tensor& epoch, int64_t world, const optio
   check_rc(oscar_wait_flags(reinterpret_cast<const unsigned*>(signals), ptr<int>(epoch), (int)world,
                             optr<int>(status), budget_ns, stream()),
            "wait_flags");
+}
+
+// One sampling pass over a vocabulary shard: out [n, ceil(V / 4096), 5] per row and chunk.
+void sample_pass(const Tensor& logits, int64_t vocab_begin, const Tensor& temp, const Tensor& tau, const Tensor& draft,
+                 const Tensor& seed, const Tensor& pos, Tensor& out) {
+  CHECK_CUDA(logits);
+  CHECK_DTYPE(logits, at::kBFloat16);
+  CHECK_DTYPE(temp, at::kFloat);
+  CHECK_DTYPE(tau, at::kFloat);
+  CHECK_DTYPE(draft, at::kInt);
+  CHECK_DTYPE(seed, at::kInt);
+  CHECK_DTYPE(pos, at::kInt);
+  CHECK_DTYPE(out, at::kFloat);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample_pass: logits [n, V] with unit column stride");
+  const int n = logits.size(0), V = logits.size(1);
+  TORCH_CHECK(temp.numel() >= n && tau.numel() >= n && draft.numel() >= n && seed.numel() >= n && pos.numel() >= n,
+              "sample_pass: one entry per row");
+  TORCH_CHECK(out.is_contiguous() && out.numel() >= (int64_t)n * ((V + 4095) / 4096) * 5, "sample_pass: out size");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  check_rc(oscar_sample_pass(ptr<__nv_bfloat16>(logits), logits.stride(0), n, V, (int)vocab_begin, ptr<float>(temp),
+                             ptr<float>(tau), ptr<int>(draft), ptr<int>(seed), ptr<int>(pos), ptr<float>(out),
+                             stream()),
+           "sample_pass");
 }
 
 // Install a per-CTA timeline buffer for the tcgen05 attention kernel (0 removes it).
@@ -632,6 +658,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_i8_rs", &gemm_i8_rs);
   m.def("rmsnorm_ag", &rmsnorm_ag);
   m.def("wait_flags", &wait_flags);
+  m.def("sample_pass", &sample_pass);
   m.def("num_sms", &num_sms);
   m.def("kv_store", &kv_store);
   m.def("paged_attention", &paged_attention);

@@ -406,6 +406,24 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
           continue;
         }
+        if (ep.mode == 5 && splits == 1 && !ep.trans) {
+          // reduce-scatter of whole-K prefill tiles: 16-byte stores of this thread's row
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              if (nb + j + 3 < N) {
+                const float4 sb = __ldg(reinterpret_cast<const float4*>(ep.scale_b + nb + j));
+                red_to_owner(ep, m, nb + j,
+                             make_float4((float)(int)r[j] * sa * sb.x, (float)(int)r[j + 1] * sa * sb.y,
+                                         (float)(int)r[j + 2] * sa * sb.z, (float)(int)r[j + 3] * sa * sb.w));
+              } else {
+                for (int e = 0; e < 4 && nb + j + e < N; ++e)
+                  red_to_owner1(ep, m, nb + j + e, (float)(int)r[j + e] * sa * ep.scale_b[nb + j + e]);
+              }
+            }
+          }
+          continue;
+        }
         if (!row_ok) continue;
         if (ep.mode == 0 && !ep.trans && nb + 32 <= N && (ep.ldo % 8) == 0 &&
             (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0) {
@@ -445,6 +463,9 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               reinterpret_cast<__nv_bfloat16*>(ep.out)[idx] = __float2bfloat16(v);
             } else if (ep.mode == 1) {
               atomicAdd(reinterpret_cast<float*>(ep.out) + idx, v);
+            } else if (ep.mode == 5 && splits == 1) {
+              // reduce-scatter of a whole-K tile: straight to the owning rank
+              red_to_owner1(ep, ep.trans ? n : m, ep.trans ? m : n, v);
             } else if (ep.mode >= 3) {
               // stage in the local workspace; the reduction through the switch (mode 3),
               // the bf16 store (mode 4) or the reduce-scatter into the owning rank (mode 5)
@@ -462,7 +483,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&acc_empty[acc]);
-      if (ep.mode >= 3) {
+      if (ep.mode >= 3 && !(ep.mode == 5 && splits == 1)) {
         // The rows of this (tile, row quarter) are complete in the workspace once every
         // split has added its part (split-K: counted in tile_cnt; else this warp alone).
         // The last contributor reads them back from L2 and reduces them into every rank
@@ -846,10 +867,12 @@ namespace oscar {
 template <int BN>
 int run_bn(const CUtensorMap& ta, const CUtensorMap& tb, GemmEpi ep, int M, int N, int K, int splits, int* status,
            cudaStream_t stream) {
-  // Split-K GEMMs reduce through a thread-block cluster when the tiles x slices fit
-  // on the GPU at once (modes that accumulate the slices: 1, 3, 4, 5).
+  // Split-K GEMMs whose slices meet in a workspace (modes 3, 4, 5) reduce through a
+  // thread-block cluster instead when the tiles x slices fit on the GPU at once.  The
+  // fp32 accumulate mode (1) keeps its fire-and-forget reductions into the output:
+  // measured faster than the cluster's two barriers at decode sizes.
   ep.cluster_k = 0;
-  if (splits > 1 && ep.mode != 0 && ep.mode != 2 && cluster_enabled()) {
+  if (splits > 1 && ep.mode >= 3 && cluster_enabled()) {
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int S = pick_cluster<BN>(tiles, splits);
     if (S >= 2) {

@@ -13,7 +13,7 @@ at ``W`` ranks, for M = 32, 128, 2048 and 16384 tokens; int8 weights uniform in
 
 Two implementations of each:
 
-* ``fused``  - this package's sequence-parallel path: the tcgen05 GEMM's epilogue adds
+* ``fused``  - this package's sequence-parallel path: the tcgen05 GEMM's epilogue stores
   every fp32 row straight into the owning rank's buffer over NVLink (reduce-scatter),
   the RMSNorm kernel pushes its int8 rows into every rank's activation buffer
   (all-gather) and the next GEMM, a programmatic dependent of a one-warp flag wait,
@@ -28,7 +28,9 @@ warm-up, the max over ranks.  Roofline of the fused path: the slower of the GEMM
 FLOPs at the int8 peak (twice the measured bf16 GEMM peak, ``--bf16-tflops``) and the
 bytes each rank must move over NVLink at the measured 770 GB/s per direction
 (``--nvlink-gbs``): ``(W-1)/W * M * 5120 * 4`` for the fp32 reduce-scatter and
-``(W-1)/W * M * 5120`` for the int8 all-gather.
+``(W-1)/W * M * 5120`` for the int8 all-gather.  ``roofline_hbm_ms`` also counts the
+int8 weights each rank streams from HBM at the measured copy bandwidth (``--hbm-gbs``),
+the bound that decides the small-M cases.
 
     torchrun --nproc-per-node W -m oscar_b200.bench.tp_linear [--m 32,128,2048,16384]
 """
@@ -68,6 +70,7 @@ def main(argv=None):
     ap.add_argument("--bf16-tflops", type=float, default=1661.4,
                     help="measured bf16 GEMM peak (the int8 peak is taken as twice this)")
     ap.add_argument("--nvlink-gbs", type=float, default=770.0, help="measured peer bandwidth per direction")
+    ap.add_argument("--hbm-gbs", type=float, default=6554.9, help="measured HBM copy bandwidth")
     args = ap.parse_args(argv)
     rank, world, local = init_distributed("nccl", timeout_s=120)
     torch.cuda.set_device(local)
@@ -153,8 +156,12 @@ def main(argv=None):
         b_rs = (world - 1) / world * M * H * 4
         b_ag = (world - 1) / world * M * H
         link = args.nvlink_gbs * 1e9
+        hbm = args.hbm_gbs * 1e9
+        w_rs, w_ag = H * Kd, Ngu * H  # int8 weight bytes streamed per rank
         roof = {"rs": max(f_rs / int8_peak, b_rs / link), "ag": max(f_ag / int8_peak, b_ag / link),
                 "chain": max((f_rs + f_ag) / int8_peak, (b_rs + b_ag) / link)}
+        roof_hbm = {"rs": max(roof["rs"], w_rs / hbm), "ag": max(roof["ag"], w_ag / hbm),
+                    "chain": max(roof["chain"], (w_rs + w_ag) / hbm)}
         if rank == 0:
             line = {"tp": world, "M": M, "down_K": Kd, "gate_up_N": Ngu, "rel_err_gemm": err_gemm,
                     "rel_err_residual": err_res}
@@ -162,7 +169,9 @@ def main(argv=None):
                 lib_ms, fused_ms = res[f"lib_{op}"], res[f"fused_{op}"]
                 line[op] = {"lib_ms": round(lib_ms, 4), "fused_ms": round(fused_ms, 4),
                             "speedup": round(lib_ms / fused_ms, 3), "roofline_ms": round(roof[op] * 1e3, 4),
-                            "fused_frac_of_roofline": round(roof[op] * 1e3 / fused_ms, 3)}
+                            "fused_frac_of_roofline": round(roof[op] * 1e3 / fused_ms, 3),
+                            "roofline_hbm_ms": round(roof_hbm[op] * 1e3, 4),
+                            "fused_frac_of_roofline_hbm": round(roof_hbm[op] * 1e3 / fused_ms, 3)}
             print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()

@@ -30,6 +30,12 @@ while the row's token equals the draft") serves greedy and sampled requests alik
 
 Rows with ``temperature <= 0`` are greedy: the token is the argmax of the logits.
 
+On the GPU the per-element work (scaling, truncation mask, the max and exponential sum,
+the draft's mass, the hashed Gumbel noise and the masked arg-max) is one pass of the
+``sample_pass`` kernel over the vocabulary shard, in 4,096-column chunks; only steps
+with top-k / top-p rows also run :func:`phase1` (the candidate top-k) for the
+threshold.  The CPU path computes the same quantities with torch ops (the test oracle).
+
 The reference serves through vLLM's sampler (``delivery/serve_oscar.sh:76-99`` runs
 ``vllm serve``); its benchmark decodes greedily, like this framework's bench.
 """
@@ -95,6 +101,7 @@ class SampleRows:
     seed: torch.Tensor         # i32 [n], non-negative
     pos: torch.Tensor          # i32 [n], position of the token this row samples
     draft: torch.Tensor        # i32 [n], global id of the draft verified at this row, -1: none
+    truncated: bool = True     # some row has top_k > 0 or top_p < 1 (then phase 1 runs)
 
 
 def host_rows(params: list, seeds: list, positions: list, drafts: list) -> dict:
@@ -102,14 +109,18 @@ def host_rows(params: list, seeds: list, positions: list, drafts: list) -> dict:
     the engine uploads with the rest of a step's metadata."""
     t = np.asarray([p.temperature if p is not None else 0.0 for p in params], dtype=np.float32)
     tp = np.asarray([p.top_p if p is not None else 1.0 for p in params], dtype=np.float32)
+    trunc = any(p is not None and p.temperature > 0 and (p.top_k > 0 or p.top_p < 1.0) for p in params)
+    # whether any row is truncated is carried in the shape of "samp_trunc" (length 1 or 0),
+    # so that steps with and without the threshold phase are different CUDA graphs
     return {"samp_t": t.view(np.int32), "samp_k": [p.top_k if p is not None else 0 for p in params],
             "samp_p": tp.view(np.int32), "samp_seed": [s & 0x7FFFFFFF for s in seeds], "samp_pos": positions,
-            "samp_draft": drafts}
+            "samp_draft": drafts, "samp_trunc": np.zeros(1 if trunc else 0, dtype=np.int32)}
 
 
 def rows_from_arrays(d: dict) -> SampleRows:
+    trunc = "samp_trunc" not in d or d["samp_trunc"].numel() > 0
     return SampleRows(d["samp_t"].view(torch.float32), d["samp_k"], d["samp_p"].view(torch.float32),
-                      d["samp_seed"], d["samp_pos"], d["samp_draft"])
+                      d["samp_seed"], d["samp_pos"], d["samp_draft"], trunc)
 
 
 # ----------------------------------------------------------------------------- hashing
@@ -223,10 +234,64 @@ def combine2(parts: torch.Tensor, rows: SampleRows) -> torch.Tensor:
     return torch.where(accept, d, tok)
 
 
+def _pass_cuda(logits: torch.Tensor, vocab_begin: int, rows: SampleRows, tau: torch.Tensor) -> torch.Tensor:
+    """This rank's ``[n, 5]``: max ``m`` of the allowed scaled logits, ``sum exp(z - m)``,
+    the draft's scaled logit (or -inf), the best (Gumbel) score and its global token id
+    - one ``sample_pass`` kernel over the shard, then a merge of its chunks."""
+    from ._ext import ext
+
+    n, V = logits.shape
+    chunk = 4096
+    nc = (V + chunk - 1) // chunk
+    part = torch.empty(n, nc, 5, dtype=torch.float32, device=logits.device)
+    ext().sample_pass(logits, vocab_begin, rows.temperature.float().contiguous(), tau.float().contiguous(),
+                      rows.draft.int().contiguous(), rows.seed.int().contiguous(), rows.pos.int().contiguous(), part)
+    m_c, s_c, zd_c, b_c, id_c = part.unbind(2)
+    m = m_c.max(dim=1).values
+    finite = m_c > float("-inf")
+    s = torch.where(finite, s_c * torch.exp(m_c - torch.where(finite, m, torch.zeros_like(m)).unsqueeze(1)),
+                    torch.zeros_like(s_c)).sum(dim=1)
+    zd = zd_c.max(dim=1).values
+    best, at = b_c.max(dim=1)  # first chunk on ties: the lowest token id
+    tok = id_c.gather(1, at.unsqueeze(1)).squeeze(1)
+    return torch.stack([m, s, zd, best, tok], dim=1)
+
+
+def _combine_cuda(parts: torch.Tensor, rows: SampleRows) -> torch.Tensor:
+    """``parts [world, n, 5]`` of every rank -> token ids ``[n]`` (int64)."""
+    mr, sr, zdr, br, idr = parts.unbind(2)
+    m = mr.max(dim=0).values
+    mm = torch.where(m > float("-inf"), m, torch.zeros_like(m))
+    Z = torch.where(mr > float("-inf"), sr * torch.exp(mr - mm), torch.zeros_like(sr)).sum(dim=0)
+    pd = torch.exp(zdr.max(dim=0).values - mm) / Z.clamp_min(1e-30)
+    r = br.argmax(dim=0)  # first rank with the best score
+    tok = idr.gather(0, r.unsqueeze(0)).squeeze(0).long()
+    key = _row_key(rows.seed, rows.pos)
+    u = uniform(key, torch.full_like(key, _ACCEPT_SALT))
+    d = rows.draft.long()
+    accept = (rows.temperature > 0) & (d >= 0) & (u < pd)
+    return torch.where(accept, d, tok)
+
+
 def sample(logits: torch.Tensor, vocab_begin: int, rows: SampleRows, tp=None) -> torch.Tensor:
     """Token of every row of this rank's vocabulary shard ``logits [n, V_local]``; every
-    rank of ``tp`` returns the same tokens (two all-gathers of ``[n, 2 + C]`` and ``[n, 4]``)."""
+    rank of ``tp`` returns the same tokens (two all-gathers of ``[n, 2 + C]`` and ``[n, 4]``
+    on the CPU path; on the GPU one of ``[n, 5]``, plus the threshold's when some row is
+    truncated)."""
     world = 1 if tp is None else tp.world
+    if logits.is_cuda:
+        n = logits.shape[0]
+        if rows.truncated:
+            st = phase1(logits, rows).unsqueeze(0)
+            if world > 1:
+                st = tp.all_gather(st)
+            _, tau = combine1(st, rows)
+        else:
+            tau = torch.full((n,), float("-inf"), dtype=torch.float32, device=logits.device)
+        parts = _pass_cuda(logits, vocab_begin, rows, tau).unsqueeze(0)
+        if world > 1:
+            parts = tp.all_gather(parts)
+        return _combine_cuda(parts, rows)
     st = phase1(logits, rows).unsqueeze(0)
     if world > 1:
         st = tp.all_gather(st)

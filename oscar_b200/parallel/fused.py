@@ -64,13 +64,17 @@ class FullRows:
 
 
 class NcclRowReduce(FullRows):
-    """Baseline: local fp32 delta, GEMM accumulate, NCCL all-reduce."""
+    """Baseline: local fp32 delta, GEMM accumulate, NCCL all-reduce.  The delta buffer is
+    zero between reductions: the consuming RMSNorm adds it into the residual and clears
+    it, so no separate fill precedes each GEMM."""
 
     fused = False
 
-    def __init__(self, tp: TPGroup):
+    def __init__(self, tp: TPGroup, max_rows: int = 0, H: int = 0, device=None):
         self.tp = tp
         self.delta = None
+        if max_rows > 0 and H > 0 and device is not None:
+            self.delta = torch.zeros(max_rows, H, dtype=torch.float32, device=device)
 
     def begin(self, T: int, H: int, device) -> None:
         if self.delta is None or self.delta.shape[0] < T or self.delta.shape[1] != H or self.delta.device != device:
@@ -80,10 +84,9 @@ class NcclRowReduce(FullRows):
     def gemm(self, xq, xs, w, k: int, status=None) -> dict:
         """``delta = all_reduce(xq @ w^T)``; returns the kwargs of the consuming RMSNorm."""
         d = self.delta[:self._T]
-        d.zero_()
         F.linear_i8(xq, xs, w.q, w.s, out=d, accumulate=True, status=status)
         self.tp.all_reduce_(d)
-        return {"delta": d}
+        return {"delta": d, "zero_delta": True}
 
 
 class FusedRowReduce(FullRows):
@@ -163,7 +166,7 @@ def make_row_reduce(tp: TPGroup, max_rows: int, H: int, device):
     it was asked for explicitly."""
     dev = torch.device(device)
     if tp.world == 1 or dev.type != "cuda":
-        return NcclRowReduce(tp)
+        return NcclRowReduce(tp, max_rows, H, dev)
     mode = tp_comm_mode()
     explicit = bool(os.environ.get("OSCAR_TP_COMM")) or os.environ.get("OSCAR_FUSED_AR") == "1"
     try:
@@ -176,4 +179,4 @@ def make_row_reduce(tp: TPGroup, max_rows: int, H: int, device):
         if explicit:
             raise
         print(f"[oscar_b200] {mode} tensor-parallel path unavailable ({exc}); using NCCL all-reduce")
-    return NcclRowReduce(tp)
+    return NcclRowReduce(tp, max_rows, H, dev)
