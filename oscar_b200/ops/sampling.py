@@ -249,8 +249,8 @@ def _pass_cuda(logits: torch.Tensor, vocab_begin: int, rows: SampleRows, tau: to
     m_c, s_c, zd_c, b_c, id_c = part.unbind(2)
     m = m_c.max(dim=1).values
     finite = m_c > float("-inf")
-    s = torch.where(finite, s_c * torch.exp(m_c - torch.where(finite, m, torch.zeros_like(m)).unsqueeze(1)),
-                    torch.zeros_like(s_c)).sum(dim=1)
+    mm = torch.where(m > float("-inf"), m, torch.zeros_like(m))
+    s = torch.where(finite, s_c * torch.exp(m_c - mm.unsqueeze(1)), torch.zeros_like(s_c)).sum(dim=1)
     zd = zd_c.max(dim=1).values
     best, at = b_c.max(dim=1)  # first chunk on ties: the lowest token id
     tok = id_c.gather(1, at.unsqueeze(1)).squeeze(1)
