@@ -42,7 +42,7 @@ int oscar_act_quant(const __nv_bfloat16* x, long long ld, int T, int K, int8_t* 
 int oscar_embed(const int* tok, const __nv_bfloat16* table, int T, int H, int vocab_begin, int vocab_end, float* out,
                 cudaStream_t s);
 int oscar_argmax(const __nv_bfloat16* logits, long long ld, int T, int V, int index_offset, float* best_val,
-                 int* best_idx, cudaStream_t s);
+                 int* best_idx, void* ws, cudaStream_t s);
 int oscar_f32_to_bf16(const float* x, long long n, __nv_bfloat16* y, cudaStream_t s);
 int oscar_gemm_i8_rs(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                      const float* scale_a, const float* scale_b, int trans, int bn, int splits, float* const* peer_out,
@@ -635,8 +635,12 @@ void argmax(const Tensor& logits, int64_t index_offset, Tensor& best_val, Tensor
   CHECK_DTYPE(logits, at::kBFloat16);
   TORCH_CHECK(logits.stride(1) == 1, "argmax: rows must be contiguous");
   const c10::cuda::CUDAGuard guard(logits.device());
-  check_rc(oscar_argmax(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), logits.size(1), index_offset,
-                        ptr<float>(best_val), ptr<int>(best_idx), stream()),
+  const int64_t T = logits.size(0), V = logits.size(1);
+  // chunk partials (value, index) from the caching allocator: graph-capture safe
+  const int64_t chunks = (V + 8191) / 8192;
+  Tensor ws = at::empty({2 * T * chunks}, logits.options().dtype(at::kFloat));
+  check_rc(oscar_argmax(ptr<__nv_bfloat16>(logits), logits.stride(0), (int)T, (int)V, index_offset,
+                        ptr<float>(best_val), ptr<int>(best_idx), ws.data_ptr(), stream()),
            "argmax");
 }
 

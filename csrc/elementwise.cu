@@ -13,6 +13,7 @@ namespace oscar {
 namespace {
 
 constexpr int kT = 256;  // threads of the argmax kernel
+constexpr int kArgmaxChunk = 8192;  // logits per argmax CTA
 
 // Vectorised row kernels: thread t owns vectors t, t + NT, ... of the row (4 fp32
 // or 8 bf16 per 16-byte vector), all loaded before any arithmetic.
@@ -213,13 +214,20 @@ __global__ void embed_kernel(const int* __restrict__ tok, const __nv_bfloat16* _
 }
 
 // Row argmax with ties broken toward the lowest index (torch.argmax semantics).
+// Grid (rows, chunks): CTA (t, c) scans columns [c * chunk, (c + 1) * chunk) of row t and
+// writes its (max, lowest index of the max) to the partials [t][c]; argmax_reduce_kernel
+// then combines a row's chunks.  Splitting the vocabulary keeps every SM streaming logits
+// at decode sizes (a few dozen rows of 31K-248K columns).
 __global__ void __launch_bounds__(kT) argmax_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V,
-                                                 int index_offset, float* __restrict__ best_val,
-                                                 int* __restrict__ best_idx) {
+                                                 int chunk, float* __restrict__ part_val,
+                                                 int* __restrict__ part_idx) {
   __shared__ float sv[kT / 32];
   __shared__ int si[kT / 32];
   const int t = blockIdx.x;
-  const __nv_bfloat16* r = logits + (long long)t * ld;
+  const int c0 = blockIdx.y * chunk;
+  const __nv_bfloat16* r = logits + (long long)t * ld + c0;
+  const int base = c0;
+  V = min(V - c0, chunk);
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   auto take = [&](float x, int i) {
@@ -282,9 +290,38 @@ __global__ void __launch_bounds__(kT) argmax_kernel(const __nv_bfloat16* __restr
       }
     }
     if (l == 0) {
-      best_val[t] = bv;
-      best_idx[t] = bi + index_offset;
+      part_val[(long long)t * gridDim.y + blockIdx.y] = bv;
+      part_idx[(long long)t * gridDim.y + blockIdx.y] = bi == 0x7fffffff ? bi : bi + base;
     }
+  }
+}
+
+__global__ void argmax_reduce_kernel(const float* __restrict__ part_val, const int* __restrict__ part_idx,
+                                     int chunks, int index_offset, float* __restrict__ best_val,
+                                     int* __restrict__ best_idx) {
+  const int t = blockIdx.x, l = threadIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = l; c < chunks; c += 32) {
+    const float x = part_val[(long long)t * chunks + c];
+    const int i = part_idx[(long long)t * chunks + c];
+    if (x > bv || (x == bv && i < bi)) {
+      bv = x;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (l == 0) {
+    best_val[t] = bv;
+    best_idx[t] = (bi == 0x7fffffff ? 0 : bi) + index_offset;
   }
 }
 
@@ -522,10 +559,16 @@ extern "C" int oscar_embed(const int* tok, const __nv_bfloat16* table, int T, in
   return (int)cudaGetLastError();
 }
 
+// ws: 2 * T * ceil(V / kArgmaxChunk) 32-bit words of scratch (chunk partials).
 extern "C" int oscar_argmax(const __nv_bfloat16* logits, long long ld, int T, int V, int index_offset, float* best_val,
-                            int* best_idx, cudaStream_t s) {
+                            int* best_idx, void* ws, cudaStream_t s) {
   if (T <= 0) return 0;
-  argmax_kernel<<<T, kT, 0, s>>>(logits, ld, V, index_offset, best_val, best_idx);
+  if (V <= 0 || !ws) return -402;
+  const int chunks = (V + kArgmaxChunk - 1) / kArgmaxChunk;
+  float* pv = static_cast<float*>(ws);
+  int* pi = reinterpret_cast<int*>(pv + (long long)T * chunks);
+  argmax_kernel<<<dim3(T, chunks), kT, 0, s>>>(logits, ld, V, kArgmaxChunk, pv, pi);
+  argmax_reduce_kernel<<<T, 32, 0, s>>>(pv, pi, chunks, index_offset, best_val, best_idx);
   return (int)cudaGetLastError();
 }
 

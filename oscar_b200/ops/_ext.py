@@ -11,7 +11,7 @@ import importlib
 from ..utils import launches as _launches
 
 # launches per binding call (all others launch exactly one kernel)
-_MULTI = {"num_sms": 0}
+_MULTI = {"num_sms": 0, "argmax": 2}
 _EXT = None
 _ERR: Exception | None = None
 

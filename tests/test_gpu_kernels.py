@@ -127,7 +127,7 @@ def test_embed_argmax():
     ref = torch.empty(T, H)
     F.embed(tok.cpu(), table.cpu(), 500, ref)
     assert torch.equal(out.cpu(), ref)
-    for V_ in (70000, 70003):  # 16-byte rows (vector path), odd rows (tail / scalar path)
+    for V_ in (70000, 70003, 248320):  # 16-byte rows (vector path), odd rows (scalar path), 31 chunks
         logits = torch.randn(T, V_, device=DEV).to(torch.bfloat16)
         logits[1, 5] = logits[1, 60001] = 9.0  # a tie resolves to the lower index
         v, i = F.argmax(logits, 123)
