@@ -400,7 +400,7 @@ extern "C" int oscar_params_layout(long long* out, int cap) {
       OSCAR_A(D), OSCAR_A(scale), OSCAR_A(kv_mode), OSCAR_A(pool), OSCAR_A(page_bytes), OSCAR_A(kc), OSCAR_A(vc),
       OSCAR_A(stage_k), OSCAR_A(stage_v), OSCAR_A(owner), OSCAR_A(stage_rows), OSCAR_A(block_tables),
       OSCAR_A(bt_stride), OSCAR_A(q_start), OSCAR_A(seq_lens), OSCAR_A(work), OSCAR_A(n_work), OSCAR_A(part_o),
-      OSCAR_A(part_lse), OSCAR_A(status),
+      OSCAR_A(part_lse), OSCAR_A(status), OSCAR_A(stage_req_slot), OSCAR_A(stage_sink), OSCAR_A(stage_ring),
       (long long)sizeof(MergeParams), OSCAR_M(part_o), OSCAR_M(part_lse), OSCAR_M(item_first), OSCAR_M(item_count),
       OSCAR_M(max_rb), OSCAR_M(tok_req), OSCAR_M(q_start), OSCAR_M(Hq), OSCAR_M(Hk), OSCAR_M(D), OSCAR_M(RvT),
       OSCAR_M(gate), OSCAR_M(gate_ld), OSCAR_M(gate_hstride), OSCAR_M(out_bf16), OSCAR_M(out_i8),

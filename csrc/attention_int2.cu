@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_kernel(AttnParams 
     sm100::mbar_arrive_expect_tx(&full[s], page_tx);
     sm100::bulk_load(dst, p.pool + ((long long)blk * p.Hk + hk) * p.page_bytes, p.page_bytes, &full[s]);
     if (staging)
-      sm100::bulk_load(dst + ((p.page_bytes + 15) / 16) * 16, p.owner + (long long)(blk % p.stage_rows) * kPage,
+      sm100::bulk_load(dst + ((p.page_bytes + 15) / 16) * 16, p.owner + (long long)stage_row_of(p, req, p_first + i, blk) * kPage,
                        kPage * 4, &full[s]);
   };
   if (tid == 0)
@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_kernel(AttnParams 
           par = make_float4(1.f, 0.f, 1.f, 0.f);
           value_tok = true;
         } else if (staging && own[j] == blk) {  // staged sink/recent token: fp32 values
-          const long long base = ((long long)((blk % p.stage_rows) * kPage + j) * p.Hk + hk) * kD + d0;
+          const long long base = ((long long)(stage_row_of(p, req, p_first + i, blk) * kPage + j) * p.Hk + hk) * kD + d0;
           const float4* kf = reinterpret_cast<const float4*>(p.stage_k + base);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -344,7 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_kernel(AttnParams 
             if (ps >= prefix) {
               v = __half2float(p.v_fresh[((long long)(q0 + ps - prefix) * p.Hk + hk) * kD + d]);
             } else if (staging && own[jp] == blk) {
-              v = __ldg(p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage + (long long)d * kPage + jp);
+              v = __ldg(p.stage_v + ((long long)stage_row_of(p, req, p_first + i, blk) * p.Hk + hk) * kD * kPage +
+                        (long long)d * kPage + jp);
             } else {
               continue;
             }

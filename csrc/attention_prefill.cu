@@ -226,7 +226,7 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
         sm100::mbar_arrive_expect_tx(&raw_full[rs], tx);
         sm100::bulk_load(dst, p.pool + ((long long)blk * p.Hk + hk) * kPageBytes, kPageBytes, &raw_full[rs]);
         if (staging)
-          sm100::bulk_load(dst + kPageBytes, p.owner + (long long)(blk % p.stage_rows) * kPage, kPage * 4,
+          sm100::bulk_load(dst + kPageBytes, p.owner + (long long)stage_row_of(p, req, i, blk) * kPage, kPage * 4,
                            &raw_full[rs]);
         raw_issued = i + 1;
       }
@@ -384,7 +384,9 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
               // K rows: key ct, dims 64c .. 64c + 63
               const int j = ct;
               if ((smk[j >> 5] >> (j & 31)) & 1u) {
-                k_row_staged(dst, j, p.stage_k + ((long long)((blk % p.stage_rows) * kPage + j) * p.Hk + hk) * kD + 64 * c);
+                k_row_staged(dst, j,
+                             p.stage_k + ((long long)(stage_row_of(p, req, ti, blk) * kPage + j) * p.Hk + hk) * kD +
+                                 64 * c);
               } else {
                 const uint4 cw = *reinterpret_cast<const uint4*>(pg + j * 64 + ((c ^ ((j >> 1) & 3)) << 4));
                 uint32_t r[32];
@@ -404,7 +406,7 @@ int2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
               for (int k = 0; k < 32; ++k)
                 r[k] = hfma2_u32(r[k], __shfl_sync(0xffffffffu, vsp, k), __shfl_sync(0xffffffffu, vzp, k));
               if (m != 0ull)  // warp-uniform: staged keys carry their own values
-                merge_staged_v(r, p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage +
+                merge_staged_v(r, p.stage_v + ((long long)stage_row_of(p, req, ti, blk) * p.Hk + hk) * kD * kPage +
                                       (long long)d * kPage + hf * 64,
                                m);
               store_row(dst + hf * 8192, dl, r);

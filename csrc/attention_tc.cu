@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         sm100::mbar_arrive_expect_tx(&B.raw_full[s], tx);
         sm100::bulk_load(dst, p.pool + ((long long)blk * p.Hk + hk) * kPageBytes, kPageBytes, &B.raw_full[s]);
         if (staging)
-          sm100::bulk_load(dst + kPageBytes, p.owner + (long long)(blk % p.stage_rows) * kPage, kPage * 4,
+          sm100::bulk_load(dst + kPageBytes, p.owner + (long long)stage_row_of(p, req, p_first + i, blk) * kPage, kPage * 4,
                            &B.raw_full[s]);
         issued = i + 1;
         if (i < 8) trace(tr, 8 + i);
@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         const int kind = !in ? 0 : stg_j ? 2 : pos >= prefix ? 1 : 3;
         if (__any_sync(0xffffffffu, kind == 1 || kind == 2)) {
           const __half* kf = kind == 1 ? p.k_fresh + ((long long)(q0 + pos - prefix) * p.Hk + hk) * kD : nullptr;
-          const float* sk = kind == 2 ? p.stage_k + ((long long)((blk % p.stage_rows) * kPage + j) * p.Hk + hk) * kD
+          const float* sk = kind == 2 ? p.stage_k + ((long long)(stage_row_of(p, req, p_first + i, blk) * kPage + j) * p.Hk + hk) * kD
                                       : nullptr;
           k_row_mixed(tbase + lrow + kColK, pg, j, kind, kf, sk);
         } else {
@@ -532,7 +532,8 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           if ((sm | fm) != 0ull) {
             // staged tokens: this dim's 64 values of the page half are contiguous fp32
             // in the dim-major staging arena
-            const float* srow = sm != 0ull ? p.stage_v + ((long long)(blk % p.stage_rows) * p.Hk + hk) * kD * kPage +
+            const float* srow = sm != 0ull ? p.stage_v + ((long long)stage_row_of(p, req, p_first + i, blk) * p.Hk + hk) *
+                                                     kD * kPage +
                                                  (long long)d * kPage + hf * 64
                                            : nullptr;
             const long long fbase = ((long long)(q0 + page_pos + hf * 64 - prefix) * p.Hk + hk) * kD + d;

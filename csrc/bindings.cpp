@@ -372,7 +372,8 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
                      const optional<Tensor>& owner, int64_t stage_rows, const Tensor& block_tables,
                      const Tensor& q_start, const Tensor& seq_lens, const Tensor& work, Tensor& part_o,
                      Tensor& part_lse, const optional<Tensor>& status, int64_t rows_per_item,
-                     const optional<Tensor>& tiles, int64_t n_tiles, int64_t n_short) {
+                     const optional<Tensor>& tiles, int64_t n_tiles, int64_t n_short,
+                     const optional<Tensor>& stage_req_slot, int64_t stage_sink, int64_t stage_ring) {
   CHECK_CUDA(q);
   CHECK_DTYPE(q, at::kHalf);
   CHECK_DTYPE(k_fresh, at::kHalf);
@@ -415,6 +416,11 @@ void paged_attention(const Tensor& q, const Tensor& k_fresh, const Tensor& v_fre
   p.part_o = ptr<float>(part_o);
   p.part_lse = ptr<float>(part_lse);
   p.status = optr<int>(status);
+  p.stage_req_slot = optr<int>(stage_req_slot);
+  p.stage_sink = (int)stage_sink;
+  p.stage_ring = p.stage_req_slot ? (int)stage_ring : 0;
+  TORCH_CHECK(stage_ring == 0 || (p.stage_req_slot && stage_req_slot->numel() >= q_start.numel() - 1),
+              "paged_attention: the window staging layout needs one state slot per request");
   CHECK_DTYPE(part_o, at::kFloat);
   CHECK_DTYPE(part_lse, at::kFloat);
   CHECK_CONTIG(part_o);

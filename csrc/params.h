@@ -111,7 +111,23 @@ struct AttnParams {
   float* part_o;    // [n_work, Hk, 64, D]
   float* part_lse;  // [n_work, Hk, 64]
   int* status;
+  // Staging rows per request (stage_ring > 0): logical page lp of request r uses row
+  // stage_req_slot[r] * (stage_sink + stage_ring) + (lp < stage_sink ? lp
+  // : stage_sink + lp % stage_ring), so the sink pages keep rows of their own and the
+  // recent pages cycle through stage_ring rows.  stage_ring == 0: the hashed arena of
+  // the reference (row = physical block % stage_rows).
+  const int* stage_req_slot;
+  int stage_sink, stage_ring;
 };
+
+#ifdef __CUDACC__
+__device__ __forceinline__ int stage_row_of(const AttnParams& p, int req, int lp, int blk) {
+  if (p.stage_ring > 0)
+    return p.stage_req_slot[req] * (p.stage_sink + p.stage_ring) +
+           (lp < p.stage_sink ? lp : p.stage_sink + lp % p.stage_ring);
+  return blk % p.stage_rows;
+}
+#endif
 
 struct MergeParams {
   const float* part_o;

@@ -83,6 +83,11 @@ class OscarConfig:
     sink_tokens: int = 128
     recent_tokens: int = 256
     staging_tokens: int = 8192
+    # "window": every request has staging rows of its own - its sink pages keep theirs and
+    # its recent pages cycle through a small ring - so the sink is never evicted;
+    # "hashed": the reference's arena shared by all requests (row = block % rows), whose
+    # sink rows are overwritten once a sequence passes staging_tokens.
+    staging_layout: str = "window"
     group_size: int = 0
     window_enabled: bool = True
     batched_tokens: int = 15360
@@ -131,6 +136,8 @@ class OscarConfig:
             raise ValueError(f"head_dim={self.head_dim} must be divisible by 4 for INT2 packing")
         if self.paged_block_kv not in _PAGED_BLOCK_KV:
             raise ValueError("OSCAR_ASCEND_PAGED_BLOCK_KV must be 4, 16, 32, 64 or 128")
+        if self.staging_layout not in ("window", "hashed"):
+            raise ValueError("OSCAR_STAGING_LAYOUT must be window or hashed")
         self.window_enabled = self.staging_tokens > 0 and (
             self.sink_tokens > 0 or self.recent_tokens > 0
         )
@@ -148,6 +155,7 @@ class OscarConfig:
             sink_tokens=max(0, _env_int("OSCAR_ASCEND_SINK_TOKENS", 128)),
             recent_tokens=max(0, _env_int("OSCAR_ASCEND_RECENT_TOKENS", 256)),
             staging_tokens=max(0, _env_int("OSCAR_ASCEND_STAGING_TOKENS", 8192)),
+            staging_layout=(os.environ.get("OSCAR_STAGING_LAYOUT") or "window").strip().lower(),
             group_size=_env_int("OSCAR_ASCEND_GROUP_SIZE", 0),
             batched_tokens=max(1, _env_int("OSCAR_ASCEND_BATCHED_TOKENS", 15360)),
             prefill_qblock=max(128, _env_int("OSCAR_ASCEND_PREFILL_QBLOCK", 512)),

@@ -49,6 +49,7 @@ class CacheGeometry:
     page_bytes: int = 17408   # one (block, KV head) INT2 page
     shadow_layers: int = 1    # MTP draft layers with BF16 KV
     stage_rows: int = 64      # staging arena rows (x 128 tokens) per FULL layer, 0 = off
+    #                           (window layout: max_slots x (sink pages + ring); hashed: staging_tokens / 128)
     gdn_bytes_per_slot: int = 0
     max_slots: int = 0
 
@@ -219,9 +220,10 @@ def geometry_of(model, max_slots: int = 0) -> CacheGeometry:
     hk = full[0].Hk if full else 0
     D = full[0].D if full else 256
     o = model.oscar
-    from ..kv.oracle import staging_rows
+    from ..kv.oracle import arena_rows
     int2 = bool(full) and full[0].kv_mode == 0
-    rows = staging_rows(o.sink_tokens, o.recent_tokens, o.staging_tokens) if (o.window_enabled and int2) else 0
+    rows = arena_rows(o.sink_tokens, o.recent_tokens, o.staging_tokens, o.staging_layout, max(1, max_slots)) if (
+        o.window_enabled and int2) else 0
     from ..models.qwen35 import P_MAX
     per_slot = 0
     for g in gdn:  # bf16 state, two conv windows, two pending-token buffers, pending b/a

@@ -35,6 +35,7 @@ from ..ops import sampling as samp
 from . import checks
 from .block_manager import BlockManager, SlotManager
 from .staging import seat_plan
+from ..kv.oracle import window_row
 from ..utils import launches as _launches
 
 
@@ -413,8 +414,13 @@ class LLMEngine:
         slots_np = np.asarray(slots, dtype=np.int64)
         pos_np = np.asarray(poss, dtype=np.int64)
         seq_np = np.asarray(seq_lens, dtype=np.int64)[np.asarray(tok_req, dtype=np.int64)]
+        token_rows = None
+        lay = getattr(self.model, "stage_layout", None)
+        if lay is not None and self.stage_rows:  # per-request window rows (sink rows never shared)
+            slot_of_tok = np.asarray(req_slot, dtype=np.int64)[np.asarray(tok_req, dtype=np.int64)]
+            token_rows = window_row(slot_of_tok, pos_np // 128, lay[0], lay[1])
         stage_seat, owner_seat, owner_val = seat_plan(slots_np, pos_np, seq_np, self.stage_rows, self.sink,
-                                                      self.recent)
+                                                      self.recent, token_rows=token_rows)
         if self.stage_rows:
             self._owner_host[owner_seat] = owner_val
             if static:  # pad to one update per token with idempotent rewrites

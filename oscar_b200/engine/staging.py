@@ -2,7 +2,10 @@
 
 Same semantics as the reference staging write (``oscar_ascend/backend.py:439-481``):
 a token is *kept* if ``pos >= seq - recent`` or ``pos < sink_eff``; its seat is
-``(slot // 128 % rows) * 128 + slot % 128``; among tokens of a step that share a seat
+``row * 128 + slot % 128`` with ``row = slot // 128 % rows`` in the reference's hashed
+arena, or the request's own row for the token's logical page in the window layout
+(``kv.oracle.window_row``: sink pages have rows of their own, so they are never
+evicted); among tokens of a step that share a seat
 the last one (in token order) wins; the owner tag becomes the block id, or -1 when
 the winner is not kept (invalidating recycled seats).
 
@@ -18,11 +21,12 @@ PAGE = 128
 
 
 def seat_plan(slots: np.ndarray, pos: np.ndarray, seq_of_tok: np.ndarray, rows: int, sink_tokens: int,
-              recent_tokens: int, page: int = PAGE):
+              recent_tokens: int, page: int = PAGE, token_rows: np.ndarray | None = None):
     """Returns ``(stage_seat [T], owner_seat [n], owner_val [n])`` as int32 arrays.
 
     ``stage_seat[t]`` is the seat token ``t`` writes its fp32 K/V to (winner and kept),
-    else -1.
+    else -1.  ``token_rows[t]`` is token ``t``'s staging row in the per-request window
+    layout; without it the row is ``block % rows`` (the reference's hashed arena).
     """
     T = slots.shape[0]
     stage_seat = np.full(T, -1, dtype=np.int32)
@@ -32,7 +36,8 @@ def seat_plan(slots: np.ndarray, pos: np.ndarray, seq_of_tok: np.ndarray, rows: 
     keep = (pos >= seq_of_tok - recent_tokens) | (pos < sink_eff)
     valid = np.nonzero(slots >= 0)[0]
     s = slots[valid].astype(np.int64)
-    seats = (s // page % rows) * page + s % page
+    row = (s // page % rows) if token_rows is None else token_rows[valid].astype(np.int64)
+    seats = row * page + s % page
     # last writer per seat in token order: stable sort, take the final index of each run
     order = np.argsort(seats, kind="stable")
     ss = seats[order]

@@ -193,6 +193,15 @@ class HostKVStore:
         self._pending_free = []
 
     # ------------------------------------------------------------ layout
+    def _stage_rows_of(self, idx: torch.Tensor, slot: int) -> torch.Tensor:
+        """Staging row of each of a request's blocks (in logical page order)."""
+        m = self.model
+        lay = getattr(m, "stage_layout", None)
+        if lay is None:
+            return idx % m.stage_rows
+        from .oracle import window_row
+        return window_row(slot, torch.arange(idx.numel(), device=idx.device), lay[0], lay[1])
+
     def _gdn_views(self, g):
         return ((g.state, 0), (g.conv_state, 1), (g.pend_x, 1), (g.pend_ba, 0))
 
@@ -220,8 +229,7 @@ class HostKVStore:
         n_staged = 0
         owner_cleared = None
         if m.stage_rows:
-            rows = m.stage_rows
-            seats = ((idx % rows) * PAGE).unsqueeze(1) + torch.arange(PAGE, device=dev)  # [nb, 128]
+            seats = (self._stage_rows_of(idx, slot) * PAGE).unsqueeze(1) + torch.arange(PAGE, device=dev)  # [nb, 128]
             own = m.owner[seats.view(-1)].view(len(blocks), PAGE)
             maskd = own == idx.unsqueeze(1).to(own.dtype)
             sel = seats[maskd]
@@ -303,12 +311,27 @@ class HostKVStore:
         owner_upd = (None, None)
         if sw.staged_mask is not None:
             maskd = next(d)
-            rows = m.stage_rows
-            seats = ((idx % rows) * PAGE).unsqueeze(1) + torch.arange(PAGE, device=dev)
-            # no stale tag may claim the new blocks; restored tokens get their tags back
-            tags = torch.where(maskd, idx.unsqueeze(1), torch.full_like(seats, -1)).view(-1).to(m.owner.dtype)
-            m.owner[seats.view(-1)] = tags
-            owner_upd = (seats.view(-1).cpu().numpy(), tags.cpu().numpy())
+            seats = (self._stage_rows_of(idx, slot) * PAGE).unsqueeze(1) + torch.arange(PAGE, device=dev)
+            lay = getattr(m, "stage_layout", None)
+            if lay is None:
+                # no stale tag may claim the new blocks; restored tokens get their tags back
+                tags = torch.where(maskd, idx.unsqueeze(1), torch.full_like(seats, -1)).view(-1).to(m.owner.dtype)
+                m.owner[seats.view(-1)] = tags
+                owner_upd = (seats.view(-1).cpu().numpy(), tags.cpu().numpy())
+            else:
+                # the slot's rows are the request's own: clear them all, then restore the
+                # staged tokens' tags (pages sharing a ring row must not race on a seat)
+                per = lay[0] + lay[1]
+                own_seats = ((slot * per + torch.arange(per, device=dev)) * PAGE).unsqueeze(1) + torch.arange(
+                    PAGE, device=dev)
+                own_seats = own_seats.view(-1)
+                claimed = seats[maskd]
+                ctags = idx.unsqueeze(1).expand_as(seats)[maskd].to(m.owner.dtype)
+                reset = own_seats[~torch.isin(own_seats, claimed)]
+                m.owner[reset] = -1
+                m.owner[claimed] = ctags
+                owner_upd = (torch.cat([reset, claimed]).cpu().numpy(),
+                             torch.cat([torch.full_like(reset, -1).to(m.owner.dtype), ctags]).cpu().numpy())
             sel = seats[maskd]
             it = iter(staged)
             for layer in m.full_layers:

@@ -59,6 +59,34 @@ def staging_rows(sink_tokens: int, recent_tokens: int, staging_tokens: int, page
     return max((staging_tokens + page - 1) // page, sink_pages + tail_pages + 2)
 
 
+def window_layout(sink_tokens: int, recent_tokens: int, page: int = fmt.PAGE) -> tuple[int, int]:
+    """``(sink_pages, ring)`` of the per-request staging layout: the sink pages keep rows of
+    their own and the recent pages cycle through ``ring`` rows, enough that the pages
+    holding the last ``recent_tokens`` tokens (up to ``ceil(recent / page) + 1`` of them)
+    never share a row."""
+    return sink_tokens // page, (recent_tokens + page - 1) // page + 2
+
+
+def arena_rows(sink_tokens: int, recent_tokens: int, staging_tokens: int, layout: str, max_slots: int,
+               page: int = fmt.PAGE) -> int:
+    """Rows (of ``page`` tokens) of a FULL layer's staging arena: ``max_slots`` requests'
+    own rows in the window layout, the shared hashed arena otherwise."""
+    if layout == "window":
+        sp, ring = window_layout(sink_tokens, recent_tokens, page)
+        return max_slots * (sp + ring)
+    return staging_rows(sink_tokens, recent_tokens, staging_tokens, page)
+
+
+def window_row(req_slot, lp, sink_pages: int, ring: int):
+    """Staging row of logical page ``lp`` of the request in state slot ``req_slot`` (ints,
+    numpy arrays or tensors; the attention kernels use the same formula)."""
+    per = sink_pages + ring
+    if isinstance(lp, int):
+        return req_slot * per + (lp if lp < sink_pages else sink_pages + lp % ring)
+    mod = lp % ring
+    return req_slot * per + ((lp < sink_pages) * lp + (lp >= sink_pages) * (sink_pages + mod))
+
+
 def token_positions(qsl: list[int], seqs: list[int], n_tokens: int) -> tuple[torch.Tensor, torch.Tensor]:
     """Per token: request index and absolute position (``seq - q_len + i``)."""
     req = torch.full((n_tokens,), -1, dtype=torch.long)
@@ -73,18 +101,21 @@ def token_positions(qsl: list[int], seqs: list[int], n_tokens: int) -> tuple[tor
 
 
 def seat_plan(slots: torch.Tensor, pos: torch.Tensor, seq_of_token: torch.Tensor,
-              rows: int, sink_tokens: int, recent_tokens: int, page: int = fmt.PAGE):
+              rows: int, sink_tokens: int, recent_tokens: int, page: int = fmt.PAGE,
+              token_rows: torch.Tensor | None = None):
     """Deterministic staging plan for one step (shared by every FULL layer).
 
     Returns ``(token_idx, seat, owner)``: for every distinct seat the last writer in
     token order, its seat, and the owner tag to store (the block id, or -1 when the
-    token is outside the sink/recent window).
+    token is outside the sink/recent window).  ``token_rows`` gives each token's staging
+    row (the window layout); by default the row is ``block % rows`` (the hashed arena).
     """
     sink_eff = (sink_tokens // page) * page
     keep = (pos >= seq_of_token - recent_tokens) | (pos < sink_eff)
     valid = torch.nonzero(slots >= 0, as_tuple=True)[0]
     s = slots[valid].long()
-    seats = (s // page % rows) * page + s % page
+    row = (s // page % rows) if token_rows is None else token_rows[valid].long()
+    seats = row * page + s % page
     order = torch.argsort(seats, stable=True)
     ss = seats[order]
     last = torch.ones_like(ss, dtype=torch.bool)
@@ -147,14 +178,16 @@ def sdpa_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
 
 
 def gather_history(pool: torch.Tensor, block_row: torch.Tensor, count: int, D: int,
-                   stage: StagingArena | None = None):
-    """Dequantized (and staging-spliced) rotated history ``k/v [count,Hk,D]`` (fp32)."""
+                   stage: StagingArena | None = None, page_rows: torch.Tensor | None = None):
+    """Dequantized (and staging-spliced) rotated history ``k/v [count,Hk,D]`` (fp32).
+    ``page_rows[lp]``: the staging row of logical page ``lp`` (window layout); by default
+    ``block % rows`` (hashed arena)."""
     pos = torch.arange(count)
     blocks = block_row[pos // fmt.PAGE].long()
     offs = pos % fmt.PAGE
     k, v = fmt.dequant_tokens(pool, blocks, offs, D)
     if stage is not None and count:
-        rows = blocks % stage.rows
+        rows = blocks % stage.rows if page_rows is None else page_rows[pos // fmt.PAGE].long()
         hit = (stage.owner[rows, offs].long() == blocks).view(-1, 1, 1)
         k = torch.where(hit, stage.k[rows, offs], k)
         v = torch.where(hit, stage.v[rows, offs], v)

@@ -27,7 +27,7 @@ import torch
 
 from ..config import OscarConfig
 from ..kv import format as fmt
-from ..kv.oracle import staging_rows
+from ..kv.oracle import arena_rows, window_layout
 from ..kv.rotation import get_layer_rotation, random_orthogonal
 from ..ops import attention as A
 from ..ops import functional as F
@@ -224,7 +224,8 @@ class FullAttentionLayer:
         return sum(t.numel() * t.element_size() for t in (self.pool, self.kc, self.vc, self.stage_k, self.stage_v)
                    if t is not None)
 
-    def attention(self, xq, xs, b: StepBatch, rope, owner, stage_rows, write_owner: bool, status=None):
+    def attention(self, xq, xs, b: StepBatch, rope, owner, stage_rows, write_owner: bool, status=None,
+                  stage_layout=None):
         """qkv GEMM -> fused store -> paged attention -> merge. Returns (o_int8, o_scale)."""
         T = xq.shape[0]
         if self.kv_mode == 0:
@@ -249,7 +250,10 @@ class FullAttentionLayer:
         if self.calib is not None:  # rotation calibration: unquantised q / k / v of this layer
             self.calib.record(f"model.layers.{self.layer_id}.self_attn.attn", q_out, k_fr, v_fr, self.Hq, self.Hk,
                               self.D)
-        stage = (self.stage_k, self.stage_v, owner, stage_rows) if staged else None
+        stage = None
+        if staged:
+            lay = None if stage_layout is None else (b.req_slot, stage_layout[0], stage_layout[1])
+            stage = (self.stage_k, self.stage_v, owner, stage_rows, lay)
         gate = qkv[:, self.D:]  # gate of head h at columns h * 2D + D ..
         _, oq, os_ = A.attention(q_out, k_fr, v_fr, Hq=self.Hq, Hk=self.Hk, D=self.D, scale=self.scale,
                                  kv_mode=self.kv_mode, pool=self.pool, kc=self.kc, vc=self.vc, stage=stage,
@@ -388,6 +392,7 @@ class HybridModel:
         self.mtp = MTPHead(self, seed) if (mtp and cfg.num_mtp_layers > 0) else None
         self.rope = F.rope_tables(cfg.max_position, cfg.rot_dim, cfg.rope_theta, dev, cfg.rope_scaling)
         self.stage_rows = 0
+        self.stage_layout = None
         self.owner = None
         self.status = torch.zeros(1, dtype=torch.int32, device=dev) if dev.type == "cuda" else None
 
@@ -419,8 +424,11 @@ class HybridModel:
     def allocate_cache(self, num_blocks: int, max_slots: int):
         o = self.oscar
         int2 = any(m.kv_mode == 0 for m in self.full_layers)
-        self.stage_rows = staging_rows(o.sink_tokens, o.recent_tokens, o.staging_tokens) if (
-            o.window_enabled and int2) else 0
+        self.stage_rows = arena_rows(o.sink_tokens, o.recent_tokens, o.staging_tokens, o.staging_layout,
+                                     max_slots) if (o.window_enabled and int2) else 0
+        # (sink_pages, ring) of the per-request window layout, None for the hashed arena
+        self.stage_layout = window_layout(o.sink_tokens, o.recent_tokens) if (
+            self.stage_rows and o.staging_layout == "window") else None
         if self.stage_rows:
             self.owner = torch.full((self.stage_rows * fmt.PAGE,), -1, dtype=torch.int32, device=self.device)
         for m in self.full_layers:
@@ -472,7 +480,8 @@ class HybridModel:
             xq, xs, _ = red.norm(residual, mixer.input_norm, eps, pending, status=self.status)
             if isinstance(mixer, FullAttentionLayer):
                 oq, os_ = mixer.attention(xq, xs, b, self.rope, self.owner, self.stage_rows,
-                                          write_owner=first_full, status=self.status)
+                                          write_owner=first_full, status=self.status,
+                                          stage_layout=self.stage_layout)
                 first_full = False
                 w_o = mixer.o
             else:

@@ -254,8 +254,13 @@ def _history_fp16(kv_mode, pool, kc, vc, stage, bt_row, count, hk_idx, D):
         kk, vv = fmt.dequant_tokens(pool, blocks, offs, D)
         k, v = kk[:, hk_idx], vv[:, hk_idx]
     if stage is not None and count:
-        sk, sv, owner, rows = stage
-        r = blocks % rows
+        sk, sv, owner, rows = stage[:4]
+        lay = stage[4] if len(stage) > 4 else None  # (slot of this request, sink pages, ring)
+        if lay is None:
+            r = blocks % rows
+        else:
+            from ..kv.oracle import window_row
+            r = window_row(int(lay[0]), pos // fmt.PAGE, lay[1], lay[2])
         hit = (owner.view(rows, fmt.PAGE)[r, offs].long() == blocks).unsqueeze(-1)
         k = torch.where(hit, sk.view(rows, fmt.PAGE, -1, D)[r, offs, hk_idx], k)
         v = torch.where(hit, sv.view(rows, -1, D, fmt.PAGE)[r, hk_idx, :, offs], v)
@@ -274,8 +279,12 @@ def attention_ref(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, v
             continue
         n = b - a
         prefix = seq_lens[r] - n
+        st = stage
+        if stage is not None and len(stage) > 4 and stage[4] is not None:
+            lay = stage[4]  # per-request layout: this request's state slot
+            st = stage[:4] + ((int(lay[0][r]), lay[1], lay[2]),)
         for h in range(Hk):
-            kh, vh = _history_fp16(kv_mode, pool, kc, vc, stage, block_tables[r], prefix, h, D)
+            kh, vh = _history_fp16(kv_mode, pool, kc, vc, st, block_tables[r], prefix, h, D)
             kk = torch.cat([kh, k_fresh[a:b, h].float()])
             vv = torch.cat([vh, v_fresh[a:b, h].float()])
             qq = q[a:b, h * g:(h + 1) * g].float()  # [n, g, D]
@@ -306,8 +315,9 @@ def attention(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, s
               part_o=None, part_lse=None, status=None, rv_merge_split=None):
     """Attention + merge.  Returns ``(o_bf16 | None, o_int8 | None, o_scale | None)``.
 
-    ``stage`` is ``(stage_k [rows*128, Hk, D], stage_v [rows, Hk, D, 128], owner, rows)`` or
-    ``None``; ``gate`` is the bf16
+    ``stage`` is ``(stage_k [rows*128, Hk, D], stage_v [rows, Hk, D, 128], owner, rows, layout)``
+    or ``None``; ``layout`` is ``None`` (the hashed arena) or ``(req_slot [R], sink_pages,
+    ring)`` of the per-request window layout; ``gate`` is the bf16
     qkv buffer view whose ``[t, h*gate_hstride + d]`` element gates output ``(t, h, d)``.
     """
     T = q.shape[0]
@@ -326,12 +336,15 @@ def attention(q, k_fresh, v_fresh, *, Hq, Hk, D, scale, kv_mode, pool, kc, vc, s
         part_lse = torch.empty(plan.n_work * Hk * ROWS, dtype=torch.float32, device=q.device)
     sk = sv = own = None
     rows = 0
+    lay = None
     if stage is not None:
-        sk, sv, own, rows = stage
+        sk, sv, own, rows = stage[:4]
+        lay = stage[4] if len(stage) > 4 else None
     e.paged_attention(q, k_fresh, v_fresh, Hq, Hk, D, float(scale), kv_mode, pool, kc, vc, sk, sv, own, rows,
                       block_tables, q_start_t, seq_lens_t, plan.work, part_o, part_lse, status,
                       _rpi(plan, q_start, Hq // Hk), plan.tiles if (USE_TC and plan.n_tiles > 0) else None,
-                      plan.n_tiles if USE_TC else 0, plan.n_short if (USE_TC and plan.n_tiles > 0) else 0)
+                      plan.n_tiles if USE_TC else 0, plan.n_short if (USE_TC and plan.n_tiles > 0) else 0,
+                      None if lay is None else lay[0], 0 if lay is None else lay[1], 0 if lay is None else lay[2])
     if RvT is not None:
         # tensor-core merge + rotation + gate, then the vectorised row quantiser
         if rv_merge_split is None:

@@ -54,3 +54,41 @@ def test_config1_decode_vs_sdpa_oracle():
     own = stage.owner.view(-1)
     assert int((own >= 0).sum()) == hist - (hist + n - 256)
     assert int((own == 0).sum()) == 0
+
+
+def test_config1_window_layout_keeps_the_sink():
+    """The per-request window layout (this framework's default) gives the sink page rows of
+    its own: at the same 24,579-token shape every one of the first 128 tokens stays staged
+    (fp32) next to the recent window, and the read path still equals the SDPA oracle over
+    the staging-spliced cache within 1e-4."""
+    g = torch.Generator().manual_seed(0)
+    hq, hk, D, hist, n = 6, 1, 256, 24579, 4
+    q = torch.randn(n, hq, D, generator=g).to(torch.bfloat16).float()
+    k = torch.randn(hist + n, hk, D, generator=g).to(torch.bfloat16).float()
+    v = torch.randn(hist + n, hk, D, generator=g).to(torch.bfloat16).float()
+    Rk = torch.linalg.qr(torch.randn(D, D, generator=g))[0]
+    Rv = torch.linalg.qr(torch.randn(D, D, generator=g))[0]
+    pages = (hist + n + 127) // 128
+    pool = torch.zeros(pages, hk, fmt.page_head_bytes(D), dtype=torch.uint8)
+    slots = torch.arange(hist)
+    k_rot, v_rot = O.store_ref(k[:hist], v[:hist], pool, slots, Rk, Rv, 0.96, 0.92)
+    sink_pages, ring = O.window_layout(128, 256)
+    req_slot = 3
+    rows = O.arena_rows(128, 256, 8192, "window", max_slots=4)
+    token_rows = O.window_row(req_slot, slots // 128, sink_pages, ring)
+    stage = O.StagingArena(rows, hk, D)
+    stage.write(O.seat_plan(slots, slots, torch.full((hist,), hist + n), rows, 128, 256, token_rows=token_rows),
+                k_rot, v_rot)
+    page_rows = O.window_row(req_slot, torch.arange(pages), sink_pages, ring)
+    bt = torch.arange(pages, dtype=torch.int32).view(1, -1)
+    # the sink page keeps its row: all 128 tags equal its block (block 0)
+    assert int((stage.owner[int(page_rows[0])] == 0).sum()) == 128
+    kh, vh = O.gather_history(pool, bt[0], hist, D, stage, page_rows)
+    assert torch.equal(kh[:128], k_rot[:128]) and torch.equal(vh[:128], v_rot[:128])  # unquantised sink
+    assert torch.equal(kh[hist + n - 256:], k_rot[hist + n - 256:])  # and the recent window
+    scale = 1 / math.sqrt(D)
+    kk = torch.cat([kh @ Rk.t(), k[hist:]])
+    vv = torch.cat([vh @ Rv.t(), v[hist:]])
+    ref = O.sdpa_causal(q, kk, vv, scale, hist)
+    exact = O.sdpa_causal(q, k, v, scale, hist)
+    assert float((ref - exact).norm() / exact.norm()) < 1.0

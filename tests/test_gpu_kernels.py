@@ -249,6 +249,19 @@ def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
     """``mixed`` / ``prefill`` run prefill chunks (tcgen05 prefill kernel: fresh-only and
     INT2-history tiles, staged tokens, two KV heads) next to short verify/decode requests
     in the same step; ``bf16_prefill`` the same plan over a BF16 cache."""
+    _attention_case(case, use_tc, monkeypatch, window=False)
+
+
+@pytest.mark.parametrize("use_tc", [True, False], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("case", ["mtp", "long", "prefill"])
+def test_paged_attention_window_staging(case, use_tc, monkeypatch):
+    """The per-request window layout of the staging arena: rows come from each request's
+    state slot and logical page (sink pages and a ring of recent pages), in all three INT2
+    attention kernels (decode/verify tcgen05, warp-level, prefill tcgen05)."""
+    _attention_case(case, use_tc, monkeypatch, window=True)
+
+
+def _attention_case(case, use_tc, monkeypatch, window):
     if not use_tc and case in ("mixed", "prefill"):
         pytest.skip("same kernel as the tcgen05 run")
     monkeypatch.setattr(A, "USE_TC", use_tc)
@@ -283,13 +296,23 @@ def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
     vs.copy_((torch.rand(vs.shape) * 0.5 + 0.2).half())
     kz.copy_((-torch.rand(kz.shape) - 0.3).half())
     vz.copy_((-torch.rand(vz.shape) - 0.3).half())
-    rows = 4
+    from oscar_b200.kv.oracle import window_row
+    req_slot = torch.tensor([(2 * r + 1) % 5 for r in range(R)], dtype=torch.int32)  # state slots 0..4
+    sink_pages, ring = 1, 4
+    rows = 5 * (sink_pages + ring) if window else 4
     sk = torch.randn(rows * 128, Hk, D)
     sv = torch.randn(rows, Hk, D, 128)
     owner = torch.full((rows * 128,), -1, dtype=torch.int32)
-    # mark a few staged tokens for request 0: its first page and a later page
     b0 = int(bt[0, 0])
-    owner.view(rows, 128)[b0 % rows, :50] = b0
+    if window:
+        # request 0's sink page, and a page near the end of every request's history
+        owner.view(rows, 128)[window_row(int(req_slot[0]), 0, sink_pages, ring), :50] = b0
+        for r in range(R):
+            lp = max(0, (seqs[r] - qlens[r] - 1) // 128 - 1)
+            owner.view(rows, 128)[window_row(int(req_slot[r]), lp, sink_pages, ring), 30:90] = int(bt[r, lp])
+    else:
+        # mark a few staged tokens for request 0: its first page
+        owner.view(rows, 128)[b0 % rows, :50] = b0
     T = sum(qlens)
     q = (torch.randn(T, Hq, D)).half()
     kf = torch.randn(T, Hk, D).half()
@@ -302,7 +325,8 @@ def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
             b, o = int(bt[r, pos // 128]), pos % 128
             kc[b, o] = kf[q_start[r] + i].to(torch.bfloat16)
             vc[b, o] = vf[q_start[r] + i].to(torch.bfloat16)
-    stage_cpu = (sk, sv, owner, rows) if kv_mode == 0 else None
+    lay_cpu = (req_slot, sink_pages, ring) if window else None
+    stage_cpu = (sk, sv, owner, rows, lay_cpu) if kv_mode == 0 else None
     ref_b, ref_q, ref_s = A.attention(q, kf, vf, Hq=Hq, Hk=Hk, D=D, scale=1 / 16, kv_mode=kv_mode, pool=pool, kc=kc,
                                       vc=vc, stage=stage_cpu, block_tables=bt, q_start_t=None, seq_lens_t=None,
                                       q_start=q_start, seq_lens=seqs, plan=None, tok_req=None, RvT=None, gate=None,
@@ -310,7 +334,8 @@ def test_paged_attention_matches_ref(case, use_tc, monkeypatch):
     d = lambda t: t.to(DEV)  # noqa: E731
     tok_req = torch.repeat_interleave(torch.arange(R), torch.tensor(qlens)).to(torch.int32)
     plan = A.plan_attention(q_start, seqs, g, Hk, F.num_sms(torch.device(DEV)), DEV)
-    stage = (d(sk), d(sv), d(owner), rows) if kv_mode == 0 else None
+    lay = (d(req_slot), sink_pages, ring) if window else None
+    stage = (d(sk), d(sv), d(owner), rows, lay) if kv_mode == 0 else None
     out_b, _, _ = A.attention(d(q), d(kf), d(vf), Hq=Hq, Hk=Hk, D=D, scale=1 / 16, kv_mode=kv_mode, pool=d(pool),
                               kc=d(kc), vc=d(vc), stage=stage, block_tables=d(bt),
                               q_start_t=d(torch.tensor(q_start, dtype=torch.int32)),

@@ -29,7 +29,7 @@ class AttnParams(ctypes.Structure):
                 ("kv_mode", I), ("pool", P), ("page_bytes", I), ("kc", P), ("vc", P), ("stage_k", P),
                 ("stage_v", P), ("owner", P), ("stage_rows", I), ("block_tables", P), ("bt_stride", I),
                 ("q_start", P), ("seq_lens", P), ("work", P), ("n_work", I), ("part_o", P), ("part_lse", P),
-                ("status", P)]
+                ("status", P), ("stage_req_slot", P), ("stage_sink", I), ("stage_ring", I)]
 
 
 class MergeParams(ctypes.Structure):
