@@ -14,9 +14,11 @@
 //               O^T += V^T P'^T, M = 128 dims, K = 128 tokens);
 //   warps 8-11  "softmax": TMEM lane t = token t of the page.  They read the
 //               page's N scores of token t from TMEM, apply the per-token INT2
-//               scale/zero (q.k = s (q.c) + z sum(q)), keep per-row running
-//               maxima, and write P' = p * s_v as fp16 into shared memory in the
-//               MN-major layout of the B operand of the P.V product.
+//               scale (q.k = s (q.c + (z/s) sum(q)); the zero-point term comes
+//               out of the MMA through one extra K-step whose operands are
+//               (z/s) and sum(q), each split into fp16 hi + lo), keep the per-row
+//               running maxima in registers, and write P' = p * s_v as fp16 into
+//               shared memory in the MN-major layout of the B operand of P.V.
 // Operand placement keeps shared-memory traffic small: codes never go through
 // shared memory as fp16, only the 2-bit page (bulk copy), Q (once) and P' do.
 //
@@ -60,6 +62,22 @@ constexpr float kSlack = 8.f;
 constexpr uint64_t kBudgetNs = 2000000000ull;
 constexpr uint32_t kColK = 0, kColV = 128, kColS = 384, kColO = 448, kTmemCols = 512;
 constexpr int kBarSoft = 1, kBarStats = 3;
+// Initial running maximum: finite, so that exp2(s - m) needs no special case for rows
+// without a visible key yet (their scores are -inf), and any visible score moves it.
+constexpr float kNoMax = -1e30f;
+// The zero-point term z (q . 1) of a code token is folded into the S MMA as
+// (z / s) * sum(q) when |z / s| stays well inside fp16; other tokens keep it in the softmax.
+constexpr float kZsMax = 16384.f;
+
+OSCAR_DEVICE uint32_t pack_h2(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+// z / s of a code token, or 0 when its zero-point is not folded (s == 0, |z / s| too big)
+OSCAR_DEVICE float folded_zs(float ks, float kz) {
+  const float r = ks != 0.f ? kz / ks : 0.f;
+  return fabsf(r) <= kZsMax ? r : 0.f;
+}
+OSCAR_DEVICE bool zs_folded(float ks, float kz) { return ks != 0.f && fabsf(kz / ks) <= kZsMax; }
 
 // Optional per-CTA event timeline (globaltimer ns) for performance analysis; off
 // unless a buffer was installed with oscar_attn_tc_trace (slot layout: 96 u64 per CTA).
@@ -212,7 +230,11 @@ template <int N>
 struct TcLayout {
   static constexpr int kQOff = kRing * kSlot;  // 71,680: 1024-aligned
   static constexpr int kQBytes = N * 512;       // 4 chunks of 64 dims x N rows x 128 B
-  static constexpr int kPOff = kQOff + kQBytes;
+  // zero-point step of S^T = K Q^T, K-major with the 32-byte swizzle (one K-step of 16):
+  // Q side [N rows][sum(q) hi, lo, hi, 0...], K side [128 tokens][z' hi, hi, lo, 0...]
+  static constexpr int kQzOff = kQOff + kQBytes;
+  static constexpr int kZaOff = kQzOff + N * 32;
+  static constexpr int kPOff = kZaOff + kPage * 32;
   static constexpr int kPBytes = kPage * N * 2;  // one P' buffer: 128 tokens x N fp16
   static constexpr int kMisc = kPOff + 2 * kPBytes;
   static constexpr int kSq = kMisc;                  // N floats: sum(q) per row
@@ -282,6 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   uint8_t* smem = smem_raw + ((1024u - (sm100::smem_addr(smem_raw) & 1023u)) & 1023u);
   uint8_t* ring = smem;
   uint8_t* qs = smem + L::kQOff;
+  uint8_t* qz = smem + L::kQzOff;
+  uint8_t* za = smem + L::kZaOff;
   uint8_t* ps = smem + L::kPOff;
   float* sq = reinterpret_cast<float*>(smem + L::kSq);
   int* lim = reinterpret_cast<int*>(smem + L::kLim);
@@ -360,8 +384,15 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     }
     sq[tid] = acc;
     lim[tid] = tid < nrows ? prefix + (row0 + tid) / g : -1;
-    msm[tid] = -INFINITY;
+    msm[tid] = kNoMax;
+    const __half hi = __float2half_rn(acc), lo = __float2half_rn(acc - __half2float(hi));
+    const uint32_t w0 = pack_h2(hi, lo), w1 = pack_h2(hi, __float2half_rn(0.f));
+    const int sw = (tid >> 2) & 1;
+    *reinterpret_cast<uint4*>(qz + tid * 32 + (sw << 4)) = make_uint4(w0, w1, 0u, 0u);
+    *reinterpret_cast<uint4*>(qz + tid * 32 + ((sw ^ 1) << 4)) = make_uint4(0u, 0u, 0u, 0u);
   }
+  for (int idx = tid; idx < kPage * 2; idx += kThreads)
+    *reinterpret_cast<uint4*>(za + idx * 16) = make_uint4(0u, 0u, 0u, 0u);
   sm100::fence_proxy_async();  // Q tile: generic writes -> tensor-core reads
   sm100::tc_fence_before();
   __syncthreads();
@@ -404,6 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       const uint32_t idq = sm100::idesc_f16(128, N, false, false);
       const uint32_t idp = sm100::idesc_f16(128, N, false, true);
       const uint32_t qa = sm100::smem_addr(qs), pa = sm100::smem_addr(ps);
+      const uint64_t zad = sm100::smem_desc(sm100::smem_addr(za), 16, 256, 6);
+      const uint64_t qzd = sm100::smem_desc(sm100::smem_addr(qz), 16, 256, 6);
       constexpr uint32_t kPLayout = N == 32 ? 4u : 6u;  // P' rows of N fp16: 64 B / 32 B swizzle
       constexpr uint32_t kPAtom = 8 * N * 2;           // 8 tokens
       auto pv = [&](int j) -> bool {
@@ -442,6 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           const uint64_t qd = sm100::smem_desc(qa + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024, 2);
           sm100::umma_f16_tmem_a(tbase + kColS + (i & 1) * N, tbase + kColK + kk * 8, qd, idq, kk > 0 ? 1u : 0u);
         }
+        // + (z/s) sum(q): K-side and Q-side tiles in shared memory, 32-byte swizzle
+        sm100::umma_bf16(tbase + kColS + (i & 1) * N, zad, qzd, idq, 1u);
         sm100::umma_commit(&B.s_full[i & 1]);
         if (i < 8) trace(tr, 16 + i);
         sm100::umma_commit(B.k_empty);
@@ -493,6 +528,15 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         const bool in = pos >= kv_begin && pos < kv_stop;
         const bool stg_j = in && staging && own[j] == blk;
         const int kind = !in ? 0 : stg_j ? 2 : pos >= prefix ? 1 : 3;
+        {
+          // zero-point row of token j for the S MMA's extra K-step: (z/s hi, z/s hi, z/s lo)
+          // against (sum(q) hi, lo, hi) on the Q side
+          const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * 64);
+          const float zs = kind == 3 ? folded_zs(__half2float(meta[j]), __half2float(meta[kPage + j])) : 0.f;
+          const __half zh = __float2half_rn(zs), zl = __float2half_rn(zs - __half2float(zh));
+          *reinterpret_cast<uint4*>(za + j * 32 + (((j >> 2) & 1) << 4)) =
+              make_uint4(pack_h2(zh, zh), pack_h2(zl, __float2half_rn(0.f)), 0u, 0u);
+        }
         if (__any_sync(0xffffffffu, kind == 1 || kind == 2)) {
           const __half* kf = kind == 1 ? p.k_fresh + ((long long)(q0 + pos - prefix) * p.Hk + hk) * kD : nullptr;
           const float* sk = kind == 2 ? p.stage_k + ((long long)(stage_row_of(p, req, p_first + i, blk) * kPage + j) * p.Hk + hk) * kD
@@ -510,6 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         sm100::tmem_st_wait();
         sm100::tc_fence_before();
       }
+      sm100::fence_proxy_async();  // zero-point row: generic write -> tensor-core read
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(B.k_full);
       if (ct == 0 && i < 8) trace(tr, 24 + i);
@@ -648,11 +693,13 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     const int swarp = st >> 5;
     const uint32_t lrow = (uint32_t)(st & ~31) << 16;
     const float sl2 = p.scale * kLog2e;
-    // per-row constants live in registers, lane r holding row r (broadcast by shuffles:
-    // a warp reading one shared-memory word per row is far slower here)
+    // Running row maxima are read as float4 broadcasts from shared memory (they only
+    // change on the rare pages that move a maximum by more than the slack).  sum(q) and
+    // the causal limits are needed only for unfolded zero-points and the last pages:
+    // lane r holds row r, broadcast by shuffles on those pages.
     const float sq_l = sq[lane % N];
     const int lim_l = lim[lane % N];
-    float m_l = msm[lane % N];
+    const float4* mr4 = reinterpret_cast<const float4*>(msm);
     bool dead = false, aborted = false;
     for (int i = 0; i < n_pages; ++i) {
       const int s = i % kRing, b = i & 1;
@@ -698,21 +745,39 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           }
         }
         const bool hist = pos < prefix;
+        // zero-point z sum(q) of code tokens comes with S from the MMA (folded) unless
+        // |z / s| is too large for fp16 (then it is added here)
+        const bool unf = in && !(pos >= prefix || (staging && own[j] == blk)) && !zs_folded(ks, kz);
         if (i < 4) trace_dep(tr, st == 0 ? 64 + 4 * i : kTraceSlots, ks + kz + vs);
         const unsigned long long cl0 = clock_dep(ks + kz + vs);
-        // per-row constants with 16-byte shared loads; the causal limits only matter on
-        // pages that reach the current chunk
-        const float kss = ks * sl2, kzs = kz * sl2;
+        const float kss = ks * sl2, kzs = unf ? kz * sl2 : 0.f;
         const bool page_hist = (p_first + i + 1) * kPage <= prefix;
         float dmax = -INFINITY;
+        if (page_hist && !__any_sync(0xffffffffu, unf)) {
 #pragma unroll
-        for (int r = 0; r < N; ++r) {
-          const float qv = __shfl_sync(0xffffffffu, sq_l, r);
-          const int lv = page_hist ? INT_MAX : __shfl_sync(0xffffffffu, lim_l, r);
-          const float mv = __shfl_sync(0xffffffffu, m_l, r);
-          const bool vis = in && (hist || pos <= lv);
-          sc[r] = vis ? fmaf(kss, sc[r], kzs * qv) : -INFINITY;
-          dmax = fmaxf(dmax, sc[r] - mv);
+          for (int r = 0; r < N; r += 4) {
+            const float4 m4 = mr4[r / 4];
+            const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              sc[r + e] = in ? kss * sc[r + e] : -INFINITY;
+              dmax = fmaxf(dmax, sc[r + e] - mv[e]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < N; r += 4) {
+            const float4 m4 = mr4[r / 4];
+            const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float qv = __shfl_sync(0xffffffffu, sq_l, r + e);
+              const int lv = page_hist ? INT_MAX : __shfl_sync(0xffffffffu, lim_l, r + e);
+              const bool vis = in && (hist || pos <= lv);
+              sc[r + e] = vis ? fmaf(kss, sc[r + e], kzs * qv) : -INFINITY;
+              dmax = fmaxf(dmax, sc[r + e] - mv[e]);
+            }
+          }
         }
         need = dmax > kSlack;
         if (i < 4) trace_dep(tr, st == 0 ? 65 + 4 * i : kTraceSlots, sc[N - 1] + (need ? 1.f : 0.f));
@@ -723,11 +788,15 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       if (ok && i >= 2)
         ok = sm100::mbar_wait(&B.p_empty[b], ((i >> 1) - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
       if (st == 0 && i < 4) trace(tr, 50 + 4 * i);
-      if (sm100::bar_red_or(kBarSoft, 128, !ok)) {
-        aborted = true;
-        break;
+      // one barrier on the common path: abort and "a maximum moved" are both rare
+      bool upd_now = false;
+      if (sm100::bar_red_or(kBarSoft, 128, !ok || need)) {
+        if (sm100::bar_red_or(kBarSoft, 128, !ok)) {
+          aborted = true;
+          break;
+        }
+        upd_now = true;  // no warp aborted, so some warp saw a maximum move
       }
-      const bool upd_now = sm100::bar_red_or(kBarSoft, 128, need);
       if (st == 0 && i < 4) trace(tr, 51 + 4 * i);
       if (upd_now) {
         // agree on the new row maxima
@@ -751,7 +820,6 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
           if (a != 1.f) *resc_flag = 1;
         }
         sm100::bar_sync(kBarSoft, 128);
-        m_l = msm[lane % N];
         if (*resc_flag && i > 0) {  // O^T holds pages < i: rescale its columns once P.V(i-1) is done
           bool ok2 = sm100::mbar_wait(&B.p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, p.status,
                                       kTimeoutAccFull, kBudgetNs);
@@ -767,12 +835,11 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         uint32_t pk[N / 2];
-        const float mref_l = m_l == -INFINITY ? 0.f : m_l;
 #pragma unroll
-        for (int r = 0; r < N; r += 2) {
-          const float p0 = exp2f(sc[r] - __shfl_sync(0xffffffffu, mref_l, r)) * vs;
-          const float p1 = exp2f(sc[r + 1] - __shfl_sync(0xffffffffu, mref_l, r + 1)) * vs;
-          pk[r / 2] = mma::h2_u32(p0, p1);
+        for (int r = 0; r < N; r += 4) {
+          const float4 m4 = mr4[r / 4];
+          pk[r / 2] = mma::h2_u32(exp2f(sc[r] - m4.x) * vs, exp2f(sc[r + 1] - m4.y) * vs);
+          pk[r / 2 + 1] = mma::h2_u32(exp2f(sc[r + 2] - m4.z) * vs, exp2f(sc[r + 3] - m4.w) * vs);
         }
         // P' row of token st: N fp16 = N/8 chunks of 16 B, MN-major swizzled (64 B / 32 B rows)
         uint8_t* prow = ps + b * L::kPBytes + st * (N * 2);

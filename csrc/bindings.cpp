@@ -19,6 +19,7 @@ int oscar_kv_store(const oscar::StoreParams* p, cudaStream_t stream);
 int oscar_paged_attention(const oscar::AttnParams* p, cudaStream_t stream);
 int oscar_int2_attention_tc(const oscar::AttnParams* p, int rows_per_item, cudaStream_t stream);
 int oscar_attn_tc_trace(unsigned long long* buf);
+int oscar_gdn_trace(unsigned long long* buf);
 int oscar_bf16_attention_tc(const oscar::AttnParams* p, long long num_blocks, int rows_per_item, cudaStream_t stream);
 int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
 int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi, const __nv_bfloat16* Rv_lo,
@@ -283,6 +284,7 @@ void sample_pass(const Tensor& logits, int64_t vocab_begin, const Tensor& temp, 
 
 // Install a per-CTA timeline buffer for the tcgen05 attention kernel (0 removes it).
 void attn_tc_trace(int64_t ptr) { check_rc(oscar_attn_tc_trace(reinterpret_cast<unsigned long long*>(ptr)), "attn_tc_trace"); }
+void gdn_trace(int64_t ptr) { check_rc(oscar_gdn_trace(reinterpret_cast<unsigned long long*>(ptr)), "gdn_trace"); }
 
 int64_t num_sms() { return oscar_num_sms(); }
 
@@ -663,6 +665,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "oscar_b200 sm_100a kernels";
   m.def("gemm_i8", &gemm_i8);
   m.def("attn_tc_trace", &attn_tc_trace);
+  m.def("gdn_trace", &gdn_trace);
   m.def("gemm_i8_allreduce", &gemm_i8_allreduce);
   m.def("gemm_i8_split", &gemm_i8_split);
   m.def("gemm_i8_rs", &gemm_i8_rs);

@@ -387,6 +387,14 @@ OSCAR_DEVICE void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Optional per-CTA phase timeline of the decode kernel (globaltimer ns, 16 slots per CTA,
+// thread 0); off unless a buffer was installed with oscar_gdn_trace.
+__device__ unsigned long long* g_gdn_trace = nullptr;
+OSCAR_DEVICE void gdn_mark(unsigned long long* t, int ev) {
+  if (t != nullptr && threadIdx.x == 0)
+    t[((long long)blockIdx.y * gridDim.x + blockIdx.x) * 16 + ev] = globaltimer_ns();
+}
+
 __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
   __shared__ __align__(128) uint8_t sS[kD * 256];   // state, bf16 [dk][dv] swizzled
   __shared__ __align__(128) uint8_t sA[16 * 256];   // rows 0-7: k_t, 8-15: q_t (bf16 [tok][dk])
@@ -399,8 +407,9 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
   __shared__ float KK[kDecC][kDecC], KQ[kDecC][kDecC];
   __shared__ float Lg[kDecC], Bt[kDecC];
   __shared__ float red[kDecC][2][4];
-  __shared__ float pb_b[16], pb_a[16];
 
+  unsigned long long* const tr = g_gdn_trace;
+  gdn_mark(tr, 0);
   const int req = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int j = tid;
@@ -441,13 +450,39 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  if (tid < a) {
-    pb_b[tid] = __bfloat162float(pb[tid * 2 * p.Hv + h]);
-    pb_a[tid] = __bfloat162float(pb[tid * 2 * p.Hv + p.Hv + h]);
+  // ---- raw inputs of every token of the chunk, issued as independent loads (one
+  // memory latency for the chunk instead of one per token): pending tokens come from
+  // the kept raw inputs, new tokens from the projection output.  Only thread 0 reads
+  // the b / a gate inputs; it is also the only writer of this head's pending b / a,
+  // after its reads.
+  __nv_bfloat16 rq[kDecC], rk[kDecC], rv[kDecC], rz[kDecC], rb[kDecC], ra[kDecC];
+  const __nv_bfloat16 bzero = __float2bfloat16(0.f);
+#pragma unroll
+  for (int u = 0; u < kDecC; ++u) {
+    rq[u] = rk[u] = rv[u] = rz[u] = rb[u] = ra[u] = bzero;
+    const int t = u - a;
+    if (u < a) {
+      const __nv_bfloat16* prow = px + (long long)u * conv_dim;
+      rq[u] = prow[cq];
+      rk[u] = prow[ck];
+      rv[u] = prow[cv];
+      if (tid == 0) {
+        rb[u] = pb[u * 2 * p.Hv + h];
+        ra[u] = pb[u * 2 * p.Hv + p.Hv + h];
+      }
+    } else if (u < n) {
+      const __nv_bfloat16* row = p.qkvz + (long long)(t0 + t) * p.ld_qkvz + grp;
+      rq[u] = row[j];
+      rk[u] = row[p.dk + j];
+      rv[u] = row[2 * p.dk + hh * p.dv + j];
+      rz[u] = row[2 * p.dk + r * p.dv + hh * p.dv + j];
+      if (tid == 0) {
+        const __nv_bfloat16* barow = p.ba + (long long)(t0 + t) * p.ld_ba + (long long)gk * 2 * r;
+        rb[u] = barow[hh];
+        ra[u] = barow[r + hh];
+      }
+    }
   }
-  __syncthreads();
-
-  // ---- conv + SiLU of channel j for every token ----
   float wq[3], wk[3], wv[3], cwq[4], cwk[4], cwv[4];
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
@@ -461,6 +496,29 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
     cwk[i] = p.conv_w[ck * 4 + i];
     cwv[i] = p.conv_w[cv * 4 + i];
   }
+  const float A = -__expf(p.A_log[h]);
+  const float dtb = p.dt_bias[h];
+  // new tokens' raw inputs are kept pending for the next step
+  if (keep) {
+#pragma unroll
+    for (int u = 0; u < kDecC; ++u) {
+      if (u >= a && u < n) {
+        const int t = u - a;
+        __nv_bfloat16* pw = px_out + (long long)t * conv_dim;
+        if (hh == 0) {
+          pw[cq] = rq[u];
+          pw[ck] = rk[u];
+        }
+        pw[cv] = rv[u];
+        if (tid == 0) {
+          pb[t * 2 * p.Hv + h] = rb[u];
+          pb[t * 2 * p.Hv + p.Hv + h] = ra[u];
+        }
+      }
+    }
+  }
+
+  // ---- conv + SiLU of channel j for every token ----
   auto save_conv = [&]() {
     if (hh == 0)
       for (int i = 0; i < 3; ++i) {
@@ -474,47 +532,14 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
     save_conv();
     conv_saved = true;
   }
-  const float A = -__expf(p.A_log[h]);
-  const float dtb = p.dt_bias[h];
   float vv[kDecC], zz[kDecC], qv[kDecC], kv[kDecC];
   float sq_part[kDecC], sk_part[kDecC];
 #pragma unroll
   for (int u = 0; u < kDecC; ++u) {
-    vv[u] = zz[u] = qv[u] = kv[u] = 0.f;
+    vv[u] = qv[u] = kv[u] = 0.f;
+    zz[u] = __bfloat162float(rz[u]);
     if (u < n) {
-      float xq, xk, xv, braw, araw;
-      if (u < a) {
-        const __nv_bfloat16* prow = px + (long long)u * conv_dim;
-        xq = __bfloat162float(prow[cq]);
-        xk = __bfloat162float(prow[ck]);
-        xv = __bfloat162float(prow[cv]);
-        braw = pb_b[u];
-        araw = pb_a[u];
-      } else {
-        const int t = u - a;
-        const __nv_bfloat16* row = p.qkvz + (long long)(t0 + t) * p.ld_qkvz + grp;
-        const __nv_bfloat16* barow = p.ba + (long long)(t0 + t) * p.ld_ba + (long long)gk * 2 * r;
-        const __nv_bfloat16 bq = row[j], bk = row[p.dk + j], bv = row[2 * p.dk + hh * p.dv + j];
-        const __nv_bfloat16 bb = barow[hh], baa = barow[r + hh];
-        xq = __bfloat162float(bq);
-        xk = __bfloat162float(bk);
-        xv = __bfloat162float(bv);
-        braw = __bfloat162float(bb);
-        araw = __bfloat162float(baa);
-        zz[u] = __bfloat162float(row[2 * p.dk + r * p.dv + hh * p.dv + j]);
-        if (keep) {
-          __nv_bfloat16* pw = px_out + (long long)t * conv_dim;
-          if (hh == 0) {
-            pw[cq] = bq;
-            pw[ck] = bk;
-          }
-          pw[cv] = bv;
-          if (j == 0) {
-            pb[t * 2 * p.Hv + h] = bb;
-            pb[t * 2 * p.Hv + p.Hv + h] = baa;
-          }
-        }
-      }
+      const float xq = __bfloat162float(rq[u]), xk = __bfloat162float(rk[u]), xv = __bfloat162float(rv[u]);
       float q = cwq[3] * xq, k = cwk[3] * xk, v = cwv[3] * xv;
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
@@ -533,8 +558,8 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
       kv[u] = silu(k);
       vv[u] = silu(v);
       if (tid == 0) {
-        Bt[u] = sigmoidf_(braw);
-        Lg[u] = A * softplusf(araw + dtb);
+        Bt[u] = sigmoidf_(__bfloat162float(rb[u]));
+        Lg[u] = A * softplusf(__bfloat162float(ra[u]) + dtb);
       }
     }
     sq_part[u] = warp_sum(qv[u] * qv[u]);
@@ -548,6 +573,7 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
       red[u][1][warp] = sk_part[u];
     }
   __syncthreads();
+  gdn_mark(tr, 1);
   // ---- L2-normalised q (times 1/sqrt(dk)) and k: fp32 columns and bf16 MMA rows ----
   const float qscale = rsqrtf((float)p.dk);
 #pragma unroll
@@ -564,6 +590,7 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
   if (tid == 0)
     for (int u = 1; u < n; ++u) Lg[u] += Lg[u - 1];  // cumulative log decay
   __syncthreads();
+  gdn_mark(tr, 2);
   // ---- pairwise k_s.k_t and k_s.q_t (fp32) ----
   for (int pr = warp; pr < n * n; pr += kDecThreads / 32) {
     const int s_ = pr / n, t_ = pr % n;
@@ -581,8 +608,10 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
     }
   }
   // the state copies have landed (this thread's), and every thread's (barrier)
+  gdn_mark(tr, 3);
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
+  gdn_mark(tr, 4);
   // ---- pass 1 (tensor cores): rows 0-7 S0^T k_t, rows 8-15 S0^T q_t; warp w: columns 32w.. ----
   {
     float acc[4][4];
@@ -610,6 +639,7 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
     }
   }
   __syncthreads();
+  gdn_mark(tr, 5);
   // ---- per column: triangular solve for d_t, outputs o_t ----
   float dd[kDecC], ov[kDecC];
 #pragma unroll
@@ -649,6 +679,7 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
     }
   }
   __syncthreads();  // red (pass 1 values consumed) may be reused; sC complete
+  gdn_mark(tr, 6);
   if (lane == 0)
 #pragma unroll
     for (int u = 0; u < kDecC; ++u) red[u][0][warp] = os[u];
@@ -665,6 +696,7 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
       p.out[(long long)(t0 + u - a) * p.Hv * p.dv + h * p.dv + j] = __float2bfloat16(o);
     }
   }
+  gdn_mark(tr, 7);
   // ---- pass 2 (tensor cores): S_w = G_w S0 + K C; warp w: state rows 32w .. 32w+31 ----
   if (w >= 0) {
 #pragma unroll 1
@@ -712,6 +744,7 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
       }
     }
     __syncthreads();
+    gdn_mark(tr, 8);
     uint4* dst = reinterpret_cast<uint4*>(st);
 #pragma unroll 4
     for (int v = tid; v < kD * 16; v += kDecThreads) {
@@ -719,10 +752,16 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
       dst[v] = *reinterpret_cast<const uint4*>(sS + sw16(row, ch));
     }
   }
+  gdn_mark(tr, 9);
 }
 
 }  // namespace
 }  // namespace oscar
+
+// Install (or, with nullptr, remove) the per-CTA phase timeline of the decode kernel.
+extern "C" int oscar_gdn_trace(unsigned long long* buf) {
+  return (int)cudaMemcpyToSymbol(oscar::g_gdn_trace, &buf, sizeof(buf));
+}
 
 extern "C" int oscar_gdn_step(const oscar::GdnParams* params, int smem_state, cudaStream_t stream) {
   using namespace oscar;

@@ -102,7 +102,14 @@ def build_case(hist: int, batch: int, qlen: int, hq: int = 6, hk: int = 1, D: in
         stage = (sk.to(dev), sv.to(dev), owner.to(dev), rows)
     d = lambda t: t.to(dev)  # noqa: E731
     tok_req = torch.repeat_interleave(torch.arange(batch), torch.tensor([qlen] * batch)).to(torch.int32)
-    plan = A.plan_attention(q_start, seqs, hq // hk, hk, F.num_sms(dev), dev)
+    # the work list a serving step uses: fixed splits for decode / verify items
+    sms = F.num_sms(dev)
+    fixed = A.decode_splits(q_start, hq // hk, hk, sms) if qlen * hq // hk <= A.LONG_ROWS else 0
+    wt, first, count, max_rb, n_work, tt, n_short, rpi_short = A.plan_attention_host(
+        q_start, seqs, hq // hk, hk, sms, fixed_splits=fixed)
+    n_tiles = int((tt[:, 2] >= 0).sum()) if n_work > n_short else 0
+    plan = A.AttnPlan(torch.from_numpy(wt).to(dev), torch.from_numpy(first).to(dev), torch.from_numpy(count).to(dev),
+                      max_rb, n_work, torch.from_numpy(tt).to(dev), n_tiles, n_short, rpi_short)
     return dict(q=d(q), kf=d(kf), vf=d(vf), pool=d(pool), kc=d(kc), vc=d(vc), bt=d(bt), stage=stage,
                 q_start=q_start, seqs=seqs, q_start_t=d(torch.tensor(q_start, dtype=torch.int32)),
                 seq_lens_t=d(torch.tensor(seqs, dtype=torch.int32)), tok_req=d(tok_req), plan=plan, hq=hq, hk=hk,
@@ -133,7 +140,7 @@ def _kernel_only(c, kv_mode: int, use_tc: bool):
     def run():
         e.paged_attention(c["q"], c["kf"], c["vf"], c["hq"], c["hk"], c["D"], 1 / 16, kv_mode, c["pool"], c["kc"],
                           c["vc"], sk, sv, own, rows, c["bt"], c["q_start_t"], c["seq_lens_t"], plan.work, po, pl,
-                          None, rpi, tiles, plan.n_tiles if tiles is not None else 0, plan.n_short)
+                          None, rpi, tiles, plan.n_tiles if tiles is not None else 0, plan.n_short, None, 0, 0)
         return None
 
     return run
@@ -145,8 +152,8 @@ def kv_bytes(c, kv_mode: int) -> int:
     return c["pages"] * c["hk"] * per_page
 
 
-def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16_tc", "bf16")):
-    c = build_case(hist, batch, qlen)
+def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16_tc", "bf16"), hk=1):
+    c = build_case(hist, batch, qlen, hq=6 * hk, hk=hk)
     rows = qlen * c["hq"] // c["hk"]
     vs = [v for v in variants if not (v == "bf16_tc" and rows > 32)]
     # numerics: merged outputs against the first variant
@@ -185,12 +192,12 @@ def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16
 TRACE_EVENTS = {"issue": (8, 16), "qk": (16, 24), "kdone": (24, 32), "vdone": (32, 40), "pdone": (40, 48)}
 
 
-def trace_case(hist: int, batch: int, qlen: int, show: int = 3) -> dict:
+def trace_case(hist: int, batch: int, qlen: int, show: int = 3, hk: int = 1) -> dict:
     """Per-CTA timeline of the tcgen05 INT2 decode kernel (one traced launch after warm-up).
 
     Returns the kernel span, the CTA duration quantiles and, for the ``show`` longest CTAs,
     every recorded event relative to the CTA's start (µs)."""
-    c = build_case(hist, batch, qlen)
+    c = build_case(hist, batch, qlen, hq=6 * hk, hk=hk)
     fn = _kernel_only(c, 0, True)
     for _ in range(3):
         fn()
@@ -229,6 +236,8 @@ def main(argv=None):
     ap.add_argument("--batch", default="1,8,32")
     ap.add_argument("--qlen", default="1,4")
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--hk", type=int, default=1, help="KV heads (6 query heads each); 4 is the TP1 model")
+    ap.add_argument("--variants", default="int2_tc,int2_mma,bf16_tc,bf16")
     ap.add_argument("--prefill", action="store_true", help="also run the 9256-over-15360 continuation")
     ap.add_argument("--trace", action="store_true",
                     help="print the per-CTA timeline of the tcgen05 decode kernel instead of timing")
@@ -238,12 +247,13 @@ def main(argv=None):
         for hist in map(int, args.hist.split(",")):
             for batch in map(int, args.batch.split(",")):
                 for qlen in map(int, args.qlen.split(",")):
-                    print(json.dumps(trace_case(hist, batch, qlen)), flush=True)
+                    print(json.dumps(trace_case(hist, batch, qlen, hk=args.hk)), flush=True)
         return
     for hist in map(int, args.hist.split(",")):
         for batch in map(int, args.batch.split(",")):
             for qlen in map(int, args.qlen.split(",")):
-                for r in run_case(hist, batch, qlen, args.iters):
+                for r in run_case(hist, batch, qlen, args.iters, variants=tuple(args.variants.split(",")),
+                                  hk=args.hk):
                     print(json.dumps(r), flush=True)
     if args.prefill:
         for r in run_case(15360, 1, 9256, max(3, args.iters // 3), variants=("int2_tc", "int2_mma", "bf16")):

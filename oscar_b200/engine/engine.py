@@ -442,8 +442,7 @@ class LLMEngine:
             if static or decode_only:
                 # decode / verify steps use the fixed split layout whether or not they are
                 # replayed from a CUDA graph, so both paths compute the same partials
-                n_blocks = sum((q_start[i + 1] - q_start[i]) * self.g // A.ROWS + 1 for i in range(len(order)))
-                fixed = max(1, (3 * self.sms) // max(1, self.Hk * n_blocks))
+                fixed = A.decode_splits(q_start, self.g, self.Hk, self.sms)
             plan_np = A.plan_attention_host(q_start, seq_lens, self.g, self.Hk, self.sms, fixed_splits=fixed)
             arrays.update(work=plan_np[0], item_first=plan_np[1], item_count=plan_np[2], tiles=plan_np[5])
             meta["max_rb"], meta["n_work"] = plan_np[3], plan_np[4]

@@ -152,6 +152,14 @@ def plan_attention_host(q_start: list[int], seq_lens: list[int], g: int, Hk: int
     return wt, first, count, max_rb, n_work, tt, n_short, rpi_short
 
 
+def decode_splits(q_start: list[int], g: int, Hk: int, sms: int) -> int:
+    """Page-aligned splits per row block of a decode / verify step: about three CTAs per
+    SM over all (row block, KV head) pairs.  The result depends only on the batch shape,
+    which a replayed CUDA graph needs."""
+    n_blocks = sum((q_start[i + 1] - q_start[i]) * g // ROWS + 1 for i in range(len(q_start) - 1))
+    return max(1, (3 * sms) // max(1, Hk * n_blocks))
+
+
 def plan_attention(q_start: list[int], seq_lens: list[int], g: int, Hk: int, sms: int,
                    device, min_chunk: int = 256, waves: int = 3) -> AttnPlan:
     wt, first, count, max_rb, n_work, tt, n_short, rpi_short = plan_attention_host(q_start, seq_lens, g, Hk, sms,
