@@ -439,17 +439,6 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
   }
   const uint32_t sS_a = smem_u32(sS), sA_a = smem_u32(sA), sC_a = smem_u32(sC);
 
-  // state -> shared memory with asynchronous 16-byte copies (swizzled chunks); they
-  // stream in while the conv / gate / norm work below runs
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(st);
-#pragma unroll
-    for (int v = tid; v < kD * 16; v += kDecThreads) {
-      const int row = v >> 4, ch = v & 15;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sS_a + sw16(row, ch)), "l"(src + v) : "memory");
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  }
   // ---- raw inputs of every token of the chunk, issued as independent loads (one
   // memory latency for the chunk instead of one per token): pending tokens come from
   // the kept raw inputs, new tokens from the projection output.  Only thread 0 reads
@@ -495,6 +484,18 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
     cwq[i] = p.conv_w[cq * 4 + i];
     cwk[i] = p.conv_w[ck * 4 + i];
     cwv[i] = p.conv_w[cv * 4 + i];
+  }
+  // state -> shared memory with asynchronous 16-byte copies (swizzled chunks), issued
+  // after the chunk's input loads so that those are not queued behind 32 KB; they
+  // stream in while the conv / gate / norm work below runs
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(st);
+#pragma unroll
+    for (int v = tid; v < kD * 16; v += kDecThreads) {
+      const int row = v >> 4, ch = v & 15;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sS_a + sw16(row, ch)), "l"(src + v) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
   const float A = -__expf(p.A_log[h]);
   const float dtb = p.dt_bias[h];
@@ -591,20 +592,27 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
     for (int u = 1; u < n; ++u) Lg[u] += Lg[u - 1];  // cumulative log decay
   __syncthreads();
   gdn_mark(tr, 2);
-  // ---- pairwise k_s.k_t and k_s.q_t (fp32) ----
-  for (int pr = warp; pr < n * n; pr += kDecThreads / 32) {
-    const int s_ = pr / n, t_ = pr % n;
-    if (s_ > t_) continue;
+  // ---- pairwise (G_t / G_s) k_s.k_t and (G_t / G_s) k_s.q_t (fp32): pair (s, t) on two
+  // adjacent lanes, each summing half of the dims, decay factor folded in ----
+  {
+    const int pr = tid >> 1, half = tid & 1;
+    const int s_ = pr >> 3, t_ = pr & 7;
+    const bool live = s_ <= t_ && t_ < n;
     float kk = 0.f, kq = 0.f;
-    for (int i = lane; i < kD; i += 32) {
-      kk = fmaf(kT[i][s_], kT[i][t_], kk);
-      kq = fmaf(kT[i][s_], qT[i][t_], kq);
+    if (live) {
+#pragma unroll 8
+      for (int i = half * 64; i < half * 64 + 64; ++i) {
+        const float ks = kT[i][s_];
+        kk = fmaf(ks, kT[i][t_], kk);
+        kq = fmaf(ks, qT[i][t_], kq);
+      }
     }
-    kk = warp_sum(kk);
-    kq = warp_sum(kq);
-    if (lane == 0) {
-      KK[s_][t_] = kk;
-      KQ[s_][t_] = kq;
+    kk += __shfl_xor_sync(0xffffffffu, kk, 1);
+    kq += __shfl_xor_sync(0xffffffffu, kq, 1);
+    if (live && half == 0) {
+      const float e = __expf(Lg[t_] - Lg[s_]);
+      KK[s_][t_] = e * kk;
+      KQ[s_][t_] = e * kq;
     }
   }
   // the state copies have landed (this thread's), and every thread's (barrier)
@@ -649,7 +657,7 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
       float acc = vv[t] - __expf(Lg[t]) * kvq[t][j];
 #pragma unroll
       for (int s_ = 0; s_ < kDecC; ++s_)
-        if (s_ < t) acc -= __expf(Lg[t] - Lg[s_]) * KK[s_][t] * dd[s_];
+        if (s_ < t) acc = fmaf(-KK[s_][t], dd[s_], acc);  // KK holds (G_t / G_s) k_s.k_t
       dd[t] = Bt[t] * acc;
     }
   }
@@ -661,7 +669,7 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(GdnParams p) {
       o = __expf(Lg[u]) * kvq[8 + u][j];
 #pragma unroll
       for (int s_ = 0; s_ < kDecC; ++s_)
-        if (s_ <= u) o += __expf(Lg[u] - Lg[s_]) * KQ[s_][u] * dd[s_];
+        if (s_ <= u) o = fmaf(KQ[s_][u], dd[s_], o);  // KQ holds (G_u / G_s) k_s.q_u
     }
     ov[u] = o;
     os[u] = warp_sum(o * o);
