@@ -2,16 +2,19 @@
 // work items of at most 32 query rows: decode (q_len 1, rows = g) and MTP verify
 // (q_len 4, rows = 4 g = 24 for the 6:1 GQA of the target model).
 //
-// One CTA per (work item, KV head), 12 warps with fixed roles:
+// One CTA per (work item, KV head), 16 warps with fixed roles:
 //   warp 0      streams whole page-heads (17,408 B + 512 B of staging owner tags)
 //               into a 4-deep shared-memory ring with plain bulk copies, and owns
 //               the TMEM allocation (512 columns);
 //   warp 1      one thread issues every tcgen05.mma;
-//   warps 4-7   "converters": TMEM lane t.  For page i they widen the 2-bit codes
-//               to exact fp16 (0..3) straight into tensor memory - K codes of
-//               token t (A operand of S^T = K Q^T, M = 128 tokens, K = 256 dims)
-//               and the dim-major V codes of dims t and t+128 (A operand of
-//               O^T += V^T P'^T, M = 128 dims, K = 128 tokens);
+//   warps 2-3   row statistics (below);
+//   warps 4-7   "K converters": TMEM lane t.  For page i they widen the 2-bit K codes
+//               of token t to exact fp16 (0..3) straight into tensor memory (A operand
+//               of S^T = K Q^T, M = 128 tokens, K = 256 dims);
+//   warps 12-15 "V converters": TMEM lane t, the dim-major V codes of dims t and t+128
+//               (A operand of O^T += V^T P'^T, M = 128 dims, K = 128 tokens), beside
+//               the K converters: a warp stores about 45 B per cycle into TMEM, so
+//               the page's 128 KB of fp16 operands take two warpgroups;
 //   warps 8-11  "softmax": TMEM lane t = token t of the page.  They read the
 //               page's N scores of token t from TMEM, apply the per-token INT2
 //               scale (q.k = s (q.c + (z/s) sum(q)); the zero-point term comes
@@ -22,8 +25,14 @@
 // Operand placement keeps shared-memory traffic small: codes never go through
 // shared memory as fp16, only the 2-bit page (bulk copy), Q (once) and P' do.
 //
-// TMEM columns: [0,128) K codes, [128,384) two V^T buffers (2 halves x 64),
-// [384,384+2N) two S^T buffers, [448,448+2N) the O^T accumulator (2 halves).
+// TMEM columns: [0,256) K codes of two pages (double-buffered, so converting page i+1
+// overlaps the score MMAs of page i), [256,384) V^T in two token-half slots of 64
+// columns (tokens 0-63 and 64-127 of a page, each 2 dim halves x 32; a slot is refilled
+// for the next page while the other half's P.V runs), [384,384+2N) two S^T buffers,
+// [448,448+2N) the O^T accumulator (2 halves).
+// A kind::f16 MMA of M = 128, N = 32, K = 16 costs ~100 cycles whatever its operand
+// sources (about a fifth of the tensor rate at N = 256), so a page's 33 MMAs are the
+// kernel's floor (~1.7 us); the buffers exist to keep the tensor pipe busy back to back.
 //
 // Softmax bookkeeping.  A row's running max only moves when some score of the
 // page exceeds it by more than 2^8 (the probabilities stay <= 256, well inside
@@ -54,13 +63,14 @@ constexpr int kD = 256;
 constexpr int kPage = 128;
 constexpr int kPartRows = 64;  // row stride of the split-KV partials (shared with the merge)
 constexpr int kRing = 4;
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
 constexpr int kPageBytes = 17408;
 constexpr int kSlot = kPageBytes + kPage * 4;  // page + owner tags
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kSlack = 8.f;
 constexpr uint64_t kBudgetNs = 2000000000ull;
-constexpr uint32_t kColK = 0, kColV = 128, kColS = 384, kColO = 448, kTmemCols = 512;
+// K codes double-buffered (two pages of 128 columns), one V^T page, two S^T buffers, O^T
+constexpr uint32_t kColK = 0, kColV = 256, kColS = 384, kColO = 448, kTmemCols = 512;
 constexpr int kBarSoft = 1, kBarStats = 3;
 // Initial running maximum: finite, so that exp2(s - m) needs no special case for rows
 // without a visible key yet (their scores are -inf), and any visible score moves it.
@@ -80,9 +90,9 @@ OSCAR_DEVICE float folded_zs(float ks, float kz) {
 OSCAR_DEVICE bool zs_folded(float ks, float kz) { return ks != 0.f && fabsf(kz / ks) <= kZsMax; }
 
 // Optional per-CTA event timeline (globaltimer ns) for performance analysis; off
-// unless a buffer was installed with oscar_attn_tc_trace (slot layout: 96 u64 per CTA).
+// unless a buffer was installed with oscar_attn_tc_trace (slot layout: 128 u64 per CTA).
 __device__ unsigned long long* g_tc_trace = nullptr;
-constexpr int kTraceSlots = 96;
+constexpr int kTraceSlots = 128;
 // The trace buffer pointer is read once per CTA (kernel start) so that a trace point costs
 // a timer read and a store, not a global load.
 OSCAR_DEVICE void trace(unsigned long long* t, int ev) {
@@ -182,7 +192,7 @@ __device__ __noinline__ void v_half_mixed(uint32_t taddr, uint4 cw, uint64_t sm,
   }
   if (sm != 0ull) {
     const float4* s4 = reinterpret_cast<const float4*>(srow);
-#pragma unroll 4
+#pragma unroll 8
     for (int q = 0; q < 16; ++q) {
       const float4 v = __ldg(s4 + q);
       const uint32_t lo = mma::h2_u32(v.x, v.y), hi = mma::h2_u32(v.z, v.w);
@@ -234,7 +244,7 @@ struct TcLayout {
   // Q side [N rows][sum(q) hi, lo, hi, 0...], K side [128 tokens][z' hi, hi, lo, 0...]
   static constexpr int kQzOff = kQOff + kQBytes;
   static constexpr int kZaOff = kQzOff + N * 32;
-  static constexpr int kPOff = kZaOff + kPage * 32;
+  static constexpr int kPOff = kZaOff + 2 * kPage * 32;
   static constexpr int kPBytes = kPage * N * 2;  // one P' buffer: 128 tokens x N fp16
   static constexpr int kMisc = kPOff + 2 * kPBytes;
   static constexpr int kSq = kMisc;                  // N floats: sum(q) per row
@@ -250,7 +260,7 @@ struct TcLayout {
   static constexpr int kTmemSlot = kSlotBlk + kRing * 4;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kBars = (kAbort + 4 + 7) / 8 * 8;
-  static constexpr int kNumBars = 2 * kRing + 2 + 2 * 6 + 2;
+  static constexpr int kNumBars = 2 * kRing + 2 * 8 + 2;
   static constexpr int kTotal = kBars + kNumBars * 8;
   // at least half the SM's shared memory: one CTA per SM (it holds all 512 TMEM columns)
   static constexpr int kAlloc = (kTotal > 120 * 1024 ? kTotal : 120 * 1024) + 1024;  // + base alignment
@@ -259,10 +269,10 @@ struct TcLayout {
 struct Bars {
   uint64_t* raw_full;   // [kRing]
   uint64_t* raw_empty;  // [kRing]
-  uint64_t* k_full;
-  uint64_t* k_empty;
-  uint64_t* v_full;   // [2]
-  uint64_t* v_empty;  // [2]
+  uint64_t* k_full;     // [2]
+  uint64_t* k_empty;    // [2]
+  uint64_t* v_full;     // [2] token halves of the V page
+  uint64_t* v_empty;    // [2]
   uint64_t* s_full;   // [2]
   uint64_t* s_empty;  // [2]
   uint64_t* p_full;   // [2]
@@ -321,9 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kBars);
-  Bars B{bar, bar + kRing, bar + 2 * kRing, bar + 2 * kRing + 1, bar + 2 * kRing + 2, bar + 2 * kRing + 4,
-         bar + 2 * kRing + 6, bar + 2 * kRing + 8, bar + 2 * kRing + 10, bar + 2 * kRing + 12, bar + 2 * kRing + 14,
-         bar + 2 * kRing + 15};
+  Bars B{bar, bar + kRing, bar + 2 * kRing, bar + 2 * kRing + 2, bar + 2 * kRing + 4, bar + 2 * kRing + 6,
+         bar + 2 * kRing + 8, bar + 2 * kRing + 10, bar + 2 * kRing + 12, bar + 2 * kRing + 14, bar + 2 * kRing + 16,
+         bar + 2 * kRing + 17};
 
   const int item = blockIdx.x, hk = blockIdx.y;
   const int4 w = p.work[item];
@@ -348,12 +358,12 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
   }
   if (tid == 32) {
     for (int i = 0; i < L::kNumBars; ++i) sm100::mbar_init(&bar[i], 1);
-    for (int s = 0; s < kRing; ++s) sm100::mbar_init(&B.raw_empty[s], 10);  // 4 converter, 4 softmax, 2 stats warps
+    for (int s = 0; s < kRing; ++s) sm100::mbar_init(&B.raw_empty[s], 14);  // 4 + 4 converter, 4 softmax, 2 stats warps
     for (int b = 0; b < 2; ++b) sm100::mbar_init(&B.p_empty[b], 3);       // P.V commit + 2 stats warps
     sm100::mbar_init(B.stats_done, 2);
-    sm100::mbar_init(B.k_full, 4);
     for (int b = 0; b < 2; ++b) {
       sm100::mbar_init(&B.v_full[b], 4);
+      sm100::mbar_init(&B.k_full[b], 4);
       sm100::mbar_init(&B.s_empty[b], 4);
       sm100::mbar_init(&B.p_full[b], 4);
     }
@@ -391,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     *reinterpret_cast<uint4*>(qz + tid * 32 + (sw << 4)) = make_uint4(w0, w1, 0u, 0u);
     *reinterpret_cast<uint4*>(qz + tid * 32 + ((sw ^ 1) << 4)) = make_uint4(0u, 0u, 0u, 0u);
   }
-  for (int idx = tid; idx < kPage * 2; idx += kThreads)
+  for (int idx = tid; idx < 2 * kPage * 2; idx += kThreads)
     *reinterpret_cast<uint4*>(za + idx * 16) = make_uint4(0u, 0u, 0u, 0u);
   sm100::fence_proxy_async();  // Q tile: generic writes -> tensor-core reads
   sm100::tc_fence_before();
@@ -407,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       int issued = 0;
       for (int i = 0; i < n_pages; ++i) {
         const int s = i % kRing;
-        if (i >= kRing && !sm100::mbar_wait(&B.raw_empty[s], ((i / kRing) - 1) & 1, abort_flag, p.status,
+        if (i >= kRing && !sm100::mbar_wait_sleep(&B.raw_empty[s], ((i / kRing) - 1) & 1, abort_flag, p.status,
                                             kTimeoutSlotEmpty, kBudgetNs))
           break;
         const int blk = bt[p_first + i];
@@ -439,47 +449,56 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       const uint64_t qzd = sm100::smem_desc(sm100::smem_addr(qz), 16, 256, 6);
       constexpr uint32_t kPLayout = N == 32 ? 4u : 6u;  // P' rows of N fp16: 64 B / 32 B swizzle
       constexpr uint32_t kPAtom = 8 * N * 2;           // 8 tokens
+      // P.V of page j, one token half (one V slot) at a time: the V converters refill
+      // a slot while the other half's MMAs run
       auto pv = [&](int j) -> bool {
-        if (!sm100::mbar_wait(&B.v_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs))
+        if (!sm100::mbar_wait_sleep(&B.p_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs))
           return false;
-        if (!sm100::mbar_wait(&B.p_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs))
-          return false;
-        sm100::tc_fence_after();
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {
+          if (!sm100::mbar_wait_sleep(&B.v_full[hf], j & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs))
+            return false;
+          sm100::tc_fence_after();
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint64_t bd =
-                sm100::smem_desc(pa + (j & 1) * L::kPBytes + ks * 2 * kPAtom, 16, kPAtom, kPLayout);
-            sm100::umma_f16_tmem_a(tbase + kColO + h * N, tbase + kColV + (j & 1) * 128 + h * 64 + ks * 8, bd, idp,
-                                   (j > 0 || ks > 0) ? 1u : 0u);
-          }
-        sm100::umma_commit(&B.v_empty[j & 1]);
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t bd = sm100::smem_desc(pa + (j & 1) * L::kPBytes + (hf * 4 + ks) * 2 * kPAtom, 16, kPAtom,
+                                                   kPLayout);
+              sm100::umma_f16_tmem_a(tbase + kColO + h * N, tbase + kColV + hf * 64 + h * 32 + ks * 8, bd, idp,
+                                     (j > 0 || hf > 0 || ks > 0) ? 1u : 0u);
+            }
+          sm100::umma_commit(&B.v_empty[hf]);
+        }
         sm100::umma_commit(&B.p_empty[j & 1]);
         return true;
       };
       bool ok = true;
       for (int i = 0; i < n_pages && ok; ++i) {
-        if (!sm100::mbar_wait(B.k_full, i & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs)) {
+        if (!sm100::mbar_wait_sleep(&B.k_full[i & 1], (i >> 1) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs)) {
           ok = false;
           break;
         }
-        if (i >= 2 && !sm100::mbar_wait(&B.s_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
+        if (i < 4) trace(tr, 88 + i);
+        if (i >= 2 && !sm100::mbar_wait_sleep(&B.s_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
                                         kTimeoutAccEmpty, kBudgetNs)) {
           ok = false;
           break;
         }
         sm100::tc_fence_after();
+        const unsigned long long mc0 = (tr != nullptr) ? clock64() : 0ull;
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
           const uint64_t qd = sm100::smem_desc(qa + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024, 2);
-          sm100::umma_f16_tmem_a(tbase + kColS + (i & 1) * N, tbase + kColK + kk * 8, qd, idq, kk > 0 ? 1u : 0u);
+          sm100::umma_f16_tmem_a(tbase + kColS + (i & 1) * N, tbase + kColK + (i & 1) * 128 + kk * 8, qd, idq,
+                                 kk > 0 ? 1u : 0u);
         }
         // + (z/s) sum(q): K-side and Q-side tiles in shared memory, 32-byte swizzle
-        sm100::umma_bf16(tbase + kColS + (i & 1) * N, zad, qzd, idq, 1u);
+        sm100::umma_bf16(tbase + kColS + (i & 1) * N, zad + (uint64_t)(((i & 1) * kPage * 32) >> 4), qzd, idq, 1u);
+        if (i < 4 && tr != nullptr) trace_val(tr, 112 + i, clock64() - mc0);
         sm100::umma_commit(&B.s_full[i & 1]);
         if (i < 8) trace(tr, 16 + i);
-        sm100::umma_commit(B.k_empty);
+        sm100::umma_commit(&B.k_empty[i & 1]);
         if (i >= 1) ok = pv(i - 1);
       }
       if (ok && n_pages > 0) pv(n_pages - 1);
@@ -491,125 +510,164 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     }
     __syncwarp();
   } else if (warp >= 4 && warp < 8) {
-    // ------------------------------------------------------------ converters
+    // ------------------------------------------------------------ K converters
     const int ct = tid - 128;  // TMEM lane
     const uint32_t lrow = (uint32_t)(ct & ~31) << 16;
-    // No named barriers in this loop: every warp arrives on the mbarriers itself, so a
-    // warp whose bounded wait expires simply leaves (the others time out in turn).
+    // No named barriers in the converter loops: every warp arrives on the mbarriers
+    // itself, so a warp whose bounded wait expires simply leaves (the others time out
+    // in turn).  K of page i goes to TMEM slot i & 1, free once S(i - 2) is done.
     for (int i = 0; i < n_pages; ++i) {
-      const int s = i % kRing;
-      if (!sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs))
-        break;
-      if (i >= 1 && !sm100::mbar_wait(B.k_empty, (i - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs))
-        break;
-      const uint8_t* pg = ring + s * kSlot;
-      const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
-      const int blk = slot_blk[s];
-      const int page_pos = (p_first + i) * kPage;
-      // Tokens that carry values, as 128-bit masks computed by every warp for itself
-      // (lane l looks at tokens l, 32 + l, 64 + l, 96 + l): staged sink/recent tokens
-      // (owner tag == block, read from the staging arena; this includes current-chunk
-      // tokens that were staged in this step - the same values) and current-chunk
-      // tokens that are not staged (read from the fresh buffer).
-      uint32_t smk[4], fmk[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int tj = 32 * q + lane, ps_ = page_pos + tj;
-        const bool in = ps_ >= kv_begin && ps_ < kv_stop;
-        const bool stg = in && staging && own[tj] == blk;
-        const bool frs = in && !stg && ps_ >= prefix;
-        smk[q] = __ballot_sync(0xffffffffu, stg);
-        fmk[q] = __ballot_sync(0xffffffffu, frs);
-      }
-      sm100::tc_fence_after();
-      {
-        // K codes of token ct -> 128 columns of fp16 pairs
-        const int j = ct, pos = page_pos + j;
-        const bool in = pos >= kv_begin && pos < kv_stop;
-        const bool stg_j = in && staging && own[j] == blk;
-        const int kind = !in ? 0 : stg_j ? 2 : pos >= prefix ? 1 : 3;
+        const int s = i % kRing;
+        if (!sm100::mbar_wait_sleep(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull,
+                                    kBudgetNs))
+          break;
+        if (i >= 2 && !sm100::mbar_wait_sleep(&B.k_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
+                                              kTimeoutAccEmpty, kBudgetNs))
+          break;
+        const uint32_t kcol = kColK + (i & 1) * 128;
+        uint8_t* zrow = za + (i & 1) * kPage * 32;
+        if (ct == 0 && i < 4) trace(tr, 84 + i);
+        const unsigned long long kc0 = (tr != nullptr) ? clock64() : 0ull;
+        const uint8_t* pg = ring + s * kSlot;
+        const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
+        const int blk = slot_blk[s];
+        const int page_pos = (p_first + i) * kPage;
+        sm100::tc_fence_after();
         {
-          // zero-point row of token j for the S MMA's extra K-step: (z/s hi, z/s hi, z/s lo)
-          // against (sum(q) hi, lo, hi) on the Q side
-          const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * 64);
-          const float zs = kind == 3 ? folded_zs(__half2float(meta[j]), __half2float(meta[kPage + j])) : 0.f;
-          const __half zh = __float2half_rn(zs), zl = __float2half_rn(zs - __half2float(zh));
-          *reinterpret_cast<uint4*>(za + j * 32 + (((j >> 2) & 1) << 4)) =
-              make_uint4(pack_h2(zh, zh), pack_h2(zl, __float2half_rn(0.f)), 0u, 0u);
-        }
-        if (__any_sync(0xffffffffu, kind == 1 || kind == 2)) {
-          const __half* kf = kind == 1 ? p.k_fresh + ((long long)(q0 + pos - prefix) * p.Hk + hk) * kD : nullptr;
-          const float* sk = kind == 2 ? p.stage_k + ((long long)(stage_row_of(p, req, p_first + i, blk) * kPage + j) * p.Hk + hk) * kD
-                                      : nullptr;
-          k_row_mixed(tbase + lrow + kColK, pg, j, kind, kf, sk);
-        } else {
-          // out-of-range tokens keep their (finite) codes: their scores are masked
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            k_chunk_codes(pg, j, c, r);
-            sm100::tmem_st_32x32b_x32(tbase + lrow + kColK + 32 * c, r);
+          // K codes of token ct -> 128 columns of fp16 pairs
+          const int j = ct, pos = page_pos + j;
+          const bool in = pos >= kv_begin && pos < kv_stop;
+          const bool stg_j = in && staging && own[j] == blk;
+          const int kind = !in ? 0 : stg_j ? 2 : pos >= prefix ? 1 : 3;
+          {
+            // zero-point row of token j for the S MMA's extra K-step: (z/s hi, z/s hi, z/s lo)
+            // against (sum(q) hi, lo, hi) on the Q side
+            const __half* meta = reinterpret_cast<const __half*>(pg + 2 * kPage * 64);
+            const float zs = kind == 3 ? folded_zs(__half2float(meta[j]), __half2float(meta[kPage + j])) : 0.f;
+            const __half zh = __float2half_rn(zs), zl = __float2half_rn(zs - __half2float(zh));
+            *reinterpret_cast<uint4*>(zrow + j * 32 + (((j >> 2) & 1) << 4)) =
+                make_uint4(pack_h2(zh, zh), pack_h2(zl, __float2half_rn(0.f)), 0u, 0u);
           }
-        }
-        sm100::tmem_st_wait();
-        sm100::tc_fence_before();
-      }
-      sm100::fence_proxy_async();  // zero-point row: generic write -> tensor-core read
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(B.k_full);
-      if (ct == 0 && i < 8) trace(tr, 24 + i);
-
-      // V^T of dims ct and ct + 128 -> 2 x 64 columns
-      if (i >= 2 && !sm100::mbar_wait(&B.v_empty[i & 1], ((i >> 1) - 1) & 1, abort_flag, p.status,
-                                      kTimeoutAccEmpty, kBudgetNs))
-        break;
-      sm100::tc_fence_after();
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const int d = ct + 128 * h;
-        const uint4* src = reinterpret_cast<const uint4*>(pg + kPage * 64 + d * 32);
-#pragma unroll 1
-        for (int hf = 0; hf < 2; ++hf) {
-          const uint4 cw = src[hf];
-          const uint32_t taddr = tbase + lrow + kColV + (i & 1) * 128 + h * 64 + hf * 32;
-          const uint64_t sm = hf ? ((uint64_t)smk[3] << 32) | smk[2] : ((uint64_t)smk[1] << 32) | smk[0];
-          const uint64_t fm = hf ? ((uint64_t)fmk[3] << 32) | fmk[2] : ((uint64_t)fmk[1] << 32) | fmk[0];
-          if ((sm | fm) != 0ull) {
-            // staged tokens: this dim's 64 values of the page half are contiguous fp32
-            // in the dim-major staging arena
-            const float* srow = sm != 0ull ? p.stage_v + ((long long)stage_row_of(p, req, p_first + i, blk) * p.Hk + hk) *
-                                                     kD * kPage +
-                                                 (long long)d * kPage + hf * 64
-                                           : nullptr;
-            const long long fbase = ((long long)(q0 + page_pos + hf * 64 - prefix) * p.Hk + hk) * kD + d;
-            v_half_mixed(taddr, cw, sm, fm, srow, p.v_fresh, fbase, (long long)p.Hk * kD);
+          if (__any_sync(0xffffffffu, kind == 1 || kind == 2)) {
+            const __half* kf = kind == 1 ? p.k_fresh + ((long long)(q0 + pos - prefix) * p.Hk + hk) * kD : nullptr;
+            const float* sk = kind == 2 ? p.stage_k + ((long long)(stage_row_of(p, req, p_first + i, blk) * kPage + j) *
+                                                           p.Hk + hk) * kD
+                                        : nullptr;
+            k_row_mixed(tbase + lrow + kcol, pg, j, kind, kf, sk);
           } else {
-            uint32_t r[32];
-            const uint32_t w4[4] = {cw.x, cw.y, cw.z, cw.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t x4[4], y4[4];
-              mma::codes8_to_h2(w4[q], x4);
-              mma::codes8_to_h2(w4[q] >> 8, y4);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                r[8 * q + e] = x4[e];
-                r[8 * q + 4 + e] = y4[e];
-              }
+            // out-of-range tokens keep their (finite) codes: their scores are masked
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              k_chunk_codes(pg, j, c, r);
+              sm100::tmem_st_32x32b_x32(tbase + lrow + kcol + 32 * c, r);
             }
-            sm100::tmem_st_32x32b_x32(taddr, r);
+          }
+          const unsigned long long kc1 = (tr != nullptr) ? clock64() : 0ull;
+          sm100::tmem_st_wait();
+          sm100::tc_fence_before();
+          if (ct == 0 && i < 4) {
+            const unsigned long long kc2 = clock64();
+            trace_val(tr, 96 + i, kc1 - kc0);
+            trace_val(tr, 100 + i, kc2 - kc1);
           }
         }
-      }
-      sm100::tmem_st_wait();
-      sm100::tc_fence_before();
-      __syncwarp();
-      if (ct == 0 && i < 8) trace(tr, 32 + i);
-      if (lane == 0) {
-        sm100::mbar_arrive(&B.v_full[i & 1]);
-        sm100::mbar_arrive(&B.raw_empty[s]);
-      }
-    }
+        sm100::fence_proxy_async();  // zero-point row: generic write -> tensor-core read
+        __syncwarp();
+        if (lane == 0) {
+          sm100::mbar_arrive(&B.k_full[i & 1]);
+          sm100::mbar_arrive(&B.raw_empty[s]);
+        }
+        if (ct == 0 && i < 8) trace(tr, 24 + i);
+          }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------ V converters
+    // V^T of page i into the two token-half slots, each free once P.V(i - 1) of that
+    // half is done; they run beside the K converters, so a page's two conversions overlap.
+    const int ct = tid - 384;  // TMEM lane
+    const uint32_t lrow = (uint32_t)(ct & ~31) << 16;
+    uint32_t smk[4], fmk[4];  // value-token masks of the page
+    for (int i = 0; i < n_pages; ++i) {
+        // V^T of page i, dims ct and ct + 128 -> 2 x 64 columns
+        const int s = i % kRing;
+        if (!sm100::mbar_wait_sleep(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull,
+                                    kBudgetNs))
+          break;
+        const uint8_t* pg = ring + s * kSlot;
+        const int* own = reinterpret_cast<const int*>(pg + kPageBytes);
+        const int blk = slot_blk[s];
+        const int page_pos = (p_first + i) * kPage;
+        // Tokens that carry values, as 128-bit masks computed by every warp for itself
+        // (lane l looks at tokens l, 32 + l, 64 + l, 96 + l): staged sink/recent tokens
+        // (owner tag == block, read from the staging arena; this includes current-chunk
+        // tokens that were staged in this step - the same values) and current-chunk
+        // tokens that are not staged (read from the fresh buffer).
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int tj = 32 * q + lane, ps_ = page_pos + tj;
+          const bool in = ps_ >= kv_begin && ps_ < kv_stop;
+          const bool stg = in && staging && own[tj] == blk;
+          const bool frs = in && !stg && ps_ >= prefix;
+          smk[q] = __ballot_sync(0xffffffffu, stg);
+          fmk[q] = __ballot_sync(0xffffffffu, frs);
+        }
+        bool vok = true;
+#pragma unroll 1
+        for (int hf = 0; hf < 2 && vok; ++hf) {
+          // slot hf holds tokens 64 hf .. 64 hf + 63 of the page; free once P.V(i - 1) of
+          // that half is done
+          if (i >= 1 && !sm100::mbar_wait_sleep(&B.v_empty[hf], (i - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty,
+                                                kBudgetNs)) {
+            vok = false;
+            break;
+          }
+          if (ct == 0 && i < 4 && hf == 0) trace(tr, 92 + i);
+          const unsigned long long vc0 = (tr != nullptr) ? clock64() : 0ull;
+          sm100::tc_fence_after();
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const int d = ct + 128 * h;
+            const uint4 cw = reinterpret_cast<const uint4*>(pg + kPage * 64 + d * 32)[hf];
+            const uint32_t taddr = tbase + lrow + kColV + hf * 64 + h * 32;
+            const uint64_t sm = hf ? ((uint64_t)smk[3] << 32) | smk[2] : ((uint64_t)smk[1] << 32) | smk[0];
+            const uint64_t fm = hf ? ((uint64_t)fmk[3] << 32) | fmk[2] : ((uint64_t)fmk[1] << 32) | fmk[0];
+            if ((sm | fm) != 0ull) {
+              // staged tokens: this dim's 64 values of the page half are contiguous fp32
+              // in the dim-major staging arena
+              const float* srow = sm != 0ull ? p.stage_v +
+                                                   ((long long)stage_row_of(p, req, p_first + i, blk) * p.Hk + hk) *
+                                                       kD * kPage +
+                                                   (long long)d * kPage + hf * 64
+                                             : nullptr;
+              const long long fbase = ((long long)(q0 + page_pos + hf * 64 - prefix) * p.Hk + hk) * kD + d;
+              v_half_mixed(taddr, cw, sm, fm, srow, p.v_fresh, fbase, (long long)p.Hk * kD);
+            } else {
+              uint32_t r[32];
+              const uint32_t w4[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint32_t x4[4], y4[4];
+                mma::codes8_to_h2(w4[q], x4);
+                mma::codes8_to_h2(w4[q] >> 8, y4);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  r[8 * q + e] = x4[e];
+                  r[8 * q + 4 + e] = y4[e];
+                }
+              }
+              sm100::tmem_st_32x32b_x32(taddr, r);
+            }
+          }
+          if (hf == 1 && ct == 0 && i < 4 && tr != nullptr) trace_val(tr, 104 + i, clock64() - vc0);
+          sm100::tmem_st_wait();
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(&B.v_full[hf]);
+        }
+        if (!vok) break;
+        if (ct == 0 && i < 8) trace(tr, 32 + i);
+        if (lane == 0) sm100::mbar_arrive(&B.raw_empty[s]);
+          }
   } else if (warp == 2 || warp == 3) {
     // ------------------------------------------------------------ row statistics
     // l_r = sum_j p_jr and C_r = sum_j p_jr z_vj, read back from the fp16 P' tile the
@@ -623,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     bool dead = false, aborted = false;
     for (int i = 0; i < n_pages; ++i) {
       const int s = i % kRing, b = i & 1;
-      bool ok = !dead && sm100::mbar_wait(&B.p_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
+      bool ok = !dead && sm100::mbar_wait_sleep(&B.p_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
                                           kBudgetNs);
       if (ok) {
         // per-token coefficients (1/s_v, z_v/s_v) of this page
@@ -687,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     }
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(B.stats_done);
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ------------------------------------------------------------ softmax
     const int st = tid - 256;  // TMEM lane = token of the page
     const int swarp = st >> 5;
@@ -703,7 +761,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     bool dead = false, aborted = false;
     for (int i = 0; i < n_pages; ++i) {
       const int s = i % kRing, b = i & 1;
-      bool ok = !dead && sm100::mbar_wait(&B.s_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
+      bool ok = !dead && sm100::mbar_wait_sleep(&B.s_full[b], (i >> 1) & 1, abort_flag, p.status, kTimeoutAccFull,
                                           kBudgetNs);
       if (st == 0 && i < 4) trace(tr, 48 + 4 * i);
       float sc[N];
@@ -720,7 +778,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         if (lane == 0) sm100::mbar_arrive(&B.s_empty[b]);
 #pragma unroll
         for (int r = 0; r < N; ++r) sc[r] = __uint_as_float(raw[r]);
-        ok = sm100::mbar_wait(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs);
+        ok = sm100::mbar_wait_sleep(&B.raw_full[s], (i / kRing) & 1, abort_flag, p.status, kTimeoutTmaFull, kBudgetNs);
       }
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform before the shuffles below
       if (st == 0 && i < 4) trace(tr, 49 + 4 * i);
@@ -786,7 +844,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
       }
       // P' buffer b (and alpha/upd slot b) are free once P.V(i-2) and the stats of page i-2 are done
       if (ok && i >= 2)
-        ok = sm100::mbar_wait(&B.p_empty[b], ((i >> 1) - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
+        ok = sm100::mbar_wait_sleep(&B.p_empty[b], ((i >> 1) - 1) & 1, abort_flag, p.status, kTimeoutAccEmpty, kBudgetNs);
       if (st == 0 && i < 4) trace(tr, 50 + 4 * i);
       // one barrier on the common path: abort and "a maximum moved" are both rare
       bool upd_now = false;
@@ -821,7 +879,7 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
         }
         sm100::bar_sync(kBarSoft, 128);
         if (*resc_flag && i > 0) {  // O^T holds pages < i: rescale its columns once P.V(i-1) is done
-          bool ok2 = sm100::mbar_wait(&B.p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, p.status,
+          bool ok2 = sm100::mbar_wait_sleep(&B.p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, p.status,
                                       kTimeoutAccFull, kBudgetNs);
           if (ok2) {
             sm100::tc_fence_after();
@@ -861,9 +919,9 @@ __global__ void __launch_bounds__(kThreads, 1) int2_attention_tc_kernel(AttnPara
     if (!aborted) aborted = sm100::bar_red_or(kBarSoft, 128, dead);  // every softmax warp agrees
     if (!aborted) {
       // ---- output: out[r, d] = (O^T[d, r] + C_r) / l_r
-      bool ok = sm100::mbar_wait(B.stats_done, 0, abort_flag, p.status, kTimeoutAccFull, kBudgetNs);
+      bool ok = sm100::mbar_wait_sleep(B.stats_done, 0, abort_flag, p.status, kTimeoutAccFull, kBudgetNs);
       if (ok && n_pages > 0)
-        ok = sm100::mbar_wait(&B.p_empty[(n_pages - 1) & 1], ((n_pages - 1) >> 1) & 1, abort_flag, p.status,
+        ok = sm100::mbar_wait_sleep(&B.p_empty[(n_pages - 1) & 1], ((n_pages - 1) >> 1) & 1, abort_flag, p.status,
                               kTimeoutAccFull, kBudgetNs);
       // every softmax warp agrees before the named barrier below
       if (!sm100::bar_red_or(kBarSoft, 128, !ok)) {

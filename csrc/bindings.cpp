@@ -20,6 +20,8 @@ int oscar_paged_attention(const oscar::AttnParams* p, cudaStream_t stream);
 int oscar_int2_attention_tc(const oscar::AttnParams* p, int rows_per_item, cudaStream_t stream);
 int oscar_attn_tc_trace(unsigned long long* buf);
 int oscar_gdn_trace(unsigned long long* buf);
+int oscar_mma_rate(int a_smem, int chains, int n, int iters, unsigned long long* out, cudaStream_t s);
+int oscar_tmem_store_rate(int nwarps, int width, int iters, unsigned long long* out, cudaStream_t s);
 int oscar_bf16_attention_tc(const oscar::AttnParams* p, long long num_blocks, int rows_per_item, cudaStream_t stream);
 int oscar_attn_merge(const oscar::MergeParams* p, cudaStream_t stream);
 int oscar_attn_merge_rot(const oscar::MergeParams* p, const __nv_bfloat16* Rv_hi, const __nv_bfloat16* Rv_lo,
@@ -285,6 +287,28 @@ void sample_pass(const Tensor& logits, int64_t vocab_begin, const Tensor& temp, 
 // Install a per-CTA timeline buffer for the tcgen05 attention kernel (0 removes it).
 void attn_tc_trace(int64_t ptr) { check_rc(oscar_attn_tc_trace(reinterpret_cast<unsigned long long*>(ptr)), "attn_tc_trace"); }
 void gdn_trace(int64_t ptr) { check_rc(oscar_gdn_trace(reinterpret_cast<unsigned long long*>(ptr)), "gdn_trace"); }
+
+// Tensor-core / TMEM rate microbenchmarks (one CTA on the current device): cycle counts.
+std::vector<int64_t> mma_rate(int64_t a_smem, int64_t chains, int64_t n, int64_t iters) {
+  auto out = at::zeros({8}, at::TensorOptions().dtype(at::kLong).device(at::kCUDA));
+  check_rc(oscar_mma_rate((int)a_smem, (int)chains, (int)n, (int)iters,
+                          reinterpret_cast<unsigned long long*>(out.data_ptr<int64_t>()),
+                          stream()),
+           "mma_rate");
+  auto h = out.cpu();
+  return {h[0].item<int64_t>(), h[1].item<int64_t>()};
+}
+std::vector<int64_t> tmem_store_rate(int64_t nwarps, int64_t width, int64_t iters) {
+  auto out = at::zeros({16}, at::TensorOptions().dtype(at::kLong).device(at::kCUDA));
+  check_rc(oscar_tmem_store_rate((int)nwarps, (int)width, (int)iters,
+                                 reinterpret_cast<unsigned long long*>(out.data_ptr<int64_t>()),
+                                 stream()),
+           "tmem_store_rate");
+  auto h = out.cpu();
+  std::vector<int64_t> r;
+  for (int w = 0; w < nwarps; ++w) r.push_back(h[w].item<int64_t>());
+  return r;
+}
 
 int64_t num_sms() { return oscar_num_sms(); }
 
@@ -666,6 +690,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_i8", &gemm_i8);
   m.def("attn_tc_trace", &attn_tc_trace);
   m.def("gdn_trace", &gdn_trace);
+  m.def("mma_rate", &mma_rate);
+  m.def("tmem_store_rate", &tmem_store_rate);
   m.def("gemm_i8_allreduce", &gemm_i8_allreduce);
   m.def("gemm_i8_split", &gemm_i8_split);
   m.def("gemm_i8_rs", &gemm_i8_rs);

@@ -67,6 +67,37 @@ OSCAR_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_
   }
 }
 
+// try_wait that suspends the thread in hardware until the phase completes or about
+// `hint_ns` pass (instead of returning at once): waiting warps issue no instructions.
+OSCAR_DEVICE bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait with sleeping polls (same bounds: the CTA abort flag is seen within one
+// hint, the budget within one hint of expiring).
+OSCAR_DEVICE bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                  int code, uint64_t budget_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > budget_ns) {
+      *abort_flag = 1;
+      record_status(status, code);
+      return false;
+    }
+  }
+}
+
 // ----------------------------------------------------------------- TMA
 // 2-D tiled load of one box into shared memory, completing on `bar`.
 // x is the innermost (contiguous) coordinate in elements; callers keep
@@ -88,6 +119,11 @@ OSCAR_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t
           smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
+}
+
+// Hint: bring `bytes` (a multiple of 16, 16-byte aligned source) into L2.
+OSCAR_DEVICE void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // ----------------------------------------------------------------- TMEM
@@ -144,6 +180,21 @@ OSCAR_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
       "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
       "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// 64 consecutive columns of this warp's 32 lanes in one store (two 32-column halves).
+OSCAR_DEVICE void tmem_st_32x32b_x64(uint32_t taddr, const uint32_t (&a)[32], const uint32_t (&b)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};" ::"r"(taddr),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]),
+      "r"(a[8]), "r"(a[9]), "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]), "r"(a[14]), "r"(a[15]),
+      "r"(a[16]), "r"(a[17]), "r"(a[18]), "r"(a[19]), "r"(a[20]), "r"(a[21]), "r"(a[22]), "r"(a[23]),
+      "r"(a[24]), "r"(a[25]), "r"(a[26]), "r"(a[27]), "r"(a[28]), "r"(a[29]), "r"(a[30]), "r"(a[31]),
+      "r"(b[0]), "r"(b[1]), "r"(b[2]), "r"(b[3]), "r"(b[4]), "r"(b[5]), "r"(b[6]), "r"(b[7]),
+      "r"(b[8]), "r"(b[9]), "r"(b[10]), "r"(b[11]), "r"(b[12]), "r"(b[13]), "r"(b[14]), "r"(b[15]),
+      "r"(b[16]), "r"(b[17]), "r"(b[18]), "r"(b[19]), "r"(b[20]), "r"(b[21]), "r"(b[22]), "r"(b[23]),
+      "r"(b[24]), "r"(b[25]), "r"(b[26]), "r"(b[27]), "r"(b[28]), "r"(b[29]), "r"(b[30]), "r"(b[31])
       : "memory");
 }
 OSCAR_DEVICE void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {

@@ -152,8 +152,9 @@ def kv_bytes(c, kv_mode: int) -> int:
     return c["pages"] * c["hk"] * per_page
 
 
-def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16_tc", "bf16"), hk=1):
-    c = build_case(hist, batch, qlen, hq=6 * hk, hk=hk)
+def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16_tc", "bf16"), hk=1,
+             staging=True):
+    c = build_case(hist, batch, qlen, hq=6 * hk, hk=hk, staging=staging)
     rows = qlen * c["hq"] // c["hk"]
     vs = [v for v in variants if not (v == "bf16_tc" and rows > 32)]
     # numerics: merged outputs against the first variant
@@ -188,29 +189,32 @@ def run_case(hist, batch, qlen, iters=10, variants=("int2_tc", "int2_mma", "bf16
 # 0 start, 1 setup done, 2 softmax role done, 3 end; 8+i page i copy issued, 16+i S(i)
 # issued, 24+i K(i) converted, 32+i V(i) converted, 40+i P(i) written; for pages 0-3 the
 # softmax marks 48+4i S ready, 49+4i S loaded, 50+4i P buffer free, 51+4i maxima agreed,
-# 64+4i metadata loaded, 65+4i score loop done, and slot 80+i the score loop's clock64 cycles.
+# 64+4i metadata loaded, 65+4i score loop done, slot 80+i the score loop's clock64 cycles,
+# 84+i K(i) conversion started, 88+i K(i) seen by the MMA issuer, 92+i V(i) conversion started;
+# clock64 cycles (pages 0-3): 96+i K conversion issue, 100+i its TMEM store wait, 104+i / 108+i
+# the same for V, 112+i issuing the S MMAs.  128 slots per CTA.
 TRACE_EVENTS = {"issue": (8, 16), "qk": (16, 24), "kdone": (24, 32), "vdone": (32, 40), "pdone": (40, 48)}
 
 
-def trace_case(hist: int, batch: int, qlen: int, show: int = 3, hk: int = 1) -> dict:
+def trace_case(hist: int, batch: int, qlen: int, show: int = 3, hk: int = 1, staging: bool = True) -> dict:
     """Per-CTA timeline of the tcgen05 INT2 decode kernel (one traced launch after warm-up).
 
     Returns the kernel span, the CTA duration quantiles and, for the ``show`` longest CTAs,
     every recorded event relative to the CTA's start (µs)."""
-    c = build_case(hist, batch, qlen, hq=6 * hk, hk=hk)
+    c = build_case(hist, batch, qlen, hq=6 * hk, hk=hk, staging=staging)
     fn = _kernel_only(c, 0, True)
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
     n_cta = c["plan"].n_work * c["hk"]
-    buf = torch.zeros(n_cta * 96, dtype=torch.int64, device=c["q"].device)
+    buf = torch.zeros(n_cta * 128, dtype=torch.int64, device=c["q"].device)
     ext().attn_tc_trace(buf.data_ptr())
     try:
         fn()
         torch.cuda.synchronize()
     finally:
         ext().attn_tc_trace(0)
-    t = buf.view(n_cta, 96).cpu().numpy().astype(np.float64)
+    t = buf.view(n_cta, 128).cpu().numpy().astype(np.float64)
     started = t[:, 0] > 0
     t0 = t[started, 0].min()
     rel = np.where(t[:, :80] > 0, (t[:, :80] - t0) / 1000.0, np.nan)
@@ -225,6 +229,14 @@ def trace_case(hist: int, batch: int, qlen: int, show: int = 3, hk: int = 1) -> 
         ev["softmax_pages"] = [[round(float(x - r[0]), 2) for x in r[48 + 4 * q:52 + 4 * q] if not np.isnan(x)]
                                for q in range(4)]
         ev["score_loop_cycles"] = [int(t[idx, 80 + q]) for q in range(4)]
+        ext_rel = np.where(t[idx, 84:96] > 0, (t[idx, 84:96] - t0) / 1000.0 - r[0], np.nan)
+        ev["kstart"] = [round(float(x), 2) for x in ext_rel[0:4] if not np.isnan(x)]
+        ev["mma_kfull"] = [round(float(x), 2) for x in ext_rel[4:8] if not np.isnan(x)]
+        ev["vstart"] = [round(float(x), 2) for x in ext_rel[8:12] if not np.isnan(x)]
+        cyc = t[idx, 96:116].astype(np.int64)
+        ev["cycles_k_issue"], ev["cycles_k_stwait"] = cyc[0:4].tolist(), cyc[4:8].tolist()
+        ev["cycles_v_issue"], ev["cycles_v_stwait"] = cyc[8:12].tolist(), cyc[12:16].tolist()
+        ev["cycles_s_mma_issue"] = cyc[16:20].tolist()
         out["ctas_shown"].append({"cta": int(idx), "work": c["plan"].work[idx % c["plan"].n_work].tolist(),
                                   "dur_us": round(float(dur[idx]), 2), "events": ev})
     return out
@@ -238,6 +250,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--hk", type=int, default=1, help="KV heads (6 query heads each); 4 is the TP1 model")
     ap.add_argument("--variants", default="int2_tc,int2_mma,bf16_tc,bf16")
+    ap.add_argument("--no-staging", action="store_true", help="no sink/recent staging window (all tokens INT2)")
     ap.add_argument("--prefill", action="store_true", help="also run the 9256-over-15360 continuation")
     ap.add_argument("--trace", action="store_true",
                     help="print the per-CTA timeline of the tcgen05 decode kernel instead of timing")
@@ -247,13 +260,14 @@ def main(argv=None):
         for hist in map(int, args.hist.split(",")):
             for batch in map(int, args.batch.split(",")):
                 for qlen in map(int, args.qlen.split(",")):
-                    print(json.dumps(trace_case(hist, batch, qlen, hk=args.hk)), flush=True)
+                    print(json.dumps(trace_case(hist, batch, qlen, hk=args.hk, staging=not args.no_staging)),
+                          flush=True)
         return
     for hist in map(int, args.hist.split(",")):
         for batch in map(int, args.batch.split(",")):
             for qlen in map(int, args.qlen.split(",")):
                 for r in run_case(hist, batch, qlen, args.iters, variants=tuple(args.variants.split(",")),
-                                  hk=args.hk):
+                                  hk=args.hk, staging=not args.no_staging):
                     print(json.dumps(r), flush=True)
     if args.prefill:
         for r in run_case(15360, 1, 9256, max(3, args.iters // 3), variants=("int2_tc", "int2_mma", "bf16")):
