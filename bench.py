@@ -150,6 +150,8 @@ def main():
     h2d0, d2h0 = eng.stats.get("h2d_bytes", 0), eng.stats.get("d2h_bytes", 0)
     eng.record_device_time = True
     eng.device_ms()
+    if eng.host_profile is not None:
+        eng.host_profile.clear()
     launches.reset()
     gpu_ids = None
     try:
@@ -192,6 +194,9 @@ def main():
         dist.all_reduce(tt[:1])
         dist.all_reduce(tt[1:], op=dist.ReduceOp.MAX)
         tokens, mem = int(round(tt[0].item())), float(tt[1].item())
+    if eng.host_profile is not None and rank == 0:  # OSCAR_HOST_PROFILE=1: host ms per step phase
+        print(json.dumps({"host_ms_per_step": {k: round(v * 1e3 / args.steps, 3)
+                                               for k, v in eng.host_profile.items()}}), file=sys.stderr, flush=True)
     value = tokens / (busy_ms / 1e3)
     e2e = tokens / wall
     steps_tok = tokens / args.steps / (R * args.dp)  # output tokens per request per step

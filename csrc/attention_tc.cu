@@ -30,9 +30,10 @@
 // columns (tokens 0-63 and 64-127 of a page, each 2 dim halves x 32; a slot is refilled
 // for the next page while the other half's P.V runs), [384,384+2N) two S^T buffers,
 // [448,448+2N) the O^T accumulator (2 halves).
-// A kind::f16 MMA of M = 128, N = 32, K = 16 costs ~100 cycles whatever its operand
-// sources (about a fifth of the tensor rate at N = 256), so a page's 33 MMAs are the
-// kernel's floor (~1.7 us); the buffers exist to keep the tensor pipe busy back to back.
+// A kind::f16 MMA of M = 128, K = 16 costs ~136 cycles for any N up to 256 whatever its
+// operand sources (bench/tcgen05_rates.py), so at N = 32 it runs at an eighth of the
+// tensor rate and a page's 33 MMAs are the kernel's floor (~2.3 us); the buffers exist
+// to keep the tensor pipe busy back to back.
 //
 // Softmax bookkeeping.  A row's running max only moves when some score of the
 // page exceeds it by more than 2^8 (the probabilities stay <= 256, well inside

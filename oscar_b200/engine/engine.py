@@ -21,6 +21,7 @@ overwritten by the next step.
 from __future__ import annotations
 
 import itertools
+import os
 import time
 from dataclasses import dataclass, field
 
@@ -128,6 +129,9 @@ class LLMEngine:
         self.stats = {"steps": 0, "tokens_out": 0, "drafts_proposed": 0, "drafts_accepted": 0}
         # device-busy time of the model work (CUDA events around every GPU segment)
         self.record_device_time = False
+        # OSCAR_HOST_PROFILE=1: seconds of host time per step phase (see _mark)
+        self.host_profile = {} if os.environ.get("OSCAR_HOST_PROFILE") == "1" else None
+        self._mark_t = 0.0
         self._events: list = []
         # CUDA graphs of the pure-decode (verify + drafting) steps
         self.use_graphs = model.device.type == "cuda"
@@ -542,7 +546,16 @@ class LLMEngine:
         self.stats["h2d_bytes"] = self.stats.get("h2d_bytes", 0) + 4 * ent["n"]
 
     # ------------------------------------------------------------------ step
+    def _mark(self, name: str) -> None:
+        """Host-time breakdown of steps (OSCAR_HOST_PROFILE=1): seconds since the previous mark."""
+        if self.host_profile is not None:
+            now = time.perf_counter()
+            self.host_profile[name] = self.host_profile.get(name, 0.0) + now - self._mark_t
+            self._mark_t = now
+
     def step(self) -> dict:
+        if self.host_profile is not None:
+            self._mark_t = time.perf_counter()
         sched = self._schedule()
         if not sched:
             return {}
@@ -574,9 +587,11 @@ class LLMEngine:
         lp_k = max((self.requests[rid].logprobs for rid, _, _, _ in info
                     if self.requests[rid].logprobs is not None), default=None)
         static = self.use_graphs and lp_k is None and all(kind == "verify" for _, kind, _, _ in info)
+        self._mark("schedule")
         if static:
             arrays, meta = self._arrays(rows, logit_rows, commit, keep, static=True, extra=sampled)
             b = (arrays, meta)
+            self._mark("main_metadata")
             with self._segment():
                 hid, tok = self._run_phase("main", [(arrays, meta)], lambda bs: self._main_fn(bs[0]))
         else:
@@ -585,7 +600,9 @@ class LLMEngine:
                 b.extra["logprobs_k"] = lp_k
             with self._segment():
                 hid, tok = self._main_fn(b)
+        self._mark("main_launch")
         tok_h = tok.tolist()
+        self._mark("main_wait")
         lp_h = None
         if lp_k is not None:
             tl, ti, tv = self.model.last_logprobs
@@ -646,6 +663,7 @@ class LLMEngine:
                     draft_rows.append((rid, base + n - 1))
             if r.first_token_time is None and r.output:
                 r.first_token_time = now
+        self._mark("accept")
         # ---------------- MTP drafting -----------------
         if self.num_spec > 0 and draft_rows:
             self._draft(b, hid, rows, next_row_tok, draft_rows)
@@ -659,6 +677,7 @@ class LLMEngine:
                 self.bm.free(rid)
                 self.slots.release(rid)
         self.stats["steps"] += 1
+        self._mark("retire")
         return {"scheduled": sched}
 
     @staticmethod
@@ -708,6 +727,7 @@ class LLMEngine:
                 # the MTP row after ``ri`` sits one position further; tokens come from the device
                 prow = [(rid, 0, rows[ri][2] + k) for rid, ri in draft_rows]
                 specs.append(self._arrays(prow, list(range(len(prow))), {}, {}, static=True))
+            self._mark("draft_metadata")
             with self._segment():
                 drafts_t = self._run_phase("mtp", specs, chain)
         else:
@@ -720,7 +740,9 @@ class LLMEngine:
                 later.append(self._build(prow, list(range(len(prow))), {}, {}))
             with self._segment():
                 drafts_t = chain([b] + later)
+        self._mark("draft_launch")
         d = drafts_t.tolist()
+        self._mark("draft_wait")
         self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * drafts_t.numel()
         for (rid, _), row in zip(draft_rows, d):
             self.requests[rid].drafts = [int(x) for x in row]
