@@ -129,6 +129,10 @@ class LLMEngine:
         self.stats = {"steps": 0, "tokens_out": 0, "drafts_proposed": 0, "drafts_accepted": 0}
         # device-busy time of the model work (CUDA events around every GPU segment)
         self.record_device_time = False
+        # Next-step metadata built while the drafting phase runs on the device (see
+        # _prepare_next); OSCAR_LOOKAHEAD=0 turns it off.
+        self.lookahead = os.environ.get("OSCAR_LOOKAHEAD", "1") != "0"
+        self._pre = None
         # OSCAR_HOST_PROFILE=1: seconds of host time per step phase (see _mark)
         self.host_profile = {} if os.environ.get("OSCAR_HOST_PROFILE") == "1" else None
         self._mark_t = 0.0
@@ -553,9 +557,81 @@ class LLMEngine:
             self.host_profile[name] = self.host_profile.get(name, 0.0) + now - self._mark_t
             self._mark_t = now
 
+    # ------------------------------------------------------------------ lookahead
+    def _steady(self, rids) -> bool:
+        """Every running request verifies its drafts this step, greedily, nothing waits."""
+        if not self.lookahead or self.num_spec <= 0 or self.offload is not None or self.waiting or not rids:
+            return False
+        for rid in rids:
+            r = self.requests[rid]
+            if not r.prefill_done or r.finished or r.sampling is not None or r.logprobs is not None:
+                return False
+        return True
+
+    def _prepare_next(self) -> None:
+        """Build the next verify step's metadata while this step's drafting runs.
+
+        In a steady decode step every running request verifies ``1 + num_spec`` rows at
+        known positions; only the draft tokens are not known until the drafts are read
+        back, so the rows carry placeholders that ``_take_prepared`` fills in.  Block
+        allocation is done here (it is idempotent); the host mirror of the staging owner
+        tags is snapshotted so that a discarded batch leaves no trace in it.
+        """
+        self._pre = None
+        rids = list(self.running)
+        if not self.use_graphs or not self._steady(rids):
+            return
+        n = 1 + self.num_spec
+        extra = 2 * self.num_spec + 2
+        reqs = [self.requests[rid] for rid in rids]
+        if not all(self.bm.can_allocate(rid, r.num_computed + n + extra) for rid, r in zip(rids, reqs)):
+            return
+        for rid, r in zip(rids, reqs):
+            self.bm.ensure(rid, r.num_computed + n + extra)
+        snapshot = self._owner_host.copy() if self.stage_rows else None
+        rows, logit_rows, commit, keep, info = [], [], {}, {}, []
+        for rid, r in zip(rids, reqs):
+            base = len(rows)
+            keep[rid] = True
+            logit_rows.extend(range(base, base + n))
+            commit[rid] = r.pending_commit
+            rows.append((rid, r.last_token, r.num_computed))
+            rows.extend((rid, 0, r.num_computed + i) for i in range(1, n))
+            info.append((rid, "verify", n, base))
+        arrays, meta = self._arrays(rows, logit_rows, commit, keep, static=True)
+        self._pre = dict(rids=tuple(rids), nc=tuple(r.num_computed for r in reqs), rows=rows, logit_rows=logit_rows,
+                         commit=commit, keep=keep, info=info, arrays=arrays, meta=meta, snapshot=snapshot)
+
+    def _take_prepared(self):
+        """The prepared batch with its draft tokens filled in, or None (and the staging
+        mirror restored) when the running set changed since it was built."""
+        pre, self._pre = self._pre, None
+        if pre is None:
+            return None
+        rids = tuple(self.running)
+        ok = (rids == pre["rids"] and self._steady(rids)
+              and tuple(self.requests[rid].num_computed for rid in rids) == pre["nc"]
+              and all(len(self.requests[rid].drafts) == self.num_spec for rid in rids))
+        if not ok:
+            if pre["snapshot"] is not None:
+                self._owner_host[:] = pre["snapshot"]
+            return None
+        toks, rows = pre["arrays"]["tokens"], pre["rows"]
+        for rid, _, n, base in pre["info"]:
+            d = self.requests[rid].drafts
+            for i in range(1, n):
+                toks[base + i] = d[i - 1]
+                rows[base + i] = (rid, d[i - 1], rows[base + i][2])
+        return pre
+
     def step(self) -> dict:
         if self.host_profile is not None:
             self._mark_t = time.perf_counter()
+        pre = self._take_prepared()
+        if pre is not None:
+            self.stats["lookahead_steps"] = self.stats.get("lookahead_steps", 0) + 1
+            return self._step_body(pre["rows"], pre["logit_rows"], pre["commit"], pre["keep"], pre["info"], None,
+                                   None, (pre["arrays"], pre["meta"]))
         sched = self._schedule()
         if not sched:
             return {}
@@ -584,12 +660,18 @@ class LLMEngine:
         if any(r.sampling is not None for r, _, _ in sp_rows):
             sampled = samp.host_rows([r.sampling for r, _, _ in sp_rows], [r.seed for r, _, _ in sp_rows],
                                      [p for _, p, _ in sp_rows], [d for _, _, d in sp_rows])
+        return self._step_body(rows, logit_rows, commit, keep, info, sampled, sched, None)
+
+    def _step_body(self, rows, logit_rows, commit, keep, info, sampled, sched, prepared):
         lp_k = max((self.requests[rid].logprobs for rid, _, _, _ in info
                     if self.requests[rid].logprobs is not None), default=None)
         static = self.use_graphs and lp_k is None and all(kind == "verify" for _, kind, _, _ in info)
         self._mark("schedule")
         if static:
-            arrays, meta = self._arrays(rows, logit_rows, commit, keep, static=True, extra=sampled)
+            if prepared is not None:
+                arrays, meta = prepared
+            else:
+                arrays, meta = self._arrays(rows, logit_rows, commit, keep, static=True, extra=sampled)
             b = (arrays, meta)
             self._mark("main_metadata")
             with self._segment():
@@ -678,7 +760,7 @@ class LLMEngine:
                 self.slots.release(rid)
         self.stats["steps"] += 1
         self._mark("retire")
-        return {"scheduled": sched}
+        return {"scheduled": sched if sched is not None else [(rid, kind, n) for rid, kind, n, _ in info]}
 
     @staticmethod
     def _record_lp(r: Request, lp_h, row0: int, n: int) -> None:
@@ -730,6 +812,8 @@ class LLMEngine:
             self._mark("draft_metadata")
             with self._segment():
                 drafts_t = self._run_phase("mtp", specs, chain)
+            self._mark("draft_launch")
+            self._prepare_next()  # overlaps the drafting on the device
         else:
             up = self._upload({"tokens": next_row_tok, "rows": rows_sel})
             b.tokens = up["tokens"]
@@ -740,7 +824,7 @@ class LLMEngine:
                 later.append(self._build(prow, list(range(len(prow))), {}, {}))
             with self._segment():
                 drafts_t = chain([b] + later)
-        self._mark("draft_launch")
+        self._mark("prepare_next")
         d = drafts_t.tolist()
         self._mark("draft_wait")
         self.stats["d2h_bytes"] = self.stats.get("d2h_bytes", 0) + 4 * drafts_t.numel()

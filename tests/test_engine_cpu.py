@@ -44,6 +44,31 @@ def test_batching_does_not_change_outputs():
     assert together == alone
 
 
+def _gen_static(lookahead: bool, prompts, n, acceptance=None):
+    """The graph-form (static metadata) step path on CPU, with or without building the next
+    step's metadata while the drafts are computed."""
+    m = HybridModel(tiny(num_layers=4), device="cpu", seed=1)
+    eng = LLMEngine(m, num_blocks=64, max_slots=4, max_batched_tokens=512, num_spec=3, acceptance=acceptance)
+    eng.use_graphs = True
+    eng.lookahead = lookahead
+    ids = [eng.add_request(p, k) for p, k in zip(prompts, n)]
+    while eng.has_work():
+        eng.step()
+    return [eng.requests[i].output for i in ids], eng
+
+
+def test_lookahead_metadata_gives_the_same_tokens():
+    # requests of different lengths: one finishes early, which invalidates a prepared batch
+    n = [9, 4, 7]
+    want, _ = _gen_static(False, PROMPTS, n)
+    got, eng = _gen_static(True, PROMPTS, n)
+    assert got == want
+    assert eng.stats.get("lookahead_steps", 0) > 0
+    want2, _ = _gen_static(False, PROMPTS, n, acceptance=SeededAcceptance(3, 2.0, seed=3))
+    got2, _ = _gen_static(True, PROMPTS, n, acceptance=SeededAcceptance(3, 2.0, seed=3))
+    assert got2 == want2
+
+
 def test_seeded_acceptance_mean():
     acc = SeededAcceptance(3, 2.0, seed=0)  # 2 of 3 drafts accepted on average
     draws = [acc(0) for _ in range(3000)]
