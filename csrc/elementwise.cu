@@ -7,7 +7,10 @@
 //   act_quant       bf16 -> int8, scale
 //   embed           token ids -> fp32 residual rows (bf16 table)
 //   argmax          per-row (value, index) of bf16 logits, vocab-parallel aware
+#include <cstdlib>
+
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace oscar {
 namespace {
@@ -356,6 +359,10 @@ __global__ void __launch_bounds__(NT) rmsnorm_ag_kernel(float* __restrict__ x, l
                                                       const float* __restrict__ w, float off, float eps, int H,
                                                       RankWait rw, AgTargets ag) {
   __shared__ float red[NT / 32];
+  // launched as a programmatic dependent of the reduce-scatter GEMM: resident early, it
+  // touches nothing before that GEMM has completed
+  sm100::griddep_wait();
+  pdl_trigger();
   wait_ranks(rw);
   __syncthreads();
   const int tl = blockIdx.x;
@@ -454,8 +461,34 @@ __global__ void __launch_bounds__(NT) rmsnorm_ag_kernel(float* __restrict__ x, l
 // next kernel, launched as a programmatic dependent, may start meanwhile and fetch
 // whatever does not depend on the wait (the GEMM's weights).
 __global__ void wait_flags_kernel(RankWait rw) {
-  pdl_trigger();
+  pdl_trigger();          // the consuming GEMM may start its weight prefetch
+  sm100::griddep_wait();  // the expected epoch is written by the preceding norm
   wait_ranks(rw);
+}
+
+// Programmatic dependent launch (on unless OSCAR_PDL=0): the kernel may become resident
+// while its predecessor drains; it calls griddepcontrol.wait before reading anything
+// that predecessor writes.
+bool ew_pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("OSCAR_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = ew_pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 // fp32 residual rows -> bf16 (final hidden state for the lm_head / MTP head).
@@ -518,14 +551,15 @@ extern "C" int oscar_rmsnorm_ag(float* x, long long ldx, const float* delta, lon
   constexpr int NT = 256;
   RankWait rw{rs_signals, rs_epoch, world, status, (uint64_t)(budget_ns > 0 ? budget_ns : 5000000000ll)};
   const int grid = rows > 0 ? rows : 1;
-  OSCAR_PV_DISPATCH(H / 4, NT, (rmsnorm_ag_kernel<NT, PV><<<grid, NT, 0, s>>>(x, ldx, delta, ldd, n_slots, slot_stride, w, off, eps, H, rw, ag)));
+  OSCAR_PV_DISPATCH(H / 4, NT, OSCAR_RC(launch_pdl(rmsnorm_ag_kernel<NT, PV>, dim3(grid), dim3(NT), s, x, ldx, delta, ldd,
+                                                   n_slots, slot_stride, w, off, eps, H, rw, ag)));
   return (int)cudaGetLastError();
 }
 
 extern "C" int oscar_wait_flags(const unsigned* signals, const int* epoch, int world, int* status, long long budget_ns,
                                 cudaStream_t s) {
   RankWait rw{signals, epoch, world, status, (uint64_t)(budget_ns > 0 ? budget_ns : 5000000000ll)};
-  wait_flags_kernel<<<1, 32, 0, s>>>(rw);
+  OSCAR_RC(launch_pdl(wait_flags_kernel, dim3(1), dim3(32), s, rw));
   return (int)cudaGetLastError();
 }
 
