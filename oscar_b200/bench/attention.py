@@ -34,18 +34,11 @@ from ..kv import format as fmt
 from ..ops import attention as A
 from ..ops import functional as F
 from ..ops._ext import ext
-from .harness import compare_calls
+from .harness import compare_calls, peak_hbm_gbs
 
 
 def _peak_gbs() -> float:
-    here = os.path.dirname(os.path.abspath(__file__))
-    for p in (os.path.join(here, "..", "..", "MEASURED_PEAKS.json"),):
-        try:
-            with open(p) as f:
-                return float(json.load(f)["hbm_gbs"])
-        except (OSError, KeyError, ValueError):
-            pass
-    return 6650.0  # earlier measurement on this pool when the file is absent
+    return peak_hbm_gbs()
 
 
 def build_case(hist: int, batch: int, qlen: int, hq: int = 6, hk: int = 1, D: int = 256, seed: int = 0,

@@ -23,7 +23,7 @@ import sys
 import torch
 
 from ..ops.gdn import gdn_step
-from .harness import time_call
+from .harness import time_call, peak_hbm_gbs
 
 
 def run(tp: int, tokens: int, requests: int, iters: int, decode: bool = False, qlen: int = 4,
@@ -102,12 +102,7 @@ def _trace(call, n_cta: int) -> dict:
 
 
 def _peak_gbs() -> float:
-    here = os.path.dirname(os.path.abspath(__file__))
-    try:
-        with open(os.path.join(here, "..", "..", "MEASURED_PEAKS.json")) as f:
-            return float(json.load(f)["hbm_gbs"])
-    except (OSError, KeyError, ValueError):
-        return 6650.0  # earlier measurement on this pool when the file is absent
+    return peak_hbm_gbs()
 
 
 def main(argv=None):

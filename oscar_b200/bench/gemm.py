@@ -20,17 +20,11 @@ import os
 import torch
 
 from ..ops import functional as F
-from .harness import time_call
+from .harness import peak_bf16_tflops, peak_hbm_gbs, time_call
 
 
 def _peaks() -> tuple[float, float]:
-    here = os.path.dirname(os.path.abspath(__file__))
-    try:
-        with open(os.path.join(here, "..", "..", "MEASURED_PEAKS.json")) as f:
-            j = json.load(f)
-        return float(j.get("hbm_gbs", 6650.0)), float(j.get("bf16_tflops", 1590.0))
-    except (OSError, ValueError):
-        return 6650.0, 1590.0
+    return peak_hbm_gbs(), peak_bf16_tflops()
 
 
 def shapes(tp: int, H: int = 5120, I: int = 17408):

@@ -7,6 +7,8 @@ than L2 is written so that every timed call starts with a cold cache.
 """
 from __future__ import annotations
 
+import os
+
 import statistics
 from dataclasses import dataclass
 
@@ -69,3 +71,14 @@ def compare_calls(variants: dict, iters: int = 10, rtol: float = 1e-2, flush: bo
         for n in order:
             samples[n].append(time_call(variants[n], flush))
     return {n: Timing(first[n], statistics.median(samples[n]), samples[n]) for n in names}
+
+
+# Roofline denominators: a STREAM-style copy and a burst cuBLAS bf16 GEMM measured on the
+# B200s these benchmarks were developed on; override with OSCAR_PEAK_HBM_GBS /
+# OSCAR_PEAK_BF16_TFLOPS for another machine.
+def peak_hbm_gbs() -> float:
+    return float(os.environ.get("OSCAR_PEAK_HBM_GBS", "6554.9"))
+
+
+def peak_bf16_tflops() -> float:
+    return float(os.environ.get("OSCAR_PEAK_BF16_TFLOPS", "1661.4"))
