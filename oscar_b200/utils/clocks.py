@@ -4,10 +4,12 @@ Read-only: it only queries clocks; it never changes any GPU setting.
 """
 from __future__ import annotations
 
+import os
 import shutil
 import statistics
 import subprocess
 import tempfile
+import time
 
 FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
           "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -16,9 +18,17 @@ REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_powe
 
 
 class ClockSampler:
-    def __init__(self, gpu_ids: list[str] | None = None, period_ms: int = 200):
+    """``nvidia-smi -lms`` in a child process for the duration of a ``with`` block.
+
+    ``nvidia-smi`` takes a few hundred ms to print its first line, longer than a short timed
+    region (5 decode steps at TP8 is ~100 ms), so ``__enter__`` waits until the first sample
+    is written (at most ``first_sample_s``) before it returns.
+    """
+
+    def __init__(self, gpu_ids: list[str] | None = None, period_ms: int = 100, first_sample_s: float = 5.0):
         self.gpu_ids = gpu_ids
         self.period_ms = period_ms
+        self.first_sample_s = first_sample_s
         self.proc = None
         self.out = None
 
@@ -31,6 +41,11 @@ class ClockSampler:
         if self.gpu_ids:
             cmd.append("-i=" + ",".join(self.gpu_ids))
         self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
+        deadline = time.monotonic() + self.first_sample_s
+        while time.monotonic() < deadline and self.proc.poll() is None:
+            if os.path.getsize(self.out.name) > 0:
+                break
+            time.sleep(0.01)
         return self
 
     def __exit__(self, *exc):
