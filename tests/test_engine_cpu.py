@@ -180,6 +180,41 @@ def test_tp4_with_replicated_kv_heads_matches_single_rank():
     assert err < 0.15, err
 
 
+def _dp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from oscar_b200.parallel.groups import init_distributed, make_groups
+    import torch.distributed as dist
+    init_distributed("gloo", timeout_s=180)
+    try:
+        tp = make_groups(tp=2, dp=2)
+        mine = PROMPTS[:2] if tp.dp_rank == 0 else PROMPTS[2:]  # the request split of ``bench.py --dp``
+        out, _ = _gen(tp=tp, prompts=mine)
+        q.put((rank, tp.dp_rank, tp.rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dp2_tp2_replicas_serve_their_own_requests():
+    """DP2 x TP2 on four ranks: two replicas of two consecutive ranks, each running its own
+    requests with its TP collectives on its own subgroup at the same time.  The two ranks of
+    a replica agree exactly, and each replica's first tokens match TP=1 on the same prompts
+    (later tokens may differ by the per-shard activation quantisation, as in the TP=2 test)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = {r: (d, t, out) for r, d, t, out in (q.get(timeout=600) for _ in procs)}
+    for p in procs:
+        p.join(60)
+    assert [(res[r][0], res[r][1]) for r in range(4)] == [(0, 0), (0, 1), (1, 0), (1, 1)]
+    assert res[0][2] == res[1][2] and res[2][2] == res[3][2]
+    single, _ = _gen()
+    assert [o[0] for o in res[0][2] + res[2][2]] == [o[0] for o in single]
+
+
 def test_reused_state_slot_starts_from_zero_state():
     """A request that takes over a freed GDN state slot starts from a zero recurrent
     state and conv window, not from the previous occupant's: with one slot, requests
